@@ -1,0 +1,406 @@
+"""Benchmark of the quantized-linear hot path (one JSON line on rank 0).
+
+Default workload = BASELINE config 1: AWQ W4A16 linear, K=4096, N=14336,
+group 128, swept over M in {1, 16, 128, 1024, 4096} (decode GEMV through
+prefill GEMM).  One *step* = one call of the AWQ linear at every M of the
+sweep (5 launches).  ``value`` = sweep FLOPs / device time (TFLOP/s), inputs
+resident in HBM; ``e2e`` = the same metric through the public API with host
+(pinned) activations copied in and outputs copied back inside the timed region.
+
+L2 hygiene: the timed loop rotates over enough weight copies that the set
+streamed between two uses of a copy exceeds 2x the 126 MB L2.
+
+``--workload fp8`` runs config 2 instead (FP8 W8A8, (K,N)=(4096,28672),
+M in {1, 32, 512, 8192}) for measurement; the default line is config 1.
+
+``--impl reference`` times the reference side on the same workload: the
+reference has no CPU implementation of this path, so the CPU restatement in
+oracle/ (OpenMP, all host threads) is timed on a bounded sample; where the
+reference's own linear_fwd was compiled (oracle/_ref) its GPU time on the
+dequantised weights is reported next to it.
+
+Multi-GPU (torchrun, one process per GPU): every rank runs the same sweep on
+its own GPU with its own weights (replicas, weak scaling, no collective on the
+data path); timing is the max over ranks.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import pathlib
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+import torch
+
+ROOT = pathlib.Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+AWQ_K, AWQ_N, AWQ_G = 4096, 14336, 128
+AWQ_MS = [1, 16, 128, 1024, 4096]
+FP8_K, FP8_N = 4096, 28672
+FP8_MS = [1, 32, 512, 8192]
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d, "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    """nvidia-smi sampling during the timed region (SM clock, throttle reasons)."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+        self.t = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (OSError, ValueError):
+            self.proc = None
+            return
+        self.t = threading.Thread(target=self._read, daemon=True)
+        self.t.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self.t:
+            self.t.join(timeout=2)
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# --------------------------------------------------------------- workloads
+def awq_weights(device, copies, seed=0):
+    """Seeded config-1 AWQ weights (draw order q, z, s), `copies` independent copies
+    made by rotating the packed words so every copy is distinct memory."""
+    rng = np.random.default_rng(seed)
+    K, N, g = AWQ_K, AWQ_N, AWQ_G
+    q = rng.integers(0, 16, size=(K, N), dtype=np.int64).astype(np.uint32)
+    z = rng.integers(0, 16, size=(K // g, N), dtype=np.int64).astype(np.uint32)
+    s = rng.uniform(0.001, 0.02, size=(K // g, N)).astype(np.float16)
+    order = np.array([0, 2, 4, 6, 1, 3, 5, 7])
+    sh = (4 * np.arange(8, dtype=np.uint32))
+
+    def pack(a):
+        a = a.reshape(a.shape[0], -1, 8)[:, :, order]
+        return (a << sh).sum(axis=2, dtype=np.uint64).astype(np.uint32).view(np.int32)
+
+    qw = torch.from_numpy(pack(q)).to(device)
+    qz = torch.from_numpy(pack(z)).to(device)
+    sc = torch.from_numpy(s).to(device)
+    out = []
+    for c in range(copies):
+        out.append((qw.roll(c, 0).contiguous() if c else qw, qz, sc))
+    return out
+
+
+def awq_flops(M):
+    return 2.0 * M * AWQ_K * AWQ_N
+
+
+def awq_bytes(M):
+    K, N, g = AWQ_K, AWQ_N, AWQ_G
+    return K * N / 2 + (K // g) * (N // 8) * 4 + (K // g) * N * 2 + 2 * M * K + 2 * M * N
+
+
+def fp8_flops(M):
+    return 2.0 * M * FP8_K * FP8_N
+
+
+def fp8_bytes(M):
+    return 2 * M * FP8_K + FP8_N * FP8_K + 4 * FP8_N + 2 * M * FP8_N
+
+
+# ------------------------------------------------------------------ timing
+def time_sweep(calls, steps, warmup, stream):
+    """calls: list of (name, fn).  Returns (total_ms, per-call mean ms)."""
+    for _ in range(warmup):
+        for _, fn in calls:
+            fn(0)
+    torch.cuda.synchronize()
+    ev = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in calls] for _ in range(steps)]
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for i in range(steps):
+        for j, (_, fn) in enumerate(calls):
+            ev[i][j][0].record(stream)
+            fn(i + 1)
+            ev[i][j][1].record(stream)
+    t1.record(stream)
+    torch.cuda.synchronize()
+    total = t0.elapsed_time(t1)
+    per = [sum(ev[i][j][0].elapsed_time(ev[i][j][1]) for i in range(steps)) / steps
+           for j in range(len(calls))]
+    return total, per
+
+
+def max_over_ranks(v, dist_on, device):
+    if not dist_on:
+        return v
+    import torch.distributed as dist
+    t = torch.tensor([v], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def run_awq(args, device, dist_on, world, rank):
+    import lmrs_b200 as L
+    copies = 8
+    W = awq_weights(device, copies)
+    K, N, g = AWQ_K, AWQ_N, AWQ_G
+    gen = torch.Generator(device="cpu").manual_seed(1)
+    xs = {M: torch.randn(M, K, generator=gen).half().to(device) for M in AWQ_MS}
+    ys = {M: torch.empty(M, N, dtype=torch.float16, device=device) for M in AWQ_MS}
+    stream = torch.cuda.current_stream(device)
+
+    def mk(M):
+        def f(i):
+            qw, qz, sc = W[i % copies]
+            L.awq_linear(xs[M], qw, qz, sc, None, g, out=ys[M])
+        return f
+
+    calls = [(f"M={M}", mk(M)) for M in AWQ_MS]
+    if dist_on:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    clk = ClockSampler(torch.cuda.current_device() if "CUDA_VISIBLE_DEVICES" not in os.environ
+                       else int(os.environ["CUDA_VISIBLE_DEVICES"].split(",")[torch.cuda.current_device()]))
+    clk.start()
+    total_ms, per_ms = time_sweep(calls, args.steps, args.warmup, stream)
+    clocks = clk.stop()
+    if dist_on:
+        torch.distributed.barrier()
+    total_ms = max_over_ranks(total_ms, dist_on, device)
+    flops_step = sum(awq_flops(M) for M in AWQ_MS)
+    ms_step = total_ms / args.steps
+    value = world * flops_step / (ms_step * 1e-3) / 1e12
+
+    # ---- e2e: host activations in (pinned), outputs back, through the public API
+    hx = {M: xs[M].cpu().pin_memory() for M in AWQ_MS}
+    hy = {M: torch.empty(M, N, dtype=torch.float16).pin_memory() for M in AWQ_MS}
+
+    def e2e_step(i):
+        for M in AWQ_MS:
+            qw, qz, sc = W[i % copies]
+            xd = hx[M].to(device, non_blocking=True)
+            y = L.awq_linear(xd, qw, qz, sc, None, g)
+            hy[M].copy_(y, non_blocking=True)
+
+    for i in range(args.warmup):
+        e2e_step(i)
+    torch.cuda.synchronize()
+    if dist_on:
+        torch.distributed.barrier()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for i in range(args.steps):
+        e2e_step(i + 1)
+    b.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(a.elapsed_time(b) / args.steps, dist_on, device)
+    h2d = sum(2 * M * K for M in AWQ_MS)
+    d2h = sum(2 * M * N for M in AWQ_MS)
+
+    pk, pk_kind = peaks()
+    sweep = []
+    for M, t in zip(AWQ_MS, per_ms):
+        bound = "hbm" if M <= 64 else "tensor"
+        gbs = awq_bytes(M) / (t * 1e-3) / 1e9
+        tfl = awq_flops(M) / (t * 1e-3) / 1e12
+        frac = gbs / pk["hbm_gbs"] if bound == "hbm" else tfl / pk["bf16_tflops"]
+        sweep.append({"M": M, "us": round(t * 1e3, 2), "GB_s": round(gbs, 1),
+                      "TFLOP_s": round(tfl, 2), "bound": bound, "frac": round(frac, 4)})
+    # dominant kernel: the one with the largest share of step time
+    dom = max(range(len(AWQ_MS)), key=lambda j: per_ms[j])
+    Md = AWQ_MS[dom]
+    ach = awq_flops(Md) / (per_ms[dom] * 1e-3) / 1e12
+    roof = {"bound": "tensor", "kernel": f"awq_gemm_tc_kernel (M={Md})", "achieved": round(ach, 2),
+            "peak": pk["bf16_tflops"], "unit": "TFLOP/s", "frac": round(ach / pk["bf16_tflops"], 4),
+            "peak_source": f"{pk_kind} bf16 dense (burst)", "traffic": None,
+            "algorithmic_bytes": awq_bytes(Md), "algorithmic_flops": awq_flops(Md)}
+    return dict(
+        metric="awq_w4a16_linear_throughput_config1_sweep", value=round(value, 3), unit="TFLOP/s",
+        ms_per_step=round(ms_step, 4), dtype="f16 (int4 weights, fp32 accumulate)",
+        config={"workload": "config1: AWQ W4A16 K=4096 N=14336 g=128, M in {1,16,128,1024,4096}",
+                "global_batch": sum(AWQ_MS), "parallelism": f"replicas{world}",
+                "l2": f"rotating {copies} weight copies ({copies * awq_bytes(0) / 1e6:.0f} MB > 2x L2)"},
+        roofline=roof, sweep=sweep, clocks=clocks,
+        e2e={"value": round(world * flops_step / (e2e_ms * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
+             "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        gpu_launches=args.steps * len(AWQ_MS),
+        _peaks=pk, _weights=W)
+
+
+def cpu_baseline_awq(nthreads, ms=(1, 16, 128, 1024)):
+    """Oracle (CPU restatement, OpenMP) over a bounded sample of the sweep."""
+    from oracle import oracle as O
+    d = O.awq_inputs(max(ms), AWQ_K, AWQ_N, AWQ_G, seed=0)
+    t = 0.0
+    fl = 0.0
+    for M in ms:
+        x = np.ascontiguousarray(d["x"][:M])
+        t0 = time.perf_counter()
+        O.c_awq_linear(x, d["qweight"], d["qzeros"], d["scales"], None, M, AWQ_K, AWQ_N, AWQ_G,
+                       nthreads=nthreads)
+        t += time.perf_counter() - t0
+        fl += awq_flops(M)
+    return {"value": round(fl / t / 1e12, 5), "unit": "TFLOP/s", "cores": nthreads, "kind": "port",
+            "sample": f"one AWQ linear (dequant + fp32-FMA GEMM) at each M in {list(ms)}, "
+                      f"K=4096 N=14336; M=4096 omitted to bound CPU time ({t:.1f} s)"}
+
+
+def ref_gpu_linear_fwd(device, W, steps=2):
+    """The reference's own linear_fwd (oracle/_ref) on the dequantised config-1 weights."""
+    import ctypes
+    so = ROOT / "oracle" / "_ref" / "libref_ffi.so"
+    if not so.exists():
+        return None
+    import lmrs_b200 as L
+    lib = ctypes.CDLL(str(so))
+    P, I = ctypes.c_void_p, ctypes.c_int
+    lib.linear_fwd.argtypes = [P, P, P, P, I, I, I, I, P]
+    qw, qz, sc = W[0]
+    w_nk = L.awq_dequant(qw, qz, sc, AWQ_G).t().contiguous()
+    stream = torch.cuda.current_stream(device)
+    res = []
+    tot_fl, tot_ms = 0.0, 0.0
+    for M in AWQ_MS:
+        x = torch.randn(M, AWQ_K, device=device).half()
+        y = torch.empty(M, AWQ_N, dtype=torch.float16, device=device)
+        call = lambda: lib.linear_fwd(P(y.data_ptr()), P(x.data_ptr()), P(w_nk.data_ptr()), None,
+                                      M, AWQ_K, AWQ_N, 1, P(stream.cuda_stream))
+        call()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(steps):
+            call()
+        b.record(stream)
+        torch.cuda.synchronize()
+        ms = a.elapsed_time(b) / steps
+        tot_fl += awq_flops(M)
+        tot_ms += ms
+        res.append({"M": M, "us": round(ms * 1e3, 1), "TFLOP_s": round(awq_flops(M) / ms / 1e9, 3)})
+    return {"kernel": "reference linear_fwd (kernels/ffi/tensor_ffi.cu, sm_100a, fp16, "
+                      "on dequantised weights)",
+            "value": round(tot_fl / (tot_ms * 1e-3) / 1e12, 4), "unit": "TFLOP/s", "sweep": res}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["lmrs", "reference"], default="lmrs")
+    ap.add_argument("--workload", choices=["awq", "fp8"], default="awq")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dist_on = world > 1
+    if dist_on:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    nthreads = os.cpu_count() or 1
+
+    if args.impl == "reference":
+        if rank != 0:
+            if dist_on:
+                torch.distributed.destroy_process_group()
+            return
+        cb = cpu_baseline_awq(nthreads)
+        W = awq_weights(device, 1)
+        rg = ref_gpu_linear_fwd(device, W)
+        line = {"metric": "awq_w4a16_linear_throughput_config1_sweep", "value": cb["value"],
+                "unit": "TFLOP/s", "impl": "reference", "n_gpus": args.gpus, "steps": 1,
+                "warmup": 0, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "f16 (int4 weights, fp32 accumulate)", "data": "synthetic (seed 0)",
+                "config": {"workload": "config1: AWQ W4A16 K=4096 N=14336 g=128, "
+                                       "M in {1,16,128,1024,4096}", "parallelism": "cpu"},
+                "cpu_baseline": cb,
+                "e2e": {"value": cb["value"], "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0},
+                "note": "the reference has no CPU implementation of this path (no Candle in "
+                        "Cargo.lock); the CPU restatement in oracle/ stands in for it",
+                "reference_gpu": rg}
+        print(json.dumps(line), flush=True)
+        if dist_on:
+            torch.distributed.destroy_process_group()
+        return
+
+    res = run_awq(args, device, dist_on, world, rank)
+    W = res.pop("_weights")
+    res.pop("_peaks")
+    if rank == 0:
+        line = {"metric": res.pop("metric"), "value": res.pop("value"), "unit": res.pop("unit"),
+                "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": res.pop("ms_per_step"), "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": res.pop("dtype"),
+                "data": "synthetic (seeded AWQ weights/activations, config-1 distributions)"}
+        line.update(res)
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline_awq(nthreads)
+        print(json.dumps(line), flush=True)
+    if dist_on:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

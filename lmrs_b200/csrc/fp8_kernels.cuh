@@ -1,0 +1,235 @@
+// fp8_kernels.cuh — FP8 e4m3 W8A8: per-row quantisation and the decode GEMV.
+//
+// Quantisation (per token for activations, per output channel for weights):
+//   s[r] = absmax_k |x[r,k]| / 448 (fp32 IEEE division),
+//   q[r,k] = e4m3 RNE satfinite (x[r,k] / s[r])   (IEEE division, then cvt),
+//   rows with s == 0 quantise to 0.
+// One CTA per row: pass 1 reduces the absmax with 16-byte loads, pass 2 re-reads
+// the row (L1/L2 resident) and writes 8 e4m3 per thread per step.
+//
+// Decode GEMV (small M), swap-AB mma.sync m16n8k32 e4m3 x e4m3 -> fp32:
+// output channels are the MMA "M" rows (W's K-contiguous rows are exactly the
+// row-major A fragment), tokens are "N".  Each lane streams 16-byte chunks of
+// two weight rows per 128-byte K unit (ld.global.nc.L1::no_allocate).  The 32
+// k-slots of the four MMAs of a unit are a permutation of the unit's 128 bytes
+// chosen so that every lane's A bytes are two contiguous 16-byte chunks; the
+// token fragment is gathered with the same permutation.  Split-K across the
+// warps of a CTA and across a thread-block cluster, reduced in (distributed)
+// shared memory, scaled by s_x[m] * s_w[n] in the epilogue.
+#pragma once
+#include <cooperative_groups.h>
+#include "lmrs_ptx.cuh"
+
+namespace lmrs {
+namespace cg = cooperative_groups;
+
+template <int DT>
+struct IoType;
+template <>
+struct IoType<0> {
+  using T = __nv_bfloat16;
+  static __device__ __forceinline__ float to_f(T v) { return __bfloat162float(v); }
+};
+template <>
+struct IoType<1> {
+  using T = __half;
+  static __device__ __forceinline__ float to_f(T v) { return __half2float(v); }
+};
+template <>
+struct IoType<2> {
+  using T = float;
+  static __device__ __forceinline__ float to_f(T v) { return v; }
+};
+
+constexpr int kQuantThreads = 256;
+
+template <int DT>
+__global__ void __launch_bounds__(kQuantThreads) fp8_quant_rows_kernel(
+    uint8_t* __restrict__ q, float* __restrict__ scale, const typename IoType<DT>::T* __restrict__ x,
+    int K) {
+  using T = typename IoType<DT>::T;
+  constexpr int VEC = 16 / sizeof(T);  // elements per 16-byte load
+  __shared__ float red[kQuantThreads / 32];
+  const int row = blockIdx.x;
+  const T* xr = x + static_cast<int64_t>(row) * K;
+  uint8_t* qr = q + static_cast<int64_t>(row) * K;
+
+  float amax = 0.f;
+  for (int k = threadIdx.x * VEC; k < K; k += kQuantThreads * VEC) {
+    const uint4 v = __ldg(reinterpret_cast<const uint4*>(xr + k));
+    const T* e = reinterpret_cast<const T*>(&v);
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) amax = fmaxf(amax, fabsf(IoType<DT>::to_f(e[i])));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
+  __syncthreads();
+  float m = red[0];
+#pragma unroll
+  for (int w = 1; w < kQuantThreads / 32; ++w) m = fmaxf(m, red[w]);
+  const float s = __fdiv_rn(m, 448.0f);
+  if (threadIdx.x == 0) scale[row] = s;
+
+  // 8 elements per step -> one 8-byte store
+  for (int k = threadIdx.x * 8; k < K; k += kQuantThreads * 8) {
+    float f[8];
+    if (sizeof(T) == 2) {
+      const uint4 v = __ldg(reinterpret_cast<const uint4*>(xr + k));
+      const T* e = reinterpret_cast<const T*>(&v);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) f[i] = IoType<DT>::to_f(e[i]);
+    } else {
+      const uint4 v0 = __ldg(reinterpret_cast<const uint4*>(xr + k));
+      const uint4 v1 = __ldg(reinterpret_cast<const uint4*>(xr + k) + 1);
+      f[0] = __uint_as_float(v0.x); f[1] = __uint_as_float(v0.y);
+      f[2] = __uint_as_float(v0.z); f[3] = __uint_as_float(v0.w);
+      f[4] = __uint_as_float(v1.x); f[5] = __uint_as_float(v1.y);
+      f[6] = __uint_as_float(v1.z); f[7] = __uint_as_float(v1.w);
+    }
+    uint32_t out[2] = {0u, 0u};
+    if (s != 0.f) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 pr = make_float2(__fdiv_rn(f[2 * i], s), __fdiv_rn(f[2 * i + 1], s));
+        const uint32_t b = static_cast<uint32_t>(__nv_cvt_float2_to_fp8x2(pr, __NV_SATFINITE, __NV_E4M3));
+        out[i >> 1] |= b << ((i & 1) * 16);
+      }
+    }
+    *reinterpret_cast<uint2*>(qr + k) = make_uint2(out[0], out[1]);
+  }
+}
+
+// ------------------------------------------------------------------ GEMV
+__device__ __forceinline__ uint4 ldg_stream_u4(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+__device__ __forceinline__ void mma_e4m3_16832(float (&d)[4], uint32_t a0, uint32_t a1,
+                                               uint32_t a2, uint32_t a3, uint32_t b0,
+                                               uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.f32.e4m3.e4m3.f32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+constexpr int kF8GemvRows = 32;  // output channels per warp strip (two 16-row MMA tiles)
+
+template <int MT>
+__global__ void __launch_bounds__(256) fp8_gemv_kernel(
+    __nv_bfloat16* __restrict__ y, const uint8_t* __restrict__ xq, const float* __restrict__ sx,
+    const uint8_t* __restrict__ wq, const float* __restrict__ sw,
+    const __nv_bfloat16* __restrict__ bias, int M, int K, int N) {
+  constexpr int MP = 8 * MT;
+  constexpr int R = kF8GemvRows / 16;
+  extern __shared__ __align__(16) float red[];  // [W][MP][32]
+
+  cg::cluster_group cluster = cg::this_cluster();
+  const int C = static_cast<int>(cluster.num_blocks());
+  const int rank = static_cast<int>(cluster.block_rank());
+  const int strip = blockIdx.x / C;
+  const int W = blockDim.x >> 5;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int nbase = strip * kF8GemvRows;
+
+  const int units = (K + 127) >> 7;
+  const int KS = C * W;
+  const int slice = rank * W + warp;
+  const int u0 = static_cast<int>((static_cast<long long>(slice) * units) / KS);
+  const int u1 = static_cast<int>((static_cast<long long>(slice + 1) * units) / KS);
+
+  float acc[MT][R][4];
+#pragma unroll
+  for (int a = 0; a < MT; ++a)
+#pragma unroll
+    for (int b = 0; b < R; ++b)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) acc[a][b][c] = 0.f;
+
+  const uint4 zero4 = make_uint4(0u, 0u, 0u, 0u);
+  for (int u = u0; u < u1; ++u) {
+    const int kb = u << 7;
+    const int ka = kb + 16 * t, kc = kb + 64 + 16 * t;  // this lane's two 16-byte chunks
+    const bool oka = ka < K, okc = kc < K;
+    uint4 wa[R][2][2];  // [tile][row g / g+8][chunk a / c]
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int n = nbase + 16 * r + 8 * h + g;
+        const uint8_t* wr = wq + static_cast<int64_t>(n) * K;
+        const bool nok = n < N;
+        wa[r][h][0] = (nok && oka) ? ldg_stream_u4(wr + ka) : zero4;
+        wa[r][h][1] = (nok && okc) ? ldg_stream_u4(wr + kc) : zero4;
+      }
+    uint4 xb[MT][2];
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt) {
+      const int m = mt * 8 + g;
+      const uint8_t* xr = xq + static_cast<int64_t>(m) * K;
+      xb[mt][0] = (m < M && oka) ? __ldg(reinterpret_cast<const uint4*>(xr + ka)) : zero4;
+      xb[mt][1] = (m < M && okc) ? __ldg(reinterpret_cast<const uint4*>(xr + kc)) : zero4;
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int c = j >> 1;
+      const bool hi = j & 1;
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        const uint4 g0 = wa[r][0][c], g8 = wa[r][1][c];
+        const uint32_t a0 = hi ? g0.z : g0.x, a2 = hi ? g0.w : g0.y;
+        const uint32_t a1 = hi ? g8.z : g8.x, a3 = hi ? g8.w : g8.y;
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt) {
+          const uint4 xv = xb[mt][c];
+          mma_e4m3_16832(acc[mt][r], a0, a1, a2, a3, hi ? xv.z : xv.x, hi ? xv.w : xv.y);
+        }
+      }
+    }
+  }
+
+  // partials: D rows g / g+8 = channels 16r+g / 16r+g+8, cols 2t, 2t+1 = tokens
+  float* rw = red + static_cast<size_t>(warp) * MP * kF8GemvRows;
+#pragma unroll
+  for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const int ch = 16 * r + g;
+      const int m0 = mt * 8 + 2 * t;
+      rw[(m0 + 0) * kF8GemvRows + ch] = acc[mt][r][0];
+      rw[(m0 + 1) * kF8GemvRows + ch] = acc[mt][r][1];
+      rw[(m0 + 0) * kF8GemvRows + ch + 8] = acc[mt][r][2];
+      rw[(m0 + 1) * kF8GemvRows + ch + 8] = acc[mt][r][3];
+    }
+  __syncthreads();
+  for (int e = threadIdx.x; e < MP * kF8GemvRows; e += blockDim.x) {
+    float s = red[e];
+    for (int w = 1; w < W; ++w) s += red[static_cast<size_t>(w) * MP * kF8GemvRows + e];
+    red[e] = s;
+  }
+  cluster.sync();
+  const int c0 = (rank * kF8GemvRows) / C, c1 = ((rank + 1) * kF8GemvRows) / C;
+  const int ncol = c1 - c0;
+  for (int e = threadIdx.x; e < M * ncol; e += blockDim.x) {
+    const int m = e / ncol;
+    const int ch = c0 + (e - m * ncol);
+    const int n = nbase + ch;
+    float s = 0.f;
+    for (int r = 0; r < C; ++r) s += cluster.map_shared_rank(red, r)[m * kF8GemvRows + ch];
+    if (n < N) {
+      float v = __fmul_rn(__fmul_rn(s, sx[m]), sw[n]);
+      if (bias != nullptr) v = __fadd_rn(v, __bfloat162float(bias[n]));
+      y[static_cast<int64_t>(m) * N + n] = __float2bfloat16_rn(v);
+    }
+  }
+  cluster.sync();
+}
+
+}  // namespace lmrs

@@ -1,0 +1,478 @@
+// lmrs_capi.cu — the C-ABI (include/lmrs_quant.h) and host-side dispatch.
+//
+// Unity translation unit: every kernel header is included here so the device
+// error word (lmrs::g_device_error) is one symbol without relocatable device
+// code.  Host responsibilities, mirroring the reference's `kernels::linear`
+// (crates/kernels/src/tensor_ops.rs:225-246) plus what the reference leaves
+// unchecked (kernels/ffi/tensor_ffi.cu:830-840 ignores a bad dtype silently):
+//   * argument validation -> int status, nothing launched on rejection;
+//   * dispatch by M: register-dequant tensor-core GEMV (decode) or tcgen05 GEMM
+//     (prefill);
+//   * TMA tensor maps (cuTensorMapEncodeTiled via the runtime's driver entry
+//     point, so the library has no link-time libcuda dependency);
+//   * cluster launches (cudaLaunchKernelEx) for the split-K GEMVs.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+
+#include "../../include/lmrs_quant.h"
+#include "awq_gemv.cuh"
+#include "awq_pack.cuh"
+#include "fp8_kernels.cuh"
+#include "lmrs_ptx.cuh"
+#include "tc_gemm.cuh"
+
+namespace {
+
+constexpr int kVersion = 1;
+constexpr int kMaxDevices = 64;
+thread_local int t_last_cuda_error = 0;
+
+// ---- tuning knobs (lmrs_set_tuning); defaults chosen from B200 measurements
+struct Tuning {
+  int awq_gemv_max_m = 16;   // M above this -> tcgen05 GEMM
+  int fp8_gemv_max_m = 32;
+  int gemv_warps = 4;        // warps per CTA in the split-K GEMVs
+  int gemv_target_warps = 148 * 16;
+  int awq_gemv_cluster = 0;  // 0 = heuristic
+  int fp8_gemv_cluster = 0;
+};
+Tuning g_tune;
+
+int record(cudaError_t e) {
+  t_last_cuda_error = static_cast<int>(e);
+  return LMRS_ERR_CUDA;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// ---- per-device checks (cached)
+std::atomic<int> g_dev_ok[kMaxDevices];  // 0 unknown, 1 ok, -1 not sm_100
+
+int check_device(int* dev_out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return record(e);
+  if (dev < 0 || dev >= kMaxDevices) return LMRS_ERR_DEVICE;
+  int st = g_dev_ok[dev].load(std::memory_order_relaxed);
+  if (st == 0) {
+    int major = 0;
+    e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+    if (e != cudaSuccess) return record(e);
+    st = (major == 10) ? 1 : -1;
+    g_dev_ok[dev].store(st, std::memory_order_relaxed);
+  }
+  if (dev_out) *dev_out = dev;
+  return st == 1 ? LMRS_OK : LMRS_ERR_DEVICE;
+}
+
+// ---- dynamic shared memory opt-in, once per (kernel, device)
+template <typename K>
+int ensure_smem(K kernel, int bytes, std::atomic<int>* done, int dev) {
+  if (done[dev].load(std::memory_order_acquire) >= bytes) return LMRS_OK;
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess) return record(e);
+  done[dev].store(bytes, std::memory_order_release);
+  return LMRS_OK;
+}
+
+// ---- TMA descriptors
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// 2-D tensor map: dim0 innermost (contiguous), row stride in bytes.
+int make_tmap(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t dim0,
+              uint64_t dim1, uint64_t row_bytes, uint32_t box0, uint32_t box1,
+              CUtensorMapSwizzle sw) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return LMRS_ERR_CUDA;
+  cuuint64_t dims[2] = {dim0, dim1};
+  cuuint64_t strides[1] = {row_bytes};
+  cuuint32_t box[2] = {box0, box1};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    t_last_cuda_error = static_cast<int>(r);
+    return LMRS_ERR_CUDA;
+  }
+  return LMRS_OK;
+}
+
+int after_launch() {
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? LMRS_OK : record(e);
+}
+
+int clampi(int v, int lo, int hi) { return v < lo ? lo : (v > hi ? hi : v); }
+
+// split-K factor for a GEMV with `strips` independent column strips and
+// `units` K units: fill ~target warps, W warps per CTA, cluster <= 8.
+void gemv_grid(int strips, int units, int forced_cluster, int* W_out, int* C_out) {
+  const int W = clampi(g_tune.gemv_warps, 1, 8);
+  int C = forced_cluster;
+  if (C <= 0) {
+    const int want = (g_tune.gemv_target_warps + strips - 1) / strips;  // warps per strip
+    C = (want + W - 1) / W;
+  }
+  C = clampi(C, 1, 8);
+  while (C > 1 && C * W > units) --C;  // keep every warp busy
+  *W_out = W;
+  *C_out = C;
+}
+
+template <typename Kern, typename... Args>
+int launch_cluster(Kern kernel, int grid_x, int cluster, int threads, int smem,
+                   cudaStream_t stream, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid_x, 1, 1);
+  cfg.blockDim = dim3(threads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = cluster;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, args...);
+  if (e != cudaSuccess) return record(e);
+  return LMRS_OK;
+}
+
+std::atomic<int> g_smem_awq_gemm[kMaxDevices];
+std::atomic<int> g_smem_f8_gemm[kMaxDevices];
+std::atomic<int> g_smem_awq_gemv[3][kMaxDevices];
+std::atomic<int> g_smem_f8_gemv[3][kMaxDevices];
+
+// ------------------------------------------------------------------ AWQ
+int awq_gemv_launch(__half* y, const __half* x, const uint32_t* qw, const uint32_t* qz,
+                    const __half* sc, const __half* bias, int M, int K, int N, int group,
+                    cudaStream_t stream, int dev) {
+  const int strips = (N + lmrs::kAwqGemvStrip - 1) / lmrs::kAwqGemvStrip;
+  int W, C;
+  gemv_grid(strips, K / 64, g_tune.awq_gemv_cluster, &W, &C);
+  const int MT = M <= 8 ? 1 : 2;
+  const int smem = W * 8 * MT * lmrs::kAwqGemvStrip * 4;
+  int rc;
+  if (MT == 1) {
+    rc = ensure_smem(lmrs::awq_gemv_kernel<1>, smem, g_smem_awq_gemv[0], dev);
+    if (rc) return rc;
+    rc = launch_cluster(lmrs::awq_gemv_kernel<1>, strips * C, C, 32 * W, smem, stream, y, x, qw,
+                        qz, sc, bias, M, K, N, group);
+  } else {
+    rc = ensure_smem(lmrs::awq_gemv_kernel<2>, smem, g_smem_awq_gemv[1], dev);
+    if (rc) return rc;
+    rc = launch_cluster(lmrs::awq_gemv_kernel<2>, strips * C, C, 32 * W, smem, stream, y, x, qw,
+                        qz, sc, bias, M, K, N, group);
+  }
+  return rc ? rc : after_launch();
+}
+
+int awq_gemm_launch(__half* y, const __half* x, const int32_t* qw, const int32_t* qz,
+                    const __half* sc, const __half* bias, int M, int K, int N, int group,
+                    cudaStream_t stream, int dev) {
+  CUtensorMap tx, tq, ts, tz;
+  int rc;
+  if ((rc = make_tmap(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, x, K, M, uint64_t(K) * 2, 64, 128,
+                      CU_TENSOR_MAP_SWIZZLE_128B)))
+    return rc;
+  if ((rc = make_tmap(&tq, CU_TENSOR_MAP_DATA_TYPE_INT32, qw, N / 8, K, uint64_t(N / 8) * 4, 32,
+                      64, CU_TENSOR_MAP_SWIZZLE_NONE)))
+    return rc;
+  if ((rc = make_tmap(&ts, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, sc, N, K / group, uint64_t(N) * 2,
+                      256, 1, CU_TENSOR_MAP_SWIZZLE_NONE)))
+    return rc;
+  if ((rc = make_tmap(&tz, CU_TENSOR_MAP_DATA_TYPE_INT32, qz, N / 8, K / group,
+                      uint64_t(N / 8) * 4, 32, 1, CU_TENSOR_MAP_SWIZZLE_NONE)))
+    return rc;
+  if ((rc = ensure_smem(lmrs::awq_gemm_tc_kernel, lmrs::kAwqSmemBytes, g_smem_awq_gemm, dev)))
+    return rc;
+  dim3 grid((N + lmrs::kTcBN - 1) / lmrs::kTcBN, (M + lmrs::kTcBM - 1) / lmrs::kTcBM);
+  lmrs::awq_gemm_tc_kernel<<<grid, lmrs::kAwqGemmThreads, lmrs::kAwqSmemBytes, stream>>>(
+      tx, tq, ts, tz, y, bias, M, K, N, group);
+  return after_launch();
+}
+
+// ------------------------------------------------------------------ FP8
+int fp8_quant_launch(uint8_t* q, float* s, const void* x, int rows, int K, int dt,
+                     cudaStream_t stream) {
+  if (rows == 0) return LMRS_OK;
+  switch (dt) {
+    case LMRS_DTYPE_BF16:
+      lmrs::fp8_quant_rows_kernel<0><<<rows, lmrs::kQuantThreads, 0, stream>>>(
+          q, s, static_cast<const __nv_bfloat16*>(x), K);
+      break;
+    case LMRS_DTYPE_F16:
+      lmrs::fp8_quant_rows_kernel<1><<<rows, lmrs::kQuantThreads, 0, stream>>>(
+          q, s, static_cast<const __half*>(x), K);
+      break;
+    default:
+      lmrs::fp8_quant_rows_kernel<2><<<rows, lmrs::kQuantThreads, 0, stream>>>(
+          q, s, static_cast<const float*>(x), K);
+      break;
+  }
+  return after_launch();
+}
+
+int fp8_gemv_launch(__nv_bfloat16* y, const uint8_t* xq, const float* sx, const uint8_t* wq,
+                    const float* sw, const __nv_bfloat16* bias, int M, int K, int N,
+                    cudaStream_t stream, int dev) {
+  const int strips = (N + lmrs::kF8GemvRows - 1) / lmrs::kF8GemvRows;
+  int W, C;
+  gemv_grid(strips, (K + 127) / 128, g_tune.fp8_gemv_cluster, &W, &C);
+  const int MT = M <= 8 ? 1 : (M <= 16 ? 2 : 4);
+  const int smem = W * 8 * MT * lmrs::kF8GemvRows * 4;
+  int rc;
+  if (MT == 1) {
+    if ((rc = ensure_smem(lmrs::fp8_gemv_kernel<1>, smem, g_smem_f8_gemv[0], dev))) return rc;
+    rc = launch_cluster(lmrs::fp8_gemv_kernel<1>, strips * C, C, 32 * W, smem, stream, y, xq, sx,
+                        wq, sw, bias, M, K, N);
+  } else if (MT == 2) {
+    if ((rc = ensure_smem(lmrs::fp8_gemv_kernel<2>, smem, g_smem_f8_gemv[1], dev))) return rc;
+    rc = launch_cluster(lmrs::fp8_gemv_kernel<2>, strips * C, C, 32 * W, smem, stream, y, xq, sx,
+                        wq, sw, bias, M, K, N);
+  } else {
+    if ((rc = ensure_smem(lmrs::fp8_gemv_kernel<4>, smem, g_smem_f8_gemv[2], dev))) return rc;
+    rc = launch_cluster(lmrs::fp8_gemv_kernel<4>, strips * C, C, 32 * W, smem, stream, y, xq, sx,
+                        wq, sw, bias, M, K, N);
+  }
+  return rc ? rc : after_launch();
+}
+
+int fp8_gemm_launch(__nv_bfloat16* y, const uint8_t* xq, const float* sx, const uint8_t* wq,
+                    const float* sw, const __nv_bfloat16* bias, int M, int K, int N,
+                    cudaStream_t stream, int dev) {
+  CUtensorMap ta, tb;
+  int rc;
+  if ((rc = make_tmap(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, xq, K, M, uint64_t(K), 128, 128,
+                      CU_TENSOR_MAP_SWIZZLE_128B)))
+    return rc;
+  if ((rc = make_tmap(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, wq, K, N, uint64_t(K), 128, 256,
+                      CU_TENSOR_MAP_SWIZZLE_128B)))
+    return rc;
+  if ((rc = ensure_smem(lmrs::fp8_gemm_tc_kernel, lmrs::kF8SmemBytes, g_smem_f8_gemm, dev)))
+    return rc;
+  dim3 grid((N + lmrs::kTcBN - 1) / lmrs::kTcBN, (M + lmrs::kTcBM - 1) / lmrs::kTcBM);
+  lmrs::fp8_gemm_tc_kernel<<<grid, lmrs::kF8Threads, lmrs::kF8SmemBytes, stream>>>(
+      ta, tb, y, sx, sw, bias, M, K, N);
+  return after_launch();
+}
+
+int fp8_linear_prequant_impl(void* y, const uint8_t* xq, const float* x_scale, const uint8_t* wq,
+                             const float* w_scale, const void* bias, int M, int K, int N,
+                             cudaStream_t stream, int dev) {
+  auto* yb = static_cast<__nv_bfloat16*>(y);
+  auto* bb = static_cast<const __nv_bfloat16*>(bias);
+  if (M <= g_tune.fp8_gemv_max_m && M <= 32)
+    return fp8_gemv_launch(yb, xq, x_scale, wq, w_scale, bb, M, K, N, stream, dev);
+  return fp8_gemm_launch(yb, xq, x_scale, wq, w_scale, bb, M, K, N, stream, dev);
+}
+
+size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+}  // namespace
+
+// =================================================================== C-ABI
+extern "C" {
+
+int lmrs_version(void) { return kVersion; }
+
+const char* lmrs_status_string(int status) {
+  switch (status) {
+    case LMRS_OK: return "ok";
+    case LMRS_ERR_SHAPE: return "invalid shape";
+    case LMRS_ERR_DTYPE: return "unsupported dtype";
+    case LMRS_ERR_ALIGN: return "pointer not 16-byte aligned";
+    case LMRS_ERR_GROUP: return "group size must divide K and be a multiple of 64";
+    case LMRS_ERR_WORKSPACE: return "workspace missing or too small";
+    case LMRS_ERR_CUDA: return "CUDA call failed";
+    case LMRS_ERR_DEVICE: return "current device is not sm_100 (B200)";
+    case LMRS_ERR_NULL: return "required pointer is NULL";
+    case LMRS_ERR_TIMEOUT: return "kernel wait timed out";
+    default: return "unknown status";
+  }
+}
+
+int lmrs_last_cuda_error(void) { return t_last_cuda_error; }
+
+int lmrs_read_device_error(int* out_flags) {
+  if (!out_flags) return LMRS_ERR_NULL;
+  int rc = check_device(nullptr);
+  if (rc) return rc;
+  uint32_t v = 0, zero = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, lmrs::g_device_error, sizeof(v));
+  if (e != cudaSuccess) return record(e);
+  e = cudaMemcpyToSymbol(lmrs::g_device_error, &zero, sizeof(zero));
+  if (e != cudaSuccess) return record(e);
+  *out_flags = static_cast<int>(v);
+  return LMRS_OK;
+}
+
+// Tuning knobs for measurement sweeps; returns 0 on a known key.
+int lmrs_set_tuning(const char* key, int value) {
+  if (!key) return LMRS_ERR_NULL;
+  if (!strcmp(key, "awq_gemv_max_m")) g_tune.awq_gemv_max_m = value;
+  else if (!strcmp(key, "fp8_gemv_max_m")) g_tune.fp8_gemv_max_m = value;
+  else if (!strcmp(key, "gemv_warps")) g_tune.gemv_warps = value;
+  else if (!strcmp(key, "gemv_target_warps")) g_tune.gemv_target_warps = value;
+  else if (!strcmp(key, "awq_gemv_cluster")) g_tune.awq_gemv_cluster = value;
+  else if (!strcmp(key, "fp8_gemv_cluster")) g_tune.fp8_gemv_cluster = value;
+  else return LMRS_ERR_SHAPE;
+  return LMRS_OK;
+}
+
+int lmrs_awq_unpack(int8_t* q_out, const int32_t* packed, int rows, int cols,
+                    lmrs_stream_t stream) {
+  if (rows < 0 || cols < 0 || cols % 8) return LMRS_ERR_SHAPE;
+  if (rows == 0 || cols == 0) return LMRS_OK;
+  if (!q_out || !packed) return LMRS_ERR_NULL;
+  if ((reinterpret_cast<uintptr_t>(q_out) & 7u) || (reinterpret_cast<uintptr_t>(packed) & 3u))
+    return LMRS_ERR_ALIGN;
+  int rc = check_device(nullptr);
+  if (rc) return rc;
+  const int64_t words = int64_t(rows) * (cols / 8);
+  const int64_t blocks = (words + 255) / 256;
+  lmrs::awq_unpack_kernel<<<static_cast<unsigned>(blocks), 256, 0,
+                            reinterpret_cast<cudaStream_t>(stream)>>>(
+      q_out, reinterpret_cast<const uint32_t*>(packed), words);
+  return after_launch();
+}
+
+int lmrs_awq_dequant(void* w_out, const int32_t* qweight, const int32_t* qzeros,
+                     const void* scales, int K, int N, int group, lmrs_stream_t stream) {
+  if (K < 0 || N < 0 || N % 8) return LMRS_ERR_SHAPE;
+  if (group <= 0 || K % group) return LMRS_ERR_GROUP;
+  if (K == 0 || N == 0) return LMRS_OK;
+  if (!w_out || !qweight || !qzeros || !scales) return LMRS_ERR_NULL;
+  if (!aligned16(w_out) || !aligned16(scales) || (reinterpret_cast<uintptr_t>(qweight) & 3u) ||
+      (reinterpret_cast<uintptr_t>(qzeros) & 3u))
+    return LMRS_ERR_ALIGN;
+  int rc = check_device(nullptr);
+  if (rc) return rc;
+  const int64_t words = int64_t(K) * (N / 8);
+  lmrs::awq_dequant_kernel<<<static_cast<unsigned>((words + 255) / 256), 256, 0,
+                             reinterpret_cast<cudaStream_t>(stream)>>>(
+      static_cast<__half*>(w_out), reinterpret_cast<const uint32_t*>(qweight),
+      reinterpret_cast<const uint32_t*>(qzeros), static_cast<const __half*>(scales), K, N / 8,
+      group);
+  return after_launch();
+}
+
+size_t lmrs_awq_linear_workspace_bytes(int M, int K, int N, int group) {
+  (void)M; (void)K; (void)N; (void)group;
+  return 0;
+}
+
+int lmrs_awq_linear(void* y, const void* x, const int32_t* qweight, const int32_t* qzeros,
+                    const void* scales, const void* bias_or_null, int M, int K, int N, int group,
+                    int act_dtype, void* workspace, size_t workspace_bytes,
+                    lmrs_stream_t stream) {
+  (void)workspace; (void)workspace_bytes;
+  if (act_dtype != LMRS_DTYPE_F16) return LMRS_ERR_DTYPE;
+  if (M < 0 || K <= 0 || N <= 0 || N % 32) return LMRS_ERR_SHAPE;
+  if (group <= 0 || group % 64 || K % group) return LMRS_ERR_GROUP;
+  if (M == 0) return LMRS_OK;
+  if (!y || !x || !qweight || !qzeros || !scales) return LMRS_ERR_NULL;
+  if (!aligned16(y) || !aligned16(x) || !aligned16(qweight) || !aligned16(qzeros) ||
+      !aligned16(scales) || (bias_or_null && !aligned16(bias_or_null)))
+    return LMRS_ERR_ALIGN;
+  int dev = 0;
+  int rc = check_device(&dev);
+  if (rc) return rc;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  auto* yh = static_cast<__half*>(y);
+  auto* xh = static_cast<const __half*>(x);
+  auto* sh = static_cast<const __half*>(scales);
+  auto* bh = static_cast<const __half*>(bias_or_null);
+  if (M <= g_tune.awq_gemv_max_m && M <= 16)
+    return awq_gemv_launch(yh, xh, reinterpret_cast<const uint32_t*>(qweight),
+                           reinterpret_cast<const uint32_t*>(qzeros), sh, bh, M, K, N, group, st,
+                           dev);
+  return awq_gemm_launch(yh, xh, qweight, qzeros, sh, bh, M, K, N, group, st, dev);
+}
+
+int lmrs_fp8_quant_rows(uint8_t* q, float* scale, const void* x, int rows, int K, int x_dtype,
+                        lmrs_stream_t stream) {
+  if (x_dtype < 0 || x_dtype > 2) return LMRS_ERR_DTYPE;
+  if (rows < 0 || K <= 0 || K % 16) return LMRS_ERR_SHAPE;
+  if (rows == 0) return LMRS_OK;
+  if (!q || !scale || !x) return LMRS_ERR_NULL;
+  if (!aligned16(q) || !aligned16(x) || (reinterpret_cast<uintptr_t>(scale) & 3u))
+    return LMRS_ERR_ALIGN;
+  int rc = check_device(nullptr);
+  if (rc) return rc;
+  return fp8_quant_launch(q, scale, x, rows, K, x_dtype, reinterpret_cast<cudaStream_t>(stream));
+}
+
+size_t lmrs_fp8_linear_workspace_bytes(int M, int K, int N) {
+  (void)N;
+  if (M <= 0 || K <= 0) return 0;
+  return round_up(size_t(M) * size_t(K), 256) + round_up(size_t(M) * 4, 256);
+}
+
+int lmrs_fp8_linear_prequant(void* y, const uint8_t* xq, const float* x_scale, const uint8_t* wq,
+                             const float* w_scale, const void* bias_or_null, int M, int K, int N,
+                             lmrs_stream_t stream) {
+  if (M < 0 || K <= 0 || N <= 0 || K % 16) return LMRS_ERR_SHAPE;
+  if (M == 0) return LMRS_OK;
+  if (!y || !xq || !x_scale || !wq || !w_scale) return LMRS_ERR_NULL;
+  if (!aligned16(xq) || !aligned16(wq) || (reinterpret_cast<uintptr_t>(y) & 3u) ||
+      (reinterpret_cast<uintptr_t>(x_scale) & 3u) || (reinterpret_cast<uintptr_t>(w_scale) & 3u) ||
+      (reinterpret_cast<uintptr_t>(bias_or_null) & 1u))
+    return LMRS_ERR_ALIGN;
+  if (N % 8 && M > g_tune.fp8_gemv_max_m) return LMRS_ERR_SHAPE;  // GEMM epilogue stores
+  int dev = 0;
+  int rc = check_device(&dev);
+  if (rc) return rc;
+  return fp8_linear_prequant_impl(y, xq, x_scale, wq, w_scale, bias_or_null, M, K, N,
+                                  reinterpret_cast<cudaStream_t>(stream), dev);
+}
+
+int lmrs_fp8_linear(void* y, const void* x, const uint8_t* wq, const float* w_scale,
+                    const void* bias_or_null, int M, int K, int N, void* workspace,
+                    size_t workspace_bytes, lmrs_stream_t stream) {
+  if (M < 0 || K <= 0 || N <= 0 || K % 16) return LMRS_ERR_SHAPE;
+  if (M == 0) return LMRS_OK;
+  if (!y || !x || !wq || !w_scale) return LMRS_ERR_NULL;
+  const size_t need = lmrs_fp8_linear_workspace_bytes(M, K, N);
+  if (!workspace || workspace_bytes < need) return LMRS_ERR_WORKSPACE;
+  if (!aligned16(workspace) || !aligned16(x) || !aligned16(wq) ||
+      (reinterpret_cast<uintptr_t>(y) & 3u) || (reinterpret_cast<uintptr_t>(w_scale) & 3u) ||
+      (reinterpret_cast<uintptr_t>(bias_or_null) & 1u))
+    return LMRS_ERR_ALIGN;
+  if (N % 8 && M > g_tune.fp8_gemv_max_m) return LMRS_ERR_SHAPE;
+  int dev = 0;
+  int rc = check_device(&dev);
+  if (rc) return rc;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  uint8_t* xq = static_cast<uint8_t*>(workspace);
+  float* sx = reinterpret_cast<float*>(xq + round_up(size_t(M) * size_t(K), 256));
+  if ((rc = fp8_quant_launch(xq, sx, x, M, K, LMRS_DTYPE_BF16, st))) return rc;
+  return fp8_linear_prequant_impl(y, xq, sx, wq, w_scale, bias_or_null, M, K, N, st, dev);
+}
+
+}  // extern "C"

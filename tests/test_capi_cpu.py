@@ -1,0 +1,93 @@
+"""The C-ABI library on a machine without a GPU: it loads, exports exactly the
+symbols include/lmrs_quant.h declares, and rejects bad arguments with the
+documented status codes before touching the device (no compute is launched)."""
+import ctypes
+import pathlib
+import re
+
+import pytest
+
+from lmrs_b200 import _lib
+
+ROOT = pathlib.Path(__file__).resolve().parent.parent
+HEADER = ROOT / "include" / "lmrs_quant.h"
+
+
+def header_symbols():
+    text = HEADER.read_text()
+    return set(re.findall(r"LMRS_API\s+[\w\s\*]*?\b(lmrs_\w+)\s*\(", text))
+
+
+def test_library_loads_and_exports_header():
+    lib = _lib.load()
+    syms = header_symbols()
+    assert len(syms) >= 12
+    for s in syms:
+        assert hasattr(lib, s), s
+    assert set(_lib.SIGNATURES) == syms
+    assert lib.lmrs_version() >= 1
+
+
+def test_status_strings():
+    for code in range(10):
+        assert _lib.status_string(code)
+    assert "sm_100" in _lib.status_string(_lib.LMRS_ERR_DEVICE)
+
+
+FAKE = ctypes.c_void_p(0x10000)  # 16-byte aligned, never dereferenced
+
+
+def test_awq_validation_codes():
+    lib = _lib.load()
+    f = lib.lmrs_awq_linear
+    # act dtype must be fp16
+    assert f(FAKE, FAKE, FAKE, FAKE, FAKE, None, 4, 256, 64, 128, 0, None, 0, None) == _lib.LMRS_ERR_DTYPE
+    # N % 32
+    assert f(FAKE, FAKE, FAKE, FAKE, FAKE, None, 4, 256, 40, 128, 1, None, 0, None) == _lib.LMRS_ERR_SHAPE
+    # group must divide K and be a multiple of 64
+    assert f(FAKE, FAKE, FAKE, FAKE, FAKE, None, 4, 256, 64, 96, 1, None, 0, None) == _lib.LMRS_ERR_GROUP
+    assert f(FAKE, FAKE, FAKE, FAKE, FAKE, None, 4, 192, 64, 128, 1, None, 0, None) == _lib.LMRS_ERR_GROUP
+    # NULL and misaligned pointers
+    assert f(None, FAKE, FAKE, FAKE, FAKE, None, 4, 256, 64, 128, 1, None, 0, None) == _lib.LMRS_ERR_NULL
+    assert f(ctypes.c_void_p(0x10002), FAKE, FAKE, FAKE, FAKE, None, 4, 256, 64, 128, 1, None, 0,
+             None) == _lib.LMRS_ERR_ALIGN
+    # M == 0 is a successful no-op
+    assert f(FAKE, FAKE, FAKE, FAKE, FAKE, None, 0, 256, 64, 128, 1, None, 0, None) == _lib.LMRS_OK
+    assert lib.lmrs_awq_linear_workspace_bytes(16, 4096, 14336, 128) == 0
+
+
+def test_awq_pack_validation_codes():
+    lib = _lib.load()
+    assert lib.lmrs_awq_unpack(FAKE, FAKE, 4, 12, None) == _lib.LMRS_ERR_SHAPE
+    assert lib.lmrs_awq_unpack(FAKE, FAKE, 0, 16, None) == _lib.LMRS_OK
+    assert lib.lmrs_awq_dequant(FAKE, FAKE, FAKE, FAKE, 100, 64, 64, None) == _lib.LMRS_ERR_GROUP
+    assert lib.lmrs_awq_dequant(FAKE, FAKE, FAKE, FAKE, 128, 60, 64, None) == _lib.LMRS_ERR_SHAPE
+
+
+def test_fp8_validation_codes():
+    lib = _lib.load()
+    need = lib.lmrs_fp8_linear_workspace_bytes(4, 256, 64)
+    assert need >= 4 * 256 + 4 * 4 and need % 256 == 0
+    f = lib.lmrs_fp8_linear
+    assert f(FAKE, FAKE, FAKE, FAKE, None, 4, 250, 64, FAKE, need, None) == _lib.LMRS_ERR_SHAPE
+    assert f(FAKE, FAKE, FAKE, FAKE, None, 4, 256, 64, FAKE, need - 1, None) == _lib.LMRS_ERR_WORKSPACE
+    assert f(FAKE, FAKE, FAKE, FAKE, None, 4, 256, 64, None, need, None) == _lib.LMRS_ERR_WORKSPACE
+    assert f(FAKE, FAKE, FAKE, FAKE, None, 0, 256, 64, None, 0, None) == _lib.LMRS_OK
+    assert lib.lmrs_fp8_quant_rows(FAKE, FAKE, FAKE, 4, 256, 7, None) == _lib.LMRS_ERR_DTYPE
+    assert lib.lmrs_fp8_quant_rows(FAKE, FAKE, FAKE, 4, 24, 0, None) == _lib.LMRS_ERR_SHAPE
+
+
+def test_valid_call_without_gpu_fails_cleanly():
+    """Arguments that pass validation reach the device check, which reports a
+    CUDA error (no device here) instead of launching or crashing."""
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("has a GPU")
+    lib = _lib.load()
+    rc = lib.lmrs_awq_linear(FAKE, FAKE, FAKE, FAKE, FAKE, None, 4, 256, 64, 128, 1, None, 0, None)
+    assert rc in (_lib.LMRS_ERR_CUDA, _lib.LMRS_ERR_DEVICE)
+
+
+def test_tuning_keys():
+    assert _lib.load().lmrs_set_tuning(b"no_such_key", 1) == _lib.LMRS_ERR_SHAPE
+    _lib.set_tuning("awq_gemv_max_m", 16)
