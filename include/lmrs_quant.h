@@ -63,7 +63,8 @@ enum {
   LMRS_ERR_CUDA = 6,         /* a CUDA runtime/driver call failed (see lmrs_last_cuda_error) */
   LMRS_ERR_DEVICE = 7,       /* current device is not sm_100 */
   LMRS_ERR_NULL = 8,         /* a required pointer is NULL */
-  LMRS_ERR_TIMEOUT = 9       /* a kernel's bounded wait gave up (lmrs_read_device_error) */
+  LMRS_ERR_TIMEOUT = 9,      /* a kernel's bounded wait gave up (lmrs_read_device_error) */
+  LMRS_ERR_TOO_LARGE = 10    /* problem needs more scratch than lmrs_fp8_linear_noalloc holds */
 };
 
 enum { LMRS_DTYPE_BF16 = 0, LMRS_DTYPE_F16 = 1, LMRS_DTYPE_F32 = 2 };
@@ -145,6 +146,38 @@ LMRS_API int lmrs_fp8_linear_prequant(void* y, const uint8_t* xq, const float* x
                              const uint8_t* wq, const float* w_scale,
                              const void* bias_or_null, int M, int K, int N,
                              lmrs_stream_t stream);
+
+/* ---- FP8 W8A8 without any device allocation -------------------------------
+ * No counterpart in the reference: lmrs's `kernels::linear` always allocates
+ * its output on the stream (crates/kernels/src/tensor_ops.rs:236-237) and has
+ * no scratch; this entry point exists for callers that cannot allocate.
+ *
+ * Same result as lmrs_fp8_linear (same kernels), but the quantised activations
+ * live in a scratch array compiled into this library: a file-scope
+ * `static __device__` array of LMRS_FP8_NOALLOC_SCRATCH_BYTES, which every GPU
+ * that loads the library holds until the process exits.  For callers that
+ * cannot call cudaMalloc or any allocator at the point of the call — a host
+ * runtime whose device memory is owned by its own pool with no hook for a
+ * plugin's scratch, a decode loop that must not allocate after warm-up, a
+ * process that must keep its device footprint fixed after load.  The caller
+ * still owns and passes x, wq, w_scale, bias and y.
+ *
+ *   - Limit: lmrs_fp8_linear_workspace_bytes(M, K, N) must not exceed
+ *     LMRS_FP8_NOALLOC_SCRATCH_BYTES (4 MiB: e.g. M*K up to about 4.1 million
+ *     e4m3 bytes — M=256 at K=14336, M=1024 at K=4096); larger problems return
+ *     LMRS_ERR_TOO_LARGE and launch nothing.
+ *   - The first call on each device looks up the array's device address
+ *     (cudaGetSymbolAddress, with that device current); make that first call
+ *     before any stream capture.
+ *   - Every call on a device shares the one array and leaves its contents
+ *     behind; nothing in it needs to start at zero (each call overwrites the
+ *     bytes it reads).  Calls that overlap on the GPU — on two streams, or from
+ *     two threads — race on the array: serialise them.
+ *   - Allocates nothing: no cudaMalloc, cudaFree or allocating library call. */
+#define LMRS_FP8_NOALLOC_SCRATCH_BYTES (4u * 1024u * 1024u)
+LMRS_API int lmrs_fp8_linear_noalloc(void* y, const void* x, const uint8_t* wq,
+                                     const float* w_scale, const void* bias_or_null, int M,
+                                     int K, int N, lmrs_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -24,6 +24,8 @@ LMRS_ERR_CUDA = 6
 LMRS_ERR_DEVICE = 7
 LMRS_ERR_NULL = 8
 LMRS_ERR_TIMEOUT = 9
+LMRS_ERR_TOO_LARGE = 10
+FP8_NOALLOC_SCRATCH_BYTES = 4 * 1024 * 1024
 
 # KernelDType (crates/kernels/src/raw.rs:9-13)
 DTYPE_BF16 = 0
@@ -49,6 +51,7 @@ SIGNATURES = {
     "lmrs_fp8_linear_workspace_bytes": (SZ, [I, I, I]),
     "lmrs_fp8_linear": (I, [P, P, P, P, P, I, I, I, P, SZ, P]),
     "lmrs_fp8_linear_prequant": (I, [P, P, P, P, P, P, I, I, I, P]),
+    "lmrs_fp8_linear_noalloc": (I, [P, P, P, P, P, I, I, I, P]),
 }
 
 

@@ -313,6 +313,7 @@ const char* lmrs_status_string(int status) {
     case LMRS_ERR_DEVICE: return "current device is not sm_100 (B200)";
     case LMRS_ERR_NULL: return "required pointer is NULL";
     case LMRS_ERR_TIMEOUT: return "kernel wait timed out";
+    case LMRS_ERR_TOO_LARGE: return "problem exceeds the no-allocation scratch limit";
     default: return "unknown status";
   }
 }
@@ -476,3 +477,52 @@ int lmrs_fp8_linear(void* y, const void* x, const uint8_t* wq, const float* w_sc
 }
 
 }  // extern "C"
+
+// ======================================== FP8 linear with library-held scratch
+// For callers that cannot allocate device memory (see lmrs_quant.h).  The
+// scratch is a file-scope device array; in host code its name is only a
+// host-side stand-in, so the device address is looked up once per device with
+// cudaGetSymbolAddress (with that device current) and passed to the kernels.
+static __device__ __align__(256) uint8_t lmrs_fp8_noalloc_scratch[LMRS_FP8_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[kMaxDevices];  // device address per device, nullptr until looked up
+
+int noalloc_scratch(int dev, void** out) {
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, lmrs_fp8_noalloc_scratch);
+    if (e != cudaSuccess) return record(e);
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return LMRS_OK;
+}
+}  // namespace
+
+extern "C" int lmrs_fp8_linear_noalloc(void* y, const void* x, const uint8_t* wq,
+                                       const float* w_scale, const void* bias_or_null, int M,
+                                       int K, int N, lmrs_stream_t stream) {
+  if (M < 0 || K <= 0 || N <= 0 || K % 16) return LMRS_ERR_SHAPE;
+  if (M == 0) return LMRS_OK;
+  if (!y || !x || !wq || !w_scale) return LMRS_ERR_NULL;
+  if (lmrs_fp8_linear_workspace_bytes(M, K, N) > LMRS_FP8_NOALLOC_SCRATCH_BYTES)
+    return LMRS_ERR_TOO_LARGE;
+  if (!aligned16(x) || !aligned16(wq) || (reinterpret_cast<uintptr_t>(y) & 3u) ||
+      (reinterpret_cast<uintptr_t>(w_scale) & 3u) ||
+      (reinterpret_cast<uintptr_t>(bias_or_null) & 1u))
+    return LMRS_ERR_ALIGN;
+  if (N % 8 && M > g_tune.fp8_gemv_max_m) return LMRS_ERR_SHAPE;
+  int dev = 0;
+  int rc = check_device(&dev);
+  if (rc) return rc;
+  void* scratch = nullptr;
+  if ((rc = noalloc_scratch(dev, &scratch))) return rc;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  uint8_t* xq = static_cast<uint8_t*>(scratch);
+  float* sx = reinterpret_cast<float*>(xq + round_up(size_t(M) * size_t(K), 256));
+  if ((rc = fp8_quant_launch(xq, sx, x, M, K, LMRS_DTYPE_BF16, st))) return rc;
+  return fp8_linear_prequant_impl(y, xq, sx, wq, w_scale, bias_or_null, M, K, N, st, dev);
+}
