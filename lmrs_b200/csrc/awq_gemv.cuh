@@ -2,26 +2,25 @@
 //
 // y[m, n] = sum_k x[m, k] * w[k, n],  w = fp16_rne((q - z) * s)  (AWQ int4).
 //
-// Design (swap-AB tensor-core GEMV, register dequant):
+// Design (TMA-fed, swap-AB tensor-core GEMV, register dequant):
+//   * A CTA owns a 128-column strip (16 packed words per row) and a slice of K.
+//     A producer warp streams the strip's packed rows into a ring of
+//     shared-memory slots with 2-D TMA boxes (16 words x 64 rows, 64-byte
+//     swizzle), so each SM keeps ~200 KB of weights in flight with no
+//     register cost — decode is a pure HBM stream.
+//   * Four consumer warps: warp (h, p) takes columns 64h..64h+63 and alternate
+//     pairs of boxes p.  Lane (g, t) (g = lane/4, t = lane%4) reads word 8h+g of
+//     rows 2t, 2t+1, 2t+8, 2t+9 of each 16-row step; the 64-byte swizzle plus
+//     loading odd-t lanes' rows in swapped order makes every 32-bit LDS
+//     conflict-free.
 //   * Output columns play the MMA "M" role (16 per m16n8k16 tile), tokens play
-//     "N" (8 per tile, MT tiles), k is the reduction.  No shared-memory staging
-//     of weights: packed words go HBM -> registers with 64-bit streaming loads
-//     (ld.global.nc.L1::no_allocate), are dequantised in registers and fed to
-//     mma.sync as the A fragment.
-//   * A warp owns a 128-column strip (16 packed words per row).  Lane (g, t)
-//     (g = lane/4, t = lane%4) loads words 2g, 2g+1 of rows k0+2t, k0+2t+1,
-//     k0+2t+8, k0+2t+9 of each 16-row step: each load instruction touches four
-//     64-byte row segments, all bytes used.
-//   * prmt pairs rows (k, k+1) of the same word, and because AWQ puts columns
-//     (2i, 2i+1) in nibbles (i, i+4), (P >> 4i) & 0x000F000F | 0x6400.. yields
-//     the half2 (1024+q[k][c], 1024+q[k+1][c]) that the A fragment wants.
-//     Dequant is the canonical fp16 (q - z) * s (hsub2 exact, hmul2 rounds
-//     once), so the MMA sees the bit-exact dequantised weights.
-//   * Split-K: a thread-block cluster of C CTAs x W warps shares one strip; each
-//     warp takes a contiguous run of 64-row units (group % 64 == 0, so a unit
-//     never straddles a quantisation group).  Warp partials are summed in
-//     shared memory, CTA partials across the cluster through distributed
-//     shared memory; no global scratch, one launch.
+//     "N" (8 per tile, MT tiles).  prmt pairs rows (k, k+1) of the word, and
+//     because AWQ puts columns (2i, 2i+1) in nibbles (i, i+4), the half2
+//     (1024+q[k][c], 1024+q[k+1][c]) is one shift + one lop3.  Dequant is the
+//     canonical fp16 (q - z) * s (hsub2 exact, hmul2 rounds once), so the MMA
+//     sees the bit-exact dequantised weights.
+//   * Split-K across a thread-block cluster: CTA partials are summed through
+//     distributed shared memory by the cluster; no global scratch, one launch.
 #pragma once
 #include <cooperative_groups.h>
 #include "lmrs_ptx.cuh"
@@ -29,18 +28,16 @@
 namespace lmrs {
 namespace cg = cooperative_groups;
 
-__device__ __forceinline__ uint2 ldg_stream_u2(const uint32_t* p) {
-  uint2 v;
-  asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0, %1}, [%2];"
-               : "=r"(v.x), "=r"(v.y)
-               : "l"(p));
-  return v;
-}
-
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
   uint32_t r;
   asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
   return r;
+}
+
+__device__ __forceinline__ uint32_t lds_u32(uint32_t addr) {
+  uint32_t v;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr));
+  return v;
 }
 
 __device__ __forceinline__ void mma_f16_16816(float (&d)[4], const uint32_t (&a)[4],
@@ -52,150 +49,189 @@ __device__ __forceinline__ void mma_f16_16816(float (&d)[4], const uint32_t (&a)
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
-constexpr int kAwqGemvStrip = 128;  // output columns per warp / per cluster
+__device__ __forceinline__ void named_bar_sync(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
 
-// MT: number of 8-token MMA tiles (M <= 8 * MT).  W warps per CTA (blockDim = 32W).
+constexpr int kAwqGemvStrip = 128;      // output columns per CTA
+constexpr int kAwqGemvBoxRows = 64;     // k rows per TMA box
+constexpr int kAwqGemvBoxBytes = kAwqGemvBoxRows * (kAwqGemvStrip / 8) * 4;  // 4 KB
+constexpr int kAwqGemvThreads = 160;    // 4 consumer warps + 1 producer warp
+constexpr int kAwqGemvMaxRing = 12;
+
+// byte offset of (row r, word j) inside a 64-byte-swizzled box
+__device__ __forceinline__ uint32_t sw64(int r, int j) {
+  const uint32_t off = static_cast<uint32_t>(r * 64 + j * 4);
+  return off ^ (((off >> 7) & 3u) << 4);
+}
+
 template <int MT>
-__global__ void __launch_bounds__(256) awq_gemv_kernel(
-    __half* __restrict__ y, const __half* __restrict__ x, const uint32_t* __restrict__ qweight,
+__global__ void __launch_bounds__(kAwqGemvThreads, 4) awq_gemv_kernel(
+    const __grid_constant__ CUtensorMap tm_q, __half* __restrict__ y, const __half* __restrict__ x,
     const uint32_t* __restrict__ qzeros, const __half* __restrict__ scales,
-    const __half* __restrict__ bias, int M, int K, int N, int group) {
+    const __half* __restrict__ bias, int M, int K, int N, int group, int ring) {
   constexpr int MP = 8 * MT;  // padded token count
-  extern __shared__ __align__(16) float red[];  // [W][MP][128], then reused
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* slots = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                              ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(slots + ring * kAwqGemvBoxBytes);
+  uint64_t* empty = full + ring;
 
   cg::cluster_group cluster = cg::this_cluster();
   const int C = static_cast<int>(cluster.num_blocks());
   const int rank = static_cast<int>(cluster.block_rank());
   const int strip = blockIdx.x / C;
-  const int W = blockDim.x >> 5;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int g = lane >> 2, t = lane & 3;
   const int words_n = N >> 3;
-  const int wc = strip * (kAwqGemvStrip / 8) + 2 * g;  // thread's first word column
-  const bool col_ok = wc < words_n;                     // N % 16 == 0: both words or none
 
-  const int units = K >> 6;  // 64-row units
-  const int KS = C * W;
-  const int slice = rank * W + warp;
-  const int u0 = static_cast<int>((static_cast<long long>(slice) * units) / KS);
-  const int u1 = static_cast<int>((static_cast<long long>(slice + 1) * units) / KS);
+  const int nb_all = K / kAwqGemvBoxRows;
+  const int b_lo = static_cast<int>((static_cast<long long>(rank) * nb_all) / C);
+  const int b_hi = static_cast<int>((static_cast<long long>(rank + 1) * nb_all) / C);
+  const int nbox = b_hi - b_lo;
 
-  float acc[MT][8][4];
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < ring; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 2);  // two consumer warps (h = 0, 1) read every box
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  float acc[MT][4][4];
 #pragma unroll
   for (int a = 0; a < MT; ++a)
 #pragma unroll
-    for (int b = 0; b < 8; ++b)
+    for (int b = 0; b < 4; ++b)
 #pragma unroll
       for (int c = 0; c < 4; ++c) acc[a][b][c] = 0.f;
+  const int g = lane >> 2, t = lane & 3;
+  const int h = warp & 1, p = (warp >> 1) & 1;
+  const int wj = strip * (kAwqGemvStrip / 8) + 8 * h + g;  // this lane's word column
+  const bool col_ok = wj < words_n;
 
-  // per word column c (0/1) and nibble pair i (0..3): duplicated (1024+z) and s
-  // for the A-fragment rows g (column 2i) and g+8 (column 2i+1).
-  uint32_t zlo[2][4], zhi[2][4], slo[2][4], shi[2][4];
-  int cur_group = -1;
-
-  const uint32_t* qrow_base = qweight + wc;
-  for (int u = u0; u < u1; ++u) {
-    const int kb = u << 6;
-    const int gi = kb / group;
-    if (gi != cur_group) {
-      cur_group = gi;
-      uint2 zw = make_uint2(0u, 0u);
-      uint4 s0 = make_uint4(0u, 0u, 0u, 0u), s1 = s0;
-      if (col_ok) {
-        zw = __ldg(reinterpret_cast<const uint2*>(qzeros + static_cast<int64_t>(gi) * words_n + wc));
-        const uint4* sp = reinterpret_cast<const uint4*>(scales + static_cast<int64_t>(gi) * N + wc * 8);
-        s0 = __ldg(sp);
-        s1 = __ldg(sp + 1);
+  if (warp == 4) {
+    // ---------------- producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tm_q);
+      for (int b = 0; b < nbox; ++b) {
+        const int s = b % ring;
+        if (!mbar_wait(&empty[s], ((b / ring) & 1) ^ 1, kErrWaitEmpty)) break;
+        mbar_arrive_expect_tx(&full[s], kAwqGemvBoxBytes);
+        tma_load_2d(&tm_q, &full[s], slots + s * kAwqGemvBoxBytes,
+                    strip * (kAwqGemvStrip / 8), (b_lo + b) * kAwqGemvBoxRows);
       }
-      const uint32_t zwv[2] = {zw.x, zw.y};
-      const uint32_t sv[2][4] = {{s0.x, s0.y, s0.z, s0.w}, {s1.x, s1.y, s1.z, s1.w}};
-#pragma unroll
-      for (int c = 0; c < 2; ++c)
+    }
+  } else {
+    // ---------------- consumers: boxes 2p, 2p+1, 2p+4, 2p+5, ...
+    const int odd = t & 1;
+    uint32_t zlo[4], zhi[4], slo[4], shi[4];
+    int cur_group = -1;
+    uint32_t zw_n = 0;
+    uint4 sv_n = make_uint4(0u, 0u, 0u, 0u);
+    int pre_group = -1;
+    auto fetch = [&](int gi) {
+      pre_group = gi;
+      if (col_ok) {
+        zw_n = __ldg(qzeros + static_cast<int64_t>(gi) * words_n + wj);
+        sv_n = __ldg(reinterpret_cast<const uint4*>(scales + static_cast<int64_t>(gi) * N + wj * 8));
+      }
+    };
+    bool ok = true;
+    int first = 2 * p;
+    if (first < nbox) fetch(((b_lo + first) * kAwqGemvBoxRows) / group);
+    for (int b = first; b < nbox && ok; b += ((b & 1) ? 3 : 1)) {
+      const int krow = (b_lo + b) * kAwqGemvBoxRows;
+      const int gi = krow / group;
+      if (gi != cur_group) {
+        cur_group = gi;
+        if (pre_group != gi) fetch(gi);
+        const uint32_t sv[4] = {sv_n.x, sv_n.y, sv_n.z, sv_n.w};
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          const uint32_t zp = lop3_and_or(zwv[c] >> (4 * i), 0x000F000Fu, 0x64006400u);
-          zlo[c][i] = prmt(zp, zp, 0x1010);  // (lo, lo)
-          zhi[c][i] = prmt(zp, zp, 0x3232);  // (hi, hi)
-          slo[c][i] = prmt(sv[c][i], sv[c][i], 0x1010);
-          shi[c][i] = prmt(sv[c][i], sv[c][i], 0x3232);
+          const uint32_t zp = lop3_and_or(zw_n >> (4 * i), 0x000F000Fu, 0x64006400u);
+          zlo[i] = prmt(zp, zp, 0x1010);  // (1024+z[2i], same)
+          zhi[i] = prmt(zp, zp, 0x3232);  // (1024+z[2i+1], same)
+          slo[i] = prmt(sv[i], sv[i], 0x1010);
+          shi[i] = prmt(sv[i], sv[i], 0x3232);
         }
-    }
-
-    // issue all loads of the 4 steps of this unit first
-    uint2 wv[4][4];  // [step][row slot: 2t, 2t+1, 2t+8, 2t+9]
-    uint32_t bx[4][MT][2];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int k0 = kb + 16 * j;
-      const int rows[4] = {k0 + 2 * t, k0 + 2 * t + 1, k0 + 2 * t + 8, k0 + 2 * t + 9};
-#pragma unroll
-      for (int r = 0; r < 4; ++r)
-        wv[j][r] = col_ok ? ldg_stream_u2(qrow_base + static_cast<int64_t>(rows[r]) * words_n)
-                          : make_uint2(0u, 0u);
-#pragma unroll
-      for (int mt = 0; mt < MT; ++mt) {
-        const int m = mt * 8 + g;
-        if (m < M) {
-          const uint32_t* xr = reinterpret_cast<const uint32_t*>(x + static_cast<int64_t>(m) * K + k0);
-          bx[j][mt][0] = __ldg(xr + t);
-          bx[j][mt][1] = __ldg(xr + 4 + t);
-        } else {
-          bx[j][mt][0] = 0u;
-          bx[j][mt][1] = 0u;
+        // prefetch the next group this warp will meet
+        const int bn = b + ((b & 1) ? 3 : 1);
+        if (bn < nbox) {
+          const int gn = ((b_lo + bn) * kAwqGemvBoxRows) / group;
+          if (gn != gi) fetch(gn);
         }
       }
-    }
-
+      // token fragments of the 4 steps (L1/L2 resident), before waiting on the box
+      uint32_t bx[4][MT][2];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
+      for (int s4 = 0; s4 < 4; ++s4)
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        const uint32_t w0 = c ? wv[j][0].y : wv[j][0].x;
-        const uint32_t w1 = c ? wv[j][1].y : wv[j][1].x;
-        const uint32_t w8 = c ? wv[j][2].y : wv[j][2].x;
-        const uint32_t w9 = c ? wv[j][3].y : wv[j][3].x;
+        for (int mt = 0; mt < MT; ++mt) {
+          const int m = mt * 8 + g;
+          if (m < M) {
+            const uint32_t* xr =
+                reinterpret_cast<const uint32_t*>(x + static_cast<int64_t>(m) * K + krow + 16 * s4);
+            bx[s4][mt][0] = __ldg(xr + t);
+            bx[s4][mt][1] = __ldg(xr + 4 + t);
+          } else {
+            bx[s4][mt][0] = 0u;
+            bx[s4][mt][1] = 0u;
+          }
+        }
+      const int slot = b % ring;
+      if (!(ok = mbar_wait(&full[slot], (b / ring) & 1, kErrWaitFull))) break;
+      const uint32_t sbase = smem_u32(slots + slot * kAwqGemvBoxBytes);
+      const int jj = 8 * h + g;
+#pragma unroll
+      for (int s4 = 0; s4 < 4; ++s4) {
+        const int r0 = 16 * s4 + 2 * t;
+        // odd-t lanes load the pair in swapped order: every LDS hits 32 distinct banks
+        const uint32_t v0 = lds_u32(sbase + sw64(r0 + odd, jj));
+        const uint32_t v1 = lds_u32(sbase + sw64(r0 + 1 - odd, jj));
+        const uint32_t v8 = lds_u32(sbase + sw64(r0 + 8 + odd, jj));
+        const uint32_t v9 = lds_u32(sbase + sw64(r0 + 9 - odd, jj));
+        const uint32_t w0 = odd ? v1 : v0, w1 = odd ? v0 : v1;
+        const uint32_t w8 = odd ? v9 : v8, w9 = odd ? v8 : v9;
         const uint32_t plo01 = prmt(w0, w1, 0x5410), phi01 = prmt(w0, w1, 0x7632);
         const uint32_t plo89 = prmt(w8, w9, 0x5410), phi89 = prmt(w8, w9, 0x7632);
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           uint32_t a[4];
-          a[0] = dq_h2(lop3_and_or(plo01 >> (4 * i), 0x000F000Fu, 0x64006400u), zlo[c][i], slo[c][i]);
-          a[1] = dq_h2(lop3_and_or(phi01 >> (4 * i), 0x000F000Fu, 0x64006400u), zhi[c][i], shi[c][i]);
-          a[2] = dq_h2(lop3_and_or(plo89 >> (4 * i), 0x000F000Fu, 0x64006400u), zlo[c][i], slo[c][i]);
-          a[3] = dq_h2(lop3_and_or(phi89 >> (4 * i), 0x000F000Fu, 0x64006400u), zhi[c][i], shi[c][i]);
+          a[0] = dq_h2(lop3_and_or(plo01 >> (4 * i), 0x000F000Fu, 0x64006400u), zlo[i], slo[i]);
+          a[1] = dq_h2(lop3_and_or(phi01 >> (4 * i), 0x000F000Fu, 0x64006400u), zhi[i], shi[i]);
+          a[2] = dq_h2(lop3_and_or(plo89 >> (4 * i), 0x000F000Fu, 0x64006400u), zlo[i], slo[i]);
+          a[3] = dq_h2(lop3_and_or(phi89 >> (4 * i), 0x000F000Fu, 0x64006400u), zhi[i], shi[i]);
 #pragma unroll
-          for (int mt = 0; mt < MT; ++mt) mma_f16_16816(acc[mt][c * 4 + i], a, bx[j][mt][0], bx[j][mt][1]);
+          for (int mt = 0; mt < MT; ++mt) mma_f16_16816(acc[mt][i], a, bx[s4][mt][0], bx[s4][mt][1]);
         }
       }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[slot]);
     }
   }
 
-  // ---- warp partials -> shared memory: red[warp][m][col], col in [0,128)
-  // D fragment: d0,d1 = (row g, tokens 2t, 2t+1); d2,d3 = (row g+8, same tokens).
-  // tile (c, i): row g = column 16g + 8c + 2i, row g+8 = that column + 1.
-  float* rw = red + static_cast<size_t>(warp) * MP * kAwqGemvStrip;
+  // ---- reduction: red[p][m][col] in the (drained) ring, then over p, then the cluster
+  float* red = reinterpret_cast<float*>(slots);
+  if (warp < 4) {
+    named_bar_sync(1, 128);  // every consumer is done reading the ring
+    // D fragment: d0,d1 = (row g, tokens 2t, 2t+1); d2,d3 = (row g+8, same tokens).
+    // tile i: row g = column 8*(8h+g) + 2i, row g+8 = that column + 1.
+    float* rp = red + static_cast<size_t>(p) * MP * kAwqGemvStrip;
 #pragma unroll
-  for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-    for (int c = 0; c < 2; ++c)
+    for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        const int col = 16 * g + 8 * c + 2 * i;
+        const int col = 8 * (8 * h + g) + 2 * i;
         const int m0 = mt * 8 + 2 * t;
-        const float* d = acc[mt][c * 4 + i];
-        rw[(m0 + 0) * kAwqGemvStrip + col] = d[0];
-        rw[(m0 + 1) * kAwqGemvStrip + col] = d[1];
-        rw[(m0 + 0) * kAwqGemvStrip + col + 1] = d[2];
-        rw[(m0 + 1) * kAwqGemvStrip + col + 1] = d[3];
+        rp[(m0 + 0) * kAwqGemvStrip + col] = acc[mt][i][0];
+        rp[(m0 + 1) * kAwqGemvStrip + col] = acc[mt][i][1];
+        rp[(m0 + 0) * kAwqGemvStrip + col + 1] = acc[mt][i][2];
+        rp[(m0 + 1) * kAwqGemvStrip + col + 1] = acc[mt][i][3];
       }
-  __syncthreads();
-  // sum over warps into red[0]
-  for (int e = threadIdx.x; e < MP * kAwqGemvStrip; e += blockDim.x) {
-    float s = red[e];
-    for (int w = 1; w < W; ++w) s += red[static_cast<size_t>(w) * MP * kAwqGemvStrip + e];
-    red[e] = s;
+    named_bar_sync(1, 128);
+    for (int e = threadIdx.x; e < MP * kAwqGemvStrip; e += 128) red[e] += red[MP * kAwqGemvStrip + e];
   }
-  // ---- cluster reduction: rank r finalises columns [r*128/C, (r+1)*128/C)
   cluster.sync();
   const int c0 = (rank * kAwqGemvStrip) / C, c1 = ((rank + 1) * kAwqGemvStrip) / C;
   const int ncol = c1 - c0;
@@ -204,10 +240,7 @@ __global__ void __launch_bounds__(256) awq_gemv_kernel(
     const int col = c0 + (e - m * ncol);
     const int n = strip * kAwqGemvStrip + col;
     float s = 0.f;
-    for (int r = 0; r < C; ++r) {
-      const float* peer = cluster.map_shared_rank(red, r);
-      s += peer[m * kAwqGemvStrip + col];
-    }
+    for (int r = 0; r < C; ++r) s += cluster.map_shared_rank(red, r)[m * kAwqGemvStrip + col];
     if (n < N) {
       if (bias != nullptr) s += __half2float(bias[n]);
       y[static_cast<int64_t>(m) * N + n] = __float2half_rn(s);

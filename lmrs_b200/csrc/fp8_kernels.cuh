@@ -9,13 +9,13 @@
 //
 // Decode GEMV (small M), swap-AB mma.sync m16n8k32 e4m3 x e4m3 -> fp32:
 // output channels are the MMA "M" rows (W's K-contiguous rows are exactly the
-// row-major A fragment), tokens are "N".  Each lane streams 16-byte chunks of
-// two weight rows per 128-byte K unit (ld.global.nc.L1::no_allocate).  The 32
-// k-slots of the four MMAs of a unit are a permutation of the unit's 128 bytes
-// chosen so that every lane's A bytes are two contiguous 16-byte chunks; the
-// token fragment is gathered with the same permutation.  Split-K across the
-// warps of a CTA and across a thread-block cluster, reduced in (distributed)
-// shared memory, scaled by s_x[m] * s_w[n] in the epilogue.
+// row-major A fragment), tokens are "N".  A producer warp streams weight tiles
+// into a shared-memory ring with TMA, consumer warps read 16-byte chunks of two
+// rows per 128-byte K unit.  The 32 k-slots of the four MMAs of a unit are a
+// permutation of the unit's 128 bytes chosen so that every lane's A bytes are
+// two contiguous 16-byte chunks; the token fragment is gathered with the same
+// permutation.  Split-K across a thread-block cluster, reduced through
+// distributed shared memory, scaled by s_x[m] * s_w[n] in the epilogue.
 #pragma once
 #include <cooperative_groups.h>
 #include "lmrs_ptx.cuh"
@@ -101,14 +101,6 @@ __global__ void __launch_bounds__(kQuantThreads) fp8_quant_rows_kernel(
 }
 
 // ------------------------------------------------------------------ GEMV
-__device__ __forceinline__ uint4 ldg_stream_u4(const void* p) {
-  uint4 v;
-  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "l"(p));
-  return v;
-}
-
 __device__ __forceinline__ void mma_e4m3_16832(float (&d)[4], uint32_t a0, uint32_t a1,
                                                uint32_t a2, uint32_t a3, uint32_t b0,
                                                uint32_t b1) {
@@ -119,100 +111,128 @@ __device__ __forceinline__ void mma_e4m3_16832(float (&d)[4], uint32_t a0, uint3
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-constexpr int kF8GemvRows = 32;  // output channels per warp strip (two 16-row MMA tiles)
+__device__ __forceinline__ uint4 lds_u4(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(addr));
+  return v;
+}
 
+constexpr int kF8GemvRows = 64;          // output channels per CTA strip (4 MMA tiles)
+constexpr int kF8GemvBoxBytes = kF8GemvRows * 128;  // 64 rows x 128 bytes of K = 8 KB
+constexpr int kF8GemvThreads = 160;      // 4 consumer warps + 1 producer warp
+constexpr int kF8GemvMaxRing = 6;
+
+// MT: 8-token MMA tiles (M <= 8 * MT).  A producer warp streams the strip's
+// weight rows (TMA boxes of 128 bytes of K x 64 rows, 128-byte swizzle) into a
+// ring of shared-memory slots; consumer warp w owns MMA tile w (channels
+// 16w..16w+15).  Within each 128-byte K unit, lane (g, t) takes the 16-byte
+// chunks t and 4+t of its two rows: the 32 k-slots of the unit's four MMAs are
+// a fixed permutation of the unit's bytes, and the token fragment (xq, read
+// through L1) uses the same permutation.
 template <int MT>
-__global__ void __launch_bounds__(256) fp8_gemv_kernel(
-    __nv_bfloat16* __restrict__ y, const uint8_t* __restrict__ xq, const float* __restrict__ sx,
-    const uint8_t* __restrict__ wq, const float* __restrict__ sw,
-    const __nv_bfloat16* __restrict__ bias, int M, int K, int N) {
+__global__ void __launch_bounds__(kF8GemvThreads, 4) fp8_gemv_kernel(
+    const __grid_constant__ CUtensorMap tm_w, __nv_bfloat16* __restrict__ y,
+    const uint8_t* __restrict__ xq, const float* __restrict__ sx, const float* __restrict__ sw,
+    const __nv_bfloat16* __restrict__ bias, int M, int K, int N, int ring) {
   constexpr int MP = 8 * MT;
-  constexpr int R = kF8GemvRows / 16;
-  extern __shared__ __align__(16) float red[];  // [W][MP][32]
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* slots = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                              ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(slots + ring * kF8GemvBoxBytes);
+  uint64_t* empty = full + ring;
 
   cg::cluster_group cluster = cg::this_cluster();
   const int C = static_cast<int>(cluster.num_blocks());
   const int rank = static_cast<int>(cluster.block_rank());
   const int strip = blockIdx.x / C;
-  const int W = blockDim.x >> 5;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
   const int nbase = strip * kF8GemvRows;
 
   const int units = (K + 127) >> 7;
-  const int KS = C * W;
-  const int slice = rank * W + warp;
-  const int u0 = static_cast<int>((static_cast<long long>(slice) * units) / KS);
-  const int u1 = static_cast<int>((static_cast<long long>(slice + 1) * units) / KS);
+  const int u_lo = static_cast<int>((static_cast<long long>(rank) * units) / C);
+  const int u_hi = static_cast<int>((static_cast<long long>(rank + 1) * units) / C);
+  const int nbox = u_hi - u_lo;
 
-  float acc[MT][R][4];
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < ring; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 4);  // every consumer warp reads every box
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  float acc[MT][4];
 #pragma unroll
   for (int a = 0; a < MT; ++a)
 #pragma unroll
-    for (int b = 0; b < R; ++b)
-#pragma unroll
-      for (int c = 0; c < 4; ++c) acc[a][b][c] = 0.f;
+    for (int c = 0; c < 4; ++c) acc[a][c] = 0.f;
 
-  const uint4 zero4 = make_uint4(0u, 0u, 0u, 0u);
-  for (int u = u0; u < u1; ++u) {
-    const int kb = u << 7;
-    const int ka = kb + 16 * t, kc = kb + 64 + 16 * t;  // this lane's two 16-byte chunks
-    const bool oka = ka < K, okc = kc < K;
-    uint4 wa[R][2][2];  // [tile][row g / g+8][chunk a / c]
-#pragma unroll
-    for (int r = 0; r < R; ++r)
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int n = nbase + 16 * r + 8 * h + g;
-        const uint8_t* wr = wq + static_cast<int64_t>(n) * K;
-        const bool nok = n < N;
-        wa[r][h][0] = (nok && oka) ? ldg_stream_u4(wr + ka) : zero4;
-        wa[r][h][1] = (nok && okc) ? ldg_stream_u4(wr + kc) : zero4;
+  if (warp == 4) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tm_w);
+      for (int b = 0; b < nbox; ++b) {
+        const int s = b % ring;
+        if (!mbar_wait(&empty[s], ((b / ring) & 1) ^ 1, kErrWaitEmpty)) break;
+        mbar_arrive_expect_tx(&full[s], kF8GemvBoxBytes);
+        tma_load_2d(&tm_w, &full[s], slots + s * kF8GemvBoxBytes, (u_lo + b) * 128, nbase);
       }
-    uint4 xb[MT][2];
-#pragma unroll
-    for (int mt = 0; mt < MT; ++mt) {
-      const int m = mt * 8 + g;
-      const uint8_t* xr = xq + static_cast<int64_t>(m) * K;
-      xb[mt][0] = (m < M && oka) ? __ldg(reinterpret_cast<const uint4*>(xr + ka)) : zero4;
-      xb[mt][1] = (m < M && okc) ? __ldg(reinterpret_cast<const uint4*>(xr + kc)) : zero4;
     }
+  } else {
+    const uint4 zero4 = make_uint4(0u, 0u, 0u, 0u);
+    const int r0 = 16 * warp + g;  // rows r0 and r0 + 8 of the box; (r0 % 8) == g
+    for (int b = 0; b < nbox; ++b) {
+      const int kb = (u_lo + b) << 7;
+      const int ka = kb + 16 * t, kc = kb + 64 + 16 * t;
+      uint4 xb[MT][2];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int c = j >> 1;
-      const bool hi = j & 1;
+      for (int mt = 0; mt < MT; ++mt) {
+        const int m = mt * 8 + g;
+        const uint8_t* xr = xq + static_cast<int64_t>(m) * K;
+        xb[mt][0] = (m < M && ka < K) ? __ldg(reinterpret_cast<const uint4*>(xr + ka)) : zero4;
+        xb[mt][1] = (m < M && kc < K) ? __ldg(reinterpret_cast<const uint4*>(xr + kc)) : zero4;
+      }
+      const int slot = b % ring;
+      if (!mbar_wait(&full[slot], (b / ring) & 1, kErrWaitFull)) break;
+      const uint32_t sb = smem_u32(slots + slot * kF8GemvBoxBytes);
+      // 128-byte swizzle: chunk c of row r sits at chunk c ^ (r % 8)
+      const uint4 ga = lds_u4(sb + r0 * 128 + ((t ^ g) << 4));
+      const uint4 gc = lds_u4(sb + r0 * 128 + (((4 + t) ^ g) << 4));
+      const uint4 ha = lds_u4(sb + (r0 + 8) * 128 + ((t ^ g) << 4));
+      const uint4 hc = lds_u4(sb + (r0 + 8) * 128 + (((4 + t) ^ g) << 4));
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[slot]);
 #pragma unroll
-      for (int r = 0; r < R; ++r) {
-        const uint4 g0 = wa[r][0][c], g8 = wa[r][1][c];
+      for (int j = 0; j < 4; ++j) {
+        const uint4 g0 = (j >> 1) ? gc : ga, g8 = (j >> 1) ? hc : ha;
+        const bool hi = j & 1;
         const uint32_t a0 = hi ? g0.z : g0.x, a2 = hi ? g0.w : g0.y;
         const uint32_t a1 = hi ? g8.z : g8.x, a3 = hi ? g8.w : g8.y;
 #pragma unroll
         for (int mt = 0; mt < MT; ++mt) {
-          const uint4 xv = xb[mt][c];
-          mma_e4m3_16832(acc[mt][r], a0, a1, a2, a3, hi ? xv.z : xv.x, hi ? xv.w : xv.y);
+          const uint4 xv = xb[mt][j >> 1];
+          mma_e4m3_16832(acc[mt], a0, a1, a2, a3, hi ? xv.z : xv.x, hi ? xv.w : xv.y);
         }
       }
     }
   }
 
-  // partials: D rows g / g+8 = channels 16r+g / 16r+g+8, cols 2t, 2t+1 = tokens
-  float* rw = red + static_cast<size_t>(warp) * MP * kF8GemvRows;
+  // ---- partials in the drained ring: red[m][row], rows 0..63 of the strip
+  float* red = reinterpret_cast<float*>(slots);
+  if (warp < 4) {
+    asm volatile("bar.sync 1, 128;" ::: "memory");
 #pragma unroll
-  for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-    for (int r = 0; r < R; ++r) {
-      const int ch = 16 * r + g;
+    for (int mt = 0; mt < MT; ++mt) {
+      const int ch = 16 * warp + g;
       const int m0 = mt * 8 + 2 * t;
-      rw[(m0 + 0) * kF8GemvRows + ch] = acc[mt][r][0];
-      rw[(m0 + 1) * kF8GemvRows + ch] = acc[mt][r][1];
-      rw[(m0 + 0) * kF8GemvRows + ch + 8] = acc[mt][r][2];
-      rw[(m0 + 1) * kF8GemvRows + ch + 8] = acc[mt][r][3];
+      red[(m0 + 0) * kF8GemvRows + ch] = acc[mt][0];
+      red[(m0 + 1) * kF8GemvRows + ch] = acc[mt][1];
+      red[(m0 + 0) * kF8GemvRows + ch + 8] = acc[mt][2];
+      red[(m0 + 1) * kF8GemvRows + ch + 8] = acc[mt][3];
     }
-  __syncthreads();
-  for (int e = threadIdx.x; e < MP * kF8GemvRows; e += blockDim.x) {
-    float s = red[e];
-    for (int w = 1; w < W; ++w) s += red[static_cast<size_t>(w) * MP * kF8GemvRows + e];
-    red[e] = s;
   }
   cluster.sync();
   const int c0 = (rank * kF8GemvRows) / C, c1 = ((rank + 1) * kF8GemvRows) / C;
@@ -230,6 +250,7 @@ __global__ void __launch_bounds__(256) fp8_gemv_kernel(
     }
   }
   cluster.sync();
+  (void)MP;
 }
 
 }  // namespace lmrs

@@ -37,8 +37,7 @@ thread_local int t_last_cuda_error = 0;
 struct Tuning {
   int awq_gemv_max_m = 16;   // M above this -> tcgen05 GEMM
   int fp8_gemv_max_m = 32;
-  int gemv_warps = 4;        // warps per CTA in the split-K GEMVs
-  int gemv_target_warps = 148 * 16;
+  int gemv_ctas_per_sm = 4;  // resident CTAs per SM the GEMV grids are sized for
   int awq_gemv_cluster = 0;  // 0 = heuristic
   int fp8_gemv_cluster = 0;
 };
@@ -69,6 +68,25 @@ int check_device(int* dev_out) {
   }
   if (dev_out) *dev_out = dev;
   return st == 1 ? LMRS_OK : LMRS_ERR_DEVICE;
+}
+
+// ---- SM count per device (persistent grids)
+std::atomic<int> g_sm_count[kMaxDevices];
+
+int sm_count(int dev) {
+  int v = g_sm_count[dev].load(std::memory_order_relaxed);
+  if (v == 0) {
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0)
+      v = 148;
+    g_sm_count[dev].store(v, std::memory_order_relaxed);
+  }
+  return v;
+}
+
+int sm_count_cached() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return 148;
+  return sm_count(dev);
 }
 
 // ---- dynamic shared memory opt-in, once per (kernel, device)
@@ -128,21 +146,6 @@ int after_launch() {
 
 int clampi(int v, int lo, int hi) { return v < lo ? lo : (v > hi ? hi : v); }
 
-// split-K factor for a GEMV with `strips` independent column strips and
-// `units` K units: fill ~target warps, W warps per CTA, cluster <= 8.
-void gemv_grid(int strips, int units, int forced_cluster, int* W_out, int* C_out) {
-  const int W = clampi(g_tune.gemv_warps, 1, 8);
-  int C = forced_cluster;
-  if (C <= 0) {
-    const int want = (g_tune.gemv_target_warps + strips - 1) / strips;  // warps per strip
-    C = (want + W - 1) / W;
-  }
-  C = clampi(C, 1, 8);
-  while (C > 1 && C * W > units) --C;  // keep every warp busy
-  *W_out = W;
-  *C_out = C;
-}
-
 template <typename Kern, typename... Args>
 int launch_cluster(Kern kernel, int grid_x, int cluster, int threads, int smem,
                    cudaStream_t stream, Args... args) {
@@ -169,25 +172,39 @@ std::atomic<int> g_smem_awq_gemv[3][kMaxDevices];
 std::atomic<int> g_smem_f8_gemv[3][kMaxDevices];
 
 // ------------------------------------------------------------------ AWQ
-int awq_gemv_launch(__half* y, const __half* x, const uint32_t* qw, const uint32_t* qz,
+// Cluster size for a TMA-fed GEMV: split K over C CTAs so that every CTA of
+// the grid is resident at once (~4 per SM), C <= 8 and C <= K units.
+int gemv_cluster(int strips, int units, int forced) {
+  int C = forced > 0 ? forced : (sm_count_cached() * g_tune.gemv_ctas_per_sm) / (strips > 0 ? strips : 1);
+  C = clampi(C, 1, 8);
+  if (C > units) C = units > 0 ? units : 1;
+  return C;
+}
+
+int awq_gemv_launch(__half* y, const __half* x, const int32_t* qw, const uint32_t* qz,
                     const __half* sc, const __half* bias, int M, int K, int N, int group,
                     cudaStream_t stream, int dev) {
   const int strips = (N + lmrs::kAwqGemvStrip - 1) / lmrs::kAwqGemvStrip;
-  int W, C;
-  gemv_grid(strips, K / 64, g_tune.awq_gemv_cluster, &W, &C);
-  const int MT = M <= 8 ? 1 : 2;
-  const int smem = W * 8 * MT * lmrs::kAwqGemvStrip * 4;
+  const int nb_all = K / lmrs::kAwqGemvBoxRows;
+  const int C = gemv_cluster(strips, nb_all, g_tune.awq_gemv_cluster);
+  const int per_cta = (nb_all + C - 1) / C;
+  int ring = per_cta < lmrs::kAwqGemvMaxRing ? per_cta : lmrs::kAwqGemvMaxRing;
+  if (ring < 4) ring = 4;  // the drained ring also holds the 2 x 16 x 128 fp32 partials
+  const int smem = 1024 + ring * lmrs::kAwqGemvBoxBytes + ring * 16;
+  CUtensorMap tq;
   int rc;
+  if ((rc = make_tmap(&tq, CU_TENSOR_MAP_DATA_TYPE_INT32, qw, N / 8, K, uint64_t(N / 8) * 4,
+                      lmrs::kAwqGemvStrip / 8, lmrs::kAwqGemvBoxRows, CU_TENSOR_MAP_SWIZZLE_64B)))
+    return rc;
+  const int MT = M <= 8 ? 1 : 2;
   if (MT == 1) {
-    rc = ensure_smem(lmrs::awq_gemv_kernel<1>, smem, g_smem_awq_gemv[0], dev);
-    if (rc) return rc;
-    rc = launch_cluster(lmrs::awq_gemv_kernel<1>, strips * C, C, 32 * W, smem, stream, y, x, qw,
-                        qz, sc, bias, M, K, N, group);
+    if ((rc = ensure_smem(lmrs::awq_gemv_kernel<1>, smem, g_smem_awq_gemv[0], dev))) return rc;
+    rc = launch_cluster(lmrs::awq_gemv_kernel<1>, strips * C, C, lmrs::kAwqGemvThreads, smem,
+                        stream, tq, y, x, qz, sc, bias, M, K, N, group, ring);
   } else {
-    rc = ensure_smem(lmrs::awq_gemv_kernel<2>, smem, g_smem_awq_gemv[1], dev);
-    if (rc) return rc;
-    rc = launch_cluster(lmrs::awq_gemv_kernel<2>, strips * C, C, 32 * W, smem, stream, y, x, qw,
-                        qz, sc, bias, M, K, N, group);
+    if ((rc = ensure_smem(lmrs::awq_gemv_kernel<2>, smem, g_smem_awq_gemv[1], dev))) return rc;
+    rc = launch_cluster(lmrs::awq_gemv_kernel<2>, strips * C, C, lmrs::kAwqGemvThreads, smem,
+                        stream, tq, y, x, qz, sc, bias, M, K, N, group, ring);
   }
   return rc ? rc : after_launch();
 }
@@ -211,7 +228,8 @@ int awq_gemm_launch(__half* y, const __half* x, const int32_t* qw, const int32_t
     return rc;
   if ((rc = ensure_smem(lmrs::awq_gemm_tc_kernel, lmrs::kAwqSmemBytes, g_smem_awq_gemm, dev)))
     return rc;
-  dim3 grid((N + lmrs::kTcBN - 1) / lmrs::kTcBN, (M + lmrs::kTcBM - 1) / lmrs::kTcBM);
+  const int tiles = ((N + lmrs::kTcBN - 1) / lmrs::kTcBN) * ((M + lmrs::kTcBM - 1) / lmrs::kTcBM);
+  const int grid = tiles < sm_count(dev) ? tiles : sm_count(dev);
   lmrs::awq_gemm_tc_kernel<<<grid, lmrs::kAwqGemmThreads, lmrs::kAwqSmemBytes, stream>>>(
       tx, tq, ts, tz, y, bias, M, K, N, group);
   return after_launch();
@@ -242,23 +260,30 @@ int fp8_gemv_launch(__nv_bfloat16* y, const uint8_t* xq, const float* sx, const 
                     const float* sw, const __nv_bfloat16* bias, int M, int K, int N,
                     cudaStream_t stream, int dev) {
   const int strips = (N + lmrs::kF8GemvRows - 1) / lmrs::kF8GemvRows;
-  int W, C;
-  gemv_grid(strips, (K + 127) / 128, g_tune.fp8_gemv_cluster, &W, &C);
-  const int MT = M <= 8 ? 1 : (M <= 16 ? 2 : 4);
-  const int smem = W * 8 * MT * lmrs::kF8GemvRows * 4;
+  const int units = (K + 127) / 128;
+  const int C = gemv_cluster(strips, units, g_tune.fp8_gemv_cluster);
+  const int per_cta = (units + C - 1) / C;
+  int ring = per_cta < lmrs::kF8GemvMaxRing ? per_cta : lmrs::kF8GemvMaxRing;
+  if (ring < 1) ring = 1;
+  const int smem = 1024 + ring * lmrs::kF8GemvBoxBytes + ring * 16;
+  CUtensorMap tw;
   int rc;
+  if ((rc = make_tmap(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, wq, K, N, uint64_t(K), 128,
+                      lmrs::kF8GemvRows, CU_TENSOR_MAP_SWIZZLE_128B)))
+    return rc;
+  const int MT = M <= 8 ? 1 : (M <= 16 ? 2 : 4);
   if (MT == 1) {
     if ((rc = ensure_smem(lmrs::fp8_gemv_kernel<1>, smem, g_smem_f8_gemv[0], dev))) return rc;
-    rc = launch_cluster(lmrs::fp8_gemv_kernel<1>, strips * C, C, 32 * W, smem, stream, y, xq, sx,
-                        wq, sw, bias, M, K, N);
+    rc = launch_cluster(lmrs::fp8_gemv_kernel<1>, strips * C, C, lmrs::kF8GemvThreads, smem,
+                        stream, tw, y, xq, sx, sw, bias, M, K, N, ring);
   } else if (MT == 2) {
     if ((rc = ensure_smem(lmrs::fp8_gemv_kernel<2>, smem, g_smem_f8_gemv[1], dev))) return rc;
-    rc = launch_cluster(lmrs::fp8_gemv_kernel<2>, strips * C, C, 32 * W, smem, stream, y, xq, sx,
-                        wq, sw, bias, M, K, N);
+    rc = launch_cluster(lmrs::fp8_gemv_kernel<2>, strips * C, C, lmrs::kF8GemvThreads, smem,
+                        stream, tw, y, xq, sx, sw, bias, M, K, N, ring);
   } else {
     if ((rc = ensure_smem(lmrs::fp8_gemv_kernel<4>, smem, g_smem_f8_gemv[2], dev))) return rc;
-    rc = launch_cluster(lmrs::fp8_gemv_kernel<4>, strips * C, C, 32 * W, smem, stream, y, xq, sx,
-                        wq, sw, bias, M, K, N);
+    rc = launch_cluster(lmrs::fp8_gemv_kernel<4>, strips * C, C, lmrs::kF8GemvThreads, smem,
+                        stream, tw, y, xq, sx, sw, bias, M, K, N, ring);
   }
   return rc ? rc : after_launch();
 }
@@ -276,7 +301,8 @@ int fp8_gemm_launch(__nv_bfloat16* y, const uint8_t* xq, const float* sx, const 
     return rc;
   if ((rc = ensure_smem(lmrs::fp8_gemm_tc_kernel, lmrs::kF8SmemBytes, g_smem_f8_gemm, dev)))
     return rc;
-  dim3 grid((N + lmrs::kTcBN - 1) / lmrs::kTcBN, (M + lmrs::kTcBM - 1) / lmrs::kTcBM);
+  const int tiles = ((N + lmrs::kTcBN - 1) / lmrs::kTcBN) * ((M + lmrs::kTcBM - 1) / lmrs::kTcBM);
+  const int grid = tiles < sm_count(dev) ? tiles : sm_count(dev);
   lmrs::fp8_gemm_tc_kernel<<<grid, lmrs::kF8Threads, lmrs::kF8SmemBytes, stream>>>(
       ta, tb, y, sx, sw, bias, M, K, N);
   return after_launch();
@@ -338,8 +364,7 @@ int lmrs_set_tuning(const char* key, int value) {
   if (!key) return LMRS_ERR_NULL;
   if (!strcmp(key, "awq_gemv_max_m")) g_tune.awq_gemv_max_m = value;
   else if (!strcmp(key, "fp8_gemv_max_m")) g_tune.fp8_gemv_max_m = value;
-  else if (!strcmp(key, "gemv_warps")) g_tune.gemv_warps = value;
-  else if (!strcmp(key, "gemv_target_warps")) g_tune.gemv_target_warps = value;
+  else if (!strcmp(key, "gemv_ctas_per_sm")) g_tune.gemv_ctas_per_sm = value;
   else if (!strcmp(key, "awq_gemv_cluster")) g_tune.awq_gemv_cluster = value;
   else if (!strcmp(key, "fp8_gemv_cluster")) g_tune.fp8_gemv_cluster = value;
   else return LMRS_ERR_SHAPE;
@@ -410,9 +435,8 @@ int lmrs_awq_linear(void* y, const void* x, const int32_t* qweight, const int32_
   auto* sh = static_cast<const __half*>(scales);
   auto* bh = static_cast<const __half*>(bias_or_null);
   if (M <= g_tune.awq_gemv_max_m && M <= 16)
-    return awq_gemv_launch(yh, xh, reinterpret_cast<const uint32_t*>(qweight),
-                           reinterpret_cast<const uint32_t*>(qzeros), sh, bh, M, K, N, group, st,
-                           dev);
+    return awq_gemv_launch(yh, xh, qweight, reinterpret_cast<const uint32_t*>(qzeros), sh, bh, M,
+                           K, N, group, st, dev);
   return awq_gemm_launch(yh, xh, qweight, qzeros, sh, bh, M, K, N, group, st, dev);
 }
 

@@ -3,20 +3,26 @@
 //   awq_gemm_tc_kernel : y fp16 [M,N] = x fp16 [M,K] @ dequant(AWQ int4) (+bias)
 //   fp8_gemm_tc_kernel : y bf16 [M,N] = (xq e4m3 [M,K] @ wq e4m3 [N,K]^T) * sx[m] * sw[n] (+bias)
 //
-// Shared structure (one 128 x 256 output tile per CTA, cta_group::1):
-//   warp 0      TMA producer: one elected thread streams K-blocks into a ring of
-//               shared-memory stages (cp.async.bulk.tensor, 128-byte swizzle,
-//               completion counted on a per-stage mbarrier).
-//   warp 1      TMEM owner + MMA issuer: one thread issues tcgen05.mma with
-//               shared-memory descriptors, fp32 accumulator in TMEM (256 cols);
-//               tcgen05.commit frees each stage when its MMAs have read it.
-//   warps 2..   AWQ only: dequant warps turn the TMA-staged packed int4 tile
-//               into fp16 in the UMMA MN-major 128B-swizzled layout (operand B)
-//               — the dequant is fused into the shared-memory stage, weights are
-//               read from HBM once, as int4.
-//   epilogue    tcgen05.ld (32 lanes x 32 bit) -> scale / bias / round -> global.
+// Both are persistent, warp-specialised kernels: one CTA per SM walks output
+// tiles (128 x 256) tile = blockIdx.x, blockIdx.x + gridDim.x, ...  (M-major
+// order, so CTAs running together share the x tile in L2).
+//
+//   warp 0        TMA producer: one thread streams K-blocks into a ring of
+//                 shared-memory stages (cp.async.bulk.tensor, 128B swizzle,
+//                 per-stage mbarrier with transaction count).
+//   warp 1        TMEM owner (512 columns = two 128x256 fp32 accumulators) and
+//                 MMA issuer: one thread issues tcgen05.mma from shared-memory
+//                 descriptors; tcgen05.commit frees each stage and, at the end
+//                 of a tile, hands the accumulator to the epilogue.
+//   warps 2..5    epilogue: tcgen05.ld (32 lanes x 32 bit) -> scale/bias/round ->
+//                 global, then release the accumulator buffer.  Double
+//                 buffering lets tile i's epilogue overlap tile i+1's mainloop.
+//   warps 6..13   AWQ only: dequant warps turn the TMA-staged packed int4 tile
+//                 into fp16 directly in the UMMA MN-major 128B-swizzled layout
+//                 (operand B): the dequant is fused into the shared-memory
+//                 stage and weights cross HBM once, as int4.
 // Every mbarrier wait is bounded (lmrs_ptx.cuh): on expiry the kernel records
-// the site in the device error word and unwinds, TMEM is always released.
+// the site in the device error word and unwinds; TMEM is always released.
 #pragma once
 #include "lmrs_ptx.cuh"
 
@@ -24,7 +30,9 @@ namespace lmrs {
 
 constexpr int kTcBM = 128;
 constexpr int kTcBN = 256;
-constexpr uint32_t kTcTmemCols = 256;
+constexpr uint32_t kTcTmemCols = 512;  // two accumulators of kTcBN fp32 columns
+constexpr int kTcEpiWarp0 = 2;         // epilogue warps 2..5
+constexpr int kTcEpiWarps = 4;
 
 __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
   return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
@@ -36,12 +44,26 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint4 v) {
                : "memory");
 }
 
+// Accumulator hand-off barriers (MMA -> epilogue -> MMA), two buffers.
+struct AccBars {
+  uint64_t full[2];
+  uint64_t empty[2];
+};
+
+__device__ __forceinline__ void acc_bars_init(AccBars* b) {
+  for (int i = 0; i < 2; ++i) {
+    mbar_init(&b->full[i], 1);
+    mbar_init(&b->empty[i], kTcEpiWarps);
+  }
+}
+
 // ============================================================ AWQ W4A16 GEMM
 constexpr int kAwqBK = 64;        // k rows per stage (one 128-byte fp16 row of A)
 constexpr int kAwqSA = 4;         // TMA stages: A tile + packed tile + scales + zeros
 constexpr int kAwqSB = 3;         // dequantised B stages
+constexpr int kAwqDqWarp0 = 6;
 constexpr int kAwqDqWarps = 8;
-constexpr int kAwqGemmThreads = 32 * (2 + kAwqDqWarps);
+constexpr int kAwqGemmThreads = 32 * (kAwqDqWarp0 + kAwqDqWarps);  // 448
 constexpr int kAwqABytes = kTcBM * kAwqBK * 2;        // 16 KB
 constexpr int kAwqBBytes = kTcBN * kAwqBK * 2;        // 32 KB
 constexpr int kAwqPBytes = kAwqBK * (kTcBN / 8) * 4;  // 8 KB
@@ -68,12 +90,14 @@ __global__ void __launch_bounds__(kAwqGemmThreads, 1)
   uint64_t* empty = full + kAwqSA;
   uint64_t* bfull = empty + kAwqSA;
   uint64_t* bempty = bfull + kAwqSB;
-  uint64_t* accum = bempty + kAwqSB;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
+  AccBars* acc = reinterpret_cast<AccBars*>(bempty + kAwqSB);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n0 = blockIdx.x * kTcBN, m0 = blockIdx.y * kTcBM;
   const int KB = K / kAwqBK;
+  const int n_tiles = (N + kTcBN - 1) / kTcBN;
+  const int m_tiles = (M + kTcBM - 1) / kTcBM;
+  const int tiles = n_tiles * m_tiles;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kAwqSA; ++s) {
@@ -84,7 +108,7 @@ __global__ void __launch_bounds__(kAwqGemmThreads, 1)
       mbar_init(&bfull[s], kAwqDqWarps);
       mbar_init(&bempty[s], 1);
     }
-    mbar_init(accum, 1);
+    acc_bars_init(acc);
     fence_mbar_init();
   }
   if (warp == 0 && lane == 0) {
@@ -105,87 +129,69 @@ __global__ void __launch_bounds__(kAwqGemmThreads, 1)
   if (warp == 0) {
     if (lane == 0) {
       const uint64_t keep = policy_evict_last();  // x tile is re-read by every N tile
-      for (int kb = 0; kb < KB; ++kb) {
-        const int s = kb % kAwqSA;
-        if (!mbar_wait(&empty[s], ((kb / kAwqSA) & 1) ^ 1, kErrWaitEmpty)) break;
-        mbar_arrive_expect_tx(&full[s], kAwqStageTx);
-        const int k = kb * kAwqBK;
-        const int gi = k / group;
-        tma_load_2d_hint(&tm_x, &full[s], sA + s * kAwqABytes, k, m0, keep);
-        tma_load_2d(&tm_q, &full[s], sP + s * kAwqPBytes, n0 / 8, k);
-        tma_load_2d(&tm_s, &full[s], sS + s * kAwqSBytes, n0, gi);
-        tma_load_2d(&tm_z, &full[s], sZ + s * kAwqZBytes, n0 / 8, gi);
+      uint32_t kg = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+        const int m0 = (t / n_tiles) * kTcBM, n0 = (t % n_tiles) * kTcBN;
+        for (int kb = 0; kb < KB; ++kb, ++kg) {
+          const int s = kg % kAwqSA;
+          if (!(ok = mbar_wait(&empty[s], ((kg / kAwqSA) & 1) ^ 1, kErrWaitEmpty))) break;
+          mbar_arrive_expect_tx(&full[s], kAwqStageTx);
+          const int k = kb * kAwqBK;
+          const int gi = k / group;
+          tma_load_2d_hint(&tm_x, &full[s], sA + s * kAwqABytes, k, m0, keep);
+          tma_load_2d(&tm_q, &full[s], sP + s * kAwqPBytes, n0 / 8, k);
+          tma_load_2d(&tm_s, &full[s], sS + s * kAwqSBytes, n0, gi);
+          tma_load_2d(&tm_z, &full[s], sZ + s * kAwqZBytes, n0 / 8, gi);
+        }
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
       constexpr uint32_t idesc = make_idesc(0, 0, /*a K-major*/ 0, /*b MN-major*/ 1, kTcBM, kTcBN);
+      uint32_t kg = 0, it = 0;
       bool ok = true;
-      for (int kb = 0; kb < KB && ok; ++kb) {
-        const int s = kb % kAwqSA, sb = kb % kAwqSB;
-        ok = mbar_wait(&bfull[sb], (kb / kAwqSB) & 1, kErrWaitDequant) &&
-             mbar_wait(&full[s], (kb / kAwqSA) & 1, kErrWaitFull);
-        if (!ok) break;
+      for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++it) {
+        const uint32_t a = it & 1;
+        if (!(ok = mbar_wait(&acc->empty[a], ((it >> 1) & 1) ^ 1, kErrWaitAccum))) break;
         tc_fence_after();
-        const uint32_t a0 = smem_u32(sA + s * kAwqABytes);
-        const uint32_t b0 = smem_u32(sB + sb * kAwqBBytes);
+        const uint32_t d = tmem + a * kTcBN;
+        for (int kb = 0; kb < KB; ++kb, ++kg) {
+          const int s = kg % kAwqSA, sb = kg % kAwqSB;
+          ok = mbar_wait(&bfull[sb], (kg / kAwqSB) & 1, kErrWaitDequant) &&
+               mbar_wait(&full[s], (kg / kAwqSA) & 1, kErrWaitFull);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sA + s * kAwqABytes);
+          const uint32_t b0 = smem_u32(sB + sb * kAwqBBytes);
 #pragma unroll
-        for (int kk = 0; kk < kAwqBK / 16; ++kk) {
-          const uint64_t ad = make_sdesc(a0 + kk * 32, 16, 1024);
-          const uint64_t bd = make_sdesc(b0 + kk * 2048, 8192, 1024);
-          umma_f16(tmem, ad, bd, idesc, (kb | kk) != 0 ? 1u : 0u);
+          for (int kk = 0; kk < kAwqBK / 16; ++kk) {
+            const uint64_t ad = make_sdesc(a0 + kk * 32, 16, 1024);
+            const uint64_t bd = make_sdesc(b0 + kk * 2048, 8192, 1024);
+            umma_f16(d, ad, bd, idesc, (kb | kk) != 0 ? 1u : 0u);
+          }
+          umma_commit(&empty[s]);
+          umma_commit(&bempty[sb]);
         }
-        umma_commit(&empty[s]);
-        umma_commit(&bempty[sb]);
+        if (ok) umma_commit(&acc->full[a]);
       }
-      if (ok) umma_commit(accum);
     }
-  } else {
-    // ---------------- dequant warps
-    const int dw = warp - 2;
-    const int bblk = lane >> 3, chunk = lane & 7;
-    bool ok = true;
-    for (int kb = 0; kb < KB; ++kb) {
-      const int s = kb % kAwqSA, sb = kb % kAwqSB;
-      ok = mbar_wait(&full[s], (kb / kAwqSA) & 1, kErrWaitFull) &&
-           mbar_wait(&bempty[sb], ((kb / kAwqSB) & 1) ^ 1, kErrWaitEmpty);
-      if (!ok) break;
-      const uint32_t zw = reinterpret_cast<const uint32_t*>(sZ + s * kAwqZBytes)[lane];
-      const uint4 sv = reinterpret_cast<const uint4*>(sS + s * kAwqSBytes)[lane];
-      uint32_t zb[4];
-      awq_word_to_h2_biased(zw, zb);
-      const uint32_t* prow = reinterpret_cast<const uint32_t*>(sP + s * kAwqPBytes);
-      const uint32_t bbase = smem_u32(sB + sb * kAwqBBytes) + bblk * 8192;
-#pragma unroll
-      for (int rr = 0; rr < kAwqBK / kAwqDqWarps; ++rr) {
-        const int r = dw * (kAwqBK / kAwqDqWarps) + rr;
-        const uint32_t w = prow[r * 32 + lane];
-        uint32_t qb[4];
-        awq_word_to_h2_biased(w, qb);
-        uint4 o;
-        o.x = dq_h2(qb[0], zb[0], sv.x);
-        o.y = dq_h2(qb[1], zb[1], sv.y);
-        o.z = dq_h2(qb[2], zb[2], sv.z);
-        o.w = dq_h2(qb[3], zb[3], sv.w);
-        const uint32_t addr = bbase + (r >> 3) * 1024 + (r & 7) * 128 + ((chunk ^ (r & 7)) << 4);
-        st_shared_v4(addr, o);
-      }
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bfull[sb]);
-    }
-    // ---------------- epilogue: warps 2..9, two per TMEM lane quarter
-    if (ok && mbar_wait(accum, 0, kErrWaitAccum)) {
+  } else if (warp < kTcEpiWarp0 + kTcEpiWarps) {
+    // ---------------- epilogue: warp w reads TMEM lanes 32*(w%4) .. +31
+    const int quarter = warp & 3;
+    uint32_t it = 0;
+    for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++it) {
+      const uint32_t a = it & 1;
+      if (!mbar_wait(&acc->full[a], (it >> 1) & 1, kErrWaitAccum)) break;
       tc_fence_after();
-      const int quarter = warp & 3;
-      const int half = (warp - 2) >> 2;
+      const int m0 = (t / n_tiles) * kTcBM, n0 = (t % n_tiles) * kTcBN;
       const int row = m0 + quarter * 32 + lane;
-      for (int ch = 0; ch < 8; ++ch) {
-        const int col = half * 128 + ch * 16;
+      const uint32_t tbase = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + a * kTcBN;
+      for (int ch = 0; ch < kTcBN / 16; ++ch) {
         uint32_t r[16];
-        tmem_ld16(tmem + (static_cast<uint32_t>(quarter * 32) << 16) + col, r);
+        tmem_ld16(tbase + ch * 16, r);
         tmem_ld_wait();
-        const int n = n0 + col;
+        const int n = n0 + ch * 16;
         if (row < M && n < N) {
           uint32_t packed[8];
 #pragma unroll
@@ -202,6 +208,49 @@ __global__ void __launch_bounds__(kAwqGemmThreads, 1)
           dst[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
         }
       }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc->empty[a]);
+    }
+  } else {
+    // ---------------- dequant warps: packed int4 stage -> fp16 MN-major SW128 B stage
+    const int dw = warp - kAwqDqWarp0;
+    const int bblk = lane >> 3, chunk = lane & 7;
+    uint32_t kg = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+      for (int kb = 0; kb < KB; ++kb, ++kg) {
+        const int s = kg % kAwqSA, sb = kg % kAwqSB;
+        ok = mbar_wait(&full[s], (kg / kAwqSA) & 1, kErrWaitFull) &&
+             mbar_wait(&bempty[sb], ((kg / kAwqSB) & 1) ^ 1, kErrWaitEmpty);
+        if (!ok) break;
+        const uint32_t zw = reinterpret_cast<const uint32_t*>(sZ + s * kAwqZBytes)[lane];
+        const uint4 sv = reinterpret_cast<const uint4*>(sS + s * kAwqSBytes)[lane];
+        uint32_t zb[4];
+        awq_word_to_h2_biased(zw, zb);
+        const uint32_t* prow = reinterpret_cast<const uint32_t*>(sP + s * kAwqPBytes);
+        const uint32_t bbase = smem_u32(sB + sb * kAwqBBytes) + bblk * 8192;
+        uint32_t w[kAwqBK / kAwqDqWarps];
+#pragma unroll
+        for (int rr = 0; rr < kAwqBK / kAwqDqWarps; ++rr)
+          w[rr] = prow[(dw * (kAwqBK / kAwqDqWarps) + rr) * 32 + lane];
+#pragma unroll
+        for (int rr = 0; rr < kAwqBK / kAwqDqWarps; ++rr) {
+          const int r = dw * (kAwqBK / kAwqDqWarps) + rr;
+          uint32_t qb[4];
+          awq_word_to_h2_biased(w[rr], qb);
+          uint4 o;
+          o.x = dq_h2(qb[0], zb[0], sv.x);
+          o.y = dq_h2(qb[1], zb[1], sv.y);
+          o.z = dq_h2(qb[2], zb[2], sv.z);
+          o.w = dq_h2(qb[3], zb[3], sv.w);
+          const uint32_t addr = bbase + (r >> 3) * 1024 + (r & 7) * 128 + ((chunk ^ (r & 7)) << 4);
+          st_shared_v4(addr, o);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bfull[sb]);
+      }
     }
   }
   tc_fence_before();
@@ -215,7 +264,7 @@ __global__ void __launch_bounds__(kAwqGemmThreads, 1)
 // ============================================================ FP8 W8A8 GEMM
 constexpr int kF8BK = 128;  // bytes (= e4m3 elements) of K per stage
 constexpr int kF8Stages = 4;
-constexpr int kF8Threads = 192;  // producer, MMA, 4 epilogue warps
+constexpr int kF8Threads = 32 * (kTcEpiWarp0 + kTcEpiWarps);  // 192
 constexpr int kF8ABytes = kTcBM * kF8BK;  // 16 KB
 constexpr int kF8BBytes = kTcBN * kF8BK;  // 32 KB
 constexpr int kF8SmemBytes = 1024 + kF8Stages * (kF8ABytes + kF8BBytes) + 256;
@@ -231,19 +280,21 @@ __global__ void __launch_bounds__(kF8Threads, 1)
   uint8_t* sB = sA + kF8Stages * kF8ABytes;
   uint64_t* full = reinterpret_cast<uint64_t*>(sB + kF8Stages * kF8BBytes);
   uint64_t* empty = full + kF8Stages;
-  uint64_t* accum = empty + kF8Stages;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
+  AccBars* acc = reinterpret_cast<AccBars*>(empty + kF8Stages);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n0 = blockIdx.x * kTcBN, m0 = blockIdx.y * kTcBM;
   const int KB = (K + kF8BK - 1) / kF8BK;
+  const int n_tiles = (N + kTcBN - 1) / kTcBN;
+  const int m_tiles = (M + kTcBM - 1) / kTcBM;
+  const int tiles = n_tiles * m_tiles;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kF8Stages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(accum, 1);
+    acc_bars_init(acc);
     fence_mbar_init();
   }
   if (warp == 0 && lane == 0) {
@@ -262,47 +313,63 @@ __global__ void __launch_bounds__(kF8Threads, 1)
   if (warp == 0) {
     if (lane == 0) {
       const uint64_t keep = policy_evict_last();
-      for (int kb = 0; kb < KB; ++kb) {
-        const int s = kb % kF8Stages;
-        if (!mbar_wait(&empty[s], ((kb / kF8Stages) & 1) ^ 1, kErrWaitEmpty)) break;
-        mbar_arrive_expect_tx(&full[s], kF8ABytes + kF8BBytes);
-        tma_load_2d_hint(&tm_a, &full[s], sA + s * kF8ABytes, kb * kF8BK, m0, keep);
-        tma_load_2d(&tm_b, &full[s], sB + s * kF8BBytes, kb * kF8BK, n0);
+      uint32_t kg = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+        const int m0 = (t / n_tiles) * kTcBM, n0 = (t % n_tiles) * kTcBN;
+        for (int kb = 0; kb < KB; ++kb, ++kg) {
+          const int s = kg % kF8Stages;
+          if (!(ok = mbar_wait(&empty[s], ((kg / kF8Stages) & 1) ^ 1, kErrWaitEmpty))) break;
+          mbar_arrive_expect_tx(&full[s], kF8ABytes + kF8BBytes);
+          tma_load_2d_hint(&tm_a, &full[s], sA + s * kF8ABytes, kb * kF8BK, m0, keep);
+          tma_load_2d(&tm_b, &full[s], sB + s * kF8BBytes, kb * kF8BK, n0);
+        }
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
       constexpr uint32_t idesc = make_idesc(0, 0, 0, 0, kTcBM, kTcBN);  // e4m3 x e4m3, K-major
+      uint32_t kg = 0, it = 0;
       bool ok = true;
-      for (int kb = 0; kb < KB; ++kb) {
-        const int s = kb % kF8Stages;
-        if (!(ok = mbar_wait(&full[s], (kb / kF8Stages) & 1, kErrWaitFull))) break;
+      for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++it) {
+        const uint32_t a = it & 1;
+        if (!(ok = mbar_wait(&acc->empty[a], ((it >> 1) & 1) ^ 1, kErrWaitAccum))) break;
         tc_fence_after();
-        const uint32_t a0 = smem_u32(sA + s * kF8ABytes);
-        const uint32_t b0 = smem_u32(sB + s * kF8BBytes);
+        const uint32_t d = tmem + a * kTcBN;
+        for (int kb = 0; kb < KB; ++kb, ++kg) {
+          const int s = kg % kF8Stages;
+          if (!(ok = mbar_wait(&full[s], (kg / kF8Stages) & 1, kErrWaitFull))) break;
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sA + s * kF8ABytes);
+          const uint32_t b0 = smem_u32(sB + s * kF8BBytes);
 #pragma unroll
-        for (int kk = 0; kk < kF8BK / 32; ++kk) {
-          const uint64_t ad = make_sdesc(a0 + kk * 32, 16, 1024);
-          const uint64_t bd = make_sdesc(b0 + kk * 32, 16, 1024);
-          umma_f8(tmem, ad, bd, idesc, (kb | kk) != 0 ? 1u : 0u);
+          for (int kk = 0; kk < kF8BK / 32; ++kk) {
+            const uint64_t ad = make_sdesc(a0 + kk * 32, 16, 1024);
+            const uint64_t bd = make_sdesc(b0 + kk * 32, 16, 1024);
+            umma_f8(d, ad, bd, idesc, (kb | kk) != 0 ? 1u : 0u);
+          }
+          umma_commit(&empty[s]);
         }
-        umma_commit(&empty[s]);
+        if (ok) umma_commit(&acc->full[a]);
       }
-      if (ok) umma_commit(accum);
     }
   } else {
     // epilogue warps 2..5 -> TMEM lane quarters 2,3,0,1
-    if (mbar_wait(accum, 0, kErrWaitAccum)) {
+    const int quarter = warp & 3;
+    uint32_t it = 0;
+    for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++it) {
+      const uint32_t a = it & 1;
+      if (!mbar_wait(&acc->full[a], (it >> 1) & 1, kErrWaitAccum)) break;
       tc_fence_after();
-      const int quarter = warp & 3;
+      const int m0 = (t / n_tiles) * kTcBM, n0 = (t % n_tiles) * kTcBN;
       const int row = m0 + quarter * 32 + lane;
       const float rs = row < M ? sx[row] : 0.f;
+      const uint32_t tbase = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + a * kTcBN;
       for (int ch = 0; ch < kTcBN / 16; ++ch) {
-        const int col = ch * 16;
         uint32_t r[16];
-        tmem_ld16(tmem + (static_cast<uint32_t>(quarter * 32) << 16) + col, r);
+        tmem_ld16(tbase + ch * 16, r);
         tmem_ld_wait();
-        const int n = n0 + col;
+        const int n = n0 + ch * 16;
         if (row < M && n < N) {
           uint32_t packed[8];
 #pragma unroll
@@ -332,6 +399,9 @@ __global__ void __launch_bounds__(kF8Threads, 1)
           }
         }
       }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc->empty[a]);
     }
   }
   tc_fence_before();
