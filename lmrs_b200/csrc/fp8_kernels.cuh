@@ -122,7 +122,7 @@ __device__ __forceinline__ uint4 lds_u4(uint32_t addr) {
 constexpr int kF8GemvRows = 64;          // output channels per CTA strip (4 MMA tiles)
 constexpr int kF8GemvBoxBytes = kF8GemvRows * 128;  // 64 rows x 128 bytes of K = 8 KB
 constexpr int kF8GemvThreads = 160;      // 4 consumer warps + 1 producer warp
-constexpr int kF8GemvMaxRing = 6;
+constexpr int kF8GemvMaxRing = 4;  // 4 x (8 KB + token tile): 5 CTAs per SM
 
 // MT: 8-token MMA tiles (M <= 8 * MT).  A producer warp streams the strip's
 // weight rows (TMA boxes of 128 bytes of K x 64 rows, 128-byte swizzle) into a
@@ -133,14 +133,15 @@ constexpr int kF8GemvMaxRing = 6;
 // through L1) uses the same permutation.
 template <int MT>
 __global__ void __launch_bounds__(kF8GemvThreads, 4) fp8_gemv_kernel(
-    const __grid_constant__ CUtensorMap tm_w, __nv_bfloat16* __restrict__ y,
-    const uint8_t* __restrict__ xq, const float* __restrict__ sx, const float* __restrict__ sw,
+    const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
+    __nv_bfloat16* __restrict__ y, const float* __restrict__ sx, const float* __restrict__ sw,
     const __nv_bfloat16* __restrict__ bias, int M, int K, int N, int ring) {
   constexpr int MP = 8 * MT;
+  constexpr int kSlot = kF8GemvBoxBytes + MP * 128;  // weights + token tile (MP rows x 128 B)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* slots = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                               ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(slots + ring * kF8GemvBoxBytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(slots + ring * kSlot);
   uint64_t* empty = full + ring;
 
   cg::cluster_group cluster = cg::this_cluster();
@@ -174,35 +175,33 @@ __global__ void __launch_bounds__(kF8GemvThreads, 4) fp8_gemv_kernel(
   if (warp == 4) {
     if (lane == 0) {
       tma_prefetch_desc(&tm_w);
+      tma_prefetch_desc(&tm_x);
       for (int b = 0; b < nbox; ++b) {
         const int s = b % ring;
         if (!mbar_wait(&empty[s], ((b / ring) & 1) ^ 1, kErrWaitEmpty)) break;
-        mbar_arrive_expect_tx(&full[s], kF8GemvBoxBytes);
-        tma_load_2d(&tm_w, &full[s], slots + s * kF8GemvBoxBytes, (u_lo + b) * 128, nbase);
+        mbar_arrive_expect_tx(&full[s], kSlot);
+        tma_load_2d(&tm_w, &full[s], slots + s * kSlot, (u_lo + b) * 128, nbase);
+        tma_load_2d(&tm_x, &full[s], slots + s * kSlot + kF8GemvBoxBytes, (u_lo + b) * 128, 0);
       }
     }
   } else {
-    const uint4 zero4 = make_uint4(0u, 0u, 0u, 0u);
     const int r0 = 16 * warp + g;  // rows r0 and r0 + 8 of the box; (r0 % 8) == g
     for (int b = 0; b < nbox; ++b) {
-      const int kb = (u_lo + b) << 7;
-      const int ka = kb + 16 * t, kc = kb + 64 + 16 * t;
-      uint4 xb[MT][2];
-#pragma unroll
-      for (int mt = 0; mt < MT; ++mt) {
-        const int m = mt * 8 + g;
-        const uint8_t* xr = xq + static_cast<int64_t>(m) * K;
-        xb[mt][0] = (m < M && ka < K) ? __ldg(reinterpret_cast<const uint4*>(xr + ka)) : zero4;
-        xb[mt][1] = (m < M && kc < K) ? __ldg(reinterpret_cast<const uint4*>(xr + kc)) : zero4;
-      }
       const int slot = b % ring;
       if (!mbar_wait(&full[slot], (b / ring) & 1, kErrWaitFull)) break;
-      const uint32_t sb = smem_u32(slots + slot * kF8GemvBoxBytes);
+      const uint32_t sb = smem_u32(slots + slot * kSlot);
       // 128-byte swizzle: chunk c of row r sits at chunk c ^ (r % 8)
       const uint4 ga = lds_u4(sb + r0 * 128 + ((t ^ g) << 4));
       const uint4 gc = lds_u4(sb + r0 * 128 + (((4 + t) ^ g) << 4));
       const uint4 ha = lds_u4(sb + (r0 + 8) * 128 + ((t ^ g) << 4));
       const uint4 hc = lds_u4(sb + (r0 + 8) * 128 + (((4 + t) ^ g) << 4));
+      uint4 xb[MT][2];
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt) {
+        const uint32_t xr = sb + kF8GemvBoxBytes + (mt * 8 + g) * 128;  // token rows >= M are zero
+        xb[mt][0] = lds_u4(xr + ((t ^ g) << 4));
+        xb[mt][1] = lds_u4(xr + (((4 + t) ^ g) << 4));
+      }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[slot]);
 #pragma unroll

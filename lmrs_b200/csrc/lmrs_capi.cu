@@ -20,7 +20,7 @@
 #include <cstring>
 #include <mutex>
 
-#include "../../include/lmrs_quant.h"
+#include "lmrs_quant.h"
 #include "awq_gemv.cuh"
 #include "awq_pack.cuh"
 #include "fp8_kernels.cuh"
@@ -190,21 +190,25 @@ int awq_gemv_launch(__half* y, const __half* x, const int32_t* qw, const uint32_
   const int per_cta = (nb_all + C - 1) / C;
   int ring = per_cta < lmrs::kAwqGemvMaxRing ? per_cta : lmrs::kAwqGemvMaxRing;
   if (ring < 4) ring = 4;  // the drained ring also holds the 2 x 16 x 128 fp32 partials
-  const int smem = 1024 + ring * lmrs::kAwqGemvBoxBytes + ring * 16;
-  CUtensorMap tq;
+  const int MT = M <= 8 ? 1 : 2;
+  const int slot = lmrs::kAwqGemvBoxBytes + lmrs::kAwqGemvBoxRows * 2 * 8 * MT;
+  const int smem = 1024 + ring * slot + ring * 16;
+  CUtensorMap tq, tx;
   int rc;
   if ((rc = make_tmap(&tq, CU_TENSOR_MAP_DATA_TYPE_INT32, qw, N / 8, K, uint64_t(N / 8) * 4,
                       lmrs::kAwqGemvStrip / 8, lmrs::kAwqGemvBoxRows, CU_TENSOR_MAP_SWIZZLE_64B)))
     return rc;
-  const int MT = M <= 8 ? 1 : 2;
+  if ((rc = make_tmap(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, x, K, M, uint64_t(K) * 2,
+                      lmrs::kAwqGemvBoxRows, 8 * MT, CU_TENSOR_MAP_SWIZZLE_128B)))
+    return rc;
   if (MT == 1) {
     if ((rc = ensure_smem(lmrs::awq_gemv_kernel<1>, smem, g_smem_awq_gemv[0], dev))) return rc;
     rc = launch_cluster(lmrs::awq_gemv_kernel<1>, strips * C, C, lmrs::kAwqGemvThreads, smem,
-                        stream, tq, y, x, qz, sc, bias, M, K, N, group, ring);
+                        stream, tq, tx, y, qz, sc, bias, M, K, N, group, ring);
   } else {
     if ((rc = ensure_smem(lmrs::awq_gemv_kernel<2>, smem, g_smem_awq_gemv[1], dev))) return rc;
     rc = launch_cluster(lmrs::awq_gemv_kernel<2>, strips * C, C, lmrs::kAwqGemvThreads, smem,
-                        stream, tq, y, x, qz, sc, bias, M, K, N, group, ring);
+                        stream, tq, tx, y, qz, sc, bias, M, K, N, group, ring);
   }
   return rc ? rc : after_launch();
 }
@@ -263,27 +267,32 @@ int fp8_gemv_launch(__nv_bfloat16* y, const uint8_t* xq, const float* sx, const 
   const int units = (K + 127) / 128;
   const int C = gemv_cluster(strips, units, g_tune.fp8_gemv_cluster);
   const int per_cta = (units + C - 1) / C;
-  int ring = per_cta < lmrs::kF8GemvMaxRing ? per_cta : lmrs::kF8GemvMaxRing;
+  const int MT = M <= 8 ? 1 : (M <= 16 ? 2 : 4);
+  const int slot = lmrs::kF8GemvBoxBytes + 8 * MT * 128;
+  const int max_ring = lmrs::kF8GemvMaxRing;
+  int ring = per_cta < max_ring ? per_cta : max_ring;
   if (ring < 1) ring = 1;
-  const int smem = 1024 + ring * lmrs::kF8GemvBoxBytes + ring * 16;
-  CUtensorMap tw;
+  const int smem = 1024 + ring * slot + ring * 16;
+  CUtensorMap tw, tx;
   int rc;
   if ((rc = make_tmap(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, wq, K, N, uint64_t(K), 128,
                       lmrs::kF8GemvRows, CU_TENSOR_MAP_SWIZZLE_128B)))
     return rc;
-  const int MT = M <= 8 ? 1 : (M <= 16 ? 2 : 4);
+  if ((rc = make_tmap(&tx, CU_TENSOR_MAP_DATA_TYPE_UINT8, xq, K, M, uint64_t(K), 128, 8 * MT,
+                      CU_TENSOR_MAP_SWIZZLE_128B)))
+    return rc;
   if (MT == 1) {
     if ((rc = ensure_smem(lmrs::fp8_gemv_kernel<1>, smem, g_smem_f8_gemv[0], dev))) return rc;
     rc = launch_cluster(lmrs::fp8_gemv_kernel<1>, strips * C, C, lmrs::kF8GemvThreads, smem,
-                        stream, tw, y, xq, sx, sw, bias, M, K, N, ring);
+                        stream, tw, tx, y, sx, sw, bias, M, K, N, ring);
   } else if (MT == 2) {
     if ((rc = ensure_smem(lmrs::fp8_gemv_kernel<2>, smem, g_smem_f8_gemv[1], dev))) return rc;
     rc = launch_cluster(lmrs::fp8_gemv_kernel<2>, strips * C, C, lmrs::kF8GemvThreads, smem,
-                        stream, tw, y, xq, sx, sw, bias, M, K, N, ring);
+                        stream, tw, tx, y, sx, sw, bias, M, K, N, ring);
   } else {
     if ((rc = ensure_smem(lmrs::fp8_gemv_kernel<4>, smem, g_smem_f8_gemv[2], dev))) return rc;
     rc = launch_cluster(lmrs::fp8_gemv_kernel<4>, strips * C, C, lmrs::kF8GemvThreads, smem,
-                        stream, tw, y, xq, sx, sw, bias, M, K, N, ring);
+                        stream, tw, tx, y, sx, sw, bias, M, K, N, ring);
   }
   return rc ? rc : after_launch();
 }

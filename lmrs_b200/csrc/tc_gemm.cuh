@@ -4,8 +4,8 @@
 //   fp8_gemm_tc_kernel : y bf16 [M,N] = (xq e4m3 [M,K] @ wq e4m3 [N,K]^T) * sx[m] * sw[n] (+bias)
 //
 // Both are persistent, warp-specialised kernels: one CTA per SM walks output
-// tiles (128 x 256) tile = blockIdx.x, blockIdx.x + gridDim.x, ...  (M-major
-// order, so CTAs running together share the x tile in L2).
+// tiles (128 x 256) tile = blockIdx.x, blockIdx.x + gridDim.x, ... in grouped
+// order (tile_coords) so the tiles in flight share x and weight tiles in L2.
 //
 //   warp 0        TMA producer: one thread streams K-blocks into a ring of
 //                 shared-memory stages (cp.async.bulk.tensor, 128B swizzle,
@@ -17,10 +17,11 @@
 //   warps 2..5    epilogue: tcgen05.ld (32 lanes x 32 bit) -> scale/bias/round ->
 //                 global, then release the accumulator buffer.  Double
 //                 buffering lets tile i's epilogue overlap tile i+1's mainloop.
-//   warps 6..13   AWQ only: dequant warps turn the TMA-staged packed int4 tile
+//   warps 6..21   AWQ only: dequant warps turn the TMA-staged packed int4 tile
 //                 into fp16 directly in the UMMA MN-major 128B-swizzled layout
 //                 (operand B): the dequant is fused into the shared-memory
-//                 stage and weights cross HBM once, as int4.
+//                 stage and weights cross HBM once, as int4.  Two groups of
+//                 8 warps alternate K-blocks to hide the dequant latency.
 // Every mbarrier wait is bounded (lmrs_ptx.cuh): on expiry the kernel records
 // the site in the device error word and unwinds; TMEM is always released.
 #pragma once
@@ -44,6 +45,21 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint4 v) {
                : "memory");
 }
 
+// Tile order: groups of kTcGroupM M-tiles walked N-tile by N-tile, M fastest,
+// so the ~148 tiles in flight touch about 8 x-tiles and 19 weight tiles — both
+// stay resident in L2 and each is fetched from HBM about once.
+constexpr int kTcGroupM = 8;
+
+__device__ __forceinline__ void tile_coords(int t, int m_tiles, int n_tiles, int& m0, int& n0) {
+  const int per_group = kTcGroupM * n_tiles;
+  const int grp = t / per_group;
+  const int first_m = grp * kTcGroupM;
+  const int gm = min(m_tiles - first_m, kTcGroupM);
+  const int local = t - grp * per_group;
+  m0 = (first_m + local % gm) * kTcBM;
+  n0 = (local / gm) * kTcBN;
+}
+
 // Accumulator hand-off barriers (MMA -> epilogue -> MMA), two buffers.
 struct AccBars {
   uint64_t full[2];
@@ -61,9 +77,10 @@ __device__ __forceinline__ void acc_bars_init(AccBars* b) {
 constexpr int kAwqBK = 64;        // k rows per stage (one 128-byte fp16 row of A)
 constexpr int kAwqSA = 4;         // TMA stages: A tile + packed tile + scales + zeros
 constexpr int kAwqSB = 3;         // dequantised B stages
+constexpr int kAwqDqGroups = 2;   // dequant warp groups, alternating K-blocks
 constexpr int kAwqDqWarp0 = 6;
-constexpr int kAwqDqWarps = 8;
-constexpr int kAwqGemmThreads = 32 * (kAwqDqWarp0 + kAwqDqWarps);  // 448
+constexpr int kAwqDqWarps = 8;    // per group, 8 rows of the 64-row K-block each
+constexpr int kAwqGemmThreads = 32 * (kAwqDqWarp0 + kAwqDqWarps * kAwqDqGroups);  // 704
 constexpr int kAwqABytes = kTcBM * kAwqBK * 2;        // 16 KB
 constexpr int kAwqBBytes = kTcBN * kAwqBK * 2;        // 32 KB
 constexpr int kAwqPBytes = kAwqBK * (kTcBN / 8) * 4;  // 8 KB
@@ -132,7 +149,8 @@ __global__ void __launch_bounds__(kAwqGemmThreads, 1)
       uint32_t kg = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
-        const int m0 = (t / n_tiles) * kTcBM, n0 = (t % n_tiles) * kTcBN;
+        int m0, n0;
+        tile_coords(t, m_tiles, n_tiles, m0, n0);
         for (int kb = 0; kb < KB; ++kb, ++kg) {
           const int s = kg % kAwqSA;
           if (!(ok = mbar_wait(&empty[s], ((kg / kAwqSA) & 1) ^ 1, kErrWaitEmpty))) break;
@@ -184,7 +202,8 @@ __global__ void __launch_bounds__(kAwqGemmThreads, 1)
       const uint32_t a = it & 1;
       if (!mbar_wait(&acc->full[a], (it >> 1) & 1, kErrWaitAccum)) break;
       tc_fence_after();
-      const int m0 = (t / n_tiles) * kTcBM, n0 = (t % n_tiles) * kTcBN;
+      int m0, n0;
+        tile_coords(t, m_tiles, n_tiles, m0, n0);
       const int row = m0 + quarter * 32 + lane;
       const uint32_t tbase = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + a * kTcBN;
       for (int ch = 0; ch < kTcBN / 16; ++ch) {
@@ -214,12 +233,16 @@ __global__ void __launch_bounds__(kAwqGemmThreads, 1)
     }
   } else {
     // ---------------- dequant warps: packed int4 stage -> fp16 MN-major SW128 B stage
-    const int dw = warp - kAwqDqWarp0;
+    // two groups of 8 warps take alternate K-blocks, so two K-blocks are being
+    // dequantised while the tensor core consumes a third
+    const int dwa = warp - kAwqDqWarp0;
+    const int dgrp = dwa / kAwqDqWarps, dw = dwa % kAwqDqWarps;
     const int bblk = lane >> 3, chunk = lane & 7;
     uint32_t kg = 0;
     bool ok = true;
     for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
       for (int kb = 0; kb < KB; ++kb, ++kg) {
+        if (static_cast<int>(kg % kAwqDqGroups) != dgrp) continue;
         const int s = kg % kAwqSA, sb = kg % kAwqSB;
         ok = mbar_wait(&full[s], (kg / kAwqSA) & 1, kErrWaitFull) &&
              mbar_wait(&bempty[sb], ((kg / kAwqSB) & 1) ^ 1, kErrWaitEmpty);
@@ -316,7 +339,8 @@ __global__ void __launch_bounds__(kF8Threads, 1)
       uint32_t kg = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
-        const int m0 = (t / n_tiles) * kTcBM, n0 = (t % n_tiles) * kTcBN;
+        int m0, n0;
+        tile_coords(t, m_tiles, n_tiles, m0, n0);
         for (int kb = 0; kb < KB; ++kb, ++kg) {
           const int s = kg % kF8Stages;
           if (!(ok = mbar_wait(&empty[s], ((kg / kF8Stages) & 1) ^ 1, kErrWaitEmpty))) break;
@@ -361,7 +385,8 @@ __global__ void __launch_bounds__(kF8Threads, 1)
       const uint32_t a = it & 1;
       if (!mbar_wait(&acc->full[a], (it >> 1) & 1, kErrWaitAccum)) break;
       tc_fence_after();
-      const int m0 = (t / n_tiles) * kTcBM, n0 = (t % n_tiles) * kTcBN;
+      int m0, n0;
+        tile_coords(t, m_tiles, n_tiles, m0, n0);
       const int row = m0 + quarter * 32 + lane;
       const float rs = row < M ? sx[row] : 0.f;
       const uint32_t tbase = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + a * kTcBN;
