@@ -80,7 +80,9 @@ LMRS_API int lmrs_read_device_error(int* out_flags);
 /* Library version, for the binding's sanity check. */
 LMRS_API int lmrs_version(void);
 /* Measurement knobs (dispatch thresholds, split-K shape); 0 on a known key,
- * LMRS_ERR_SHAPE otherwise.  Keys: "awq_gemv_max_m", "fp8_gemv_max_m",
+ * LMRS_ERR_SHAPE otherwise.  Keys: "awq_gemv_max_m", "awq_swap_max_m", "awq_swap_cluster",
+ * "awq_gemm_pair",
+ * "fp8_gemv_max_m",
  * "gemv_ctas_per_sm", "awq_gemv_cluster", "fp8_gemv_cluster".
  * Process-wide, not thread-safe against concurrent launches. */
 LMRS_API int lmrs_set_tuning(const char* key, int value);
@@ -110,8 +112,10 @@ LMRS_API size_t lmrs_awq_linear_workspace_bytes(int M, int K, int N, int group);
 /* y[M,N] = x[M,K] @ dequant(qweight, qzeros, scales) (+ bias[N]).
  * act_dtype must be LMRS_DTYPE_F16 (x, y, bias fp16).  Requirements:
  * K % group == 0, group % 64 == 0, N % 32 == 0, 16-byte aligned pointers.
- * Small M runs a register-dequant tensor-core GEMV (HBM bound); large M a
- * tcgen05 GEMM with dequant fused into the shared-memory stage.
+ * M <= 8 runs a register-dequant tensor-core GEMV (HBM bound); M <= 64 a
+ * swap-AB split-K tcgen05 kernel; larger M a persistent tcgen05 GEMM (one SM
+ * per 128x256 tile, or CTA pairs with "awq_gemm_pair").  The tcgen05 paths fuse
+ * the dequant into the shared-memory stage.
  * Replaces `linear_fwd` (kernels/ffi/tensor_ffi.cu:820-841) for AWQ layers. */
 LMRS_API int lmrs_awq_linear(void* y, const void* x, const int32_t* qweight,
                     const int32_t* qzeros, const void* scales,

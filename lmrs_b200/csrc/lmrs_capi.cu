@@ -21,11 +21,13 @@
 #include <mutex>
 
 #include "lmrs_quant.h"
+#include "awq_gemm_swap.cuh"
 #include "awq_gemv.cuh"
 #include "awq_pack.cuh"
 #include "fp8_kernels.cuh"
 #include "lmrs_ptx.cuh"
 #include "tc_gemm.cuh"
+#include "tc_gemm2.cuh"
 
 namespace {
 
@@ -35,10 +37,13 @@ thread_local int t_last_cuda_error = 0;
 
 // ---- tuning knobs (lmrs_set_tuning); defaults chosen from B200 measurements
 struct Tuning {
-  int awq_gemv_max_m = 16;   // M above this -> tcgen05 GEMM
+  int awq_gemv_max_m = 8;    // M up to this -> register-dequant GEMV
+  int awq_swap_max_m = 64;   // M up to this -> swap-AB split-K tcgen05; above -> tile GEMM
   int fp8_gemv_max_m = 32;
   int gemv_ctas_per_sm = 4;  // resident CTAs per SM the GEMV grids are sized for
   int awq_gemv_cluster = 0;  // 0 = heuristic
+  int awq_swap_cluster = 0;  // 0 = heuristic
+  int awq_gemm_pair = 0;     // 1: CTA-pair (cta_group::2) GEMM for large M; 0: one-SM tiles
   int fp8_gemv_cluster = 0;
 };
 Tuning g_tune;
@@ -213,6 +218,75 @@ int awq_gemv_launch(__half* y, const __half* x, const int32_t* qw, const uint32_
   return rc ? rc : after_launch();
 }
 
+std::atomic<int> g_smem_awq_swap[4][kMaxDevices];
+
+template <int NT>
+int awq_swap_launch_nt(__half* y, const __half* x, const int32_t* qw, const int32_t* qz,
+                       const __half* sc, const __half* bias, int M, int K, int N, int group,
+                       cudaStream_t stream, int dev, int slot) {
+  CUtensorMap tx, tq, ts, tz;
+  int rc;
+  if ((rc = make_tmap(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, x, K, M, uint64_t(K) * 2, lmrs::kSwBK,
+                      NT, CU_TENSOR_MAP_SWIZZLE_128B)))
+    return rc;
+  if ((rc = make_tmap(&tq, CU_TENSOR_MAP_DATA_TYPE_INT32, qw, N / 8, K, uint64_t(N / 8) * 4,
+                      lmrs::kSwBN / 8, lmrs::kSwBK, CU_TENSOR_MAP_SWIZZLE_NONE)))
+    return rc;
+  if ((rc = make_tmap(&ts, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, sc, N, K / group, uint64_t(N) * 2,
+                      lmrs::kSwBN, 1, CU_TENSOR_MAP_SWIZZLE_NONE)))
+    return rc;
+  if ((rc = make_tmap(&tz, CU_TENSOR_MAP_DATA_TYPE_INT32, qz, N / 8, K / group,
+                      uint64_t(N / 8) * 4, lmrs::kSwBN / 8, 1, CU_TENSOR_MAP_SWIZZLE_NONE)))
+    return rc;
+  constexpr int smem = lmrs::sw_smem_bytes(NT);
+  if ((rc = ensure_smem(lmrs::awq_gemm_swap_kernel<NT>, smem, g_smem_awq_swap[slot], dev))) return rc;
+  const int tiles = (N + lmrs::kSwBN - 1) / lmrs::kSwBN;
+  const int KB = K / lmrs::kSwBK;
+  int C = g_tune.awq_swap_cluster > 0 ? g_tune.awq_swap_cluster : (2 * sm_count(dev)) / tiles;
+  C = clampi(C, 1, 8);
+  if (C > KB) C = KB;
+  rc = launch_cluster(lmrs::awq_gemm_swap_kernel<NT>, tiles * C, C, lmrs::kSwThreads, smem, stream,
+                      tx, tq, ts, tz, y, bias, M, K, N, group);
+  return rc ? rc : after_launch();
+}
+
+int awq_swap_launch(__half* y, const __half* x, const int32_t* qw, const int32_t* qz,
+                    const __half* sc, const __half* bias, int M, int K, int N, int group,
+                    cudaStream_t stream, int dev) {
+  if (M <= 16) return awq_swap_launch_nt<16>(y, x, qw, qz, sc, bias, M, K, N, group, stream, dev, 0);
+  if (M <= 32) return awq_swap_launch_nt<32>(y, x, qw, qz, sc, bias, M, K, N, group, stream, dev, 1);
+  if (M <= 64) return awq_swap_launch_nt<64>(y, x, qw, qz, sc, bias, M, K, N, group, stream, dev, 2);
+  return awq_swap_launch_nt<128>(y, x, qw, qz, sc, bias, M, K, N, group, stream, dev, 3);
+}
+
+std::atomic<int> g_smem_awq_gemm2[kMaxDevices];
+
+int awq_gemm2_launch(__half* y, const __half* x, const int32_t* qw, const int32_t* qz,
+                     const __half* sc, const __half* bias, int M, int K, int N, int group,
+                     cudaStream_t stream, int dev) {
+  CUtensorMap tx, tq, ts, tz;
+  int rc;
+  if ((rc = make_tmap(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, x, K, M, uint64_t(K) * 2, 64, 128,
+                      CU_TENSOR_MAP_SWIZZLE_128B)))
+    return rc;
+  if ((rc = make_tmap(&tq, CU_TENSOR_MAP_DATA_TYPE_INT32, qw, N / 8, K, uint64_t(N / 8) * 4, 16,
+                      64, CU_TENSOR_MAP_SWIZZLE_NONE)))
+    return rc;
+  if ((rc = make_tmap(&ts, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, sc, N, K / group, uint64_t(N) * 2,
+                      128, 1, CU_TENSOR_MAP_SWIZZLE_NONE)))
+    return rc;
+  if ((rc = make_tmap(&tz, CU_TENSOR_MAP_DATA_TYPE_INT32, qz, N / 8, K / group,
+                      uint64_t(N / 8) * 4, 16, 1, CU_TENSOR_MAP_SWIZZLE_NONE)))
+    return rc;
+  if ((rc = ensure_smem(lmrs::awq_gemm_tc2_kernel, lmrs::kP2SmemBytes, g_smem_awq_gemm2, dev)))
+    return rc;
+  const int tiles = ((N + lmrs::kP2BN - 1) / lmrs::kP2BN) * ((M + lmrs::kP2BM - 1) / lmrs::kP2BM);
+  const int pairs = tiles < sm_count(dev) / 2 ? tiles : sm_count(dev) / 2;
+  rc = launch_cluster(lmrs::awq_gemm_tc2_kernel, 2 * pairs, 2, lmrs::kP2Threads,
+                      lmrs::kP2SmemBytes, stream, tx, tq, ts, tz, y, bias, M, K, N, group);
+  return rc ? rc : after_launch();
+}
+
 int awq_gemm_launch(__half* y, const __half* x, const int32_t* qw, const int32_t* qz,
                     const __half* sc, const __half* bias, int M, int K, int N, int group,
                     cudaStream_t stream, int dev) {
@@ -372,6 +446,9 @@ int lmrs_read_device_error(int* out_flags) {
 int lmrs_set_tuning(const char* key, int value) {
   if (!key) return LMRS_ERR_NULL;
   if (!strcmp(key, "awq_gemv_max_m")) g_tune.awq_gemv_max_m = value;
+  else if (!strcmp(key, "awq_swap_max_m")) g_tune.awq_swap_max_m = value;
+  else if (!strcmp(key, "awq_swap_cluster")) g_tune.awq_swap_cluster = value;
+  else if (!strcmp(key, "awq_gemm_pair")) g_tune.awq_gemm_pair = value;
   else if (!strcmp(key, "fp8_gemv_max_m")) g_tune.fp8_gemv_max_m = value;
   else if (!strcmp(key, "gemv_ctas_per_sm")) g_tune.gemv_ctas_per_sm = value;
   else if (!strcmp(key, "awq_gemv_cluster")) g_tune.awq_gemv_cluster = value;
@@ -446,6 +523,10 @@ int lmrs_awq_linear(void* y, const void* x, const int32_t* qweight, const int32_
   if (M <= g_tune.awq_gemv_max_m && M <= 16)
     return awq_gemv_launch(yh, xh, qweight, reinterpret_cast<const uint32_t*>(qzeros), sh, bh, M,
                            K, N, group, st, dev);
+  if (M <= g_tune.awq_swap_max_m && M <= 128)
+    return awq_swap_launch(yh, xh, qweight, qzeros, sh, bh, M, K, N, group, st, dev);
+  if (g_tune.awq_gemm_pair)
+    return awq_gemm2_launch(yh, xh, qweight, qzeros, sh, bh, M, K, N, group, st, dev);
   return awq_gemm_launch(yh, xh, qweight, qzeros, sh, bh, M, K, N, group, st, dev);
 }
 

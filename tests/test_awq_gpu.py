@@ -82,7 +82,7 @@ def test_linear_gemv_small(cuda, M, bias):
     assert err < TIGHT, err
 
 
-@pytest.mark.parametrize("M", [17, 100, 128, 129, 300])
+@pytest.mark.parametrize("M", [17, 100, 128, 129, 300, 512])
 @pytest.mark.parametrize("bias", [False, True])
 def test_linear_gemm_small(cuda, M, bias):
     import lmrs_b200 as L
@@ -100,7 +100,7 @@ def test_linear_ragged_n(cuda, N):
     """N not a multiple of the 128/256-column tiles (AWQ needs N % 32 == 0 here)."""
     import lmrs_b200 as L
     K, g = 256, 64
-    for M in (4, 40):
+    for M in (4, 40, 200):
         d = O.awq_inputs(M, K, N, g, seed=N + M, with_bias=True)
         qw, qz, sc, x, b = _awq_dev(d, cuda)
         y = L.awq_linear(x, qw, qz, sc, b, g)
