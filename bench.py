@@ -10,8 +10,10 @@ resident in HBM; ``e2e`` = the same metric through the public API with host
 L2 hygiene: the timed loop rotates over enough weight copies that the set
 streamed between two uses of a copy exceeds 2x the 126 MB L2.
 
-``--workload fp8`` runs config 2 instead (FP8 W8A8, (K,N)=(4096,28672),
-M in {1, 32, 512, 8192}) for measurement; the default line is config 1.
+The line also carries ``fp8_sweep``: BASELINE config 2 (FP8 W8A8, (K, N) in
+{(4096,4096), (4096,28672), (14336,4096)} x M in {1, 32, 512, 8192}), device
+time per quant+GEMM call, as context (``--no-fp8`` skips it).  ``--case`` runs
+a few launches of one shape for ncu captures (see profiles/).
 
 ``--impl reference`` times the reference side on the same workload: the
 reference has no CPU implementation of this path, so the CPU restatement in
@@ -47,6 +49,9 @@ AWQ_K, AWQ_N, AWQ_G = 4096, 14336, 128
 AWQ_MS = [1, 16, 128, 1024, 4096]
 FP8_K, FP8_N = 4096, 28672
 FP8_MS = [1, 32, 512, 8192]
+# No FP8 figure in MEASURED_PEAKS.json: torch._scaled_mm e4m3 8192^3 measured on
+# this pool's B200s (dense, burst) stands in as the FP8 tensor denominator.
+FP8_PEAK_TFLOPS = 3008.0
 
 
 def peaks():
@@ -334,15 +339,85 @@ def ref_gpu_linear_fwd(device, W, steps=2):
             "value": round(tot_fl / (tot_ms * 1e-3) / 1e12, 4), "unit": "TFLOP/s", "sweep": res}
 
 
+def run_case(case, launches=3):
+    """A handful of launches of one kernel shape, for ncu captures."""
+    import lmrs_b200 as L
+    dev = torch.device("cuda", 0)
+    kind, *dims = case.split(":")
+    if kind == "awq":
+        M = int(dims[0])
+        W = awq_weights(dev, 1)
+        x = torch.randn(M, AWQ_K, device=dev).half()
+        for _ in range(launches):
+            L.awq_linear(x, *W[0], None, AWQ_G)
+    elif kind == "fp8":
+        M, K, N = (int(v) for v in dims)
+        w = (torch.randn(N, K, device=dev) * 0.02).bfloat16()
+        wq, sw = L.quantize_fp8_weight(w)
+        x = torch.randn(M, K, device=dev).bfloat16()
+        ws = L.Workspace()
+        for _ in range(launches):
+            L.fp8_linear(x, wq, sw, None, ws)
+    else:
+        raise SystemExit(f"unknown case {case}")
+    torch.cuda.synchronize()
+    print(f"case {case}: ok, device error word {L.read_device_error()}")
+
+
+def fp8_sweep(device, steps=5):
+    """Config 2: FP8 W8A8 (K, N) x M, device time per call (context for the line)."""
+    import lmrs_b200 as L
+    out = []
+    pk, _ = peaks()
+    fp8_peak = pk.get("fp8_tflops", FP8_PEAK_TFLOPS)
+    for K, N in ((4096, 4096), (4096, 28672), (14336, 4096)):
+        copies = max(2, int(3e8 // (N * K)))
+        w = (torch.randn(N, K, device=device) * 0.02).bfloat16()
+        wqs = [L.quantize_fp8_weight(w.roll(i, 0).contiguous()) for i in range(copies)]
+        del w
+        for M in FP8_MS:
+            x = torch.randn(M, K, device=device).bfloat16()
+            y = torch.empty(M, N, dtype=torch.bfloat16, device=device)
+            ws = L.Workspace()
+            for i in range(3):
+                L.fp8_linear(x, *wqs[i % copies], None, ws, out=y)
+            torch.cuda.synchronize()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            for i in range(steps):
+                L.fp8_linear(x, *wqs[i % copies], None, ws, out=y)
+            b.record()
+            torch.cuda.synchronize()
+            us = a.elapsed_time(b) / steps * 1e3
+            byts = 2 * M * K + N * K + 4 * N + 2 * M * N
+            tfl = 2.0 * M * K * N / us / 1e6
+            gbs = byts / us / 1e3
+            bound = "hbm" if M <= 256 else "tensor"
+            frac = gbs / pk["hbm_gbs"] if bound == "hbm" else tfl / fp8_peak
+            out.append({"K": K, "N": N, "M": M, "us": round(us, 2), "GB_s": round(gbs, 1),
+                        "TFLOP_s": round(tfl, 2), "bound": bound, "frac": round(frac, 4)})
+        del wqs
+        torch.cuda.empty_cache()
+    return {"config": "config2: FP8 W8A8, quant + GEMM per call, bf16 in/out",
+            "fp8_peak_tflops": fp8_peak, "fp8_peak_source": "torch._scaled_mm e4m3 8192^3 on this pool",
+            "points": out}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["lmrs", "reference"], default="lmrs")
-    ap.add_argument("--workload", choices=["awq", "fp8"], default="awq")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-fp8", action="store_true", help="skip the config-2 FP8 context sweep")
+    ap.add_argument("--case", default=None,
+                    help="profiling mode: run a few launches of one case and exit, e.g. "
+                         "awq:4096 (config-1 shape, M=4096) or fp8:8192:4096:28672 (M:K:N)")
     args = ap.parse_args()
+    if args.case:
+        run_case(args.case)
+        return
     args.warmup = max(args.warmup, 3)
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -396,6 +471,8 @@ def main():
         line.update(res)
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline_awq(nthreads)
+        if world == 1 and not args.no_fp8:
+            line["fp8_sweep"] = fp8_sweep(device)
         print(json.dumps(line), flush=True)
     if dist_on:
         torch.distributed.barrier()

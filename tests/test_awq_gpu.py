@@ -188,3 +188,30 @@ def test_status_codes(cuda):
                              torch.cuda.current_stream().cuda_stream)
     assert rc == 0
     assert L.read_device_error() == 0
+
+
+@pytest.mark.parametrize("knob,value,Ms", [("awq_gemm_pair", 1, (129, 300, 512)),
+                                           ("awq_gemv_max_m", 16, (9, 12, 16)),
+                                           ("awq_swap_max_m", 128, (65, 100, 128))])
+def test_opt_in_paths(cuda, knob, value, Ms):
+    """Kernels the default dispatch does not pick for these M (CTA-pair GEMM,
+    the two-token-tile GEMV, swap-AB up to 128 tokens) stay correct and
+    deterministic when selected."""
+    import torch
+    import lmrs_b200 as L
+    from lmrs_b200 import _lib
+    defaults = {"awq_gemm_pair": 0, "awq_gemv_max_m": 8, "awq_swap_max_m": 64}
+    K, N, g = 1024, 1280, 128
+    try:
+        L.set_tuning(knob, value)
+        for M in Ms:
+            d = O.awq_inputs(M, K, N, g, seed=M + 7, with_bias=True)
+            qw, qz, sc, x, b = _awq_dev(d, cuda)
+            y = L.awq_linear(x, qw, qz, sc, b, g)
+            ref = O.c_awq_linear(d["x"], d["qweight"], d["qzeros"], d["scales"], d["bias"], M, K, N, g)
+            assert O.max_rel_err(y.cpu().numpy(), ref) < TIGHT, (knob, M)
+            for _ in range(3):
+                assert torch.equal(L.awq_linear(x, qw, qz, sc, b, g), y), (knob, M, "nondeterministic")
+    finally:
+        L.set_tuning(knob, defaults[knob])
+    assert L.read_device_error() == 0
