@@ -52,6 +52,9 @@ FP8_MS = [1, 32, 512, 8192]
 # No FP8 figure in MEASURED_PEAKS.json: torch._scaled_mm e4m3 8192^3 measured on
 # this pool's B200s (dense, burst) stands in as the FP8 tensor denominator.
 FP8_PEAK_TFLOPS = 3008.0
+# DRAM bytes (read + write) of one awq_gemm_tc_kernel launch at M=4096, from the
+# ncu capture recorded in profiles/awq_gemm_tc_config1_M2048.md (update with the kernel).
+AWQ_GEMM_M4096_DRAM_BYTES = 74558464 + 74811136
 
 
 def peaks():
@@ -269,7 +272,9 @@ def run_awq(args, device, dist_on, world, rank):
     ach = awq_flops(Md) / (per_ms[dom] * 1e-3) / 1e12
     roof = {"bound": "tensor", "kernel": f"awq_gemm_tc_kernel (M={Md})", "achieved": round(ach, 2),
             "peak": pk["bf16_tflops"], "unit": "TFLOP/s", "frac": round(ach / pk["bf16_tflops"], 4),
-            "peak_source": f"{pk_kind} bf16 dense (burst)", "traffic": None,
+            "peak_source": f"{pk_kind} bf16 dense (burst)",
+            "traffic": AWQ_GEMM_M4096_DRAM_BYTES if Md == 4096 else None,
+            "traffic_unit": "bytes per launch (ncu dram__bytes_read.sum + dram__bytes_write.sum)",
             "algorithmic_bytes": awq_bytes(Md), "algorithmic_flops": awq_flops(Md)}
     return dict(
         metric="awq_w4a16_linear_throughput_config1_sweep", value=round(value, 3), unit="TFLOP/s",
@@ -364,6 +369,30 @@ def run_case(case, launches=3):
     print(f"case {case}: ok, device error word {L.read_device_error()}")
 
 
+def graph_time(fn, steps):
+    """Device time per call with host launch overhead removed: `steps` calls are
+    captured into one CUDA graph after 3 eager warm-up calls and replayed."""
+    for i in range(3):
+        fn(i)
+    torch.cuda.synchronize()
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            for i in range(steps):
+                fn(i)
+    torch.cuda.synchronize()
+    g.replay()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    g.replay()
+    b.record()
+    torch.cuda.synchronize()
+    del g
+    return a.elapsed_time(b) / steps * 1e3
+
+
 def fp8_sweep(device, steps=5):
     """Config 2: FP8 W8A8 (K, N) x M, device time per call (context for the line)."""
     import lmrs_b200 as L
@@ -379,16 +408,8 @@ def fp8_sweep(device, steps=5):
             x = torch.randn(M, K, device=device).bfloat16()
             y = torch.empty(M, N, dtype=torch.bfloat16, device=device)
             ws = L.Workspace()
-            for i in range(3):
-                L.fp8_linear(x, *wqs[i % copies], None, ws, out=y)
-            torch.cuda.synchronize()
-            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            a.record()
-            for i in range(steps):
-                L.fp8_linear(x, *wqs[i % copies], None, ws, out=y)
-            b.record()
-            torch.cuda.synchronize()
-            us = a.elapsed_time(b) / steps * 1e3
+            ws.get(L.load_library().lmrs_fp8_linear_workspace_bytes(M, K, N), device)
+            us = graph_time(lambda i: L.fp8_linear(x, *wqs[i % copies], None, ws, out=y), steps)
             byts = 2 * M * K + N * K + 4 * N + 2 * M * N
             tfl = 2.0 * M * K * N / us / 1e6
             gbs = byts / us / 1e3
@@ -398,7 +419,8 @@ def fp8_sweep(device, steps=5):
                         "TFLOP_s": round(tfl, 2), "bound": bound, "frac": round(frac, 4)})
         del wqs
         torch.cuda.empty_cache()
-    return {"config": "config2: FP8 W8A8, quant + GEMM per call, bf16 in/out",
+    return {"config": "config2: FP8 W8A8, quant + GEMM per call, bf16 in/out; device time per "
+                      "call from a CUDA-graph replay (host launch overhead excluded)",
             "fp8_peak_tflops": fp8_peak, "fp8_peak_source": "torch._scaled_mm e4m3 8192^3 on this pool",
             "points": out}
 

@@ -44,6 +44,7 @@ struct Tuning {
   int awq_gemv_cluster = 0;  // 0 = heuristic
   int awq_swap_cluster = 0;  // 0 = heuristic
   int awq_gemm_pair = 0;     // 1: CTA-pair (cta_group::2) GEMM for large M; 0: one-SM tiles
+  int gemm_bn = 256;         // one-SM GEMM tile width: 256 or 224; 0 = pick by wave count
   int fp8_gemv_cluster = 0;
 };
 Tuning g_tune;
@@ -287,30 +288,63 @@ int awq_gemm2_launch(__half* y, const __half* x, const int32_t* qw, const int32_
   return rc ? rc : after_launch();
 }
 
-int awq_gemm_launch(__half* y, const __half* x, const int32_t* qw, const int32_t* qz,
-                    const __half* sc, const __half* bias, int M, int K, int N, int group,
-                    cudaStream_t stream, int dev) {
+// Tile width for the one-SM tcgen05 GEMMs: 256 by default (measured fastest on
+// B200 for the config shapes); 224 can be forced, and 0 picks the width with the
+// fewer tile-columns x waves (a 224-wide tile costs more than 224/256 of a
+// 256-wide one, so the wave count alone mispredicts).
+int pick_bn(int M, int N, int sms) {
+  if (g_tune.gemm_bn == 256 || g_tune.gemm_bn == 224) return g_tune.gemm_bn;
+  long best_cost = -1;
+  int best = 256;
+  for (int bn : {256, 224}) {
+    const long tiles = long((N + bn - 1) / bn) * ((M + lmrs::kTcBM - 1) / lmrs::kTcBM);
+    const long waves = (tiles + sms - 1) / sms;
+    const long cost = waves * bn;
+    if (best_cost < 0 || cost < best_cost) {
+      best_cost = cost;
+      best = bn;
+    }
+  }
+  return best;
+}
+
+std::atomic<int> g_smem_awq_gemm224[kMaxDevices];
+
+template <int BN>
+int awq_gemm_launch_bn(__half* y, const __half* x, const int32_t* qw, const int32_t* qz,
+                       const __half* sc, const __half* bias, int M, int K, int N, int group,
+                       cudaStream_t stream, int dev, std::atomic<int>* smem_done) {
   CUtensorMap tx, tq, ts, tz;
   int rc;
   if ((rc = make_tmap(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, x, K, M, uint64_t(K) * 2, 64, 128,
                       CU_TENSOR_MAP_SWIZZLE_128B)))
     return rc;
-  if ((rc = make_tmap(&tq, CU_TENSOR_MAP_DATA_TYPE_INT32, qw, N / 8, K, uint64_t(N / 8) * 4, 32,
-                      64, CU_TENSOR_MAP_SWIZZLE_NONE)))
+  if ((rc = make_tmap(&tq, CU_TENSOR_MAP_DATA_TYPE_INT32, qw, N / 8, K, uint64_t(N / 8) * 4,
+                      BN / 8, 64, CU_TENSOR_MAP_SWIZZLE_NONE)))
     return rc;
   if ((rc = make_tmap(&ts, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, sc, N, K / group, uint64_t(N) * 2,
-                      256, 1, CU_TENSOR_MAP_SWIZZLE_NONE)))
+                      BN, 1, CU_TENSOR_MAP_SWIZZLE_NONE)))
     return rc;
   if ((rc = make_tmap(&tz, CU_TENSOR_MAP_DATA_TYPE_INT32, qz, N / 8, K / group,
-                      uint64_t(N / 8) * 4, 32, 1, CU_TENSOR_MAP_SWIZZLE_NONE)))
+                      uint64_t(N / 8) * 4, BN / 8, 1, CU_TENSOR_MAP_SWIZZLE_NONE)))
     return rc;
-  if ((rc = ensure_smem(lmrs::awq_gemm_tc_kernel, lmrs::kAwqSmemBytes, g_smem_awq_gemm, dev)))
-    return rc;
-  const int tiles = ((N + lmrs::kTcBN - 1) / lmrs::kTcBN) * ((M + lmrs::kTcBM - 1) / lmrs::kTcBM);
+  constexpr int smem = lmrs::AwqTile<BN>::kSmem;
+  if ((rc = ensure_smem(lmrs::awq_gemm_tc_kernel<BN>, smem, smem_done, dev))) return rc;
+  const int tiles = ((N + BN - 1) / BN) * ((M + lmrs::kTcBM - 1) / lmrs::kTcBM);
   const int grid = tiles < sm_count(dev) ? tiles : sm_count(dev);
-  lmrs::awq_gemm_tc_kernel<<<grid, lmrs::kAwqGemmThreads, lmrs::kAwqSmemBytes, stream>>>(
+  lmrs::awq_gemm_tc_kernel<BN><<<grid, lmrs::kAwqGemmThreads, smem, stream>>>(
       tx, tq, ts, tz, y, bias, M, K, N, group);
   return after_launch();
+}
+
+int awq_gemm_launch(__half* y, const __half* x, const int32_t* qw, const int32_t* qz,
+                    const __half* sc, const __half* bias, int M, int K, int N, int group,
+                    cudaStream_t stream, int dev) {
+  if (pick_bn(M, N, sm_count(dev)) == 224)
+    return awq_gemm_launch_bn<224>(y, x, qw, qz, sc, bias, M, K, N, group, stream, dev,
+                                   g_smem_awq_gemm224);
+  return awq_gemm_launch_bn<256>(y, x, qw, qz, sc, bias, M, K, N, group, stream, dev,
+                                 g_smem_awq_gemm);
 }
 
 // ------------------------------------------------------------------ FP8
@@ -371,24 +405,35 @@ int fp8_gemv_launch(__nv_bfloat16* y, const uint8_t* xq, const float* sx, const 
   return rc ? rc : after_launch();
 }
 
-int fp8_gemm_launch(__nv_bfloat16* y, const uint8_t* xq, const float* sx, const uint8_t* wq,
-                    const float* sw, const __nv_bfloat16* bias, int M, int K, int N,
-                    cudaStream_t stream, int dev) {
+std::atomic<int> g_smem_f8_gemm224[kMaxDevices];
+
+template <int BN>
+int fp8_gemm_launch_bn(__nv_bfloat16* y, const uint8_t* xq, const float* sx, const uint8_t* wq,
+                       const float* sw, const __nv_bfloat16* bias, int M, int K, int N,
+                       cudaStream_t stream, int dev, std::atomic<int>* smem_done) {
   CUtensorMap ta, tb;
   int rc;
   if ((rc = make_tmap(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, xq, K, M, uint64_t(K), 128, 128,
                       CU_TENSOR_MAP_SWIZZLE_128B)))
     return rc;
-  if ((rc = make_tmap(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, wq, K, N, uint64_t(K), 128, 256,
+  if ((rc = make_tmap(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, wq, K, N, uint64_t(K), 128, BN,
                       CU_TENSOR_MAP_SWIZZLE_128B)))
     return rc;
-  if ((rc = ensure_smem(lmrs::fp8_gemm_tc_kernel, lmrs::kF8SmemBytes, g_smem_f8_gemm, dev)))
-    return rc;
-  const int tiles = ((N + lmrs::kTcBN - 1) / lmrs::kTcBN) * ((M + lmrs::kTcBM - 1) / lmrs::kTcBM);
+  constexpr int smem = lmrs::F8Tile<BN>::kSmem;
+  if ((rc = ensure_smem(lmrs::fp8_gemm_tc_kernel<BN>, smem, smem_done, dev))) return rc;
+  const int tiles = ((N + BN - 1) / BN) * ((M + lmrs::kTcBM - 1) / lmrs::kTcBM);
   const int grid = tiles < sm_count(dev) ? tiles : sm_count(dev);
-  lmrs::fp8_gemm_tc_kernel<<<grid, lmrs::kF8Threads, lmrs::kF8SmemBytes, stream>>>(
-      ta, tb, y, sx, sw, bias, M, K, N);
+  lmrs::fp8_gemm_tc_kernel<BN><<<grid, lmrs::kF8Threads, smem, stream>>>(ta, tb, y, sx, sw, bias,
+                                                                          M, K, N);
   return after_launch();
+}
+
+int fp8_gemm_launch(__nv_bfloat16* y, const uint8_t* xq, const float* sx, const uint8_t* wq,
+                    const float* sw, const __nv_bfloat16* bias, int M, int K, int N,
+                    cudaStream_t stream, int dev) {
+  if (pick_bn(M, N, sm_count(dev)) == 224)
+    return fp8_gemm_launch_bn<224>(y, xq, sx, wq, sw, bias, M, K, N, stream, dev, g_smem_f8_gemm224);
+  return fp8_gemm_launch_bn<256>(y, xq, sx, wq, sw, bias, M, K, N, stream, dev, g_smem_f8_gemm);
 }
 
 int fp8_linear_prequant_impl(void* y, const uint8_t* xq, const float* x_scale, const uint8_t* wq,
@@ -449,6 +494,7 @@ int lmrs_set_tuning(const char* key, int value) {
   else if (!strcmp(key, "awq_swap_max_m")) g_tune.awq_swap_max_m = value;
   else if (!strcmp(key, "awq_swap_cluster")) g_tune.awq_swap_cluster = value;
   else if (!strcmp(key, "awq_gemm_pair")) g_tune.awq_gemm_pair = value;
+  else if (!strcmp(key, "gemm_bn")) g_tune.gemm_bn = value;
   else if (!strcmp(key, "fp8_gemv_max_m")) g_tune.fp8_gemv_max_m = value;
   else if (!strcmp(key, "gemv_ctas_per_sm")) g_tune.gemv_ctas_per_sm = value;
   else if (!strcmp(key, "awq_gemv_cluster")) g_tune.awq_gemv_cluster = value;

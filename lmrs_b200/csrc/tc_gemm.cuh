@@ -50,14 +50,14 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint4 v) {
 // stay resident in L2 and each is fetched from HBM about once.
 constexpr int kTcGroupM = 8;
 
-__device__ __forceinline__ void tile_coords(int t, int m_tiles, int n_tiles, int& m0, int& n0) {
+__device__ __forceinline__ void tile_coords(int t, int m_tiles, int n_tiles, int bn, int& m0, int& n0) {
   const int per_group = kTcGroupM * n_tiles;
   const int grp = t / per_group;
   const int first_m = grp * kTcGroupM;
   const int gm = min(m_tiles - first_m, kTcGroupM);
   const int local = t - grp * per_group;
   m0 = (first_m + local % gm) * kTcBM;
-  n0 = (local / gm) * kTcBN;
+  n0 = (local / gm) * bn;
 }
 
 // Accumulator hand-off barriers (MMA -> epilogue -> MMA), two buffers.
@@ -82,14 +82,26 @@ constexpr int kAwqDqWarp0 = 6;
 constexpr int kAwqDqWarps = 8;    // per group, 8 rows of the 64-row K-block each
 constexpr int kAwqGemmThreads = 32 * (kAwqDqWarp0 + kAwqDqWarps * kAwqDqGroups);  // 704
 constexpr int kAwqABytes = kTcBM * kAwqBK * 2;        // 16 KB
-constexpr int kAwqBBytes = kTcBN * kAwqBK * 2;        // 32 KB
-constexpr int kAwqPBytes = kAwqBK * (kTcBN / 8) * 4;  // 8 KB
-constexpr int kAwqSBytes = kTcBN * 2;                 // 512 B
-constexpr int kAwqZBytes = (kTcBN / 8) * 4;           // 128 B
-constexpr int kAwqStageTx = kAwqABytes + kAwqPBytes + kAwqSBytes + kAwqZBytes;
-constexpr int kAwqSmemBytes = 1024 + kAwqSA * (kAwqABytes + kAwqPBytes + kAwqSBytes + kAwqZBytes) +
-                              kAwqSB * kAwqBBytes + 256;
+constexpr int kAwqBBytes = 256 * kAwqBK * 2;          // 32 KB: B stage sized for 4 blocks of 64 columns
+// BN = 256 or 224 output columns per tile (224 evens out the waves of N = 14336);
+// the B stage keeps four 64-column blocks, a 224-wide tile leaves half of the last unused.
+// Every TMA destination in shared memory starts on a 128-byte boundary, so each
+// per-stage region is padded to a multiple of 128 bytes (the transaction count
+// stays the true box size).
+constexpr int align128(int b) { return (b + 127) / 128 * 128; }
+template <int BN> struct AwqTile {
+  static constexpr int kWords = BN / 8;                       // packed words per k row
+  static constexpr int kP = align128(kAwqBK * kWords * 4);    // packed stage
+  static constexpr int kS = align128(BN * 2);                 // scales of one group
+  static constexpr int kZ = align128(kWords * 4);             // zeros of one group
+  static constexpr int kTx = kAwqABytes + kAwqBK * kWords * 4 + BN * 2 + kWords * 4;
+  static constexpr int kSmem = 1024 + kAwqSA * (kAwqABytes + kP + kS + kZ) + kAwqSB * kAwqBBytes + 256;
+  static_assert(kAwqABytes % 1024 == 0 && kAwqBBytes % 1024 == 0 && (kAwqSA * kP) % 128 == 0,
+                "TMA destinations must stay 128-byte aligned");
+};
+constexpr int kAwqSmemBytes = AwqTile<256>::kSmem;
 
+template <int BN>
 __global__ void __launch_bounds__(kAwqGemmThreads, 1)
     awq_gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x,
                        const __grid_constant__ CUtensorMap tm_q,
@@ -100,10 +112,11 @@ __global__ void __launch_bounds__(kAwqGemmThreads, 1)
   uint8_t* smem = align1024(smem_raw);
   uint8_t* sA = smem;
   uint8_t* sB = sA + kAwqSA * kAwqABytes;
+  using T = AwqTile<BN>;
   uint8_t* sP = sB + kAwqSB * kAwqBBytes;
-  uint8_t* sS = sP + kAwqSA * kAwqPBytes;
-  uint8_t* sZ = sS + kAwqSA * kAwqSBytes;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sZ + kAwqSA * kAwqZBytes);
+  uint8_t* sS = sP + kAwqSA * T::kP;
+  uint8_t* sZ = sS + kAwqSA * T::kS;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sZ + kAwqSA * T::kZ);
   uint64_t* empty = full + kAwqSA;
   uint64_t* bfull = empty + kAwqSA;
   uint64_t* bempty = bfull + kAwqSB;
@@ -112,7 +125,7 @@ __global__ void __launch_bounds__(kAwqGemmThreads, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int KB = K / kAwqBK;
-  const int n_tiles = (N + kTcBN - 1) / kTcBN;
+  const int n_tiles = (N + BN - 1) / BN;
   const int m_tiles = (M + kTcBM - 1) / kTcBM;
   const int tiles = n_tiles * m_tiles;
 
@@ -150,30 +163,30 @@ __global__ void __launch_bounds__(kAwqGemmThreads, 1)
       bool ok = true;
       for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
         int m0, n0;
-        tile_coords(t, m_tiles, n_tiles, m0, n0);
+        tile_coords(t, m_tiles, n_tiles, BN, m0, n0);
         for (int kb = 0; kb < KB; ++kb, ++kg) {
           const int s = kg % kAwqSA;
           if (!(ok = mbar_wait(&empty[s], ((kg / kAwqSA) & 1) ^ 1, kErrWaitEmpty))) break;
-          mbar_arrive_expect_tx(&full[s], kAwqStageTx);
+          mbar_arrive_expect_tx(&full[s], T::kTx);
           const int k = kb * kAwqBK;
           const int gi = k / group;
           tma_load_2d_hint(&tm_x, &full[s], sA + s * kAwqABytes, k, m0, keep);
-          tma_load_2d(&tm_q, &full[s], sP + s * kAwqPBytes, n0 / 8, k);
-          tma_load_2d(&tm_s, &full[s], sS + s * kAwqSBytes, n0, gi);
-          tma_load_2d(&tm_z, &full[s], sZ + s * kAwqZBytes, n0 / 8, gi);
+          tma_load_2d(&tm_q, &full[s], sP + s * T::kP, n0 / 8, k);
+          tma_load_2d(&tm_s, &full[s], sS + s * T::kS, n0, gi);
+          tma_load_2d(&tm_z, &full[s], sZ + s * T::kZ, n0 / 8, gi);
         }
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t idesc = make_idesc(0, 0, /*a K-major*/ 0, /*b MN-major*/ 1, kTcBM, kTcBN);
+      constexpr uint32_t idesc = make_idesc(0, 0, /*a K-major*/ 0, /*b MN-major*/ 1, kTcBM, BN);
       uint32_t kg = 0, it = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++it) {
         const uint32_t a = it & 1;
         if (!(ok = mbar_wait(&acc->empty[a], ((it >> 1) & 1) ^ 1, kErrWaitAccum))) break;
         tc_fence_after();
-        const uint32_t d = tmem + a * kTcBN;
+        const uint32_t d = tmem + a * BN;
         for (int kb = 0; kb < KB; ++kb, ++kg) {
           const int s = kg % kAwqSA, sb = kg % kAwqSB;
           ok = mbar_wait(&bfull[sb], (kg / kAwqSB) & 1, kErrWaitDequant) &&
@@ -203,10 +216,10 @@ __global__ void __launch_bounds__(kAwqGemmThreads, 1)
       if (!mbar_wait(&acc->full[a], (it >> 1) & 1, kErrWaitAccum)) break;
       tc_fence_after();
       int m0, n0;
-        tile_coords(t, m_tiles, n_tiles, m0, n0);
+        tile_coords(t, m_tiles, n_tiles, BN, m0, n0);
       const int row = m0 + quarter * 32 + lane;
-      const uint32_t tbase = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + a * kTcBN;
-      for (int ch = 0; ch < kTcBN / 16; ++ch) {
+      const uint32_t tbase = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + a * BN;
+      for (int ch = 0; ch < BN / 16; ++ch) {
         uint32_t r[16];
         tmem_ld16(tbase + ch * 16, r);
         tmem_ld_wait();
@@ -247,16 +260,18 @@ __global__ void __launch_bounds__(kAwqGemmThreads, 1)
         ok = mbar_wait(&full[s], (kg / kAwqSA) & 1, kErrWaitFull) &&
              mbar_wait(&bempty[sb], ((kg / kAwqSB) & 1) ^ 1, kErrWaitEmpty);
         if (!ok) break;
-        const uint32_t zw = reinterpret_cast<const uint32_t*>(sZ + s * kAwqZBytes)[lane];
-        const uint4 sv = reinterpret_cast<const uint4*>(sS + s * kAwqSBytes)[lane];
+        // lane = word column of the tile (BN/8 words; a 224-wide tile idles lanes 28..31)
+        const bool live = lane < T::kWords;
+        const uint32_t zw = live ? reinterpret_cast<const uint32_t*>(sZ + s * T::kZ)[lane] : 0u;
+        const uint4 sv = live ? reinterpret_cast<const uint4*>(sS + s * T::kS)[lane] : make_uint4(0u, 0u, 0u, 0u);
         uint32_t zb[4];
         awq_word_to_h2_biased(zw, zb);
-        const uint32_t* prow = reinterpret_cast<const uint32_t*>(sP + s * kAwqPBytes);
+        const uint32_t* prow = reinterpret_cast<const uint32_t*>(sP + s * T::kP);
         const uint32_t bbase = smem_u32(sB + sb * kAwqBBytes) + bblk * 8192;
         uint32_t w[kAwqBK / kAwqDqWarps];
 #pragma unroll
         for (int rr = 0; rr < kAwqBK / kAwqDqWarps; ++rr)
-          w[rr] = prow[(dw * (kAwqBK / kAwqDqWarps) + rr) * 32 + lane];
+          w[rr] = live ? prow[(dw * (kAwqBK / kAwqDqWarps) + rr) * T::kWords + lane] : 0u;
 #pragma unroll
         for (int rr = 0; rr < kAwqBK / kAwqDqWarps; ++rr) {
           const int r = dw * (kAwqBK / kAwqDqWarps) + rr;
@@ -268,7 +283,7 @@ __global__ void __launch_bounds__(kAwqGemmThreads, 1)
           o.z = dq_h2(qb[2], zb[2], sv.z);
           o.w = dq_h2(qb[3], zb[3], sv.w);
           const uint32_t addr = bbase + (r >> 3) * 1024 + (r & 7) * 128 + ((chunk ^ (r & 7)) << 4);
-          st_shared_v4(addr, o);
+          if (live) st_shared_v4(addr, o);
         }
         fence_proxy_async_smem();
         __syncwarp();
@@ -289,9 +304,14 @@ constexpr int kF8BK = 128;  // bytes (= e4m3 elements) of K per stage
 constexpr int kF8Stages = 4;
 constexpr int kF8Threads = 32 * (kTcEpiWarp0 + kTcEpiWarps);  // 192
 constexpr int kF8ABytes = kTcBM * kF8BK;  // 16 KB
-constexpr int kF8BBytes = kTcBN * kF8BK;  // 32 KB
-constexpr int kF8SmemBytes = 1024 + kF8Stages * (kF8ABytes + kF8BBytes) + 256;
+template <int BN> struct F8Tile {
+  static constexpr int kB = BN * kF8BK;  // weight rows of the tile x 128 bytes of K
+  static constexpr int kSmem = 1024 + kF8Stages * (kF8ABytes + kB) + 256;
+  static_assert(kB % 1024 == 0 && kF8ABytes % 1024 == 0, "128B-swizzled stages are 1024-byte aligned");
+};
+constexpr int kF8SmemBytes = F8Tile<256>::kSmem;
 
+template <int BN>
 __global__ void __launch_bounds__(kF8Threads, 1)
     fp8_gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_a,
                        const __grid_constant__ CUtensorMap tm_b, __nv_bfloat16* __restrict__ y,
@@ -301,6 +321,7 @@ __global__ void __launch_bounds__(kF8Threads, 1)
   uint8_t* smem = align1024(smem_raw);
   uint8_t* sA = smem;
   uint8_t* sB = sA + kF8Stages * kF8ABytes;
+  constexpr int kF8BBytes = F8Tile<BN>::kB;
   uint64_t* full = reinterpret_cast<uint64_t*>(sB + kF8Stages * kF8BBytes);
   uint64_t* empty = full + kF8Stages;
   AccBars* acc = reinterpret_cast<AccBars*>(empty + kF8Stages);
@@ -308,7 +329,7 @@ __global__ void __launch_bounds__(kF8Threads, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int KB = (K + kF8BK - 1) / kF8BK;
-  const int n_tiles = (N + kTcBN - 1) / kTcBN;
+  const int n_tiles = (N + BN - 1) / BN;
   const int m_tiles = (M + kTcBM - 1) / kTcBM;
   const int tiles = n_tiles * m_tiles;
 
@@ -340,7 +361,7 @@ __global__ void __launch_bounds__(kF8Threads, 1)
       bool ok = true;
       for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
         int m0, n0;
-        tile_coords(t, m_tiles, n_tiles, m0, n0);
+        tile_coords(t, m_tiles, n_tiles, BN, m0, n0);
         for (int kb = 0; kb < KB; ++kb, ++kg) {
           const int s = kg % kF8Stages;
           if (!(ok = mbar_wait(&empty[s], ((kg / kF8Stages) & 1) ^ 1, kErrWaitEmpty))) break;
@@ -352,14 +373,14 @@ __global__ void __launch_bounds__(kF8Threads, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t idesc = make_idesc(0, 0, 0, 0, kTcBM, kTcBN);  // e4m3 x e4m3, K-major
+      constexpr uint32_t idesc = make_idesc(0, 0, 0, 0, kTcBM, BN);  // e4m3 x e4m3, K-major
       uint32_t kg = 0, it = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++it) {
         const uint32_t a = it & 1;
         if (!(ok = mbar_wait(&acc->empty[a], ((it >> 1) & 1) ^ 1, kErrWaitAccum))) break;
         tc_fence_after();
-        const uint32_t d = tmem + a * kTcBN;
+        const uint32_t d = tmem + a * BN;
         for (int kb = 0; kb < KB; ++kb, ++kg) {
           const int s = kg % kF8Stages;
           if (!(ok = mbar_wait(&full[s], (kg / kF8Stages) & 1, kErrWaitFull))) break;
@@ -386,11 +407,11 @@ __global__ void __launch_bounds__(kF8Threads, 1)
       if (!mbar_wait(&acc->full[a], (it >> 1) & 1, kErrWaitAccum)) break;
       tc_fence_after();
       int m0, n0;
-        tile_coords(t, m_tiles, n_tiles, m0, n0);
+        tile_coords(t, m_tiles, n_tiles, BN, m0, n0);
       const int row = m0 + quarter * 32 + lane;
       const float rs = row < M ? sx[row] : 0.f;
-      const uint32_t tbase = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + a * kTcBN;
-      for (int ch = 0; ch < kTcBN / 16; ++ch) {
+      const uint32_t tbase = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + a * BN;
+      for (int ch = 0; ch < BN / 16; ++ch) {
         uint32_t r[16];
         tmem_ld16(tbase + ch * 16, r);
         tmem_ld_wait();

@@ -180,7 +180,7 @@ __global__ void __launch_bounds__(kP2Threads, 1)
         const uint32_t a = it & 1;
         if (!(ok = mbar_wait(&accempty[a], ((it >> 1) & 1) ^ 1, kErrWaitAccum))) break;
         tc_fence_after();
-        const uint32_t d = tmem + a * kTcBN;
+        const uint32_t d = tmem + a * kP2BN;
         for (int kb = 0; kb < KB; ++kb, ++kg) {
           const int s = kg % kP2SA, sb = kg % kP2SB;
           ok = mbar_wait(&bfull[sb], (kg / kP2SB) & 1, kErrWaitDequant) &&
@@ -213,7 +213,7 @@ __global__ void __launch_bounds__(kP2Threads, 1)
       int m0, n0;
       coords(t, m0, n0);
       const int row = m0 + 128 * static_cast<int>(rank) + quarter * 32 + lane;
-      const uint32_t tbase = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + a * kTcBN;
+      const uint32_t tbase = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + a * kP2BN;
       for (int ch = 0; ch < kP2BN / 16; ++ch) {
         uint32_t r[16];
         tmem_ld16(tbase + ch * 16, r);

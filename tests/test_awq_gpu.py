@@ -192,7 +192,9 @@ def test_status_codes(cuda):
 
 @pytest.mark.parametrize("knob,value,Ms", [("awq_gemm_pair", 1, (129, 300, 512)),
                                            ("awq_gemv_max_m", 16, (9, 12, 16)),
-                                           ("awq_swap_max_m", 128, (65, 100, 128))])
+                                           ("awq_swap_max_m", 128, (65, 100, 128)),
+                                           ("gemm_bn", 0, (100, 300, 512)),
+                                           ("gemm_bn", 224, (100, 300, 512))])
 def test_opt_in_paths(cuda, knob, value, Ms):
     """Kernels the default dispatch does not pick for these M (CTA-pair GEMM,
     the two-token-tile GEMV, swap-AB up to 128 tokens) stay correct and
@@ -200,7 +202,7 @@ def test_opt_in_paths(cuda, knob, value, Ms):
     import torch
     import lmrs_b200 as L
     from lmrs_b200 import _lib
-    defaults = {"awq_gemm_pair": 0, "awq_gemv_max_m": 8, "awq_swap_max_m": 64}
+    defaults = {"awq_gemm_pair": 0, "awq_gemv_max_m": 8, "awq_swap_max_m": 64, "gemm_bn": 256}
     K, N, g = 1024, 1280, 128
     try:
         L.set_tuning(knob, value)

@@ -166,3 +166,22 @@ def test_workspace_and_status(cuda):
     torch.cuda.synchronize()
     assert torch.count_nonzero(y.float()) == 0
     assert L.read_device_error() == 0
+
+
+@pytest.mark.parametrize("bn", [256, 224])
+def test_gemm_tile_widths(cuda, bn):
+    """Both tcgen05 tile widths (the dispatcher picks per shape) against the oracle."""
+    import lmrs_b200 as L
+    K, N, M = 1024, 1000, 300  # N % 8 == 0 but not a multiple of either tile width
+    f = O.fp8_inputs(M, K, N, seed=bn, with_bias=True)
+    x, w, b = _dev_fp8(f, cuda, True)
+    try:
+        L.set_tuning("gemm_bn", bn)
+        wq, sw = L.quantize_fp8_weight(w)
+        y = L.fp8_linear(x, wq, sw, b)
+    finally:
+        L.set_tuning("gemm_bn", 256)
+    wq_ref, sw_ref = O.c_fp8_quant_rows(f["w_bf16"], 0)
+    y_ref, _, _ = O.c_fp8_linear(f["x_bf16"], wq_ref, sw_ref, f["bias_bf16"])
+    err = O.max_rel_err(O.bf16_bits_to_f32(bits16(y)), O.bf16_bits_to_f32(y_ref))
+    assert err < TIGHT, err
