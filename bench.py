@@ -425,6 +425,153 @@ def fp8_sweep(device, steps=5):
             "points": out}
 
 
+# ----------------------------------------------------------- decode (configs 3/4)
+DECODE_PRESETS = {
+    # name: (config attribute, context, batches, BASELINE config)
+    "8b-awq": ("LLAMA3_8B_AWQ", 2048, (1, 16, 64), "config3"),
+    "70b-fp8": ("LLAMA3_70B_FP8", 4096, (1, 32, 256), "config4"),
+}
+
+
+def _graph_ms(g, steps, warmup, stream, dist_on, device):
+    """Per-replay device time of a captured graph: `warmup` untimed replays, then
+    `steps` replays each bracketed by events; barrier + synchronize on both sides;
+    returns (mean ms, median ms), each the max over ranks."""
+    for _ in range(warmup):
+        g.replay()
+    torch.cuda.synchronize()
+    if dist_on:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(steps)]
+    for a, b in ev:
+        a.record(stream)
+        g.replay()
+        b.record(stream)
+    torch.cuda.synchronize()
+    if dist_on:
+        torch.distributed.barrier()
+    ts = [a.elapsed_time(b) for a, b in ev]
+    return (max_over_ranks(sum(ts) / len(ts), dist_on, device),
+            max_over_ranks(statistics.median(ts), dist_on, device))
+
+
+def run_decode(args, device, dist_on, world, rank):
+    """Configs 3/4: one decode step of the Llama-shaped decoder (tensor parallel
+    over the ranks), captured as one CUDA graph (NCCL all-reduces included) and
+    replayed.  tok/s = batch / step time; the linear share replays the step's
+    quantized projections alone."""
+    from lmrs_b200 import decoder as D
+    attr, ctx, batches, cname = DECODE_PRESETS[args.decode]
+    cfg = getattr(D, attr)
+    if args.ctx:
+        ctx = args.ctx
+    if args.batch:
+        batches = tuple(int(b) for b in args.batch.split(","))
+    pg = torch.distributed.group.WORLD if dist_on else None
+    stream = torch.cuda.current_stream(device)
+    total = torch.cuda.get_device_properties(device).total_memory
+    act_bytes = 2
+    lin_b = cfg.linear_bytes(world)
+    head_b = cfg.vocab // world * cfg.hidden * act_bytes
+    embed_b = cfg.vocab * cfg.hidden * act_bytes
+    pk, pk_kind = peaks()
+    dec, points = None, []
+    t_init = time.perf_counter()
+    clk = ClockSampler(torch.cuda.current_device() if "CUDA_VISIBLE_DEVICES" not in os.environ
+                       else int(os.environ["CUDA_VISIBLE_DEVICES"].split(",")[torch.cuda.current_device()]))
+    clk_started = False
+    for B in batches:
+        kv_b = D.QuantDecoder.kv_bytes(cfg, B, ctx, world)
+        need = lin_b + head_b + embed_b + kv_b
+        if need > total - (8 << 30):  # same decision on every rank (all shapes are equal)
+            points.append({"batch": B, "status": "does not fit",
+                           "need_gb_per_gpu": round(need / 1e9, 1),
+                           "hbm_gb_per_gpu": round(total / 1e9, 1)})
+            continue
+        if dec is None:
+            dec = D.QuantDecoder(cfg, B, ctx, device, rank, world, seed=0, group=pg)
+            torch.cuda.synchronize()
+            init_s = time.perf_counter() - t_init
+        else:
+            dec.set_batch(B)
+        g, out = D.graph_step(dec)
+        gl, _ = D.graph_step(dec, dec.linears_only)
+        if not clk_started:
+            clk.start()
+            clk_started = True
+        step_ms, step_med = _graph_ms(g, args.steps, args.warmup, stream, dist_on, device)
+        lin_ms, _ = _graph_ms(gl, args.steps, args.warmup, stream, dist_on, device)
+        del gl
+        ar_ms = None
+        if dist_on:
+            y = torch.zeros(B, cfg.hidden, dtype=dec.act, device=device)
+            sg = torch.cuda.Stream(device)
+            sg.wait_stream(stream)
+            with torch.cuda.stream(sg):
+                torch.distributed.all_reduce(y, group=pg)
+            stream.wait_stream(sg)
+            torch.cuda.synchronize()
+            ga = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(ga):
+                for _ in range(2 * cfg.layers):
+                    torch.distributed.all_reduce(y, group=pg)
+            ar_ms, _ = _graph_ms(ga, args.steps, args.warmup, stream, dist_on, device)
+            del ga
+        # e2e: token ids in from pinned host memory, next tokens back, every step
+        htok = dec.tokens.cpu().pin_memory()
+        hout = torch.empty_like(out, device="cpu").pin_memory()
+        for _ in range(args.warmup):
+            dec.tokens.copy_(htok, non_blocking=True)
+            g.replay()
+            hout.copy_(out, non_blocking=True)
+        torch.cuda.synchronize()
+        if dist_on:
+            torch.distributed.barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(args.steps):
+            dec.tokens.copy_(htok, non_blocking=True)
+            g.replay()
+            hout.copy_(out, non_blocking=True)
+        b.record(stream)
+        torch.cuda.synchronize()
+        e2e_ms = max_over_ranks(a.elapsed_time(b) / args.steps, dist_on, device)
+        del g
+        byts = lin_b + head_b + kv_b   # per rank, per step (weights + LM head + KV read)
+        gbs = byts / (step_med * 1e-3) / 1e9
+        points.append({
+            "batch": B, "ms_per_step": round(step_ms, 4), "ms_median": round(step_med, 4),
+            "tok_s": round(B / (step_med * 1e-3), 1),
+            "e2e_tok_s": round(B / (e2e_ms * 1e-3), 1), "e2e_ms_per_step": round(e2e_ms, 4),
+            "linear_ms": round(lin_ms, 4), "linear_share": round(lin_ms / step_med, 4),
+            "linear_GB_s": round(lin_b / (lin_ms * 1e-3) / 1e9, 1),
+            "linear_frac_hbm": round(lin_b / (lin_ms * 1e-3) / 1e9 / pk["hbm_gbs"], 4),
+            "allreduce_ms": None if ar_ms is None else round(ar_ms, 4),
+            "bytes_per_step_per_gpu": byts, "GB_s_per_gpu": round(gbs, 1),
+            "frac_hbm": round(gbs / pk["hbm_gbs"], 4),
+            "h2d_bytes_per_step": B * 8, "d2h_bytes_per_step": B * 8})
+    clocks = clk.stop() if clk_started else None
+    ok = [p for p in points if "tok_s" in p]
+    best = max(ok, key=lambda p: p["batch"]) if ok else None
+    line = {"metric": f"decode_tok_s_{cname}", "value": best["tok_s"] if best else None,
+            "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": best["ms_median"] if best else None, "higher_is_better": True,
+            "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
+            "dtype": "f16 act, int4 weights" if cfg.quant == "awq" else "bf16 act, e4m3 W8A8",
+            "data": "synthetic (random-init weights, random KV cache and token ids)",
+            "config": {"workload": f"{cname}: {args.decode} decoder, one decode step at ctx {ctx}, "
+                                   f"value = largest batch that fits",
+                       "layers": cfg.layers, "hidden": cfg.hidden, "ctx": ctx,
+                       "parallelism": f"tp{world}", "l2": "weights + KV per step >> L2"},
+            "points": points, "clocks": clocks, "peak_hbm_gbs": pk["hbm_gbs"],
+            "peak_source": pk_kind,
+            "init_s": round(init_s, 1) if dec is not None else None}
+    del dec
+    return line
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -436,6 +583,11 @@ def main():
     ap.add_argument("--case", default=None,
                     help="profiling mode: run a few launches of one case and exit, e.g. "
                          "awq:4096 (config-1 shape, M=4096) or fp8:8192:4096:28672 (M:K:N)")
+    ap.add_argument("--decode", choices=sorted(DECODE_PRESETS), default=None,
+                    help="configs 3/4: decode tok/s of the 8B AWQ or 70B FP8 decoder "
+                         "(tensor parallel over the torchrun ranks)")
+    ap.add_argument("--batch", default=None, help="decode batches, comma separated")
+    ap.add_argument("--ctx", type=int, default=None, help="decode context length")
     args = ap.parse_args()
     if args.case:
         run_case(args.case)
@@ -478,6 +630,15 @@ def main():
                 "reference_gpu": rg}
         print(json.dumps(line), flush=True)
         if dist_on:
+            torch.distributed.destroy_process_group()
+        return
+
+    if args.decode:
+        line = run_decode(args, device, dist_on, world, rank)
+        if rank == 0:
+            print(json.dumps(line), flush=True)
+        if dist_on:
+            torch.distributed.barrier()
             torch.distributed.destroy_process_group()
         return
 

@@ -49,6 +49,8 @@ __global__ void __launch_bounds__(kSwThreads, 2)
                          const __grid_constant__ CUtensorMap tm_s,
                          const __grid_constant__ CUtensorMap tm_z, __half* __restrict__ y,
                          const __half* __restrict__ bias, int M, int K, int N, int group) {
+  pdl_wait();     // activations are the previous kernel's output
+  pdl_trigger();
   namespace cg = cooperative_groups;
   constexpr int kStage = (sw_stage_bytes(NT) + 1023) / 1024 * 1024;
   constexpr int kX = sw_xbytes(NT);

@@ -12,6 +12,8 @@ namespace lmrs {
 __global__ void __launch_bounds__(256) awq_unpack_kernel(int8_t* __restrict__ q_out,
                                                          const uint32_t* __restrict__ packed,
                                                          int64_t total_words) {
+  pdl_wait();     // activations are the previous kernel's output
+  pdl_trigger();
   const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (idx >= total_words) return;
   const uint32_t w = __ldg(packed + idx);
@@ -28,6 +30,8 @@ __global__ void __launch_bounds__(256) awq_dequant_kernel(
     __half* __restrict__ w_out, const uint32_t* __restrict__ qweight,
     const uint32_t* __restrict__ qzeros, const __half* __restrict__ scales, int K, int words_n,
     int group) {
+  pdl_wait();     // activations are the previous kernel's output
+  pdl_trigger();
   const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   const int64_t total = static_cast<int64_t>(K) * words_n;
   if (idx >= total) return;

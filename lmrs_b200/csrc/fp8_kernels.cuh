@@ -47,6 +47,8 @@ template <int DT>
 __global__ void __launch_bounds__(kQuantThreads) fp8_quant_rows_kernel(
     uint8_t* __restrict__ q, float* __restrict__ scale, const typename IoType<DT>::T* __restrict__ x,
     int K) {
+  pdl_wait();     // activations are the previous kernel's output
+  pdl_trigger();
   using T = typename IoType<DT>::T;
   constexpr int VEC = 16 / sizeof(T);  // elements per 16-byte load
   __shared__ float red[kQuantThreads / 32];
@@ -136,6 +138,8 @@ __global__ void __launch_bounds__(kF8GemvThreads, 4) fp8_gemv_kernel(
     const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
     __nv_bfloat16* __restrict__ y, const float* __restrict__ sx, const float* __restrict__ sw,
     const __nv_bfloat16* __restrict__ bias, int M, int K, int N, int ring) {
+  pdl_wait();     // activations are the previous kernel's output
+  pdl_trigger();
   constexpr int MP = 8 * MT;
   constexpr int kSlot = kF8GemvBoxBytes + MP * 128;  // weights + token tile (MP rows x 128 B)
   extern __shared__ uint8_t smem_raw[];

@@ -23,6 +23,7 @@
 #include "lmrs_quant.h"
 #include "awq_gemm_swap.cuh"
 #include "awq_gemv.cuh"
+#include "awq_gemv4.cuh"
 #include "awq_pack.cuh"
 #include "fp8_kernels.cuh"
 #include "lmrs_ptx.cuh"
@@ -37,7 +38,7 @@ thread_local int t_last_cuda_error = 0;
 
 // ---- tuning knobs (lmrs_set_tuning); defaults chosen from B200 measurements
 struct Tuning {
-  int awq_gemv_max_m = 8;    // M up to this -> register-dequant GEMV
+  int awq_gemv_max_m = 16;   // M up to this -> register-dequant GEMV (16 at most)
   int awq_swap_max_m = 64;   // M up to this -> swap-AB split-K tcgen05; above -> tile GEMM
   int fp8_gemv_max_m = 32;
   int gemv_ctas_per_sm = 4;  // resident CTAs per SM the GEMV grids are sized for
@@ -46,6 +47,11 @@ struct Tuning {
   int awq_gemm_pair = 0;     // 1: CTA-pair (cta_group::2) GEMM for large M; 0: one-SM tiles
   int gemm_bn = 256;         // one-SM GEMM tile width: 256 or 224; 0 = pick by wave count
   int fp8_gemv_cluster = 0;
+  int pdl = 1;               // programmatic dependent launch on every kernel
+  int awq_gemv_slots = 4;    // ring slots of the AWQ GEMV (even, 2..8)
+  int awq_gemv4 = 1;         // M <= 4: the permute-free GEMV (0: the general one)
+  int gemv_box_rows = 128;   // TMA GEMV box height (128 or 64; 64 forced for group 64)
+  int awq_gemv4_slots = 4;   // its ring slots (4 or 8)
 };
 Tuning g_tune;
 
@@ -152,29 +158,48 @@ int after_launch() {
 
 int clampi(int v, int lo, int hi) { return v < lo ? lo : (v > hi ? hi : v); }
 
+// Launch with a cluster dimension (0 = no cluster attribute) and, when the
+// `pdl` knob is on, programmatic stream serialisation (the kernel may start
+// while its predecessor drains; every kernel here waits with griddepcontrol
+// before touching its activations or writing global memory).
 template <typename Kern, typename... Args>
-int launch_cluster(Kern kernel, int grid_x, int cluster, int threads, int smem,
-                   cudaStream_t stream, Args... args) {
+int launch_ex(Kern kernel, int grid_x, int cluster, int threads, int smem, cudaStream_t stream,
+              Args... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid_x, 1, 1);
   cfg.blockDim = dim3(threads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = cluster;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
+  cudaLaunchAttribute attr[2];
+  int n = 0;
+  if (cluster > 0) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = cluster;
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  if (g_tune.pdl) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = n;
   cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, args...);
   if (e != cudaSuccess) return record(e);
   return LMRS_OK;
 }
 
+template <typename Kern, typename... Args>
+int launch_cluster(Kern kernel, int grid_x, int cluster, int threads, int smem,
+                   cudaStream_t stream, Args... args) {
+  return launch_ex(kernel, grid_x, cluster, threads, smem, stream, args...);
+}
+
 std::atomic<int> g_smem_awq_gemm[kMaxDevices];
 std::atomic<int> g_smem_f8_gemm[kMaxDevices];
-std::atomic<int> g_smem_awq_gemv[3][kMaxDevices];
+std::atomic<int> g_smem_awq_gemv[4][kMaxDevices];
 std::atomic<int> g_smem_f8_gemv[3][kMaxDevices];
 
 // ------------------------------------------------------------------ AWQ
@@ -187,36 +212,96 @@ int gemv_cluster(int strips, int units, int forced) {
   return C;
 }
 
+// Power-of-two cluster size for the AWQ GEMV (its reduction splits the strip's
+// 128 columns evenly over the cluster).
+int pow2_floor(int v) {
+  int r = 1;
+  while (r * 2 <= v) r *= 2;
+  return r;
+}
+
+template <int MT, int BR>
+int awq_gemv_launch_t(const CUtensorMap& tq, const CUtensorMap& tx, const CUtensorMap& ts,
+                      const CUtensorMap& tz, __half* y, const __half* bias, int M, int K, int N,
+                      int group, cudaStream_t stream, int dev, int strips, int C, int S,
+                      std::atomic<int>* done) {
+  using L = lmrs::AwqGemvLayout<MT, BR>;
+  const int smem = L::smem_bytes(S);
+  int rc;
+  if ((rc = ensure_smem(lmrs::awq_gemv_kernel<MT, BR>, smem, done, dev))) return rc;
+  rc = launch_ex(lmrs::awq_gemv_kernel<MT, BR>, strips * C, C, lmrs::kAwqGemvThreads, smem, stream,
+                 tq, tx, ts, tz, y, bias, M, K, N, group, S);
+  return rc ? rc : after_launch();
+}
+
+std::atomic<int> g_smem_awq_gemv4[2][kMaxDevices];
+
+template <int BR>
+int awq_gemv4_launch_t(const CUtensorMap& tq, const CUtensorMap& tx, const CUtensorMap& ts,
+                       const CUtensorMap& tz, __half* y, const __half* bias, int M, int K, int N,
+                       int group, cudaStream_t stream, int dev, int strips, int C, int S,
+                       std::atomic<int>* done) {
+  const int smem = lmrs::AwqGemv4Layout<BR>::smem_bytes(S);
+  int rc;
+  if ((rc = ensure_smem(lmrs::awq_gemv4_kernel<BR>, smem, done, dev))) return rc;
+  rc = launch_ex(lmrs::awq_gemv4_kernel<BR>, strips * C, C, lmrs::kAwqGemv4Threads, smem, stream,
+                 tq, tx, ts, tz, y, bias, M, K, N, group, S);
+  return rc ? rc : after_launch();
+}
+
 int awq_gemv_launch(__half* y, const __half* x, const int32_t* qw, const uint32_t* qz,
                     const __half* sc, const __half* bias, int M, int K, int N, int group,
                     cudaStream_t stream, int dev) {
-  const int strips = (N + lmrs::kAwqGemvStrip - 1) / lmrs::kAwqGemvStrip;
-  const int nb_all = K / lmrs::kAwqGemvBoxRows;
-  const int C = gemv_cluster(strips, nb_all, g_tune.awq_gemv_cluster);
-  const int per_cta = (nb_all + C - 1) / C;
-  int ring = per_cta < lmrs::kAwqGemvMaxRing ? per_cta : lmrs::kAwqGemvMaxRing;
-  if (ring < 4) ring = 4;  // the drained ring also holds the 2 x 16 x 128 fp32 partials
+  const int BR = (group % 128 == 0 && g_tune.gemv_box_rows != 64) ? 128 : 64;
   const int MT = M <= 8 ? 1 : 2;
-  const int slot = lmrs::kAwqGemvBoxBytes + lmrs::kAwqGemvBoxRows * 2 * 8 * MT;
-  const int smem = 1024 + ring * slot + ring * 16;
-  CUtensorMap tq, tx;
+  const int strips = (N + lmrs::kAwqGemvStrip - 1) / lmrs::kAwqGemvStrip;
+  const int nb_all = K / BR;
+  int C;
+  if (g_tune.awq_gemv_cluster > 0) {
+    C = pow2_floor(clampi(g_tune.awq_gemv_cluster, 1, lmrs::kAwqGemvMaxCluster));
+  } else {
+    const int cps = MT == 1 ? g_tune.gemv_ctas_per_sm : 3;
+    C = pow2_floor(clampi((sm_count(dev) * cps) / strips, 1, lmrs::kAwqGemvMaxCluster));
+  }
+  while (C > 1 && C > nb_all) C /= 2;
+  const int per_cta = (nb_all + C - 1) / C;
+  int S = clampi(g_tune.awq_gemv_slots, 2, 8) & ~1;   // even: two box streams per CTA
+  if (S > ((per_cta + 1) & ~1)) S = (per_cta + 1) & ~1;
+  if (S < 2) S = 2;
+  CUtensorMap tq, tx, ts, tz;
   int rc;
   if ((rc = make_tmap(&tq, CU_TENSOR_MAP_DATA_TYPE_INT32, qw, N / 8, K, uint64_t(N / 8) * 4,
-                      lmrs::kAwqGemvStrip / 8, lmrs::kAwqGemvBoxRows, CU_TENSOR_MAP_SWIZZLE_64B)))
+                      lmrs::kAwqGemvWords, BR, CU_TENSOR_MAP_SWIZZLE_64B)))
     return rc;
-  if ((rc = make_tmap(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, x, K, M, uint64_t(K) * 2,
-                      lmrs::kAwqGemvBoxRows, 8 * MT, CU_TENSOR_MAP_SWIZZLE_128B)))
+  if ((rc = make_tmap(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, x, K, M, uint64_t(K) * 2, 64, 8 * MT,
+                      CU_TENSOR_MAP_SWIZZLE_128B)))
     return rc;
-  if (MT == 1) {
-    if ((rc = ensure_smem(lmrs::awq_gemv_kernel<1>, smem, g_smem_awq_gemv[0], dev))) return rc;
-    rc = launch_cluster(lmrs::awq_gemv_kernel<1>, strips * C, C, lmrs::kAwqGemvThreads, smem,
-                        stream, tq, tx, y, qz, sc, bias, M, K, N, group, ring);
-  } else {
-    if ((rc = ensure_smem(lmrs::awq_gemv_kernel<2>, smem, g_smem_awq_gemv[1], dev))) return rc;
-    rc = launch_cluster(lmrs::awq_gemv_kernel<2>, strips * C, C, lmrs::kAwqGemvThreads, smem,
-                        stream, tq, tx, y, qz, sc, bias, M, K, N, group, ring);
+  if ((rc = make_tmap(&ts, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, sc, N, K / group, uint64_t(N) * 2,
+                      lmrs::kAwqGemvStrip, 1, CU_TENSOR_MAP_SWIZZLE_NONE)))
+    return rc;
+  if ((rc = make_tmap(&tz, CU_TENSOR_MAP_DATA_TYPE_INT32, qz, N / 8, K / group,
+                      uint64_t(N / 8) * 4, lmrs::kAwqGemvWords, 1, CU_TENSOR_MAP_SWIZZLE_NONE)))
+    return rc;
+  if (M <= 4 && g_tune.awq_gemv4) {
+    int S4 = g_tune.awq_gemv4_slots >= 16 ? 16 : (g_tune.awq_gemv4_slots >= 8 ? 8 : 4);
+    while (S4 > 4 && per_cta <= S4 / 2) S4 /= 2;
+    if (BR == 128)
+      return awq_gemv4_launch_t<128>(tq, tx, ts, tz, y, bias, M, K, N, group, stream, dev, strips,
+                                     C, S4, g_smem_awq_gemv4[0]);
+    return awq_gemv4_launch_t<64>(tq, tx, ts, tz, y, bias, M, K, N, group, stream, dev, strips, C,
+                                  S4, g_smem_awq_gemv4[1]);
   }
-  return rc ? rc : after_launch();
+  if (MT == 1 && BR == 128)
+    return awq_gemv_launch_t<1, 128>(tq, tx, ts, tz, y, bias, M, K, N, group, stream, dev, strips,
+                                     C, S, g_smem_awq_gemv[0]);
+  if (MT == 2 && BR == 128)
+    return awq_gemv_launch_t<2, 128>(tq, tx, ts, tz, y, bias, M, K, N, group, stream, dev, strips,
+                                     C, S, g_smem_awq_gemv[1]);
+  if (MT == 1)
+    return awq_gemv_launch_t<1, 64>(tq, tx, ts, tz, y, bias, M, K, N, group, stream, dev, strips,
+                                    C, S, g_smem_awq_gemv[2]);
+  return awq_gemv_launch_t<2, 64>(tq, tx, ts, tz, y, bias, M, K, N, group, stream, dev, strips, C,
+                                  S, g_smem_awq_gemv[3]);
 }
 
 std::atomic<int> g_smem_awq_swap[4][kMaxDevices];
@@ -332,9 +417,9 @@ int awq_gemm_launch_bn(__half* y, const __half* x, const int32_t* qw, const int3
   if ((rc = ensure_smem(lmrs::awq_gemm_tc_kernel<BN>, smem, smem_done, dev))) return rc;
   const int tiles = ((N + BN - 1) / BN) * ((M + lmrs::kTcBM - 1) / lmrs::kTcBM);
   const int grid = tiles < sm_count(dev) ? tiles : sm_count(dev);
-  lmrs::awq_gemm_tc_kernel<BN><<<grid, lmrs::kAwqGemmThreads, smem, stream>>>(
-      tx, tq, ts, tz, y, bias, M, K, N, group);
-  return after_launch();
+  rc = launch_ex(lmrs::awq_gemm_tc_kernel<BN>, grid, 0, lmrs::kAwqGemmThreads, smem, stream, tx, tq,
+                 ts, tz, y, bias, M, K, N, group);
+  return rc ? rc : after_launch();
 }
 
 int awq_gemm_launch(__half* y, const __half* x, const int32_t* qw, const int32_t* qz,
@@ -351,21 +436,22 @@ int awq_gemm_launch(__half* y, const __half* x, const int32_t* qw, const int32_t
 int fp8_quant_launch(uint8_t* q, float* s, const void* x, int rows, int K, int dt,
                      cudaStream_t stream) {
   if (rows == 0) return LMRS_OK;
+  int rc = LMRS_OK;
   switch (dt) {
     case LMRS_DTYPE_BF16:
-      lmrs::fp8_quant_rows_kernel<0><<<rows, lmrs::kQuantThreads, 0, stream>>>(
-          q, s, static_cast<const __nv_bfloat16*>(x), K);
+      rc = launch_ex(lmrs::fp8_quant_rows_kernel<0>, rows, 0, lmrs::kQuantThreads, 0, stream, q, s,
+                     static_cast<const __nv_bfloat16*>(x), K);
       break;
     case LMRS_DTYPE_F16:
-      lmrs::fp8_quant_rows_kernel<1><<<rows, lmrs::kQuantThreads, 0, stream>>>(
-          q, s, static_cast<const __half*>(x), K);
+      rc = launch_ex(lmrs::fp8_quant_rows_kernel<1>, rows, 0, lmrs::kQuantThreads, 0, stream, q, s,
+                     static_cast<const __half*>(x), K);
       break;
     default:
-      lmrs::fp8_quant_rows_kernel<2><<<rows, lmrs::kQuantThreads, 0, stream>>>(
-          q, s, static_cast<const float*>(x), K);
+      rc = launch_ex(lmrs::fp8_quant_rows_kernel<2>, rows, 0, lmrs::kQuantThreads, 0, stream, q, s,
+                     static_cast<const float*>(x), K);
       break;
   }
-  return after_launch();
+  return rc ? rc : after_launch();
 }
 
 int fp8_gemv_launch(__nv_bfloat16* y, const uint8_t* xq, const float* sx, const uint8_t* wq,
@@ -423,9 +509,9 @@ int fp8_gemm_launch_bn(__nv_bfloat16* y, const uint8_t* xq, const float* sx, con
   if ((rc = ensure_smem(lmrs::fp8_gemm_tc_kernel<BN>, smem, smem_done, dev))) return rc;
   const int tiles = ((N + BN - 1) / BN) * ((M + lmrs::kTcBM - 1) / lmrs::kTcBM);
   const int grid = tiles < sm_count(dev) ? tiles : sm_count(dev);
-  lmrs::fp8_gemm_tc_kernel<BN><<<grid, lmrs::kF8Threads, smem, stream>>>(ta, tb, y, sx, sw, bias,
-                                                                          M, K, N);
-  return after_launch();
+  rc = launch_ex(lmrs::fp8_gemm_tc_kernel<BN>, grid, 0, lmrs::kF8Threads, smem, stream, ta, tb, y,
+                 sx, sw, bias, M, K, N);
+  return rc ? rc : after_launch();
 }
 
 int fp8_gemm_launch(__nv_bfloat16* y, const uint8_t* xq, const float* sx, const uint8_t* wq,
@@ -498,6 +584,11 @@ int lmrs_set_tuning(const char* key, int value) {
   else if (!strcmp(key, "fp8_gemv_max_m")) g_tune.fp8_gemv_max_m = value;
   else if (!strcmp(key, "gemv_ctas_per_sm")) g_tune.gemv_ctas_per_sm = value;
   else if (!strcmp(key, "awq_gemv_cluster")) g_tune.awq_gemv_cluster = value;
+  else if (!strcmp(key, "pdl")) g_tune.pdl = value ? 1 : 0;
+  else if (!strcmp(key, "awq_gemv_slots")) g_tune.awq_gemv_slots = value;
+  else if (!strcmp(key, "awq_gemv4")) g_tune.awq_gemv4 = value ? 1 : 0;
+  else if (!strcmp(key, "gemv_box_rows")) g_tune.gemv_box_rows = value;
+  else if (!strcmp(key, "awq_gemv4_slots")) g_tune.awq_gemv4_slots = value;
   else if (!strcmp(key, "fp8_gemv_cluster")) g_tune.fp8_gemv_cluster = value;
   else return LMRS_ERR_SHAPE;
   return LMRS_OK;

@@ -271,6 +271,64 @@ __device__ __forceinline__ void cluster_sync_all() {
                    : "memory");
 }
 
+// Split cluster barrier: arrive early (after mbarrier init + fence_mbar_init),
+// wait just before the first access to a peer's shared memory.
+// (Non-.aligned forms: callers may reach them from divergent code.)
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait_acquire() {
+  asm volatile("barrier.cluster.wait.acquire;" ::: "memory");
+}
+
+__device__ __forceinline__ void st_cluster_f32(uint32_t cluster_addr, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(cluster_addr), "f"(v) : "memory");
+}
+
+// Asynchronous 16-byte store into a peer CTA's shared memory whose completion
+// is counted (in bytes) on an mbarrier in that CTA: no release fence needed,
+// the receiver's wait on the mbarrier makes the data visible.
+__device__ __forceinline__ void st_async_v4(uint32_t cluster_addr, float4 v, uint32_t cluster_bar) {
+  asm volatile(
+      "st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];"
+      ::"r"(cluster_addr), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w), "r"(cluster_bar)
+      : "memory");
+}
+
+// Bounded wait that also acquires at cluster scope (data written into this
+// CTA's shared memory by peer CTAs before their release-arrive).
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, uint32_t site) {
+  const long long t0 = clock64();
+  while (true) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(1000000u)
+        : "memory");
+    if (ok) return true;
+    if (clock64() - t0 > kWaitLimitCycles) {
+      atomicOr(&g_device_error, site);
+      return false;
+    }
+  }
+}
+
+// ------------------------------------------- programmatic dependent launch
+// A kernel launched with programmatic stream serialisation may start while
+// the previous kernel in the stream is still running.  pdl_trigger lets the
+// next kernel start launching; pdl_wait blocks until the previous kernel has
+// completed and its writes are visible.  Both are no-ops without the launch
+// attribute.  Every kernel here reads its activations and writes any global
+// memory only after pdl_wait; weights (never written by a predecessor) may be
+// prefetched before it.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ------------------------------------------------------- UMMA descriptors
 // Shared-memory matrix descriptor (sm_100 format):
 //   [0,14) start address >> 4, [16,30) leading byte offset >> 4,

@@ -108,6 +108,8 @@ __global__ void __launch_bounds__(kAwqGemmThreads, 1)
                        const __grid_constant__ CUtensorMap tm_s,
                        const __grid_constant__ CUtensorMap tm_z, __half* __restrict__ y,
                        const __half* __restrict__ bias, int M, int K, int N, int group) {
+  pdl_wait();     // activations are the previous kernel's output
+  pdl_trigger();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   uint8_t* sA = smem;
@@ -317,6 +319,8 @@ __global__ void __launch_bounds__(kF8Threads, 1)
                        const __grid_constant__ CUtensorMap tm_b, __nv_bfloat16* __restrict__ y,
                        const float* __restrict__ sx, const float* __restrict__ sw,
                        const __nv_bfloat16* __restrict__ bias, int M, int K, int N) {
+  pdl_wait();     // activations are the previous kernel's output
+  pdl_trigger();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   uint8_t* sA = smem;

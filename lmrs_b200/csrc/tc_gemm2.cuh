@@ -57,6 +57,8 @@ __global__ void __launch_bounds__(kP2Threads, 1)
                         const __grid_constant__ CUtensorMap tm_s,
                         const __grid_constant__ CUtensorMap tm_z, __half* __restrict__ y,
                         const __half* __restrict__ bias, int M, int K, int N, int group) {
+  pdl_wait();     // activations are the previous kernel's output
+  pdl_trigger();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   uint8_t* sT = smem;                        // [x rows | packed | scales | zeros] per stage

@@ -1,0 +1,252 @@
+"""Decode-step harness for the quantized linears (BASELINE configs 3 and 4).
+
+A Llama-shaped decoder (the reference's qwen3 block with use_qk_norm = false,
+crates/model/src/layers/block.rs:118-130) whose q/k/v/o/gate/up/down
+projections run on lmrs_b200's AWQ W4A16 or FP8 W8A8 linears.
+- q/k/v and gate/up are each merged into one column-parallel projection (one
+  launch instead of three or two).
+- o and down are row-parallel and are followed by a sum all-reduce when
+  tensor parallelism is on.
+
+The support ops (RMSNorm, RoPE, decode attention over a preallocated KV cache,
+SiLU * up, the bf16 LM head) are plain torch: they are not the hot path this
+package implements.  Weights are random (seeded), the KV cache is pre-filled
+with random values to the configured context, and one decode step feeds one
+token per sequence at position ctx - 1 (the step is replayed unchanged, which
+keeps it CUDA-graph friendly).
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+from typing import Optional
+
+import torch
+import torch.nn.functional as F
+
+from . import ops
+
+
+@dataclass(frozen=True)
+class DecoderConfig:
+    layers: int
+    hidden: int
+    heads: int
+    kv_heads: int
+    head_dim: int
+    intermediate: int
+    vocab: int
+    quant: str            # "awq" (W4A16, fp16 activations) or "fp8" (W8A8, bf16 activations)
+    group: int = 128
+    rope_theta: float = 500000.0
+    eps: float = 1e-5
+
+    def projections(self, world: int = 1):
+        """(K, N) of one rank's qkv, o, gate_up, down projections."""
+        d, H = self.head_dim, self.hidden
+        hq, hkv, inter = self.heads // world, self.kv_heads // world, self.intermediate // world
+        return [(H, (hq + 2 * hkv) * d), (hq * d, H), (H, 2 * inter), (inter, H)]
+
+    def linear_bytes(self, world: int = 1) -> int:
+        """One rank's quantized projection bytes over all layers (AWQ: packed
+        weights + zeros + fp16 scales; FP8: e4m3 weights + fp32 channel scales)."""
+        n = 0
+        for K, N in self.projections(world):
+            if self.quant == "awq":
+                g = self.group
+                n += K * N // 2 + (K // g) * (N // 8) * 4 + (K // g) * N * 2
+            else:
+                n += N * K + 4 * N
+        return n * self.layers
+
+
+LLAMA3_8B_AWQ = DecoderConfig(32, 4096, 32, 8, 128, 14336, 128256, "awq")
+LLAMA3_70B_FP8 = DecoderConfig(80, 8192, 64, 8, 128, 28672, 128256, "fp8")
+
+
+def _awq_random(K: int, N: int, group: int, gen: torch.Generator, device) -> dict:
+    """Random AWQ tensors with the config-0 distributions: uniform nibbles for q
+    and z (uniform 32-bit words), scales U[0.001, 0.02] fp16."""
+    qw = torch.randint(-2 ** 31, 2 ** 31 - 1, (K, N // 8), dtype=torch.int32, generator=gen,
+                       device=device)
+    qz = torch.randint(-2 ** 31, 2 ** 31 - 1, (K // group, N // 8), dtype=torch.int32,
+                       generator=gen, device=device)
+    sc = (torch.rand((K // group, N), generator=gen, device=device) * 0.019 + 0.001).half()
+    return dict(qweight=qw, qzeros=qz, scales=sc)
+
+
+def _fp8_random(K: int, N: int, gen: torch.Generator, device) -> dict:
+    """W ~ N(0, 0.02) bf16 [N, K], quantised per output channel to e4m3 (on the GPU)."""
+    w = (torch.randn((N, K), generator=gen, device=device) * 0.02).bfloat16()
+    wq, sw = ops.quantize_fp8_weight(w)
+    del w
+    return dict(weight_q=wq, weight_scale=sw)
+
+
+class QuantDecoder:
+    """One tensor-parallel rank of the decoder (world = 1 for a single GPU)."""
+
+    def __init__(self, cfg: DecoderConfig, batch: int, ctx: int, device, rank: int = 0,
+                 world: int = 1, seed: int = 0, group=None):
+        if cfg.heads % world or cfg.intermediate % world or cfg.kv_heads % world:
+            raise ValueError(f"tensor parallelism {world} does not divide heads / kv heads / intermediate")
+        if cfg.vocab % world:
+            raise ValueError(f"vocab {cfg.vocab} not divisible by {world}")
+        self.cfg, self.batch, self.ctx = cfg, batch, ctx
+        self.device = torch.device(device)
+        self.rank, self.world, self.pg = rank, world, group
+        self.hq, self.hkv = cfg.heads // world, cfg.kv_heads // world
+        self.inter = cfg.intermediate // world
+        self.vocab_local = cfg.vocab // world
+        self.act = torch.float16 if cfg.quant == "awq" else torch.bfloat16
+        d, H = cfg.head_dim, cfg.hidden
+        # shard-local weights from a per-rank stream; replicated tensors (embedding,
+        # norms) from one stream shared by all ranks
+        gen = torch.Generator(device=self.device).manual_seed(seed * 1000 + rank)
+        rep = torch.Generator(device=self.device).manual_seed(seed * 1000 + 999)
+
+        def lin(K, N):
+            if cfg.quant == "awq":
+                t = _awq_random(K, N, cfg.group, gen, self.device)
+                return ops.QuantLinearOp.awq(ops.LinearConfig(K, N), t["qweight"], t["qzeros"],
+                                             t["scales"], None, ops.AwqConfig(cfg.group))
+            t = _fp8_random(K, N, gen, self.device)
+            return ops.QuantLinearOp.fp8(ops.LinearConfig(K, N), t["weight_q"], t["weight_scale"])
+
+        self.embed = (torch.randn((cfg.vocab, H), generator=rep, device=self.device) * 0.02).to(self.act)
+        self.layers = []
+        shapes = cfg.projections(world)
+        for _ in range(cfg.layers):
+            self.layers.append(dict(
+                in_norm=(1.0 + 0.02 * torch.randn(H, generator=rep, device=self.device)).to(self.act),
+                post_norm=(1.0 + 0.02 * torch.randn(H, generator=rep, device=self.device)).to(self.act),
+                qkv=lin(*shapes[0]),        # column-parallel, q/k/v merged
+                o=lin(*shapes[1]),          # row-parallel
+                gate_up=lin(*shapes[2]),    # column-parallel, gate/up merged
+                down=lin(*shapes[3]),       # row-parallel
+            ))
+        self.final_norm = (1.0 + 0.02 * torch.randn(H, generator=rep, device=self.device)).to(self.act)
+        self.lm_head = (torch.randn((self.vocab_local, H), generator=gen, device=self.device)
+                        * 0.02).to(self.act)
+        pos = ctx - 1
+        inv = 1.0 / (cfg.rope_theta ** (torch.arange(0, d, 2, device=self.device, dtype=torch.float32) / d))
+        ang = pos * inv
+        self.cos = torch.cat([ang.cos(), ang.cos()]).to(self.act)
+        self.sin = torch.cat([ang.sin(), ang.sin()]).to(self.act)
+        self.kv = None
+        self.set_batch(batch, seed)
+
+    @staticmethod
+    def kv_bytes(cfg: DecoderConfig, batch: int, ctx: int, world: int = 1) -> int:
+        """Bytes of one rank's KV cache ([layers, 2, batch, kv_heads / world, ctx, head_dim])."""
+        return cfg.layers * 2 * batch * (cfg.kv_heads // world) * ctx * cfg.head_dim * 2
+
+    def set_batch(self, batch: int, seed: int = 0):
+        """(Re)allocate the KV cache, pre-filled with random values to ctx, and
+        draw random token ids for `batch` sequences; the weights are kept."""
+        cfg = self.cfg
+        self.kv = None
+        torch.cuda.empty_cache()
+        self.batch = batch
+        gen = torch.Generator(device=self.device).manual_seed(seed * 1000 + self.rank + 7)
+        kv_shape = (cfg.layers, 2, batch, self.hkv, self.ctx, cfg.head_dim)
+        self.kv = torch.empty(kv_shape, dtype=self.act, device=self.device)
+        for li in range(cfg.layers):  # per layer, in the activation dtype: no fp32 temporaries
+            self.kv[li].normal_(0.0, 0.5, generator=gen)
+        # every rank draws the same ids (replicated embedding)
+        tg = torch.Generator(device=self.device).manual_seed(seed * 1000 + 11)
+        self.tokens = torch.randint(0, cfg.vocab, (batch,), generator=tg, device=self.device)
+
+    # ---------------------------------------------------------------- pieces
+    def _rms(self, x, w):
+        xf = x.float()
+        return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + self.cfg.eps)).to(self.act) * w
+
+    def _rope(self, x):  # x [B, heads, d] — rotate-half, as the reference's pos_embed kernel
+        half = x.shape[-1] // 2
+        rot = torch.cat([-x[..., half:], x[..., :half]], dim=-1)
+        return x * self.cos + rot * self.sin
+
+    def _all_reduce(self, y):
+        if self.world > 1:
+            torch.distributed.all_reduce(y, group=self.pg)
+        return y
+
+    def step(self, tokens: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """One decode step: returns the next token of every sequence."""
+        return self._argmax(self.logits(tokens))
+
+    def logits(self, tokens: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """One decode step up to this rank's vocabulary shard of the logits."""
+        cfg, d, B = self.cfg, self.cfg.head_dim, self.batch
+        tok = self.tokens if tokens is None else tokens
+        h = self.embed[tok]                                    # [B, H]
+        pos = self.ctx - 1
+        for li, L in enumerate(self.layers):
+            r = self._rms(h, L["in_norm"])
+            qkv = L["qkv"].forward(r)                          # [B, (hq + 2 hkv) d]
+            q = qkv[:, : self.hq * d].view(B, self.hq, d)
+            k = qkv[:, self.hq * d: (self.hq + self.hkv) * d].view(B, self.hkv, d)
+            v = qkv[:, (self.hq + self.hkv) * d:].view(B, self.hkv, d)
+            q, k = self._rope(q), self._rope(k)
+            kc, vc = self.kv[li, 0], self.kv[li, 1]            # [B, hkv, ctx, d]
+            kc[:, :, pos] = k
+            vc[:, :, pos] = v
+            a = F.scaled_dot_product_attention(q.unsqueeze(2), kc, vc, enable_gqa=True)
+            a = a.reshape(B, self.hq * d).contiguous()
+            h = h + self._all_reduce(L["o"].forward(a))
+            r = self._rms(h, L["post_norm"])
+            gu = L["gate_up"].forward(r)
+            m = (F.silu(gu[:, : self.inter]) * gu[:, self.inter:]).contiguous()
+            h = h + self._all_reduce(L["down"].forward(m))
+        h = self._rms(h, self.final_norm)
+        return h @ self.lm_head.t()                            # [B, vocab / world]
+
+    def _argmax(self, logits):
+        val, idx = logits.float().max(dim=-1)
+        if self.world > 1:
+            vals = [torch.empty_like(val) for _ in range(self.world)]
+            idxs = [torch.empty_like(idx) for _ in range(self.world)]
+            torch.distributed.all_gather(vals, val, group=self.pg)
+            torch.distributed.all_gather(idxs, idx, group=self.pg)
+            allv, alli = torch.stack(vals), torch.stack(idxs)   # [world, B]
+            best = allv.argmax(dim=0)
+            idx = alli.gather(0, best.unsqueeze(0)).squeeze(0) + best * self.vocab_local
+        return idx
+
+    def linears_only(self):
+        """The step's quantized projections alone (same shapes and order), for the
+        linear-layer share of the step time."""
+        cfg, d, B = self.cfg, self.cfg.head_dim, self.batch
+        x = torch.zeros(B, cfg.hidden, dtype=self.act, device=self.device)
+        a = torch.zeros(B, self.hq * d, dtype=self.act, device=self.device)
+        m = torch.zeros(B, self.inter, dtype=self.act, device=self.device)
+        for L in self.layers:
+            L["qkv"].forward(x)
+            L["o"].forward(a)
+            L["gate_up"].forward(x)
+            L["down"].forward(m)
+
+    def weight_bytes(self) -> int:
+        n = 0
+        for L in self.layers:
+            for key in ("qkv", "o", "gate_up", "down"):
+                for t in L[key].tensors.values():
+                    n += t.numel() * t.element_size()
+        return n
+
+
+def graph_step(dec: QuantDecoder, fn=None, warmup: int = 3):
+    """Capture one decode step (or `fn`) into a CUDA graph after eager warm-ups."""
+    fn = fn or dec.step
+    s = torch.cuda.Stream(dec.device)
+    s.wait_stream(torch.cuda.current_stream(dec.device))
+    with torch.cuda.stream(s):
+        for _ in range(warmup):
+            fn()
+    torch.cuda.current_stream(dec.device).wait_stream(s)
+    torch.cuda.synchronize(dec.device)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        out = fn()
+    return g, out

@@ -191,18 +191,28 @@ def test_status_codes(cuda):
 
 
 @pytest.mark.parametrize("knob,value,Ms", [("awq_gemm_pair", 1, (129, 300, 512)),
-                                           ("awq_gemv_max_m", 16, (9, 12, 16)),
+                                           ("awq_gemv_max_m", 8, (9, 12, 16)),
                                            ("awq_swap_max_m", 128, (65, 100, 128)),
                                            ("gemm_bn", 0, (100, 300, 512)),
-                                           ("gemm_bn", 224, (100, 300, 512))])
+                                           ("gemm_bn", 224, (100, 300, 512)),
+                                           ("awq_gemv4", 0, (1, 3, 4)),
+                                           ("gemv_box_rows", 64, (1, 4, 8, 16)),
+                                           ("awq_gemv_cluster", 2, (1, 5, 16)),
+                                           ("awq_gemv_cluster", 8, (1, 5, 16)),
+                                           ("awq_gemv_slots", 8, (5, 16)),
+                                           ("awq_gemv4_slots", 8, (1, 4)),
+                                           ("pdl", 0, (1, 8, 40, 300))])
 def test_opt_in_paths(cuda, knob, value, Ms):
-    """Kernels the default dispatch does not pick for these M (CTA-pair GEMM,
-    the two-token-tile GEMV, swap-AB up to 128 tokens) stay correct and
-    deterministic when selected."""
+    """Kernels and launch shapes the default dispatch does not pick for these M
+    (CTA-pair GEMM, swap-AB below 17 or above 64 tokens, the general GEMV for
+    M <= 4, 64-row boxes, other cluster sizes and ring depths, launches without
+    programmatic dependent launch) stay correct and deterministic when selected."""
     import torch
     import lmrs_b200 as L
     from lmrs_b200 import _lib
-    defaults = {"awq_gemm_pair": 0, "awq_gemv_max_m": 8, "awq_swap_max_m": 64, "gemm_bn": 256}
+    defaults = {"awq_gemm_pair": 0, "awq_gemv_max_m": 16, "awq_swap_max_m": 64, "gemm_bn": 256,
+                "awq_gemv4": 1, "gemv_box_rows": 128, "awq_gemv_cluster": 0, "awq_gemv_slots": 4,
+                "awq_gemv4_slots": 4, "pdl": 1}
     K, N, g = 1024, 1280, 128
     try:
         L.set_tuning(knob, value)

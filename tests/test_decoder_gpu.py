@@ -1,0 +1,120 @@
+"""Decode-step harness (configs 3/4 shape, shrunk): the quantized decoder's
+logits against an fp32 torch re-computation that uses the dequantised weights
+(AWQ via lmrs_awq_dequant, FP8 as e4m3 * scale) and the same support ops."""
+import math
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+from lmrs_b200 import decoder as D
+from lmrs_b200 import ops
+
+pytestmark = pytest.mark.gpu
+
+TINY = dict(layers=2, hidden=512, heads=4, kv_heads=2, head_dim=128, intermediate=1024, vocab=1000)
+
+
+def _dense(lin):
+    """fp32 [K, N] weight of a QuantLinearOp."""
+    t = lin.tensors
+    if lin.kind == "awq":
+        return ops.awq_dequant(t["qweight"], t["qzeros"], t["scales"], lin.awq_config.group_size).float()
+    w = t["weight_q"].view(torch.float8_e4m3fn).float() * t["weight_scale"][:, None]
+    return w.t()
+
+
+def _fake_quant_rows(x):
+    """Per-token e4m3 round trip (s = absmax / 448), as the W8A8 path applies to
+    every activation row before its GEMM."""
+    s = x.abs().amax(-1, keepdim=True) / 448.0
+    q = torch.where(s > 0, x / s, torch.zeros_like(x)).to(torch.float8_e4m3fn).float()
+    return q * s
+
+
+def _reference_logits(dec):
+    cfg, d, B = dec.cfg, dec.cfg.head_dim, dec.batch
+
+    def lin(x, op):
+        if op.kind == "fp8":
+            x = _fake_quant_rows(x)
+        return x @ _dense(op)
+    pos = dec.ctx - 1
+    kv = dec.kv.float().clone()
+    cos, sin = dec.cos.float(), dec.sin.float()
+
+    def rms(x, w):
+        return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + cfg.eps) * w.float()
+
+    def rope(x):
+        half = x.shape[-1] // 2
+        return x * cos + torch.cat([-x[..., half:], x[..., :half]], -1) * sin
+
+    h = dec.embed[dec.tokens].float()
+    for li, L in enumerate(dec.layers):
+        r = rms(h, L["in_norm"])
+        qkv = lin(r, L["qkv"])
+        q = rope(qkv[:, : dec.hq * d].view(B, dec.hq, d))
+        k = rope(qkv[:, dec.hq * d: (dec.hq + dec.hkv) * d].view(B, dec.hkv, d))
+        v = qkv[:, (dec.hq + dec.hkv) * d:].view(B, dec.hkv, d)
+        kv[li, 0][:, :, pos] = k
+        kv[li, 1][:, :, pos] = v
+        a = F.scaled_dot_product_attention(q.unsqueeze(2), kv[li, 0], kv[li, 1], enable_gqa=True)
+        h = h + lin(a.reshape(B, -1), L["o"])
+        r = rms(h, L["post_norm"])
+        gu = lin(r, L["gate_up"])
+        h = h + lin(F.silu(gu[:, : dec.inter]) * gu[:, dec.inter:], L["down"])
+    return rms(h, dec.final_norm) @ dec.lm_head.float().t()
+
+
+@pytest.mark.parametrize("quant,batch", [("awq", 1), ("awq", 5), ("awq", 40), ("fp8", 1), ("fp8", 40)])
+def test_decoder_step_matches_fp32_reference(cuda, quant, batch):
+    """Whole step vs an fp32 forward.  AWQ: only fp16 rounding of the activations
+    between ops separates the two.  FP8: the per-token e4m3 round trip of a bf16
+    activation and of its fp32 counterpart differ by one e4m3 step for the ~1/16
+    of elements that sit near a rounding boundary, a few per cent per linear,
+    compounded over the layers, so the end-to-end bound there only catches
+    layout errors; each FP8 linear is held to 1e-2 by the teacher-forced test."""
+    cfg = D.DecoderConfig(quant=quant, **TINY)
+    dec = D.QuantDecoder(cfg, batch=batch, ctx=64, device=cuda, seed=3)
+    ref = _reference_logits(dec)
+    got = dec.logits().float()
+    err = ((got - ref).abs().max() / ref.abs().max()).item()
+    assert err < (2e-2 if quant == "awq" else 1.5e-1), err
+
+
+@pytest.mark.parametrize("quant,batch", [("awq", 1), ("awq", 16), ("fp8", 1), ("fp8", 40)])
+def test_decoder_linears_teacher_forced(cuda, quant, batch, monkeypatch):
+    """Every quantized projection of a decode step, on the exact activations the
+    step fed it, against fp32 on the dequantised weights (FP8: with the same
+    per-token e4m3 round trip of the input): max relative error 1e-2."""
+    cfg = D.DecoderConfig(quant=quant, **TINY)
+    dec = D.QuantDecoder(cfg, batch=batch, ctx=64, device=cuda, seed=4)
+    calls = []
+    orig = ops.QuantLinearOp.forward
+
+    def spy(self, x):
+        y = orig(self, x)
+        calls.append((self, x.clone(), y.clone()))
+        return y
+
+    monkeypatch.setattr(ops.QuantLinearOp, "forward", spy)
+    dec.logits()
+    assert len(calls) == 4 * cfg.layers
+    for op, x, y in calls:
+        xf = x.float()
+        if op.kind == "fp8":
+            xf = _fake_quant_rows(xf)
+        ref = xf.double() @ _dense(op).double()  # float64: no TF32 or reduced-precision GEMM
+        err = ((y.double() - ref).abs().max() / ref.abs().max()).item()
+        assert err < (5e-3 if op.kind == "awq" else 1e-2), (op.kind, tuple(x.shape), err)
+
+
+def test_decoder_graph_replay_matches_eager(cuda):
+    cfg = D.DecoderConfig(quant="awq", **TINY)
+    dec = D.QuantDecoder(cfg, batch=4, ctx=32, device=cuda, seed=5)
+    eager = dec.logits().clone()
+    g, out = D.graph_step(dec, dec.logits)
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(out, eager)
