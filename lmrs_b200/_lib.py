@@ -1,4 +1,4 @@
-"""ctypes binding of the C-ABI in ``include/lmrs_quant.h``.
+"""ctypes binding of the C-ABI in ``include/lmrs_quant.h`` and ``include/lmrs_decode.h``.
 
 This is the Python counterpart of the reference's raw FFI declarations
 (crates/kernels/src/tensor_ops.rs:8-22, crates/kernels/src/raw.rs:53-147): one
@@ -36,7 +36,9 @@ P = ctypes.c_void_p
 I = ctypes.c_int
 SZ = ctypes.c_size_t
 
-# name -> (restype, argtypes); mirrors include/lmrs_quant.h exactly
+F = ctypes.c_float
+
+# name -> (restype, argtypes); mirrors include/lmrs_quant.h and include/lmrs_decode.h exactly
 SIGNATURES = {
     "lmrs_version": (I, []),
     "lmrs_status_string": (ctypes.c_char_p, [I]),
@@ -52,6 +54,14 @@ SIGNATURES = {
     "lmrs_fp8_linear": (I, [P, P, P, P, P, I, I, I, P, SZ, P]),
     "lmrs_fp8_linear_prequant": (I, [P, P, P, P, P, P, I, I, I, P]),
     "lmrs_fp8_linear_noalloc": (I, [P, P, P, P, P, I, I, I, P]),
+    # lmrs_decode.h
+    "lmrs_rmsnorm": (I, [P, P, P, P, I, I, F, I, P]),
+    "lmrs_rmsnorm_fp8": (I, [P, P, P, P, P, I, I, F, I, P]),
+    "lmrs_silu_mul": (I, [P, P, I, I, I, P]),
+    "lmrs_silu_mul_fp8": (I, [P, P, P, I, I, I, P]),
+    "lmrs_rope_kv_write": (I, [P, P, P, P, P, P, P, P, I, I, I, I, I, I, I, P]),
+    "lmrs_paged_attention_workspace_bytes": (SZ, [I, I, I, I]),
+    "lmrs_paged_attention_decode": (I, [P, P, P, P, P, P, I, I, I, I, I, I, I, F, I, I, P, SZ, P]),
 }
 
 

@@ -20,7 +20,7 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
 def sources():
-    return sorted((PKG / "csrc").glob("*.cu*")) + [ROOT / "include" / "lmrs_quant.h"]
+    return sorted((PKG / "csrc").glob("*.cu*")) + sorted((ROOT / "include").glob("*.h"))
 
 
 def stale() -> bool:

@@ -1,0 +1,240 @@
+// decode_capi.cuh — the C-ABI of include/lmrs_decode.h.  Included at the end of
+// lmrs_capi.cu (one translation unit: shares its launch helpers and checks).
+#pragma once
+#include "decode_ops.cuh"
+#include "lmrs_decode.h"
+
+namespace {
+
+bool act_dtype(int dt) { return dt == LMRS_DTYPE_BF16 || dt == LMRS_DTYPE_F16; }
+
+template <typename T, bool FP8>
+int rmsnorm_launch(void* out, uint8_t* q, float* s, void* resid, const void* delta, const void* w,
+                   int rows, int H, float eps, cudaStream_t st) {
+  int rc = launch_ex(lmrs::rmsnorm_kernel<T, FP8>, rows, 0, lmrs::kNormThreads, 0, st,
+                     static_cast<T*>(out), q, s, static_cast<T*>(resid),
+                     static_cast<const T*>(delta), static_cast<const T*>(w), H, eps);
+  return rc ? rc : after_launch();
+}
+
+template <typename T, bool FP8>
+int silu_launch(void* out, uint8_t* q, float* s, const void* gu, int rows, int inter,
+                cudaStream_t st) {
+  int rc = launch_ex(lmrs::silu_mul_kernel<T, FP8>, rows, 0, lmrs::kNormThreads, 0, st,
+                     static_cast<T*>(out), q, s, static_cast<const T*>(gu), inter);
+  return rc ? rc : after_launch();
+}
+
+// context split of the decode attention: ~2 CTAs per SM, whole 64-position tiles
+void attn_split(int seqs, int hkv, int max_ctx, int sms, int* splits, int* span) {
+  const int tiles = max_ctx > 0 ? (max_ctx + lmrs::kAttnTile - 1) / lmrs::kAttnTile : 1;  // 64-pos units
+  const int work = seqs * hkv > 0 ? seqs * hkv : 1;
+  int s = clampi((g_tune.attn_ctas_per_sm * sms + work - 1) / work, 1, tiles);
+  const int per = (tiles + s - 1) / s;
+  *span = per * lmrs::kAttnTile;
+  *splits = (tiles + per - 1) / per;
+}
+
+std::atomic<int> g_smem_attn[2][3][kMaxDevices];
+// per warp: NS stages of 16 K rows + 16 V rows; at least the end-of-kernel merge buffer
+constexpr int attn_smem(int ns) {
+  return 4 * ns * 2 * 16 * lmrs::kAttnRowBytes > 4 * 16 * (lmrs::kAttnD + 2) * 4
+             ? 4 * ns * 2 * 16 * lmrs::kAttnRowBytes
+             : 4 * 16 * (lmrs::kAttnD + 2) * 4;
+}
+
+template <typename T, int NS>
+int attn_launch(void* out, void* ws, const void* q, const void* kc, const void* vc,
+                const int32_t* tables, const int32_t* lens, int seqs, int heads, int hkv,
+                int bs, int maxb, int splits, int span, float scale, int map, cudaStream_t st,
+                int dev, std::atomic<int>* done) {
+  int rc;
+  if ((rc = ensure_smem(lmrs::decode_attn_kernel<T, NS>, attn_smem(NS), done, dev))) return rc;
+  const float scale_log2 = scale * 1.4426950408889634f;
+  // grid (seqs * hkv, splits): launch_ex is 1-D, so pack the split into y here
+  cudaLaunchConfig_t c = {};
+  c.gridDim = dim3(seqs * hkv, splits, 1);
+  c.blockDim = dim3(lmrs::kAttnThreads, 1, 1);
+  c.dynamicSmemBytes = attn_smem(NS);
+  c.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  c.attrs = attr;
+  c.numAttrs = g_tune.pdl ? 1 : 0;
+  cudaError_t e = cudaLaunchKernelEx(&c, lmrs::decode_attn_kernel<T, NS>, static_cast<T*>(out),
+                                     static_cast<float*>(ws), static_cast<const T*>(q),
+                                     static_cast<const T*>(kc), static_cast<const T*>(vc), tables,
+                                     lens, heads, hkv, bs, maxb, span, scale_log2, map);
+  if (e != cudaSuccess) return record(e);
+  if ((rc = after_launch())) return rc;
+  if (splits > 1) {
+    rc = launch_ex(lmrs::decode_attn_combine_kernel<T>, seqs * heads, 0, lmrs::kAttnD, 0, st,
+                   static_cast<T*>(out), static_cast<const float*>(ws), splits);
+    if (rc) return rc;
+    return after_launch();
+  }
+  return LMRS_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+LMRS_API int lmrs_rmsnorm(void* out, void* residual, const void* delta_or_null, const void* weight,
+                          int rows, int H, float eps, int dtype, lmrs_stream_t stream) {
+  if (!act_dtype(dtype)) return LMRS_ERR_DTYPE;
+  if (rows < 0 || H <= 0 || H % 8) return LMRS_ERR_SHAPE;
+  if (rows == 0) return LMRS_OK;
+  if (!out || !residual || !weight) return LMRS_ERR_NULL;
+  if (!aligned16(out) || !aligned16(residual) || !aligned16(weight) ||
+      (delta_or_null && !aligned16(delta_or_null)))
+    return LMRS_ERR_ALIGN;
+  int rc = check_device(nullptr);
+  if (rc) return rc;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  return dtype == LMRS_DTYPE_BF16
+             ? rmsnorm_launch<__nv_bfloat16, false>(out, nullptr, nullptr, residual, delta_or_null,
+                                                    weight, rows, H, eps, st)
+             : rmsnorm_launch<__half, false>(out, nullptr, nullptr, residual, delta_or_null,
+                                             weight, rows, H, eps, st);
+}
+
+LMRS_API int lmrs_rmsnorm_fp8(uint8_t* q_out, float* scale_out, void* residual,
+                              const void* delta_or_null, const void* weight, int rows, int H,
+                              float eps, int dtype, lmrs_stream_t stream) {
+  if (!act_dtype(dtype)) return LMRS_ERR_DTYPE;
+  if (rows < 0 || H <= 0 || H % 8) return LMRS_ERR_SHAPE;
+  if (rows == 0) return LMRS_OK;
+  if (!q_out || !scale_out || !residual || !weight) return LMRS_ERR_NULL;
+  if (!aligned16(q_out) || !aligned16(residual) || !aligned16(weight) ||
+      (delta_or_null && !aligned16(delta_or_null)))
+    return LMRS_ERR_ALIGN;
+  int rc = check_device(nullptr);
+  if (rc) return rc;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  return dtype == LMRS_DTYPE_BF16
+             ? rmsnorm_launch<__nv_bfloat16, true>(nullptr, q_out, scale_out, residual,
+                                                   delta_or_null, weight, rows, H, eps, st)
+             : rmsnorm_launch<__half, true>(nullptr, q_out, scale_out, residual, delta_or_null,
+                                            weight, rows, H, eps, st);
+}
+
+LMRS_API int lmrs_silu_mul(void* out, const void* gate_up, int rows, int inter, int dtype,
+                           lmrs_stream_t stream) {
+  if (!act_dtype(dtype)) return LMRS_ERR_DTYPE;
+  if (rows < 0 || inter <= 0 || inter % 8) return LMRS_ERR_SHAPE;
+  if (rows == 0) return LMRS_OK;
+  if (!out || !gate_up) return LMRS_ERR_NULL;
+  if (!aligned16(out) || !aligned16(gate_up)) return LMRS_ERR_ALIGN;
+  int rc = check_device(nullptr);
+  if (rc) return rc;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  return dtype == LMRS_DTYPE_BF16
+             ? silu_launch<__nv_bfloat16, false>(out, nullptr, nullptr, gate_up, rows, inter, st)
+             : silu_launch<__half, false>(out, nullptr, nullptr, gate_up, rows, inter, st);
+}
+
+LMRS_API int lmrs_silu_mul_fp8(uint8_t* q_out, float* scale_out, const void* gate_up, int rows,
+                               int inter, int dtype, lmrs_stream_t stream) {
+  if (!act_dtype(dtype)) return LMRS_ERR_DTYPE;
+  if (rows < 0 || inter <= 0 || inter % 8) return LMRS_ERR_SHAPE;
+  if (rows == 0) return LMRS_OK;
+  if (!q_out || !scale_out || !gate_up) return LMRS_ERR_NULL;
+  if (!aligned16(q_out) || !aligned16(gate_up)) return LMRS_ERR_ALIGN;
+  int rc = check_device(nullptr);
+  if (rc) return rc;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  return dtype == LMRS_DTYPE_BF16
+             ? silu_launch<__nv_bfloat16, true>(nullptr, q_out, scale_out, gate_up, rows, inter, st)
+             : silu_launch<__half, true>(nullptr, q_out, scale_out, gate_up, rows, inter, st);
+}
+
+LMRS_API int lmrs_rope_kv_write(void* q_out, void* key_cache, void* value_cache, const void* qkv,
+                                const void* cos, const void* sin, const int32_t* block_tables,
+                                const int32_t* positions, int num_seqs, int num_heads,
+                                int num_kv_heads, int head_size, int block_size,
+                                int max_blocks_per_seq, int dtype, lmrs_stream_t stream) {
+  if (!act_dtype(dtype)) return LMRS_ERR_DTYPE;
+  if (num_seqs < 0 || num_heads <= 0 || num_kv_heads <= 0 || head_size <= 0 || head_size % 2 ||
+      block_size <= 0 || max_blocks_per_seq <= 0)
+    return LMRS_ERR_SHAPE;
+  if (num_seqs == 0) return LMRS_OK;
+  if (!q_out || !key_cache || !value_cache || !qkv || !cos || !sin || !block_tables || !positions)
+    return LMRS_ERR_NULL;
+  int rc = check_device(nullptr);
+  if (rc) return rc;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (dtype == LMRS_DTYPE_BF16) {
+    using T = __nv_bfloat16;
+    rc = launch_ex(lmrs::rope_kv_kernel<T>, num_seqs, 0, 256, 0, st, static_cast<T*>(q_out),
+                   static_cast<T*>(key_cache), static_cast<T*>(value_cache),
+                   static_cast<const T*>(qkv), static_cast<const T*>(cos),
+                   static_cast<const T*>(sin), block_tables, positions, num_heads, num_kv_heads,
+                   head_size, block_size, max_blocks_per_seq);
+  } else {
+    using T = __half;
+    rc = launch_ex(lmrs::rope_kv_kernel<T>, num_seqs, 0, 256, 0, st, static_cast<T*>(q_out),
+                   static_cast<T*>(key_cache), static_cast<T*>(value_cache),
+                   static_cast<const T*>(qkv), static_cast<const T*>(cos),
+                   static_cast<const T*>(sin), block_tables, positions, num_heads, num_kv_heads,
+                   head_size, block_size, max_blocks_per_seq);
+  }
+  return rc ? rc : after_launch();
+}
+
+LMRS_API size_t lmrs_paged_attention_workspace_bytes(int num_seqs, int num_heads,
+                                                     int num_kv_heads, int max_context) {
+  if (num_seqs <= 0 || num_heads <= 0 || num_kv_heads <= 0) return 0;
+  int splits, span;
+  attn_split(num_seqs, num_kv_heads, max_context, sm_count_cached(), &splits, &span);
+  if (splits <= 1) return 0;
+  return static_cast<size_t>(num_seqs) * num_heads * splits * (lmrs::kAttnD + 2) * sizeof(float);
+}
+
+LMRS_API int lmrs_paged_attention_decode(void* out, const void* query, const void* key_cache,
+                                         const void* value_cache, const int32_t* block_tables,
+                                         const int32_t* context_lens, int num_seqs, int num_heads,
+                                         int num_kv_heads, int head_size, int block_size,
+                                         int max_blocks_per_seq, int max_context, float scale,
+                                         int kv_head_map, int dtype, void* workspace,
+                                         size_t workspace_bytes, lmrs_stream_t stream) {
+  if (!act_dtype(dtype)) return LMRS_ERR_DTYPE;
+  if (num_seqs < 0 || num_heads <= 0 || num_kv_heads <= 0 || num_heads % num_kv_heads ||
+      num_heads / num_kv_heads > 16 || head_size != lmrs::kAttnD || block_size <= 0 ||
+      max_blocks_per_seq <= 0 || max_context < 0 || (kv_head_map != 0 && kv_head_map != 1))
+    return LMRS_ERR_SHAPE;
+  if (num_seqs == 0) return LMRS_OK;
+  if (!out || !query || !key_cache || !value_cache || !block_tables || !context_lens)
+    return LMRS_ERR_NULL;
+  if (!aligned16(out) || !aligned16(query) || !aligned16(key_cache) || !aligned16(value_cache))
+    return LMRS_ERR_ALIGN;
+  int dev = 0;
+  int rc = check_device(&dev);
+  if (rc) return rc;
+  int splits, span;
+  attn_split(num_seqs, num_kv_heads, max_context, sm_count(dev), &splits, &span);
+  const size_t need = splits > 1 ? static_cast<size_t>(num_seqs) * num_heads * splits *
+                                       (lmrs::kAttnD + 2) * sizeof(float)
+                                 : 0;
+  if (need && (!workspace || workspace_bytes < need)) return LMRS_ERR_WORKSPACE;
+  if (need && !aligned16(workspace)) return LMRS_ERR_ALIGN;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const int ns = clampi(g_tune.attn_stages, 2, 4);
+#define LMRS_ATTN(T, I, NS)                                                                      \
+  return attn_launch<T, NS>(out, workspace, query, key_cache, value_cache, block_tables,        \
+                            context_lens, num_seqs, num_heads, num_kv_heads, block_size,        \
+                            max_blocks_per_seq, splits, span, scale, kv_head_map, st, dev,      \
+                            g_smem_attn[I][NS - 2])
+  if (dtype == LMRS_DTYPE_BF16) {
+    if (ns == 2) LMRS_ATTN(__nv_bfloat16, 0, 2);
+    if (ns == 3) LMRS_ATTN(__nv_bfloat16, 0, 3);
+    LMRS_ATTN(__nv_bfloat16, 0, 4);
+  }
+  if (ns == 2) LMRS_ATTN(__half, 1, 2);
+  if (ns == 3) LMRS_ATTN(__half, 1, 3);
+  LMRS_ATTN(__half, 1, 4);
+#undef LMRS_ATTN
+}
+
+}  // extern "C"

@@ -1,0 +1,577 @@
+// decode_ops.cuh — the kernels around the quantized linears in a decode step.
+//
+//   * rmsnorm_kernel: residual += delta (optional), out = rmsnorm(residual) * w,
+//     one rounding to the I/O type (reference: kernels/ffi/norm_ffi.cu:9-31);
+//     FP8 form writes the e4m3 bytes and per-row scale of that rounded output
+//     instead (bit-identical to rmsnorm -> fp8_quant_rows).
+//   * rope_kv_kernel: rotate-half RoPE on q and k of the merged qkv row
+//     (reference: kernels/ffi/pos_embed_ffi.cu:9-29), q to its buffer, k and v
+//     into the paged KV cache at the step's position.
+//   * silu_mul_kernel: out = silu(gate) * up from the merged gate|up row
+//     (reference: kernels/ops/activation_kernels.cuh:40-48); FP8 form as above.
+//   * decode_attn_kernel: one decode query per sequence against a paged KV
+//     cache laid out as the reference's paged_attention_v1
+//     (kernels/attention/paged_attention.cuh:14-108: cache[block][kv_head]
+//     [block_offset][head_size], block table per sequence), GQA with the q heads
+//     of one KV head in one CTA: S = Q K^T and O += P V on mma.sync (16 q-head
+//     rows, 16 positions per warp step, fp32 accumulate), online softmax,
+//     split over the context with a combine kernel when a split has peers.
+// All are launched with programmatic dependent launch and call pdl_wait before
+// touching their inputs.
+#pragma once
+#include "fp8_kernels.cuh"
+#include "lmrs_ptx.cuh"
+
+namespace lmrs {
+
+template <typename T>
+struct Act;
+template <>
+struct Act<__half> {
+  static __device__ __forceinline__ float f(__half v) { return __half2float(v); }
+  static __device__ __forceinline__ __half t(float v) { return __float2half_rn(v); }
+};
+template <>
+struct Act<__nv_bfloat16> {
+  static __device__ __forceinline__ float f(__nv_bfloat16 v) { return __bfloat162float(v); }
+  static __device__ __forceinline__ __nv_bfloat16 t(float v) { return __float2bfloat16_rn(v); }
+};
+
+constexpr int kNormThreads = 256;
+
+__device__ __forceinline__ float block_sum(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float s = 0.f;
+#pragma unroll
+  for (int w = 0; w < kNormThreads / 32; ++w) s += red[w];
+  __syncthreads();
+  return s;
+}
+
+__device__ __forceinline__ float block_max(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float m = red[0];
+#pragma unroll
+  for (int w = 1; w < kNormThreads / 32; ++w) m = fmaxf(m, red[w]);
+  __syncthreads();
+  return m;
+}
+
+// 8 rounded activations -> 8 e4m3 bytes with the row scale s (same arithmetic
+// as fp8_quant_rows_kernel: x / s rounded to nearest even, saturating).
+__device__ __forceinline__ uint2 e4m3x8(const float (&v)[8], float s) {
+  uint32_t out[2] = {0u, 0u};
+  if (s != 0.f) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 pr = make_float2(__fdiv_rn(v[2 * i], s), __fdiv_rn(v[2 * i + 1], s));
+      const uint32_t b =
+          static_cast<uint32_t>(__nv_cvt_float2_to_fp8x2(pr, __NV_SATFINITE, __NV_E4M3));
+      out[i >> 1] |= b << ((i & 1) * 16);
+    }
+  }
+  return make_uint2(out[0], out[1]);
+}
+
+// residual (+)= delta, out = rmsnorm(residual) * w; one CTA per row, chunks of
+// 8 columns (H % 8 == 0).  FP8: out is replaced by its per-row e4m3 bytes and
+// scale (the rounded outputs are recomputed for each pass instead of stored).
+template <typename T, bool FP8>
+__global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(
+    T* __restrict__ out, uint8_t* __restrict__ qout, float* __restrict__ qscale,
+    T* __restrict__ resid, const T* __restrict__ delta, const T* __restrict__ w, int H, float eps) {
+  pdl_wait();
+  pdl_trigger();
+  __shared__ float red[kNormThreads / 32];
+  const int row = blockIdx.x;
+  T* xr = resid + static_cast<int64_t>(row) * H;
+  float ss = 0.f;
+  for (int c = threadIdx.x * 8; c < H; c += kNormThreads * 8) {
+    uint4 v = *reinterpret_cast<const uint4*>(xr + c);
+    if (delta != nullptr) {
+      const uint4 dv = *reinterpret_cast<const uint4*>(delta + static_cast<int64_t>(row) * H + c);
+      const T* e = reinterpret_cast<const T*>(&v);
+      const T* de = reinterpret_cast<const T*>(&dv);
+      uint4 sv;
+      T* se = reinterpret_cast<T*>(&sv);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) se[i] = Act<T>::t(Act<T>::f(e[i]) + Act<T>::f(de[i]));
+      *reinterpret_cast<uint4*>(xr + c) = sv;   // the updated residual stream
+      v = sv;
+    }
+    const T* e = reinterpret_cast<const T*>(&v);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float f = Act<T>::f(e[i]);
+      ss += f * f;
+    }
+  }
+  const float inv = rsqrtf(block_sum(ss, red) / H + eps);
+  auto normed = [&](int c, float (&y)[8], uint4& packed) {
+    const uint4 v = *reinterpret_cast<const uint4*>(xr + c);
+    const uint4 wv = *reinterpret_cast<const uint4*>(w + c);
+    const T* e = reinterpret_cast<const T*>(&v);
+    const T* we = reinterpret_cast<const T*>(&wv);
+    T* oe = reinterpret_cast<T*>(&packed);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      oe[i] = Act<T>::t(Act<T>::f(e[i]) * inv * Act<T>::f(we[i]));
+      y[i] = Act<T>::f(oe[i]);
+    }
+  };
+  if (!FP8) {
+    for (int c = threadIdx.x * 8; c < H; c += kNormThreads * 8) {
+      float y[8];
+      uint4 pk;
+      normed(c, y, pk);
+      *reinterpret_cast<uint4*>(out + static_cast<int64_t>(row) * H + c) = pk;
+    }
+    return;
+  }
+  float amax = 0.f;
+  for (int c = threadIdx.x * 8; c < H; c += kNormThreads * 8) {
+    float y[8];
+    uint4 pk;
+    normed(c, y, pk);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(y[i]));
+  }
+  const float sc = __fdiv_rn(block_max(amax, red), 448.0f);
+  if (threadIdx.x == 0) qscale[row] = sc;
+  for (int c = threadIdx.x * 8; c < H; c += kNormThreads * 8) {
+    float y[8];
+    uint4 pk;
+    normed(c, y, pk);
+    *reinterpret_cast<uint2*>(qout + static_cast<int64_t>(row) * H + c) = e4m3x8(y, sc);
+  }
+}
+
+// out[r, i] = silu(gu[r, i]) * gu[r, I + i]  (I = inter, I % 8 == 0); FP8 as above.
+template <typename T, bool FP8>
+__global__ void __launch_bounds__(kNormThreads) silu_mul_kernel(
+    T* __restrict__ out, uint8_t* __restrict__ qout, float* __restrict__ qscale,
+    const T* __restrict__ gu, int I) {
+  pdl_wait();
+  pdl_trigger();
+  __shared__ float red[kNormThreads / 32];
+  const int row = blockIdx.x;
+  const T* gr = gu + static_cast<int64_t>(row) * 2 * I;
+  auto act = [&](int c, float (&y)[8], uint4& packed) {
+    const uint4 gv = *reinterpret_cast<const uint4*>(gr + c);
+    const uint4 uv = *reinterpret_cast<const uint4*>(gr + I + c);
+    const T* ge = reinterpret_cast<const T*>(&gv);
+    const T* ue = reinterpret_cast<const T*>(&uv);
+    T* oe = reinterpret_cast<T*>(&packed);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float gval = Act<T>::f(ge[i]);
+      oe[i] = Act<T>::t((gval / (1.0f + expf(-gval))) * Act<T>::f(ue[i]));
+      y[i] = Act<T>::f(oe[i]);
+    }
+  };
+  if (!FP8) {
+    for (int c = threadIdx.x * 8; c < I; c += kNormThreads * 8) {
+      float y[8];
+      uint4 pk;
+      act(c, y, pk);
+      *reinterpret_cast<uint4*>(out + static_cast<int64_t>(row) * I + c) = pk;
+    }
+    return;
+  }
+  float amax = 0.f;
+  for (int c = threadIdx.x * 8; c < I; c += kNormThreads * 8) {
+    float y[8];
+    uint4 pk;
+    act(c, y, pk);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(y[i]));
+  }
+  const float sc = __fdiv_rn(block_max(amax, red), 448.0f);
+  if (threadIdx.x == 0) qscale[row] = sc;
+  for (int c = threadIdx.x * 8; c < I; c += kNormThreads * 8) {
+    float y[8];
+    uint4 pk;
+    act(c, y, pk);
+    *reinterpret_cast<uint2*>(qout + static_cast<int64_t>(row) * I + c) = e4m3x8(y, sc);
+  }
+}
+
+// One CTA per sequence.  qkv row: [q (hq*d) | k (hkv*d) | v (hkv*d)].
+// cos/sin: d/2 entries for this step's position.  Cache: paged, block table row
+// `tables[b]`, block_size positions per block.
+template <typename T>
+__global__ void __launch_bounds__(256) rope_kv_kernel(
+    T* __restrict__ q_out, T* __restrict__ k_cache, T* __restrict__ v_cache,
+    const T* __restrict__ qkv, const T* __restrict__ cosv, const T* __restrict__ sinv,
+    const int32_t* __restrict__ tables, const int32_t* __restrict__ positions, int hq, int hkv,
+    int d, int block_size, int max_blocks) {
+  pdl_wait();
+  pdl_trigger();
+  const int b = blockIdx.x;
+  const int half = d / 2;
+  const T* row = qkv + static_cast<int64_t>(b) * (hq + 2 * hkv) * d;
+  const int pos = positions[b];
+  // a position outside the table's span writes q only (no cache access)
+  const bool in_cache = pos >= 0 && pos < max_blocks * block_size;
+  const int blk = in_cache ? tables[static_cast<int64_t>(b) * max_blocks + pos / block_size] : 0;
+  const int off = in_cache ? pos % block_size : 0;
+  const int pairs = (hq + hkv) * half;
+  for (int e = threadIdx.x; e < pairs + hkv * d; e += blockDim.x) {
+    if (e < pairs) {
+      const int h = e / half, c = e - h * half;
+      const T* src = row + h * d;
+      const float x0 = Act<T>::f(src[c]), x1 = Act<T>::f(src[c + half]);
+      const float cs = Act<T>::f(cosv[c]), sn = Act<T>::f(sinv[c]);
+      const T r0 = Act<T>::t(x0 * cs - x1 * sn);   // rotate-half: first half
+      const T r1 = Act<T>::t(x1 * cs + x0 * sn);   // second half
+      if (h < hq) {
+        T* dst = q_out + (static_cast<int64_t>(b) * hq + h) * d;
+        dst[c] = r0;
+        dst[c + half] = r1;
+      } else if (in_cache) {
+        const int kh = h - hq;
+        T* dst = k_cache + ((static_cast<int64_t>(blk) * hkv + kh) * block_size + off) * d;
+        dst[c] = r0;
+        dst[c + half] = r1;
+      }
+    } else if (in_cache) {
+      const int e2 = e - pairs;
+      const int kh = e2 / d, c = e2 - kh * d;
+      v_cache[((static_cast<int64_t>(blk) * hkv + kh) * block_size + off) * d + c] =
+          row[(hq + hkv) * d + kh * d + c];
+    }
+  }
+}
+
+// ------------------------------------------------------------ attention
+constexpr int kAttnD = 128;        // head size
+constexpr int kAttnTile = 64;      // positions per CTA iteration (16 per warp)
+constexpr int kAttnThreads = 128;  // 4 warps
+constexpr int kAttnRowBytes = kAttnD * 2 + 16;  // padded smem row (conflict-free ldmatrix)
+constexpr int kAttnMaxBlocks = 512;  // block-table entries of one split cached in smem
+
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool pred) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src),
+               "r"(pred ? 16 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+template <typename T>
+struct MmaT;
+template <>
+struct MmaT<__half> {
+  static __device__ __forceinline__ void mma(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                             uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+        "{%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  }
+  static __device__ __forceinline__ uint32_t pack(float lo, float hi) {
+    __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+};
+template <>
+struct MmaT<__nv_bfloat16> {
+  static __device__ __forceinline__ void mma(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                             uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+        "{%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  }
+  static __device__ __forceinline__ uint32_t pack(float lo, float hi) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+};
+
+// grid: (num_seqs * num_kv_heads, splits).  Each CTA: one (sequence, KV head),
+// positions [split * span, (split + 1) * span) of the context, the G q heads
+// that read this KV head (G <= 16; rows >= G are padding).
+// kv_map 0: q head h reads KV head h % num_kv_heads (the reference's paged
+// kernel); 1: h / G (grouped, as torch's enable_gqa).
+// splits == 1: writes out directly; otherwise writes (O, m, l) partials to ws.
+template <typename T, int NS>
+__global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(
+    T* __restrict__ out, float* __restrict__ ws, const T* __restrict__ query,
+    const T* __restrict__ k_cache, const T* __restrict__ v_cache,
+    const int32_t* __restrict__ tables, const int32_t* __restrict__ ctx_lens, int num_heads,
+    int num_kv_heads, int block_size, int max_blocks, int span, float scale_log2, int kv_map) {
+  pdl_wait();
+  pdl_trigger();
+  extern __shared__ __align__(16) uint8_t sm[];
+  // [2 stages][K tile 64 rows | V tile 64 rows], rows padded to kAttnRowBytes
+  constexpr int kTileBytes = kAttnTile * kAttnRowBytes;
+  const int seq = blockIdx.x / num_kv_heads, kvh = blockIdx.x % num_kv_heads;
+  const int split = blockIdx.y, splits = gridDim.y;
+  const int G = num_heads / num_kv_heads;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  // never past the block table's span, never negative
+  const int ctx = max(0, min(ctx_lens[seq], max_blocks * block_size));
+  const int p0 = split * span;
+  const int p1 = min(ctx, p0 + span);
+  auto qhead = [&](int i) { return kv_map ? kvh * G + i : kvh + i * num_kv_heads; };
+
+  // the split's block-table entries, read once into shared memory (the staging
+  // loop would otherwise wait on a dependent global load before every copy)
+  __shared__ int sblk[kAttnMaxBlocks];
+  const int blk0 = p0 / block_size;
+  const int nblk = p1 > p0 ? (p1 - 1) / block_size - blk0 + 1 : 0;
+  const bool cached = nblk <= kAttnMaxBlocks;
+  if (cached)
+    for (int i = threadIdx.x; i < nblk; i += kAttnThreads)
+      sblk[i] = tables[static_cast<int64_t>(seq) * max_blocks + blk0 + i];
+  __syncthreads();
+
+  // Q fragments (A operand, 16 rows = q heads, 128 dims = 8 k-steps)
+  uint32_t qa[8][4];
+  {
+    const bool r0 = g < G, r1 = g + 8 < G;
+    const T* q0 = query + (static_cast<int64_t>(seq) * num_heads + (r0 ? qhead(g) : 0)) * kAttnD;
+    const T* q1 = query + (static_cast<int64_t>(seq) * num_heads + (r1 ? qhead(g + 8) : 0)) * kAttnD;
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk) {
+      const int c = kk * 16 + 2 * t;
+      qa[kk][0] = r0 ? *reinterpret_cast<const uint32_t*>(q0 + c) : 0u;
+      qa[kk][1] = r1 ? *reinterpret_cast<const uint32_t*>(q1 + c) : 0u;
+      qa[kk][2] = r0 ? *reinterpret_cast<const uint32_t*>(q0 + c + 8) : 0u;
+      qa[kk][3] = r1 ? *reinterpret_cast<const uint32_t*>(q1 + c + 8) : 0u;
+    }
+  }
+
+  // Each warp streams its own 16-position tiles (tiles warp, warp + 4, ... of the
+  // split) through an NS-stage cp.async ring in its own shared-memory region: no
+  // CTA-wide barrier inside the loop.
+  constexpr int kWarpTile = 16 * kAttnRowBytes;          // K (or V) rows of one tile
+  constexpr int kWarpStage = 2 * kWarpTile;
+  uint8_t* wsm = sm + warp * NS * kWarpStage;
+  auto stage = [&](int j, int buf) {
+    const uint32_t kb = smem_u32(wsm + buf * kWarpStage);
+    const uint32_t vb = kb + kWarpTile;
+    const int base = p0 + (warp + 4 * j) * 16;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int r = 2 * i + (lane >> 4), ch = lane & 15;
+      const int pos = base + r;
+      const bool ok = pos < p1;
+      const int pp = ok ? pos : p0;
+      const int bi = pp / block_size;
+      const int blk = cached ? sblk[bi - blk0] : tables[static_cast<int64_t>(seq) * max_blocks + bi];
+      const int64_t off = ((static_cast<int64_t>(blk) * num_kv_heads + kvh) * block_size +
+                           pp % block_size) * kAttnD + ch * 8;
+      cp_async16(kb + r * kAttnRowBytes + ch * 16, k_cache + off, ok);
+      cp_async16(vb + r * kAttnRowBytes + ch * 16, v_cache + off, ok);
+    }
+    cp_async_commit();
+  };
+
+  float o[16][4];
+#pragma unroll
+  for (int n = 0; n < 16; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;  // rows g, g+8
+
+  const int ntiles_all = p1 > p0 ? (p1 - p0 + 15) / 16 : 0;
+  const int ntiles = ntiles_all > warp ? (ntiles_all - warp + 3) / 4 : 0;  // this warp's
+#pragma unroll
+  for (int i = 0; i < NS - 1; ++i) {
+    if (i < ntiles) stage(i, i);
+    else cp_async_commit();  // empty group keeps the group count uniform
+  }
+  for (int tile = 0; tile < ntiles; ++tile) {
+    const int buf = tile % NS;
+    cp_async_wait<NS - 2>();  // this tile's group has landed for this lane ...
+    __syncwarp();             // ... and for every lane; tile - 1's buffer is free
+    if (tile + NS - 1 < ntiles) stage(tile + NS - 1, (tile + NS - 1) % NS);
+    else cp_async_commit();
+    const uint32_t kb = smem_u32(wsm + buf * kWarpStage);
+    const uint32_t vb = kb + kWarpTile;
+    // S[16 heads x 16 positions] = Q K^T: B operand (k = dim, n = position) from K
+    // rows (position-major) with ldmatrix (no transpose); two 8-position halves
+    float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+    for (int kk = 0; kk < 8; kk += 2) {
+      // matrices: (pos 0-7, dims kk*16..+7), (pos 0-7, +8..15), (pos 8-15, dims ..), ...
+      uint32_t kf[4];
+      const int mi = lane >> 3, ri = lane & 7;
+      // x4: m0 = pos 0-7 dims [16kk, +8), m1 = pos 0-7 dims [16kk+8, +8),
+      //     m2 = pos 0-7 dims [16(kk+1), +8), m3 = pos 0-7 dims [16(kk+1)+8, +8)
+      ldsm_x4(kf, kb + ri * kAttnRowBytes + (kk * 16 + mi * 8) * 2);
+      MmaT<T>::mma(s[0], qa[kk], kf[0], kf[1]);
+      MmaT<T>::mma(s[0], qa[kk + 1], kf[2], kf[3]);
+      ldsm_x4(kf, kb + (8 + ri) * kAttnRowBytes + (kk * 16 + mi * 8) * 2);
+      MmaT<T>::mma(s[1], qa[kk], kf[0], kf[1]);
+      MmaT<T>::mma(s[1], qa[kk + 1], kf[2], kf[3]);
+    }
+    // mask, scale (log2 domain), online softmax for rows g (s[.][0..1]) and g+8 (s[.][2..3])
+    const int pbase = p0 + (warp + 4 * tile) * 16;
+    float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+    for (int h2 = 0; h2 < 2; ++h2)
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const bool ok = pbase + h2 * 8 + 2 * t + j < p1;
+        s[h2][j] = ok ? s[h2][j] * scale_log2 : -INFINITY;
+        s[h2][2 + j] = ok ? s[h2][2 + j] * scale_log2 : -INFINITY;
+        mx0 = fmaxf(mx0, s[h2][j]);
+        mx1 = fmaxf(mx1, s[h2][2 + j]);
+      }
+#pragma unroll
+    for (int o_ = 1; o_ < 4; o_ <<= 1) {
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o_));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o_));
+    }
+    const float nm0 = fmaxf(m0, mx0), nm1 = fmaxf(m1, mx1);
+    const float c0 = nm0 == -INFINITY ? 1.f : exp2f(m0 - nm0);
+    const float c1 = nm1 == -INFINITY ? 1.f : exp2f(m1 - nm1);
+    float ps0 = 0.f, ps1 = 0.f;
+#pragma unroll
+    for (int h2 = 0; h2 < 2; ++h2)
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        s[h2][j] = nm0 == -INFINITY ? 0.f : exp2f(s[h2][j] - nm0);
+        s[h2][2 + j] = nm1 == -INFINITY ? 0.f : exp2f(s[h2][2 + j] - nm1);
+        ps0 += s[h2][j];
+        ps1 += s[h2][2 + j];
+      }
+    l0 = l0 * c0 + ps0;  // per-lane partial row sums; reduced over t at the end
+    l1 = l1 * c1 + ps1;
+    m0 = nm0;
+    m1 = nm1;
+#pragma unroll
+    for (int n = 0; n < 16; ++n) {
+      o[n][0] *= c0;
+      o[n][1] *= c0;
+      o[n][2] *= c1;
+      o[n][3] *= c1;
+    }
+    // P (A operand, k = 16 positions) from the S accumulators
+    uint32_t pa[4];
+    pa[0] = MmaT<T>::pack(s[0][0], s[0][1]);
+    pa[1] = MmaT<T>::pack(s[0][2], s[0][3]);
+    pa[2] = MmaT<T>::pack(s[1][0], s[1][1]);
+    pa[3] = MmaT<T>::pack(s[1][2], s[1][3]);
+    // O += P V: B operand (k = position, n = dim) from V rows with ldmatrix.trans
+#pragma unroll
+    for (int n = 0; n < 16; n += 2) {
+      uint32_t vf[4];
+      const int mi = lane >> 3, ri = lane & 7;
+      // x4.trans: m0 = pos 0-7 dims [8n, +8), m1 = pos 8-15 dims [8n, +8),
+      //           m2 = pos 0-7 dims [8(n+1), +8), m3 = pos 8-15 dims [8(n+1), +8)
+      ldsm_x4_t(vf, vb + ((mi & 1) * 8 + ri) * kAttnRowBytes + (n * 8 + (mi >> 1) * 8) * 2);
+      MmaT<T>::mma(o[n], pa, vf[0], vf[1]);
+      MmaT<T>::mma(o[n + 1], pa, vf[2], vf[3]);
+    }
+  }
+  cp_async_wait<0>();
+
+  // ---- merge the 4 warps (each covered a quarter of every tile)
+#pragma unroll
+  for (int o_ = 1; o_ < 4; o_ <<= 1) {
+    l0 += __shfl_xor_sync(0xffffffffu, l0, o_);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, o_);
+  }
+  float* mrg = reinterpret_cast<float*>(sm);  // [4 warps][16 rows][130] (O 128, m, l)
+  constexpr int kStride = kAttnD + 2;
+  __syncthreads();
+  {
+    float* wp = mrg + warp * 16 * kStride;
+#pragma unroll
+    for (int n = 0; n < 16; ++n) {
+      wp[g * kStride + n * 8 + 2 * t] = o[n][0];
+      wp[g * kStride + n * 8 + 2 * t + 1] = o[n][1];
+      wp[(g + 8) * kStride + n * 8 + 2 * t] = o[n][2];
+      wp[(g + 8) * kStride + n * 8 + 2 * t + 1] = o[n][3];
+    }
+    if (t == 0) {
+      wp[g * kStride + kAttnD] = m0;
+      wp[g * kStride + kAttnD + 1] = l0;
+      wp[(g + 8) * kStride + kAttnD] = m1;
+      wp[(g + 8) * kStride + kAttnD + 1] = l1;
+    }
+  }
+  __syncthreads();
+  // thread -> (row r, 16 consecutive dims)
+  for (int e = threadIdx.x; e < G * 8; e += kAttnThreads) {
+    const int r = e >> 3, d0 = (e & 7) * 16;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) M = fmaxf(M, mrg[(w * 16 + r) * kStride + kAttnD]);
+    float L = 0.f, acc[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) acc[i] = 0.f;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      const float* wr = mrg + (w * 16 + r) * kStride;
+      const float f = M == -INFINITY ? 0.f : exp2f(wr[kAttnD] - M);
+      L += f * wr[kAttnD + 1];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) acc[i] += f * wr[d0 + i];
+    }
+    const int h = qhead(r);
+    if (splits == 1) {
+      T* dst = out + (static_cast<int64_t>(seq) * num_heads + h) * kAttnD + d0;
+      const float inv = L > 0.f ? 1.f / L : 0.f;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) dst[i] = Act<T>::t(acc[i] * inv);
+    } else {
+      // partial: O (unnormalised, fp32), then m, l
+      float* pw = ws + ((static_cast<int64_t>(seq) * num_heads + h) * splits + split) * (kAttnD + 2);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) pw[d0 + i] = acc[i];
+      if (d0 == 0) {
+        pw[kAttnD] = M;
+        pw[kAttnD + 1] = L;
+      }
+    }
+  }
+}
+
+// out[seq, h, :] = sum_s 2^(m_s - M) O_s / sum_s 2^(m_s - M) l_s over the splits.
+template <typename T>
+__global__ void __launch_bounds__(128) decode_attn_combine_kernel(T* __restrict__ out,
+                                                                  const float* __restrict__ ws,
+                                                                  int splits) {
+  pdl_wait();
+  pdl_trigger();
+  const int sh = blockIdx.x;  // seq * num_heads + h
+  const float* p = ws + static_cast<int64_t>(sh) * splits * (kAttnD + 2);
+  float M = -INFINITY;
+  for (int s = 0; s < splits; ++s) M = fmaxf(M, p[s * (kAttnD + 2) + kAttnD]);
+  float L = 0.f, acc = 0.f;
+  const int d = threadIdx.x;
+  for (int s = 0; s < splits; ++s) {
+    const float* ps = p + s * (kAttnD + 2);
+    const float f = M == -INFINITY ? 0.f : exp2f(ps[kAttnD] - M);
+    L += f * ps[kAttnD + 1];
+    acc += f * ps[d];
+  }
+  out[static_cast<int64_t>(sh) * kAttnD + d] = Act<T>::t(L > 0.f ? acc / L : 0.f);
+}
+
+}  // namespace lmrs

@@ -52,6 +52,8 @@ struct Tuning {
   int awq_gemv4 = 1;         // M <= 4: the permute-free GEMV (0: the general one)
   int gemv_box_rows = 128;   // TMA GEMV box height (128 or 64; 64 forced for group 64)
   int awq_gemv4_slots = 4;   // its ring slots (4 or 8)
+  int attn_stages = 3;       // decode attention cp.async ring depth (2..4)
+  int attn_ctas_per_sm = 2;  // decode attention context split target
 };
 Tuning g_tune;
 
@@ -589,6 +591,8 @@ int lmrs_set_tuning(const char* key, int value) {
   else if (!strcmp(key, "awq_gemv4")) g_tune.awq_gemv4 = value ? 1 : 0;
   else if (!strcmp(key, "gemv_box_rows")) g_tune.gemv_box_rows = value;
   else if (!strcmp(key, "awq_gemv4_slots")) g_tune.awq_gemv4_slots = value;
+  else if (!strcmp(key, "attn_stages")) g_tune.attn_stages = value;
+  else if (!strcmp(key, "attn_ctas_per_sm")) g_tune.attn_ctas_per_sm = value;
   else if (!strcmp(key, "fp8_gemv_cluster")) g_tune.fp8_gemv_cluster = value;
   else return LMRS_ERR_SHAPE;
   return LMRS_OK;
@@ -777,3 +781,6 @@ extern "C" int lmrs_fp8_linear_noalloc(void* y, const void* x, const uint8_t* wq
   if ((rc = fp8_quant_launch(xq, sx, x, M, K, LMRS_DTYPE_BF16, st))) return rc;
   return fp8_linear_prequant_impl(y, xq, sx, wq, w_scale, bias_or_null, M, K, N, st, dev);
 }
+
+// decode-step kernels around the quantized linears (include/lmrs_decode.h)
+#include "decode_capi.cuh"

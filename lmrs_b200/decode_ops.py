@@ -1,0 +1,134 @@
+"""Host wrappers of the decode-step kernels (include/lmrs_decode.h).
+
+Argument checking and dtype dispatch mirror ``ops.py``: tensors must be CUDA,
+contiguous and of the documented dtype, outputs are allocated on the input's
+device unless given, and every call goes through the C-ABI (no torch fallback).
+"""
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+
+from . import _lib
+from .ops import DTypeMismatch, ShapeMismatch, _ptr, _require_cuda, _stream
+
+_DT = {torch.bfloat16: _lib.DTYPE_BF16, torch.float16: _lib.DTYPE_F16}
+
+
+def _code(t: torch.Tensor) -> int:
+    if t.dtype not in _DT:
+        raise DTypeMismatch(f"expected bf16 or f16, got {t.dtype}")
+    return _DT[t.dtype]
+
+
+def rmsnorm(residual: torch.Tensor, weight: torch.Tensor, eps: float,
+            delta: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None):
+    """residual (+)= delta (in place), returns rmsnorm(residual) * weight."""
+    _require_cuda(residual, "residual")
+    rows, H = residual.reshape(-1, residual.shape[-1]).shape
+    if out is None:
+        out = torch.empty_like(residual)
+    _lib.check("lmrs_rmsnorm", _lib.load().lmrs_rmsnorm(
+        _ptr(out), _ptr(residual), _ptr(delta), _ptr(weight), rows, H, float(eps),
+        _code(residual), _stream(residual)))
+    return out
+
+
+def rmsnorm_fp8(residual: torch.Tensor, weight: torch.Tensor, eps: float,
+                delta: Optional[torch.Tensor] = None, q_out=None, scale_out=None):
+    """residual (+)= delta, returns (e4m3 bytes, per-row fp32 scales) of the
+    normalised rows, as fp8_quant_rows(rmsnorm(...)) would."""
+    _require_cuda(residual, "residual")
+    rows, H = residual.reshape(-1, residual.shape[-1]).shape
+    if q_out is None:
+        q_out = torch.empty((rows, H), dtype=torch.uint8, device=residual.device)
+    if scale_out is None:
+        scale_out = torch.empty((rows,), dtype=torch.float32, device=residual.device)
+    _lib.check("lmrs_rmsnorm_fp8", _lib.load().lmrs_rmsnorm_fp8(
+        _ptr(q_out), _ptr(scale_out), _ptr(residual), _ptr(delta), _ptr(weight), rows, H,
+        float(eps), _code(residual), _stream(residual)))
+    return q_out, scale_out
+
+
+def silu_mul(gate_up: torch.Tensor, out: Optional[torch.Tensor] = None):
+    """silu(gate) * up for a merged [rows, 2 * inter] projection output."""
+    _require_cuda(gate_up, "gate_up")
+    rows, two_i = gate_up.shape
+    if two_i % 2:
+        raise ShapeMismatch("gate_up last dim must be even")
+    if out is None:
+        out = torch.empty((rows, two_i // 2), dtype=gate_up.dtype, device=gate_up.device)
+    _lib.check("lmrs_silu_mul", _lib.load().lmrs_silu_mul(
+        _ptr(out), _ptr(gate_up), rows, two_i // 2, _code(gate_up), _stream(gate_up)))
+    return out
+
+
+def silu_mul_fp8(gate_up: torch.Tensor, q_out=None, scale_out=None):
+    _require_cuda(gate_up, "gate_up")
+    rows, two_i = gate_up.shape
+    inter = two_i // 2
+    if q_out is None:
+        q_out = torch.empty((rows, inter), dtype=torch.uint8, device=gate_up.device)
+    if scale_out is None:
+        scale_out = torch.empty((rows,), dtype=torch.float32, device=gate_up.device)
+    _lib.check("lmrs_silu_mul_fp8", _lib.load().lmrs_silu_mul_fp8(
+        _ptr(q_out), _ptr(scale_out), _ptr(gate_up), rows, inter, _code(gate_up),
+        _stream(gate_up)))
+    return q_out, scale_out
+
+
+def rope_kv_write(qkv: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
+                  key_cache: torch.Tensor, value_cache: torch.Tensor,
+                  block_tables: torch.Tensor, positions: torch.Tensor, num_heads: int,
+                  num_kv_heads: int, head_size: int, q_out: Optional[torch.Tensor] = None):
+    """RoPE of q and k (cos/sin: head_size/2 entries for the step's position);
+    returns q [num_seqs, num_heads, head_size], writes k and v into the paged
+    cache [blocks, num_kv_heads, block_size, head_size] at positions."""
+    _require_cuda(qkv, "qkv")
+    seqs = qkv.shape[0]
+    if q_out is None:
+        q_out = torch.empty((seqs, num_heads, head_size), dtype=qkv.dtype, device=qkv.device)
+    block_size = key_cache.shape[2]
+    _lib.check("lmrs_rope_kv_write", _lib.load().lmrs_rope_kv_write(
+        _ptr(q_out), _ptr(key_cache), _ptr(value_cache), _ptr(qkv), _ptr(cos), _ptr(sin),
+        _ptr(block_tables), _ptr(positions), seqs, num_heads, num_kv_heads, head_size,
+        block_size, block_tables.shape[1], _code(qkv), _stream(qkv)))
+    return q_out
+
+
+class AttentionWorkspace:
+    """Grow-only split-context scratch for paged_attention_decode."""
+
+    def __init__(self):
+        self.buf = None
+
+    def get(self, nbytes: int, device):
+        if nbytes == 0:
+            return None
+        if self.buf is None or self.buf.numel() < nbytes or self.buf.device != device:
+            self.buf = torch.empty(nbytes, dtype=torch.uint8, device=device)
+        return self.buf
+
+
+def paged_attention_decode(query: torch.Tensor, key_cache: torch.Tensor,
+                           value_cache: torch.Tensor, block_tables: torch.Tensor,
+                           context_lens: torch.Tensor, max_context: int, scale: float,
+                           kv_head_map: int = 1, workspace: Optional[AttentionWorkspace] = None,
+                           out: Optional[torch.Tensor] = None):
+    """query [seqs, heads, 128] against the paged cache; kv_head_map 1 = grouped
+    heads (h / G), 0 = h % num_kv_heads (the reference's paged kernel)."""
+    _require_cuda(query, "query")
+    seqs, heads, d = query.shape
+    num_kv_heads, block_size = key_cache.shape[1], key_cache.shape[2]
+    lib = _lib.load()
+    need = lib.lmrs_paged_attention_workspace_bytes(seqs, heads, num_kv_heads, max_context)
+    ws = (workspace or AttentionWorkspace()).get(need, query.device)
+    if out is None:
+        out = torch.empty_like(query)
+    _lib.check("lmrs_paged_attention_decode", lib.lmrs_paged_attention_decode(
+        _ptr(out), _ptr(query), _ptr(key_cache), _ptr(value_cache), _ptr(block_tables),
+        _ptr(context_lens), seqs, heads, num_kv_heads, d, block_size, block_tables.shape[1],
+        int(max_context), float(scale), int(kv_head_map), _code(query), _ptr(ws), need,
+        _stream(query)))
+    return out

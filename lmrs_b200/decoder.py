@@ -8,9 +8,12 @@ projections run on lmrs_b200's AWQ W4A16 or FP8 W8A8 linears.
 - o and down are row-parallel and are followed by a sum all-reduce when
   tensor parallelism is on.
 
-The support ops (RMSNorm, RoPE, decode attention over a preallocated KV cache,
-SiLU * up, the bf16 LM head) are plain torch: they are not the hot path this
-package implements.  Weights are random (seeded), the KV cache is pre-filled
+The support ops (residual add + RMSNorm, RoPE + KV write, paged GQA decode
+attention, SiLU * up) run on this package's decode kernels (decode_ops.py,
+include/lmrs_decode.h), with the FP8 per-token quantisation folded into the
+norm and activation kernels; fused=False runs them in plain torch instead (for
+comparison).  The LM head is a plain bf16/fp16 matmul.  Weights are random
+(seeded), the KV cache is pre-filled
 with random values to the configured context, and one decode step feeds one
 token per sequence at position ctx - 1 (the step is replayed unchanged, which
 keeps it CUDA-graph friendly).
@@ -24,6 +27,7 @@ from typing import Optional
 import torch
 import torch.nn.functional as F
 
+from . import decode_ops as DO
 from . import ops
 
 
@@ -87,12 +91,13 @@ class QuantDecoder:
     """One tensor-parallel rank of the decoder (world = 1 for a single GPU)."""
 
     def __init__(self, cfg: DecoderConfig, batch: int, ctx: int, device, rank: int = 0,
-                 world: int = 1, seed: int = 0, group=None):
+                 world: int = 1, seed: int = 0, group=None, fused: bool = True):
         if cfg.heads % world or cfg.intermediate % world or cfg.kv_heads % world:
             raise ValueError(f"tensor parallelism {world} does not divide heads / kv heads / intermediate")
         if cfg.vocab % world:
             raise ValueError(f"vocab {cfg.vocab} not divisible by {world}")
         self.cfg, self.batch, self.ctx = cfg, batch, ctx
+        self.fused = fused
         self.device = torch.device(device)
         self.rank, self.world, self.pg = rank, world, group
         self.hq, self.hkv = cfg.heads // world, cfg.kv_heads // world
@@ -136,6 +141,27 @@ class QuantDecoder:
         self.kv = None
         self.set_batch(batch, seed)
 
+    # ---------------------------------------------------------------- state
+    def state(self) -> dict:
+        """Every tensor of this rank (weights, KV cache, token ids), by reference."""
+        return dict(embed=self.embed, final_norm=self.final_norm, lm_head=self.lm_head,
+                    tokens=self.tokens, kv=self.kv,
+                    layers=[dict(in_norm=L["in_norm"], post_norm=L["post_norm"],
+                                 **{k: dict(L[k].tensors) for k in ("qkv", "o", "gate_up", "down")})
+                            for L in self.layers])
+
+    def load_state(self, st: dict) -> None:
+        """Copy a state() of the same shapes into this decoder (in place)."""
+        own = self.state()
+        for key in ("embed", "final_norm", "lm_head", "tokens", "kv"):
+            own[key].copy_(st[key])
+        for mine, theirs in zip(own["layers"], st["layers"]):
+            for key in ("in_norm", "post_norm"):
+                mine[key].copy_(theirs[key])
+            for key in ("qkv", "o", "gate_up", "down"):
+                for name, t in mine[key].items():
+                    t.copy_(theirs[key][name])
+
     @staticmethod
     def kv_bytes(cfg: DecoderConfig, batch: int, ctx: int, world: int = 1) -> int:
         """Bytes of one rank's KV cache ([layers, 2, batch, kv_heads / world, ctx, head_dim])."""
@@ -156,6 +182,12 @@ class QuantDecoder:
         # every rank draws the same ids (replicated embedding)
         tg = torch.Generator(device=self.device).manual_seed(seed * 1000 + 11)
         self.tokens = torch.randint(0, cfg.vocab, (batch,), generator=tg, device=self.device)
+        # the per-layer cache [batch, kv_heads, ctx, d] read as a paged cache with one
+        # block of ctx positions per sequence (block table row b = [b])
+        self.block_tables = torch.arange(batch, dtype=torch.int32, device=self.device).view(batch, 1)
+        self.positions = torch.full((batch,), self.ctx - 1, dtype=torch.int32, device=self.device)
+        self.context_lens = torch.full((batch,), self.ctx, dtype=torch.int32, device=self.device)
+        self.attn_ws = DO.AttentionWorkspace()
 
     # ---------------------------------------------------------------- pieces
     def _rms(self, x, w):
@@ -178,6 +210,44 @@ class QuantDecoder:
 
     def logits(self, tokens: Optional[torch.Tensor] = None) -> torch.Tensor:
         """One decode step up to this rank's vocabulary shard of the logits."""
+        return self._logits_fused(tokens) if self.fused else self._logits_torch(tokens)
+
+    def _logits_fused(self, tokens: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """The step on this package's kernels: fused residual add + RMSNorm (with
+        the per-token e4m3 quantisation folded in for FP8), RoPE + KV write,
+        paged GQA decode attention, SiLU * up, and the quantized projections."""
+        cfg, d, B = self.cfg, self.cfg.head_dim, self.batch
+        tok = self.tokens if tokens is None else tokens
+        fp8 = cfg.quant == "fp8"
+        h = self.embed[tok]                                    # [B, H], residual stream
+        half = d // 2
+        cos, sin = self.cos[:half], self.sin[:half]
+        scale = 1.0 / math.sqrt(d)
+        delta = None
+        for li, L in enumerate(self.layers):
+            kc, vc = self.kv[li, 0], self.kv[li, 1]            # [B, hkv, ctx, d]
+            if fp8:
+                xq, sx = DO.rmsnorm_fp8(h, L["in_norm"], cfg.eps, delta)
+                qkv = L["qkv"].forward_prequant(xq, sx)
+            else:
+                qkv = L["qkv"].forward(DO.rmsnorm(h, L["in_norm"], cfg.eps, delta))
+            q = DO.rope_kv_write(qkv, cos, sin, kc, vc, self.block_tables, self.positions,
+                                 self.hq, self.hkv, d)
+            a = DO.paged_attention_decode(q, kc, vc, self.block_tables, self.context_lens,
+                                          self.ctx, scale, kv_head_map=1, workspace=self.attn_ws)
+            o = self._all_reduce(L["o"].forward(a.view(B, self.hq * d)))
+            if fp8:
+                xq, sx = DO.rmsnorm_fp8(h, L["post_norm"], cfg.eps, o)
+                mq, ms = DO.silu_mul_fp8(L["gate_up"].forward_prequant(xq, sx))
+                delta = self._all_reduce(L["down"].forward_prequant(mq, ms))
+            else:
+                gu = L["gate_up"].forward(DO.rmsnorm(h, L["post_norm"], cfg.eps, o))
+                delta = self._all_reduce(L["down"].forward(DO.silu_mul(gu)))
+        r = DO.rmsnorm(h, self.final_norm, cfg.eps, delta)
+        return r @ self.lm_head.t()                            # [B, vocab / world]
+
+    def _logits_torch(self, tokens: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """The same step with the support ops in plain torch (comparison path)."""
         cfg, d, B = self.cfg, self.cfg.head_dim, self.batch
         tok = self.tokens if tokens is None else tokens
         h = self.embed[tok]                                    # [B, H]
@@ -234,6 +304,46 @@ class QuantDecoder:
                 for t in L[key].tensors.values():
                     n += t.numel() * t.element_size()
         return n
+
+
+def assemble_awq_tp(states: list, cfg: DecoderConfig) -> dict:
+    """The tensor-parallelism-1 state equivalent to per-rank AWQ states (rank
+    order): column-parallel projections concatenate their q/k/v (gate/up)
+    column blocks rank by rank, row-parallel ones concatenate their K rows
+    (whole quantisation groups, so the packing stays exact), the LM head and
+    the KV cache concatenate over vocabulary / KV heads."""
+    R, d = len(states), cfg.head_dim
+    hq, hkv, inter = cfg.heads // R, cfg.kv_heads // R, cfg.intermediate // R
+
+    def cols(t, name, widths):
+        # split a column-parallel tensor of one rank into its blocks (in columns of
+        # the output; qweight / qzeros hold 8 columns per word)
+        per = 8 if name in ("qweight", "qzeros") else 1
+        if name in ("weight_q", "weight_scale"):          # FP8 [N, K] / [N]: rows
+            return list(torch.split(t, widths, dim=0))
+        return list(torch.split(t, [w // per for w in widths], dim=1))
+
+    def merge_col(parts_per_rank, name, widths):
+        blocks = [cols(t, name, widths) for t in parts_per_rank]
+        out = [blocks[r][j] for j in range(len(widths)) for r in range(R)]
+        dim = 0 if name in ("weight_q", "weight_scale") else 1
+        return torch.cat(out, dim=dim)
+
+    full = dict(embed=states[0]["embed"], final_norm=states[0]["final_norm"],
+                tokens=states[0]["tokens"],
+                lm_head=torch.cat([s_["lm_head"] for s_ in states], 0),
+                kv=torch.cat([s_["kv"] for s_ in states], 3), layers=[])
+    for li in range(cfg.layers):
+        ls = [s_["layers"][li] for s_ in states]
+        lay = dict(in_norm=ls[0]["in_norm"], post_norm=ls[0]["post_norm"])
+        lay["qkv"] = {n: merge_col([l_["qkv"][n] for l_ in ls], n, [hq * d, hkv * d, hkv * d])
+                      for n in ls[0]["qkv"]}
+        lay["gate_up"] = {n: merge_col([l_["gate_up"][n] for l_ in ls], n, [inter, inter])
+                          for n in ls[0]["gate_up"]}
+        for key in ("o", "down"):
+            lay[key] = {n: torch.cat([l_[key][n] for l_ in ls], 0) for n in ls[0][key]}
+        full["layers"].append(lay)
+    return full
 
 
 def graph_step(dec: QuantDecoder, fn=None, warmup: int = 3):

@@ -264,6 +264,14 @@ class QuantLinearOp:
 
     __call__ = forward
 
+    def forward_prequant(self, xq: torch.Tensor, x_scale: torch.Tensor) -> torch.Tensor:
+        """FP8 only: the activations already quantised per token (e4m3 bytes and
+        fp32 scales, e.g. by a fused norm or activation kernel)."""
+        if self.kind != "fp8":
+            raise DTypeMismatch("forward_prequant applies to FP8 W8A8 projections")
+        t = self.tensors
+        return fp8_linear_prequant(xq, x_scale, t["weight_q"], t["weight_scale"], self._bias)
+
     def weight(self) -> dict:
         return self.tensors
 

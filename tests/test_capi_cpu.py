@@ -1,6 +1,7 @@
 """The C-ABI library on a machine without a GPU: it loads, exports exactly the
-symbols include/lmrs_quant.h declares, and rejects bad arguments with the
-documented status codes before touching the device (no compute is launched)."""
+symbols include/lmrs_quant.h and include/lmrs_decode.h declare, and rejects bad
+arguments with the documented status codes before touching the device (no
+compute is launched)."""
 import ctypes
 import pathlib
 import re
@@ -10,11 +11,11 @@ import pytest
 from lmrs_b200 import _lib
 
 ROOT = pathlib.Path(__file__).resolve().parent.parent
-HEADER = ROOT / "include" / "lmrs_quant.h"
+HEADERS = [ROOT / "include" / "lmrs_quant.h", ROOT / "include" / "lmrs_decode.h"]
 
 
 def header_symbols():
-    text = HEADER.read_text()
+    text = "".join(h.read_text() for h in HEADERS)
     return set(re.findall(r"LMRS_API\s+[\w\s\*]*?\b(lmrs_\w+)\s*\(", text))
 
 

@@ -1,0 +1,189 @@
+"""Decode-step kernels around the quantized linears (include/lmrs_decode.h) on the
+B200, against plain torch fp32 references of the reference's semantics:
+rmsnorm (kernels/ffi/norm_ffi.cu), silu_mul (kernels/ops/activation_kernels.cuh),
+rope (kernels/ffi/pos_embed_ffi.cu) and paged decode attention
+(kernels/attention/paged_attention.cuh).  The FP8 fused forms must equal the
+unfused kernel followed by fp8_quant_rows byte for byte."""
+import math
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+DTS = [torch.bfloat16, torch.float16]
+
+
+def _ulp_close(got, ref, dtype):
+    """got within one unit in the last place of ref (the same fp32 value computed
+    in a different order, rounded once to the I/O type)."""
+    mant = 7 if dtype == torch.bfloat16 else 10
+    r = ref.float()
+    _, e = torch.frexp(r)
+    ulp = torch.ldexp(torch.ones_like(r), e - 1 - mant)
+    diff = (got.float() - r).abs()
+    return bool((diff <= ulp).all()), float((diff / ulp).max())
+
+
+@pytest.mark.parametrize("dtype", DTS)
+@pytest.mark.parametrize("rows,H", [(1, 4096), (7, 8192), (64, 4096), (3, 1032)])
+@pytest.mark.parametrize("with_delta", [False, True])
+def test_rmsnorm(cuda, dtype, rows, H, with_delta):
+    from lmrs_b200 import decode_ops as DO
+    torch.manual_seed(rows + H)
+    x = (torch.randn(rows, H, device=cuda) * 3).to(dtype)
+    w = (1 + 0.1 * torch.randn(H, device=cuda)).to(dtype)
+    d = (torch.randn(rows, H, device=cuda)).to(dtype) if with_delta else None
+    resid = x.clone()
+    y = DO.rmsnorm(resid, w, 1e-5, delta=d)
+    xs = (x.float() + d.float()).to(dtype) if with_delta else x
+    assert torch.equal(resid, xs)  # the residual add rounds once
+    xf = xs.float()
+    ref = (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-5) * w.float()).to(dtype)
+    ok, worst = _ulp_close(y, ref, dtype)
+    assert ok, worst
+
+
+@pytest.mark.parametrize("dtype", DTS)
+@pytest.mark.parametrize("rows,H", [(1, 8192), (32, 4096), (5, 1040)])
+def test_rmsnorm_fp8_equals_unfused(cuda, dtype, rows, H):
+    import lmrs_b200 as L
+    from lmrs_b200 import decode_ops as DO
+    torch.manual_seed(H)
+    x = (torch.randn(rows, H, device=cuda) * 2).to(dtype)
+    x[0] = 0  # all-zero row -> scale 0, bytes 0
+    w = (1 + 0.1 * torch.randn(H, device=cuda)).to(dtype)
+    d = torch.randn(rows, H, device=cuda).to(dtype)
+    r1, r2 = x.clone(), x.clone()
+    q, s = DO.rmsnorm_fp8(r1, w, 1e-5, delta=d)
+    y = DO.rmsnorm(r2, w, 1e-5, delta=d)
+    q_ref, s_ref = L.fp8_quant_rows(y)
+    assert torch.equal(r1, r2)
+    assert torch.equal(s, s_ref) and torch.equal(q, q_ref)
+
+
+@pytest.mark.parametrize("dtype", DTS)
+@pytest.mark.parametrize("rows,inter", [(1, 14336), (16, 7168), (40, 1024), (3, 1032)])
+def test_silu_mul(cuda, dtype, rows, inter):
+    import lmrs_b200 as L
+    from lmrs_b200 import decode_ops as DO
+    torch.manual_seed(inter)
+    gu = (torch.randn(rows, 2 * inter, device=cuda) * 3).to(dtype)
+    y = DO.silu_mul(gu)
+    g, u = gu[:, :inter].float(), gu[:, inter:].float()
+    ref = ((g / (1 + torch.exp(-g))) * u).to(dtype)
+    ok, worst = _ulp_close(y, ref, dtype)
+    assert ok, worst
+    if inter % 16:
+        return  # the standalone quantiser takes K % 16 == 0
+    q, s = DO.silu_mul_fp8(gu)
+    q_ref, s_ref = L.fp8_quant_rows(y)
+    assert torch.equal(s, s_ref) and torch.equal(q, q_ref)
+
+
+def _paged_cache(seqs, hkv, d, block_size, max_blocks, dtype, dev, seed):
+    g = torch.Generator(device=dev).manual_seed(seed)
+    nblocks = seqs * max_blocks + 3
+    kc = torch.randn(nblocks, hkv, block_size, d, generator=g, device=dev).to(dtype)
+    vc = torch.randn(nblocks, hkv, block_size, d, generator=g, device=dev).to(dtype)
+    perm = torch.randperm(nblocks, generator=g, device=dev)[: seqs * max_blocks]
+    tables = perm.view(seqs, max_blocks).to(torch.int32).contiguous()
+    return kc, vc, tables
+
+
+def _gather(cache, tables, s, n, h):
+    """positions [0, n) of sequence s, KV head h -> [n, d]"""
+    bs = cache.shape[2]
+    idx = torch.arange(n, device=cache.device)
+    blk = tables[s, idx // bs].long()
+    return cache[blk, h, idx % bs]
+
+
+@pytest.mark.parametrize("dtype", DTS)
+@pytest.mark.parametrize("seqs,hq,hkv,block_size,lens,kv_map", [
+    (1, 32, 8, 16, [2048], 1),
+    (3, 8, 8, 16, [1, 65, 700], 1),
+    (4, 64, 8, 32, [4096, 100, 0, 33], 1),
+    (2, 16, 1, 16, [513, 64], 1),
+    (2, 8, 2, 16, [77, 300], 0),
+    (64, 32, 8, 2048, [2048] * 64, 1),
+])
+def test_paged_attention_decode(cuda, dtype, seqs, hq, hkv, block_size, lens, kv_map):
+    from lmrs_b200 import decode_ops as DO
+    d = 128
+    max_ctx = max(lens)
+    max_blocks = max(1, (max_ctx + block_size - 1) // block_size)
+    kc, vc, tables = _paged_cache(seqs, hkv, d, block_size, max_blocks, dtype, cuda, seqs + hq)
+    torch.manual_seed(7)
+    q = torch.randn(seqs, hq, d, device=cuda).to(dtype)
+    ctx = torch.tensor(lens, dtype=torch.int32, device=cuda)
+    scale = 1 / math.sqrt(d)
+    out = DO.paged_attention_decode(q, kc, vc, tables, ctx, max_ctx, scale, kv_head_map=kv_map)
+    G = hq // hkv
+    for s in range(seqs):
+        n = lens[s]
+        for h in range(hq):
+            kvh = h // G if kv_map else h % hkv
+            if n == 0:
+                assert torch.all(out[s, h] == 0)
+                continue
+            K = _gather(kc, tables, s, n, kvh).float()
+            V = _gather(vc, tables, s, n, kvh).float()
+            p = torch.softmax(q[s, h].float() @ K.t() * scale, -1)
+            ref = p @ V
+            err = ((out[s, h].float() - ref).abs().max() / ref.abs().max()).item()
+            # P enters the PV MMA in the I/O type (bf16: 8 significant bits)
+            assert err < (2e-2 if dtype == torch.bfloat16 else 4e-3), (s, h, err)
+
+
+@pytest.mark.parametrize("dtype", DTS)
+def test_rope_kv_write(cuda, dtype):
+    from lmrs_b200 import decode_ops as DO
+    seqs, hq, hkv, d, bs, mb = 5, 8, 2, 128, 16, 6
+    kc, vc, tables = _paged_cache(seqs, hkv, d, bs, mb, dtype, cuda, 3)
+    k0, v0 = kc.clone(), vc.clone()
+    torch.manual_seed(3)
+    qkv = torch.randn(seqs, (hq + 2 * hkv) * d, device=cuda).to(dtype)
+    pos = torch.tensor([0, 5, 17, 63, 95], dtype=torch.int32, device=cuda)
+    inv = 1.0 / (500000.0 ** (torch.arange(0, d, 2, device=cuda).float() / d))
+    ang = 37.0 * inv
+    cos, sin = ang.cos().to(dtype), ang.sin().to(dtype)
+    q = DO.rope_kv_write(qkv, cos, sin, kc, vc, tables, pos, hq, hkv, d)
+
+    def rope(x):  # [..., d] rotate-half with the same tables, fp32 math, one rounding
+        x = x.float()
+        half = d // 2
+        c, s_ = cos.float(), sin.float()
+        return torch.cat([x[..., :half] * c - x[..., half:] * s_,
+                          x[..., half:] * c + x[..., :half] * s_], -1).to(dtype)
+
+    qr = rope(qkv[:, : hq * d].view(seqs, hq, d))
+    ok, worst = _ulp_close(q, qr, dtype)
+    assert ok, worst
+    kr = rope(qkv[:, hq * d: (hq + hkv) * d].view(seqs, hkv, d))
+    vr = qkv[:, (hq + hkv) * d:].view(seqs, hkv, d)
+    touched = torch.zeros_like(kc, dtype=torch.bool)
+    for s in range(seqs):
+        p = int(pos[s])
+        blk = int(tables[s, p // bs])
+        ok, worst = _ulp_close(kc[blk, :, p % bs], kr[s], dtype)
+        assert ok, worst
+        assert torch.equal(vc[blk, :, p % bs], vr[s])
+        touched[blk, :, p % bs] = True
+    assert torch.equal(kc[~touched], k0[~touched]) and torch.equal(vc[~touched], v0[~touched])
+
+
+def test_decode_ops_status(cuda):
+    from lmrs_b200 import _lib
+    lib = _lib.load()
+    x = torch.zeros(2, 64, dtype=torch.float32, device=cuda)
+    s = torch.cuda.current_stream().cuda_stream
+    assert lib.lmrs_rmsnorm(x.data_ptr(), x.data_ptr(), None, x.data_ptr(), 2, 64, 1e-5, 2,
+                            s) == _lib.LMRS_ERR_DTYPE
+    assert lib.lmrs_rmsnorm(x.data_ptr(), x.data_ptr(), None, x.data_ptr(), 2, 60, 1e-5, 0,
+                            s) == _lib.LMRS_ERR_SHAPE
+    assert lib.lmrs_paged_attention_decode(x.data_ptr(), x.data_ptr(), x.data_ptr(), x.data_ptr(),
+                                           x.data_ptr(), x.data_ptr(), 1, 8, 8, 64, 16, 1, 16,
+                                           0.1, 1, 0, None, 0, s) == _lib.LMRS_ERR_SHAPE
+    import lmrs_b200 as L
+    assert L.read_device_error() == 0

@@ -26,19 +26,24 @@ def _dense(lin):
 
 def _fake_quant_rows(x):
     """Per-token e4m3 round trip (s = absmax / 448), as the W8A8 path applies to
-    every activation row before its GEMM."""
-    s = x.abs().amax(-1, keepdim=True) / 448.0
-    q = torch.where(s > 0, x / s, torch.zeros_like(x)).to(torch.float8_e4m3fn).float()
-    return q * s
+    every activation row before its GEMM; quantised by the package's quantiser,
+    which the oracle pins bit-exactly (a torch cast of x / s can differ in the
+    last bit of the quotient and so flip e4m3 roundings at ties)."""
+    import lmrs_b200 as L
+    q, s = L.fp8_quant_rows(x.float().contiguous())
+    return q.view(torch.float8_e4m3fn).float() * s[:, None]
 
 
-def _reference_logits(dec):
+def _reference_logits(dec, fake_quant=True, dense=None):
+    """fp32 forward of `dec`'s step.  dense: optional per-layer {projection: fp32
+    [K, N]} replacing the decoder's own (dequantised) projection weights."""
     cfg, d, B = dec.cfg, dec.cfg.head_dim, dec.batch
 
-    def lin(x, op):
-        if op.kind == "fp8":
+    def lin(x, op, li=None, key=None):
+        if op.kind == "fp8" and fake_quant:
             x = _fake_quant_rows(x)
-        return x @ _dense(op)
+        w = dense[li][key] if dense is not None else _dense(op)
+        return x @ w
     pos = dec.ctx - 1
     kv = dec.kv.float().clone()
     cos, sin = dec.cos.float(), dec.sin.float()
@@ -53,17 +58,17 @@ def _reference_logits(dec):
     h = dec.embed[dec.tokens].float()
     for li, L in enumerate(dec.layers):
         r = rms(h, L["in_norm"])
-        qkv = lin(r, L["qkv"])
+        qkv = lin(r, L["qkv"], li, "qkv")
         q = rope(qkv[:, : dec.hq * d].view(B, dec.hq, d))
         k = rope(qkv[:, dec.hq * d: (dec.hq + dec.hkv) * d].view(B, dec.hkv, d))
         v = qkv[:, (dec.hq + dec.hkv) * d:].view(B, dec.hkv, d)
         kv[li, 0][:, :, pos] = k
         kv[li, 1][:, :, pos] = v
         a = F.scaled_dot_product_attention(q.unsqueeze(2), kv[li, 0], kv[li, 1], enable_gqa=True)
-        h = h + lin(a.reshape(B, -1), L["o"])
+        h = h + lin(a.reshape(B, -1), L["o"], li, "o")
         r = rms(h, L["post_norm"])
-        gu = lin(r, L["gate_up"])
-        h = h + lin(F.silu(gu[:, : dec.inter]) * gu[:, dec.inter:], L["down"])
+        gu = lin(r, L["gate_up"], li, "gate_up")
+        h = h + lin(F.silu(gu[:, : dec.inter]) * gu[:, dec.inter:], L["down"], li, "down")
     return rms(h, dec.final_norm) @ dec.lm_head.float().t()
 
 
@@ -91,23 +96,43 @@ def test_decoder_linears_teacher_forced(cuda, quant, batch, monkeypatch):
     cfg = D.DecoderConfig(quant=quant, **TINY)
     dec = D.QuantDecoder(cfg, batch=batch, ctx=64, device=cuda, seed=4)
     calls = []
-    orig = ops.QuantLinearOp.forward
+    orig, orig_pq = ops.QuantLinearOp.forward, ops.QuantLinearOp.forward_prequant
 
     def spy(self, x):
         y = orig(self, x)
-        calls.append((self, x.clone(), y.clone()))
+        xf = x.float()
+        calls.append((self, _fake_quant_rows(xf) if self.kind == "fp8" else xf, y.clone()))
+        return y
+
+    def spy_pq(self, xq, sx):  # fused norm / activation already quantised the rows
+        y = orig_pq(self, xq, sx)
+        calls.append((self, xq.view(torch.float8_e4m3fn).float() * sx[:, None], y.clone()))
         return y
 
     monkeypatch.setattr(ops.QuantLinearOp, "forward", spy)
+    monkeypatch.setattr(ops.QuantLinearOp, "forward_prequant", spy_pq)
     dec.logits()
     assert len(calls) == 4 * cfg.layers
-    for op, x, y in calls:
-        xf = x.float()
-        if op.kind == "fp8":
-            xf = _fake_quant_rows(xf)
+    for op, xf, y in calls:
         ref = xf.double() @ _dense(op).double()  # float64: no TF32 or reduced-precision GEMM
         err = ((y.double() - ref).abs().max() / ref.abs().max()).item()
-        assert err < (5e-3 if op.kind == "awq" else 1e-2), (op.kind, tuple(x.shape), err)
+        assert err < (5e-3 if op.kind == "awq" else 1e-2), (op.kind, tuple(xf.shape), err)
+
+
+@pytest.mark.parametrize("quant,batch", [("awq", 1), ("awq", 17), ("fp8", 1), ("fp8", 40)])
+def test_fused_step_matches_torch_ops(cuda, quant, batch):
+    """The step on the fused decode kernels vs the same step with torch support
+    ops, same weights and cache: the norm rounds once instead of twice and the
+    attention feeds P to the PV MMA in the I/O type, nothing else differs."""
+    cfg = D.DecoderConfig(quant=quant, **TINY)
+    dec = D.QuantDecoder(cfg, batch=batch, ctx=200, device=cuda, seed=6)
+    kv0 = dec.kv.clone()
+    fused = dec.logits().float()
+    dec.kv.copy_(kv0)
+    dec.fused = False
+    ref = dec.logits().float()
+    err = ((fused - ref).abs().max() / ref.abs().max()).item()
+    assert err < (2e-2 if quant == "awq" else 1.5e-1), err
 
 
 def test_decoder_graph_replay_matches_eager(cuda):
