@@ -510,13 +510,13 @@ def run_decode(args, device, dist_on, world, rank):
             sg = torch.cuda.Stream(device)
             sg.wait_stream(stream)
             with torch.cuda.stream(sg):
-                torch.distributed.all_reduce(y, group=pg)
+                dec._all_reduce(y)
             stream.wait_stream(sg)
             torch.cuda.synchronize()
             ga = torch.cuda.CUDAGraph()
             with torch.cuda.graph(ga):
                 for _ in range(2 * cfg.layers):
-                    torch.distributed.all_reduce(y, group=pg)
+                    dec._all_reduce(y)   # the step's own all-reduce path (peer or NCCL)
             ar_ms, _ = _graph_ms(ga, args.steps, args.warmup, stream, dist_on, device)
             del ga
         # e2e: token ids in from pinned host memory, next tokens back, every step
@@ -568,6 +568,8 @@ def run_decode(args, device, dist_on, world, rank):
             "points": points, "clocks": clocks, "peak_hbm_gbs": pk["hbm_gbs"],
             "peak_source": pk_kind,
             "init_s": round(init_s, 1) if dec is not None else None}
+    if dec is not None:
+        dec.close()
     del dec
     return line
 

@@ -1,4 +1,5 @@
-"""ctypes binding of the C-ABI in ``include/lmrs_quant.h`` and ``include/lmrs_decode.h``.
+"""ctypes binding of the C-ABI in ``include/lmrs_quant.h``, ``include/lmrs_decode.h``
+and ``include/lmrs_comm.h``.
 
 This is the Python counterpart of the reference's raw FFI declarations
 (crates/kernels/src/tensor_ops.rs:8-22, crates/kernels/src/raw.rs:53-147): one
@@ -38,7 +39,7 @@ SZ = ctypes.c_size_t
 
 F = ctypes.c_float
 
-# name -> (restype, argtypes); mirrors include/lmrs_quant.h and include/lmrs_decode.h exactly
+# name -> (restype, argtypes); mirrors include/lmrs_{quant,decode,comm}.h exactly
 SIGNATURES = {
     "lmrs_version": (I, []),
     "lmrs_status_string": (ctypes.c_char_p, [I]),
@@ -62,6 +63,14 @@ SIGNATURES = {
     "lmrs_rope_kv_write": (I, [P, P, P, P, P, P, P, P, I, I, I, I, I, I, I, P]),
     "lmrs_paged_attention_workspace_bytes": (SZ, [I, I, I, I]),
     "lmrs_paged_attention_decode": (I, [P, P, P, P, P, P, I, I, I, I, I, I, I, F, I, I, P, SZ, P]),
+    # lmrs_comm.h
+    "lmrs_allreduce_buffer_bytes": (SZ, [I, SZ]),
+    "lmrs_comm_alloc": (I, [ctypes.POINTER(P), SZ]),
+    "lmrs_comm_free": (I, [P]),
+    "lmrs_ipc_get_handle": (I, [P, P, SZ]),
+    "lmrs_ipc_open": (I, [P, ctypes.POINTER(P)]),
+    "lmrs_ipc_close": (I, [P]),
+    "lmrs_allreduce_sum": (I, [P, P, SZ, I, I, I, P, SZ, P]),
 }
 
 

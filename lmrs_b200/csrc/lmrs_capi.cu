@@ -784,3 +784,6 @@ extern "C" int lmrs_fp8_linear_noalloc(void* y, const void* x, const uint8_t* wq
 
 // decode-step kernels around the quantized linears (include/lmrs_decode.h)
 #include "decode_capi.cuh"
+
+// tensor-parallel all-reduce (include/lmrs_comm.h)
+#include "comm_capi.cuh"

@@ -22,6 +22,7 @@ enum : uint32_t {
   kErrWaitAccum = 1u << 2,     // epilogue waiting for the accumulator
   kErrWaitDequant = 1u << 3,   // MMA waiting for the dequantised B stage
   kErrWaitCluster = 1u << 4,   // cluster reduction waiting for peers
+  kErrWaitPeer = 1u << 5,      // all-reduce waiting for another GPU's packets
 };
 
 __device__ uint32_t g_device_error;

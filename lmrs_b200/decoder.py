@@ -91,13 +91,18 @@ class QuantDecoder:
     """One tensor-parallel rank of the decoder (world = 1 for a single GPU)."""
 
     def __init__(self, cfg: DecoderConfig, batch: int, ctx: int, device, rank: int = 0,
-                 world: int = 1, seed: int = 0, group=None, fused: bool = True):
+                 world: int = 1, seed: int = 0, group=None, fused: bool = True,
+                 allreduce: str = "peer"):
         if cfg.heads % world or cfg.intermediate % world or cfg.kv_heads % world:
             raise ValueError(f"tensor parallelism {world} does not divide heads / kv heads / intermediate")
         if cfg.vocab % world:
             raise ValueError(f"vocab {cfg.vocab} not divisible by {world}")
         self.cfg, self.batch, self.ctx = cfg, batch, ctx
         self.fused = fused
+        # row-parallel sums: the package's one-shot NVLink all-reduce ("peer") up to
+        # PEER_MAX_ELEMS elements, NCCL above that or when allreduce == "nccl"
+        self.allreduce_kind = allreduce
+        self.par = None
         self.device = torch.device(device)
         self.rank, self.world, self.pg = rank, world, group
         self.hq, self.hkv = cfg.heads // world, cfg.kv_heads // world
@@ -188,6 +193,12 @@ class QuantDecoder:
         self.positions = torch.full((batch,), self.ctx - 1, dtype=torch.int32, device=self.device)
         self.context_lens = torch.full((batch,), self.ctx, dtype=torch.int32, device=self.device)
         self.attn_ws = DO.AttentionWorkspace()
+        n = batch * cfg.hidden
+        if self.world > 1 and self.allreduce_kind == "peer" and n <= self.PEER_MAX_ELEMS:
+            if self.par is None or self.par.max_elems < n:
+                from .comm import PeerAllReduce
+                self.close()
+                self.par = PeerAllReduce(n, group=self.pg)
 
     # ---------------------------------------------------------------- pieces
     def _rms(self, x, w):
@@ -199,10 +210,21 @@ class QuantDecoder:
         rot = torch.cat([-x[..., half:], x[..., :half]], dim=-1)
         return x * self.cos + rot * self.sin
 
+    PEER_MAX_ELEMS = 1 << 20
+
     def _all_reduce(self, y):
         if self.world > 1:
-            torch.distributed.all_reduce(y, group=self.pg)
+            if self.par is not None and y.numel() <= self.par.max_elems:
+                self.par(y)
+            else:
+                torch.distributed.all_reduce(y, group=self.pg)
         return y
+
+    def close(self):
+        """Release the all-reduce buffers' IPC mappings (before the process group goes)."""
+        if self.par is not None:
+            self.par.close()
+            self.par = None
 
     def step(self, tokens: Optional[torch.Tensor] = None) -> torch.Tensor:
         """One decode step: returns the next token of every sequence."""

@@ -43,6 +43,7 @@ def _worker(rank, world, port, quant, batch, out_path):
         nxt = dec.step()  # exercises the (value, index) all-gather argmax
         state = {k: v for k, v in dec.state().items()}
         cpu = _to_cpu(state)
+        dec.close()
         states = [None] * world
         dist.all_gather_object(states, cpu)
         if rank == 0:
