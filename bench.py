@@ -21,9 +21,17 @@ oracle/ (OpenMP, all host threads) is timed on a bounded sample; where the
 reference's own linear_fwd was compiled (oracle/_ref) its GPU time on the
 dequantised weights is reported next to it.
 
-Multi-GPU (torchrun, one process per GPU): every rank runs the same sweep on
-its own GPU with its own weights (replicas, weak scaling, no collective on the
-data path); timing is the max over ranks.
+The line also carries ``decode``: BASELINE configs 3 and 4, one decode step of
+the Llama-3-8B AWQ and Llama-3-70B FP8 decoders (random weights, KV cache filled
+to the context) on this package's kernels, captured as one CUDA graph, tok/s per
+batch; ``--no-decode`` skips it, ``--decode 8b-awq|70b-fp8`` runs one of them
+alone (``--batch``, ``--ctx``).
+
+Multi-GPU (torchrun, one process per GPU): the config-1 sweep runs on every rank
+with its own weights (replicas, weak scaling, no collective on the data path);
+the decode blocks run tensor parallel over all ranks (column-parallel q/k/v and
+gate/up, row-parallel o and down with the one-shot NVLink all-reduce), so their
+tok/s at N GPUs is strong scaling of a fixed batch.  Timing is the max over ranks.
 """
 from __future__ import annotations
 
@@ -457,18 +465,18 @@ def _graph_ms(g, steps, warmup, stream, dist_on, device):
             max_over_ranks(statistics.median(ts), dist_on, device))
 
 
-def run_decode(args, device, dist_on, world, rank):
+def run_decode(args, device, dist_on, world, rank, preset=None, batches=None, ctx=None):
     """Configs 3/4: one decode step of the Llama-shaped decoder (tensor parallel
-    over the ranks), captured as one CUDA graph (NCCL all-reduces included) and
+    over the ranks), captured as one CUDA graph (all-reduces included) and
     replayed.  tok/s = batch / step time; the linear share replays the step's
     quantized projections alone."""
     from lmrs_b200 import decoder as D
-    attr, ctx, batches, cname = DECODE_PRESETS[args.decode]
+    preset = preset or args.decode
+    attr, ctx0, batches0, cname = DECODE_PRESETS[preset]
     cfg = getattr(D, attr)
-    if args.ctx:
-        ctx = args.ctx
-    if args.batch:
-        batches = tuple(int(b) for b in args.batch.split(","))
+    ctx = ctx or args.ctx or ctx0
+    if batches is None:
+        batches = tuple(int(b) for b in args.batch.split(",")) if args.batch else batches0
     pg = torch.distributed.group.WORLD if dist_on else None
     stream = torch.cuda.current_stream(device)
     total = torch.cuda.get_device_properties(device).total_memory
@@ -561,7 +569,7 @@ def run_decode(args, device, dist_on, world, rank):
             "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
             "dtype": "f16 act, int4 weights" if cfg.quant == "awq" else "bf16 act, e4m3 W8A8",
             "data": "synthetic (random-init weights, random KV cache and token ids)",
-            "config": {"workload": f"{cname}: {args.decode} decoder, one decode step at ctx {ctx}, "
+            "config": {"workload": f"{cname}: {preset} decoder, one decode step at ctx {ctx}, "
                                    f"value = largest batch that fits",
                        "layers": cfg.layers, "hidden": cfg.hidden, "ctx": ctx,
                        "parallelism": f"tp{world}", "l2": "weights + KV per step >> L2"},
@@ -590,6 +598,8 @@ def main():
                          "(tensor parallel over the torchrun ranks)")
     ap.add_argument("--batch", default=None, help="decode batches, comma separated")
     ap.add_argument("--ctx", type=int, default=None, help="decode context length")
+    ap.add_argument("--no-decode", action="store_true",
+                    help="skip the configs 3/4 decode blocks of the default line")
     args = ap.parse_args()
     if args.case:
         run_case(args.case)
@@ -647,6 +657,21 @@ def main():
     res = run_awq(args, device, dist_on, world, rank)
     W = res.pop("_weights")
     res.pop("_peaks")
+    del W
+    torch.cuda.empty_cache()
+    # decode tok/s (configs 3 and 4), tensor parallel over all ranks: every rank
+    # takes part; the blocks land in rank 0's line
+    decode = {}
+    if not args.no_decode:
+        import argparse as _ap
+        dargs = _ap.Namespace(steps=min(args.steps, 20), warmup=args.warmup, ctx=None, batch=None,
+                              decode=None)
+        for preset in ("8b-awq", "70b-fp8"):
+            blk = run_decode(dargs, device, dist_on, world, rank, preset=preset)
+            torch.cuda.empty_cache()
+            decode[blk["metric"]] = {k: blk[k] for k in ("value", "unit", "ms_per_step", "config",
+                                                          "points", "dtype", "scaling")}
+            decode[blk["metric"]]["clocks"] = blk["clocks"]
     if rank == 0:
         line = {"metric": res.pop("metric"), "value": res.pop("value"), "unit": res.pop("unit"),
                 "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
@@ -658,6 +683,8 @@ def main():
             line["cpu_baseline"] = cpu_baseline_awq(nthreads)
         if world == 1 and not args.no_fp8:
             line["fp8_sweep"] = fp8_sweep(device)
+        if decode:
+            line["decode"] = decode
         print(json.dumps(line), flush=True)
     if dist_on:
         torch.distributed.barrier()

@@ -106,7 +106,7 @@ __global__ void __launch_bounds__(kQuantThreads) fp8_quant_rows_kernel(
 __device__ __forceinline__ void mma_e4m3_16832(float (&d)[4], uint32_t a0, uint32_t a1,
                                                uint32_t a2, uint32_t a3, uint32_t b0,
                                                uint32_t b1) {
-  asm volatile(
+  asm(
       "mma.sync.aligned.m16n8k32.row.col.f32.e4m3.e4m3.f32 "
       "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
@@ -126,27 +126,44 @@ constexpr int kF8GemvBoxBytes = kF8GemvRows * 128;  // 64 rows x 128 bytes of K 
 constexpr int kF8GemvThreads = 160;      // 4 consumer warps + 1 producer warp
 constexpr int kF8GemvMaxRing = 4;  // 4 x (8 KB + token tile): 5 CTAs per SM
 
-// MT: 8-token MMA tiles (M <= 8 * MT).  A producer warp streams the strip's
+// The ring area also holds the per-CTA partials [MP tokens][64 channels] fp32
+// once drained; then the receive area [64 channels][MP] fp32 and the barriers.
+__host__ __device__ constexpr int f8_gemv_ring_bytes(int ring, int MT) {
+  return ring * (kF8GemvBoxBytes + 8 * MT * 128) > 8 * MT * kF8GemvRows * 4
+             ? ring * (kF8GemvBoxBytes + 8 * MT * 128)
+             : 8 * MT * kF8GemvRows * 4;
+}
+__host__ __device__ constexpr int f8_gemv_smem_bytes(int ring, int MT) {
+  return 1024 + f8_gemv_ring_bytes(ring, MT) + kF8GemvRows * 8 * MT * 4 + (2 * ring + 1) * 8;
+}
+
+// MT: 8-token MMA tiles (M <= 8 * MT).  A producer thread streams the strip's
 // weight rows (TMA boxes of 128 bytes of K x 64 rows, 128-byte swizzle) into a
-// ring of shared-memory slots; consumer warp w owns MMA tile w (channels
-// 16w..16w+15).  Within each 128-byte K unit, lane (g, t) takes the 16-byte
-// chunks t and 4+t of its two rows: the 32 k-slots of the unit's four MMAs are
-// a fixed permutation of the unit's bytes, and the token fragment (xq, read
-// through L1) uses the same permutation.
+// ring of shared-memory slots, the weights of the first slots before
+// griddepcontrol.wait (programmatic dependent launch) and the token tiles after
+// it; consumer warp w owns MMA tile w (channels 16w..16w+15).  Within each
+// 128-byte K unit, lane (g, t) takes the 16-byte chunks t and 4+t of its two
+// rows: the 32 k-slots of the unit's four MMAs are a fixed permutation of the
+// unit's bytes, and the token fragment uses the same permutation.  Clusters of
+// C CTAs (a power of two) split K; each CTA sends the owner of every channel
+// slice its partial sums with 16-byte st.async into the owner's shared memory
+// (completion counted on the owner's mbarrier), and the owner applies the
+// scales and bias and stores y.
 template <int MT>
-__global__ void __launch_bounds__(kF8GemvThreads, 4) fp8_gemv_kernel(
+__global__ void __launch_bounds__(kF8GemvThreads, MT == 4 ? 3 : 4) fp8_gemv_kernel(
     const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
     __nv_bfloat16* __restrict__ y, const float* __restrict__ sx, const float* __restrict__ sw,
     const __nv_bfloat16* __restrict__ bias, int M, int K, int N, int ring) {
-  pdl_wait();     // activations are the previous kernel's output
-  pdl_trigger();
   constexpr int MP = 8 * MT;
   constexpr int kSlot = kF8GemvBoxBytes + MP * 128;  // weights + token tile (MP rows x 128 B)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* slots = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                               ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(slots + ring * kSlot);
+  const int ring_bytes = f8_gemv_ring_bytes(ring, MT);
+  float* recv = reinterpret_cast<float*>(slots + ring_bytes);         // [C][cw][MP]
+  uint64_t* full = reinterpret_cast<uint64_t*>(recv + kF8GemvRows * MP);
   uint64_t* empty = full + ring;
+  uint64_t* recv_bar = empty + ring;
 
   cg::cluster_group cluster = cg::this_cluster();
   const int C = static_cast<int>(cluster.num_blocks());
@@ -155,6 +172,7 @@ __global__ void __launch_bounds__(kF8GemvThreads, 4) fp8_gemv_kernel(
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
   const int nbase = strip * kF8GemvRows;
+  const int cw = kF8GemvRows / C;  // channels per owner
 
   const int units = (K + 127) >> 7;
   const int u_lo = static_cast<int>((static_cast<long long>(rank) * units) / C);
@@ -166,9 +184,13 @@ __global__ void __launch_bounds__(kF8GemvThreads, 4) fp8_gemv_kernel(
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], 4);  // every consumer warp reads every box
     }
+    mbar_init(recv_bar, 1);
+    mbar_arrive_expect_tx(recv_bar, C * cw * MP * 4);  // every peer's st.async bytes
     fence_mbar_init();
   }
   __syncthreads();
+  cluster_arrive_relaxed();
+  pdl_trigger();
 
   float acc[MT][4];
 #pragma unroll
@@ -180,31 +202,45 @@ __global__ void __launch_bounds__(kF8GemvThreads, 4) fp8_gemv_kernel(
     if (lane == 0) {
       tma_prefetch_desc(&tm_w);
       tma_prefetch_desc(&tm_x);
-      for (int b = 0; b < nbox; ++b) {
-        const int s = b % ring;
-        if (!mbar_wait(&empty[s], ((b / ring) & 1) ^ 1, kErrWaitEmpty)) break;
+      const int pre = nbox < ring ? nbox : ring;
+      for (int b = 0; b < pre; ++b) {
+        mbar_arrive_expect_tx(&full[b], kSlot);
+        tma_load_2d(&tm_w, &full[b], slots + b * kSlot, (u_lo + b) * 128, nbase);
+      }
+      pdl_wait();  // the quantised tokens are the previous kernel's output
+      for (int b = 0; b < pre; ++b)
+        tma_load_2d(&tm_x, &full[b], slots + b * kSlot + kF8GemvBoxBytes, (u_lo + b) * 128, 0);
+      int s = 0;
+      uint32_t ph = 0;
+      for (int b = pre; b < nbox; ++b) {
+        if (!mbar_wait(&empty[s], ph, kErrWaitEmpty)) break;
         mbar_arrive_expect_tx(&full[s], kSlot);
         tma_load_2d(&tm_w, &full[s], slots + s * kSlot, (u_lo + b) * 128, nbase);
         tma_load_2d(&tm_x, &full[s], slots + s * kSlot + kF8GemvBoxBytes, (u_lo + b) * 128, 0);
+        if (++s == ring) {
+          s = 0;
+          ph ^= 1;
+        }
       }
     }
   } else {
     const int r0 = 16 * warp + g;  // rows r0 and r0 + 8 of the box; (r0 % 8) == g
+    int slot = 0;
+    uint32_t ph = 0;
     for (int b = 0; b < nbox; ++b) {
-      const int slot = b % ring;
-      if (!mbar_wait(&full[slot], (b / ring) & 1, kErrWaitFull)) break;
-      const uint32_t sb = smem_u32(slots + slot * kSlot);
+      if (!mbar_wait(&full[slot], ph, kErrWaitFull)) break;
+      const uint8_t* sb = slots + slot * kSlot;
       // 128-byte swizzle: chunk c of row r sits at chunk c ^ (r % 8)
-      const uint4 ga = lds_u4(sb + r0 * 128 + ((t ^ g) << 4));
-      const uint4 gc = lds_u4(sb + r0 * 128 + (((4 + t) ^ g) << 4));
-      const uint4 ha = lds_u4(sb + (r0 + 8) * 128 + ((t ^ g) << 4));
-      const uint4 hc = lds_u4(sb + (r0 + 8) * 128 + (((4 + t) ^ g) << 4));
+      const uint4 ga = *reinterpret_cast<const uint4*>(sb + r0 * 128 + ((t ^ g) << 4));
+      const uint4 gc = *reinterpret_cast<const uint4*>(sb + r0 * 128 + (((4 + t) ^ g) << 4));
+      const uint4 ha = *reinterpret_cast<const uint4*>(sb + (r0 + 8) * 128 + ((t ^ g) << 4));
+      const uint4 hc = *reinterpret_cast<const uint4*>(sb + (r0 + 8) * 128 + (((4 + t) ^ g) << 4));
       uint4 xb[MT][2];
 #pragma unroll
       for (int mt = 0; mt < MT; ++mt) {
-        const uint32_t xr = sb + kF8GemvBoxBytes + (mt * 8 + g) * 128;  // token rows >= M are zero
-        xb[mt][0] = lds_u4(xr + ((t ^ g) << 4));
-        xb[mt][1] = lds_u4(xr + (((4 + t) ^ g) << 4));
+        const uint8_t* xr = sb + kF8GemvBoxBytes + (mt * 8 + g) * 128;  // rows >= M are zero
+        xb[mt][0] = *reinterpret_cast<const uint4*>(xr + ((t ^ g) << 4));
+        xb[mt][1] = *reinterpret_cast<const uint4*>(xr + (((4 + t) ^ g) << 4));
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[slot]);
@@ -220,13 +256,18 @@ __global__ void __launch_bounds__(kF8GemvThreads, 4) fp8_gemv_kernel(
           mma_e4m3_16832(acc[mt], a0, a1, a2, a3, hi ? xv.z : xv.x, hi ? xv.w : xv.y);
         }
       }
+      if (++slot == ring) {
+        slot = 0;
+        ph ^= 1;
+      }
     }
   }
 
-  // ---- partials in the drained ring: red[m][row], rows 0..63 of the strip
-  float* red = reinterpret_cast<float*>(slots);
+  // ---- partials in the drained ring: red[w][m][row 0..63], then to the owners
+  float* red = reinterpret_cast<float*>(slots);  // rows of warp w only in red[w]
+  cluster_wait_acquire();  // peers have initialised their receive barriers
   if (warp < 4) {
-    asm volatile("bar.sync 1, 128;" ::: "memory");
+    asm volatile("bar.sync 1, 128;" ::: "memory");  // the ring is drained
 #pragma unroll
     for (int mt = 0; mt < MT; ++mt) {
       const int ch = 16 * warp + g;
@@ -236,24 +277,35 @@ __global__ void __launch_bounds__(kF8GemvThreads, 4) fp8_gemv_kernel(
       red[(m0 + 0) * kF8GemvRows + ch + 8] = acc[mt][2];
       red[(m0 + 1) * kF8GemvRows + ch + 8] = acc[mt][3];
     }
-  }
-  cluster.sync();
-  const int c0 = (rank * kF8GemvRows) / C, c1 = ((rank + 1) * kF8GemvRows) / C;
-  const int ncol = c1 - c0;
-  for (int e = threadIdx.x; e < M * ncol; e += blockDim.x) {
-    const int m = e / ncol;
-    const int ch = c0 + (e - m * ncol);
-    const int n = nbase + ch;
-    float s = 0.f;
-    for (int r = 0; r < C; ++r) s += cluster.map_shared_rank(red, r)[m * kF8GemvRows + ch];
-    if (n < N) {
-      float v = __fmul_rn(__fmul_rn(s, sx[m]), sw[n]);
-      if (bias != nullptr) v = __fadd_rn(v, __bfloat162float(bias[n]));
-      y[static_cast<int64_t>(m) * N + n] = __float2bfloat16_rn(v);
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+    // (channel, 4 tokens) -> owner r = channel / cw, recv[rank][channel - r*cw][tokens]
+    for (int e = threadIdx.x; e < kF8GemvRows * (MP / 4); e += 128) {
+      const int ch = e / (MP / 4), m4 = (e - ch * (MP / 4)) * 4;
+      const int r = ch / cw, cl = ch - r * cw;
+      const float4 v = make_float4(red[(m4 + 0) * kF8GemvRows + ch], red[(m4 + 1) * kF8GemvRows + ch],
+                                   red[(m4 + 2) * kF8GemvRows + ch], red[(m4 + 3) * kF8GemvRows + ch]);
+      st_async_v4(mapa_shared(smem_u32(recv + (rank * cw + cl) * MP + m4), static_cast<uint32_t>(r)),
+                  v, mapa_shared(smem_u32(recv_bar), static_cast<uint32_t>(r)));
     }
+    // ---- owner: sum the C slices in rank order, scale, bias, store
+    const bool ok = mbar_wait_cluster(recv_bar, 0, kErrWaitCluster);
+    pdl_wait();
+    if (ok) {
+      for (int e = threadIdx.x; e < M * cw; e += 128) {
+        const int m = e / cw, cl = e - m * cw;
+        const int n = nbase + rank * cw + cl;
+        float s = 0.f;
+        for (int q = 0; q < C; ++q) s += recv[(q * cw + cl) * MP + m];
+        if (n < N) {
+          float v = __fmul_rn(__fmul_rn(s, sx[m]), sw[n]);
+          if (bias != nullptr) v = __fadd_rn(v, __bfloat162float(bias[n]));
+          y[static_cast<int64_t>(m) * N + n] = __float2bfloat16_rn(v);
+        }
+      }
+    }
+  } else {
+    pdl_wait();
   }
-  cluster.sync();
-  (void)MP;
 }
 
 }  // namespace lmrs

@@ -461,14 +461,15 @@ int fp8_gemv_launch(__nv_bfloat16* y, const uint8_t* xq, const float* sx, const 
                     cudaStream_t stream, int dev) {
   const int strips = (N + lmrs::kF8GemvRows - 1) / lmrs::kF8GemvRows;
   const int units = (K + 127) / 128;
-  const int C = gemv_cluster(strips, units, g_tune.fp8_gemv_cluster);
+  // power-of-two cluster: the owner slices of the 64 channels are equal
+  int C = pow2_floor(gemv_cluster(strips, units, g_tune.fp8_gemv_cluster));
+  while (C > 1 && C > units) C /= 2;
   const int per_cta = (units + C - 1) / C;
   const int MT = M <= 8 ? 1 : (M <= 16 ? 2 : 4);
-  const int slot = lmrs::kF8GemvBoxBytes + 8 * MT * 128;
   const int max_ring = lmrs::kF8GemvMaxRing;
   int ring = per_cta < max_ring ? per_cta : max_ring;
   if (ring < 1) ring = 1;
-  const int smem = 1024 + ring * slot + ring * 16;
+  const int smem = lmrs::f8_gemv_smem_bytes(ring, MT);
   CUtensorMap tw, tx;
   int rc;
   if ((rc = make_tmap(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, wq, K, N, uint64_t(K), 128,
