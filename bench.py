@@ -371,6 +371,19 @@ def run_case(case, launches=3):
         ws = L.Workspace()
         for _ in range(launches):
             L.fp8_linear(x, wq, sw, None, ws)
+    elif kind == "attn":
+        # paged decode attention: batch, q heads, KV heads, context (grouped heads)
+        import math
+        from lmrs_b200 import decode_ops as DO
+        B, hq, hkv, ctx = (int(v) for v in dims)
+        kc = torch.randn(B, hkv, ctx, 128, device=dev).bfloat16()
+        vc = torch.randn_like(kc)
+        q = torch.randn(B, hq, 128, device=dev).bfloat16()
+        tables = torch.arange(B, dtype=torch.int32, device=dev).view(B, 1)
+        lens = torch.full((B,), ctx, dtype=torch.int32, device=dev)
+        ws = DO.AttentionWorkspace()
+        for _ in range(launches):
+            DO.paged_attention_decode(q, kc, vc, tables, lens, ctx, 1 / math.sqrt(128), 1, ws)
     else:
         raise SystemExit(f"unknown case {case}")
     torch.cuda.synchronize()
@@ -592,7 +605,8 @@ def main():
     ap.add_argument("--no-fp8", action="store_true", help="skip the config-2 FP8 context sweep")
     ap.add_argument("--case", default=None,
                     help="profiling mode: run a few launches of one case and exit, e.g. "
-                         "awq:4096 (config-1 shape, M=4096) or fp8:8192:4096:28672 (M:K:N)")
+                         "awq:4096 (config-1 shape, M=4096), fp8:8192:4096:28672 (M:K:N) or "
+                         "attn:64:32:8:2048 (paged decode attention B:q heads:KV heads:ctx)")
     ap.add_argument("--decode", choices=sorted(DECODE_PRESETS), default=None,
                     help="configs 3/4: decode tok/s of the 8B AWQ or 70B FP8 decoder "
                          "(tensor parallel over the torchrun ranks)")

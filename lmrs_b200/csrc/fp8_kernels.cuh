@@ -126,12 +126,12 @@ constexpr int kF8GemvBoxBytes = kF8GemvRows * 128;  // 64 rows x 128 bytes of K 
 constexpr int kF8GemvThreads = 160;      // 4 consumer warps + 1 producer warp
 constexpr int kF8GemvMaxRing = 4;  // 4 x (8 KB + token tile): 5 CTAs per SM
 
-// The ring area also holds the per-CTA partials [MP tokens][64 channels] fp32
+// The ring area also holds the per-CTA partials [64 channels][MP + 4] fp32
 // once drained; then the receive area [64 channels][MP] fp32 and the barriers.
 __host__ __device__ constexpr int f8_gemv_ring_bytes(int ring, int MT) {
-  return ring * (kF8GemvBoxBytes + 8 * MT * 128) > 8 * MT * kF8GemvRows * 4
+  return ring * (kF8GemvBoxBytes + 8 * MT * 128) > (8 * MT + 4) * kF8GemvRows * 4
              ? ring * (kF8GemvBoxBytes + 8 * MT * 128)
-             : 8 * MT * kF8GemvRows * 4;
+             : (8 * MT + 4) * kF8GemvRows * 4;
 }
 __host__ __device__ constexpr int f8_gemv_smem_bytes(int ring, int MT) {
   return 1024 + f8_gemv_ring_bytes(ring, MT) + kF8GemvRows * 8 * MT * 4 + (2 * ring + 1) * 8;
@@ -263,8 +263,11 @@ __global__ void __launch_bounds__(kF8GemvThreads, MT == 4 ? 3 : 4) fp8_gemv_kern
     }
   }
 
-  // ---- partials in the drained ring: red[w][m][row 0..63], then to the owners
-  float* red = reinterpret_cast<float*>(slots);  // rows of warp w only in red[w]
+  // ---- partials in the drained ring: red[channel][token] (row pitch MP + 4
+  // floats: 16-byte aligned, and the 8 channels g of a fragment store land in
+  // distinct banks), then to the owners
+  constexpr int kPitch = MP + 4;
+  float* red = reinterpret_cast<float*>(slots);
   cluster_wait_acquire();  // peers have initialised their receive barriers
   if (warp < 4) {
     asm volatile("bar.sync 1, 128;" ::: "memory");  // the ring is drained
@@ -272,18 +275,17 @@ __global__ void __launch_bounds__(kF8GemvThreads, MT == 4 ? 3 : 4) fp8_gemv_kern
     for (int mt = 0; mt < MT; ++mt) {
       const int ch = 16 * warp + g;
       const int m0 = mt * 8 + 2 * t;
-      red[(m0 + 0) * kF8GemvRows + ch] = acc[mt][0];
-      red[(m0 + 1) * kF8GemvRows + ch] = acc[mt][1];
-      red[(m0 + 0) * kF8GemvRows + ch + 8] = acc[mt][2];
-      red[(m0 + 1) * kF8GemvRows + ch + 8] = acc[mt][3];
+      red[ch * kPitch + m0] = acc[mt][0];
+      red[ch * kPitch + m0 + 1] = acc[mt][1];
+      red[(ch + 8) * kPitch + m0] = acc[mt][2];
+      red[(ch + 8) * kPitch + m0 + 1] = acc[mt][3];
     }
     asm volatile("bar.sync 1, 128;" ::: "memory");
     // (channel, 4 tokens) -> owner r = channel / cw, recv[rank][channel - r*cw][tokens]
     for (int e = threadIdx.x; e < kF8GemvRows * (MP / 4); e += 128) {
       const int ch = e / (MP / 4), m4 = (e - ch * (MP / 4)) * 4;
       const int r = ch / cw, cl = ch - r * cw;
-      const float4 v = make_float4(red[(m4 + 0) * kF8GemvRows + ch], red[(m4 + 1) * kF8GemvRows + ch],
-                                   red[(m4 + 2) * kF8GemvRows + ch], red[(m4 + 3) * kF8GemvRows + ch]);
+      const float4 v = *reinterpret_cast<const float4*>(red + ch * kPitch + m4);
       st_async_v4(mapa_shared(smem_u32(recv + (rank * cw + cl) * MP + m4), static_cast<uint32_t>(r)),
                   v, mapa_shared(smem_u32(recv_bar), static_cast<uint32_t>(r)));
     }
