@@ -29,6 +29,7 @@
 #include "lmrs_ptx.cuh"
 #include "tc_gemm.cuh"
 #include "tc_gemm2.cuh"
+#include "fp8_swap.cuh"
 
 namespace {
 
@@ -40,7 +41,9 @@ thread_local int t_last_cuda_error = 0;
 struct Tuning {
   int awq_gemv_max_m = 16;   // M up to this -> register-dequant GEMV (16 at most)
   int awq_swap_max_m = 64;   // M up to this -> swap-AB split-K tcgen05; above -> tile GEMM
-  int fp8_gemv_max_m = 32;
+  int fp8_gemv_max_m = 8;    // M up to this -> register-fed FP8 GEMV
+  int fp8_swap_max_m = 64;   // M up to this -> swap-AB tcgen05 FP8 (64 at most)
+  int fp8_swap_cluster = 0;  // 0 = heuristic
   int gemv_ctas_per_sm = 4;  // resident CTAs per SM the GEMV grids are sized for
   int awq_gemv_cluster = 0;  // 0 = heuristic
   int awq_swap_cluster = 0;  // 0 = heuristic
@@ -495,6 +498,45 @@ int fp8_gemv_launch(__nv_bfloat16* y, const uint8_t* xq, const float* sx, const 
 }
 
 std::atomic<int> g_smem_f8_gemm224[kMaxDevices];
+std::atomic<int> g_smem_f8_swap[3][kMaxDevices];
+
+template <int NT, int ST>
+int fp8_swap_launch_t(__nv_bfloat16* y, const uint8_t* xq, const float* sx, const uint8_t* wq,
+                      const float* sw, const __nv_bfloat16* bias, int M, int K, int N,
+                      cudaStream_t stream, int dev, std::atomic<int>* done) {
+  const int strips = (N + lmrs::kFsRows - 1) / lmrs::kFsRows;
+  const int units = (K + lmrs::kFsBK - 1) / lmrs::kFsBK;
+  int C = g_tune.fp8_swap_cluster > 0 ? g_tune.fp8_swap_cluster
+                                      : (2 * sm_count(dev)) / (strips > 0 ? strips : 1);
+  C = pow2_floor(clampi(C, 1, lmrs::kFsMaxCluster));
+  while (C > 1 && C > units) C /= 2;
+  CUtensorMap tw, tx;
+  int rc;
+  if ((rc = make_tmap(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, wq, K, N, uint64_t(K), lmrs::kFsBK,
+                      lmrs::kFsRows, CU_TENSOR_MAP_SWIZZLE_128B)))
+    return rc;
+  if ((rc = make_tmap(&tx, CU_TENSOR_MAP_DATA_TYPE_UINT8, xq, K, M, uint64_t(K), lmrs::kFsBK, NT,
+                      CU_TENSOR_MAP_SWIZZLE_128B)))
+    return rc;
+  constexpr int smem = lmrs::FsLayout<NT, ST>::kSmem;
+  if ((rc = ensure_smem(lmrs::fp8_swap_kernel<NT, ST>, smem, done, dev))) return rc;
+  rc = launch_ex(lmrs::fp8_swap_kernel<NT, ST>, strips * C, C, lmrs::kFsThreads, smem, stream, tw,
+                 tx, y, sx, sw, bias, M, K, N);
+  return rc ? rc : after_launch();
+}
+
+int fp8_swap_launch(__nv_bfloat16* y, const uint8_t* xq, const float* sx, const uint8_t* wq,
+                    const float* sw, const __nv_bfloat16* bias, int M, int K, int N,
+                    cudaStream_t stream, int dev) {
+  if (M <= 16)
+    return fp8_swap_launch_t<16, 5>(y, xq, sx, wq, sw, bias, M, K, N, stream, dev,
+                                    g_smem_f8_swap[0]);
+  if (M <= 32)
+    return fp8_swap_launch_t<32, 4>(y, xq, sx, wq, sw, bias, M, K, N, stream, dev,
+                                    g_smem_f8_swap[1]);
+  return fp8_swap_launch_t<64, 3>(y, xq, sx, wq, sw, bias, M, K, N, stream, dev,
+                                  g_smem_f8_swap[2]);
+}
 
 template <int BN>
 int fp8_gemm_launch_bn(__nv_bfloat16* y, const uint8_t* xq, const float* sx, const uint8_t* wq,
@@ -525,6 +567,12 @@ int fp8_gemm_launch(__nv_bfloat16* y, const uint8_t* xq, const float* sx, const 
   return fp8_gemm_launch_bn<256>(y, xq, sx, wq, sw, bias, M, K, N, stream, dev, g_smem_f8_gemm);
 }
 
+// The tile GEMM's epilogue stores 8 channels at a time (N % 8 == 0); the GEMV
+// and swap-AB kernels store single channels.
+bool fp8_uses_gemm(int M) {
+  return !(M <= g_tune.fp8_gemv_max_m && M <= 32) && !(M <= g_tune.fp8_swap_max_m && M <= 64);
+}
+
 int fp8_linear_prequant_impl(void* y, const uint8_t* xq, const float* x_scale, const uint8_t* wq,
                              const float* w_scale, const void* bias, int M, int K, int N,
                              cudaStream_t stream, int dev) {
@@ -532,6 +580,8 @@ int fp8_linear_prequant_impl(void* y, const uint8_t* xq, const float* x_scale, c
   auto* bb = static_cast<const __nv_bfloat16*>(bias);
   if (M <= g_tune.fp8_gemv_max_m && M <= 32)
     return fp8_gemv_launch(yb, xq, x_scale, wq, w_scale, bb, M, K, N, stream, dev);
+  if (M <= g_tune.fp8_swap_max_m && M <= 64)
+    return fp8_swap_launch(yb, xq, x_scale, wq, w_scale, bb, M, K, N, stream, dev);
   return fp8_gemm_launch(yb, xq, x_scale, wq, w_scale, bb, M, K, N, stream, dev);
 }
 
@@ -595,6 +645,8 @@ int lmrs_set_tuning(const char* key, int value) {
   else if (!strcmp(key, "attn_stages")) g_tune.attn_stages = value;
   else if (!strcmp(key, "attn_ctas_per_sm")) g_tune.attn_ctas_per_sm = value;
   else if (!strcmp(key, "fp8_gemv_cluster")) g_tune.fp8_gemv_cluster = value;
+  else if (!strcmp(key, "fp8_swap_max_m")) g_tune.fp8_swap_max_m = value;
+  else if (!strcmp(key, "fp8_swap_cluster")) g_tune.fp8_swap_cluster = value;
   else return LMRS_ERR_SHAPE;
   return LMRS_OK;
 }
@@ -701,7 +753,7 @@ int lmrs_fp8_linear_prequant(void* y, const uint8_t* xq, const float* x_scale, c
       (reinterpret_cast<uintptr_t>(x_scale) & 3u) || (reinterpret_cast<uintptr_t>(w_scale) & 3u) ||
       (reinterpret_cast<uintptr_t>(bias_or_null) & 1u))
     return LMRS_ERR_ALIGN;
-  if (N % 8 && M > g_tune.fp8_gemv_max_m) return LMRS_ERR_SHAPE;  // GEMM epilogue stores
+  if (N % 8 && fp8_uses_gemm(M)) return LMRS_ERR_SHAPE;  // GEMM epilogue stores
   int dev = 0;
   int rc = check_device(&dev);
   if (rc) return rc;
@@ -721,7 +773,7 @@ int lmrs_fp8_linear(void* y, const void* x, const uint8_t* wq, const float* w_sc
       (reinterpret_cast<uintptr_t>(y) & 3u) || (reinterpret_cast<uintptr_t>(w_scale) & 3u) ||
       (reinterpret_cast<uintptr_t>(bias_or_null) & 1u))
     return LMRS_ERR_ALIGN;
-  if (N % 8 && M > g_tune.fp8_gemv_max_m) return LMRS_ERR_SHAPE;
+  if (N % 8 && fp8_uses_gemm(M)) return LMRS_ERR_SHAPE;
   int dev = 0;
   int rc = check_device(&dev);
   if (rc) return rc;
@@ -770,7 +822,7 @@ extern "C" int lmrs_fp8_linear_noalloc(void* y, const void* x, const uint8_t* wq
       (reinterpret_cast<uintptr_t>(w_scale) & 3u) ||
       (reinterpret_cast<uintptr_t>(bias_or_null) & 1u))
     return LMRS_ERR_ALIGN;
-  if (N % 8 && M > g_tune.fp8_gemv_max_m) return LMRS_ERR_SHAPE;
+  if (N % 8 && fp8_uses_gemm(M)) return LMRS_ERR_SHAPE;
   int dev = 0;
   int rc = check_device(&dev);
   if (rc) return rc;

@@ -185,3 +185,52 @@ def test_gemm_tile_widths(cuda, bn):
     y_ref, _, _ = O.c_fp8_linear(f["x_bf16"], wq_ref, sw_ref, f["bias_bf16"])
     err = O.max_rel_err(O.bf16_bits_to_f32(bits16(y)), O.bf16_bits_to_f32(y_ref))
     assert err < TIGHT, err
+
+
+def _fp8_case(dev, M, K, N, seed, bias):
+    import lmrs_b200 as L
+    f = O.fp8_inputs(M, K, N, seed=seed, with_bias=bias)
+    x, w, b = _dev_fp8(f, dev, bias)
+    wq, sw = L.quantize_fp8_weight(w)
+    y = L.fp8_linear(x, wq, sw, b)
+    wq_ref, sw_ref = O.c_fp8_quant_rows(f["w_bf16"], 0)
+    y_ref, _, _ = O.c_fp8_linear(f["x_bf16"], wq_ref, sw_ref, f["bias_bf16"])
+    return O.max_rel_err(O.bf16_bits_to_f32(bits16(y)), O.bf16_bits_to_f32(y_ref))
+
+
+@pytest.mark.parametrize("M", [9, 16, 17, 31, 32, 33, 48, 64])
+@pytest.mark.parametrize("K,N", [(1024, 640), (1040, 1000), (2176, 1001)])
+@pytest.mark.parametrize("bias", [False, True])
+def test_linear_swap_ab(cuda, M, K, N, bias):
+    """9..64 tokens: the swap-AB tcgen05 kernel (weights as the MMA's 128-row
+    operand); ragged K (not a multiple of 128), ragged N (not a multiple of the
+    128-channel strip, odd N: single-channel stores)."""
+    err = _fp8_case(cuda, M, K, N, 1000 + M + K + N, bias)
+    assert err < TIGHT, err
+
+
+@pytest.mark.parametrize("C", [1, 2, 4, 8])
+@pytest.mark.parametrize("M", [12, 40])
+def test_linear_swap_ab_clusters(cuda, C, M):
+    """Every split-K cluster size of the swap-AB kernel, including K ranges that
+    do not divide evenly (17 K units over C CTAs)."""
+    import lmrs_b200 as L
+    try:
+        L.set_tuning("fp8_swap_cluster", C)
+        err = _fp8_case(cuda, M, 17 * 128, 384, 77 + C, True)
+    finally:
+        L.set_tuning("fp8_swap_cluster", 0)
+    assert err < TIGHT, err
+
+
+@pytest.mark.parametrize("M", [9, 20, 32])
+def test_linear_gemv_wide_opt_in(cuda, M):
+    """The register-fed GEMV for 9..32 tokens (off by default since the swap-AB
+    kernel took that range) stays correct when selected."""
+    import lmrs_b200 as L
+    try:
+        L.set_tuning("fp8_gemv_max_m", 32)
+        err = _fp8_case(cuda, M, 1024, 640, 5 + M, True)
+    finally:
+        L.set_tuning("fp8_gemv_max_m", 8)
+    assert err < TIGHT, err
