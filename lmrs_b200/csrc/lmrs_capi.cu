@@ -30,6 +30,7 @@
 #include "tc_gemm.cuh"
 #include "tc_gemm2.cuh"
 #include "fp8_swap.cuh"
+#include "awq_tmem.cuh"
 
 namespace {
 
@@ -41,7 +42,8 @@ thread_local int t_last_cuda_error = 0;
 struct Tuning {
   int awq_gemv_max_m = 16;   // M up to this -> register-dequant GEMV (16 at most)
   int awq_swap_max_m = 64;   // M up to this -> swap-AB split-K tcgen05; above -> tile GEMM
-  int fp8_gemv_max_m = 8;    // M up to this -> register-fed FP8 GEMV
+  int fp8_gemv_max_m = 8;    // M up to this (and K*N up to fp8_gemv_max_kn) -> register-fed FP8 GEMV
+  int fp8_gemv_max_kn = 1 << 25;  // larger weights: the swap-AB kernel streams faster
   int fp8_swap_max_m = 64;   // M up to this -> swap-AB tcgen05 FP8 (64 at most)
   int fp8_swap_cluster = 0;  // 0 = heuristic
   int gemv_ctas_per_sm = 4;  // resident CTAs per SM the GEMV grids are sized for
@@ -57,6 +59,11 @@ struct Tuning {
   int awq_gemv4_slots = 4;   // its ring slots (4 or 8)
   int attn_stages = 3;       // decode attention cp.async ring depth (2..4)
   int attn_ctas_per_sm = 2;  // decode attention context split target
+  int awq_tmem_min_m = 17;   // TMEM-staged tcgen05 AWQ linear for M in [min, max];
+  int awq_tmem_max_m = 32;   // its cost is flat in M (32 at most)
+  int awq_tmem_wide_n = 12288;  // ... and down to M = 9 when N is at least this
+  int awq_tmem_cluster = 0;  // 0 = heuristic
+  int awq_tmem_ctas_per_sm = 2;
 };
 Tuning g_tune;
 
@@ -252,6 +259,59 @@ int awq_gemv4_launch_t(const CUtensorMap& tq, const CUtensorMap& tx, const CUten
   rc = launch_ex(lmrs::awq_gemv4_kernel<BR>, strips * C, C, lmrs::kAwqGemv4Threads, smem, stream,
                  tq, tx, ts, tz, y, bias, M, K, N, group, S);
   return rc ? rc : after_launch();
+}
+
+std::atomic<int> g_smem_awq_tmem[3][kMaxDevices];
+
+template <int NT>
+int awq_tmem_launch_t(__half* y, const __half* x, const int32_t* qw, const int32_t* qz,
+                      const __half* sc, const __half* bias, int M, int K, int N, int group,
+                      cudaStream_t stream, int dev, std::atomic<int>* done) {
+  using L = lmrs::AtLayout<NT>;
+  const int strips = (N + lmrs::kAtCols - 1) / lmrs::kAtCols;
+  const int nb_all = K / lmrs::kAtRows;
+  int C = g_tune.awq_tmem_cluster > 0
+              ? g_tune.awq_tmem_cluster
+              : (g_tune.awq_tmem_ctas_per_sm * sm_count(dev)) / (strips > 0 ? strips : 1);
+  C = pow2_floor(clampi(C, 1, lmrs::kAtMaxCluster));
+  while (C > 1 && C > nb_all) C /= 2;
+  CUtensorMap tq, tx, ts, tz;
+  int rc;
+  if ((rc = make_tmap(&tq, CU_TENSOR_MAP_DATA_TYPE_INT32, qw, N / 8, K, uint64_t(N / 8) * 4,
+                      lmrs::kAtWords, lmrs::kAtRows, CU_TENSOR_MAP_SWIZZLE_NONE)))
+    return rc;
+  if ((rc = make_tmap(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, x, K, M, uint64_t(K) * 2, 64, NT,
+                      CU_TENSOR_MAP_SWIZZLE_128B)))
+    return rc;
+  if ((rc = make_tmap(&ts, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, sc, N, K / group, uint64_t(N) * 2,
+                      lmrs::kAtCols, 1, CU_TENSOR_MAP_SWIZZLE_NONE)))
+    return rc;
+  if ((rc = make_tmap(&tz, CU_TENSOR_MAP_DATA_TYPE_INT32, qz, N / 8, K / group,
+                      uint64_t(N / 8) * 4, lmrs::kAtWords, 1, CU_TENSOR_MAP_SWIZZLE_NONE)))
+    return rc;
+  constexpr int smem = L::kSmem;
+  if ((rc = ensure_smem(lmrs::awq_tmem_kernel<NT>, smem, done, dev))) return rc;
+  rc = launch_ex(lmrs::awq_tmem_kernel<NT>, strips * C, C, lmrs::kAtThreads, smem, stream, tq, tx,
+                 ts, tz, y, bias, M, K, N, group);
+  return rc ? rc : after_launch();
+}
+
+// 9..16 tokens: the register-fed GEMV is faster unless N is wide; 17..32: the
+// TMEM-staged kernel (flat in M) beats both the GEMV and the swap-AB kernel.
+bool awq_use_tmem(int M, int N) {
+  if (M > g_tune.awq_tmem_max_m || M > 32) return false;
+  if (M >= g_tune.awq_tmem_min_m) return true;
+  return M >= 9 && g_tune.awq_tmem_wide_n > 0 && N >= g_tune.awq_tmem_wide_n;
+}
+
+int awq_tmem_launch(__half* y, const __half* x, const int32_t* qw, const int32_t* qz,
+                    const __half* sc, const __half* bias, int M, int K, int N, int group,
+                    cudaStream_t stream, int dev) {
+  if (M <= 16)
+    return awq_tmem_launch_t<16>(y, x, qw, qz, sc, bias, M, K, N, group, stream, dev,
+                                 g_smem_awq_tmem[0]);
+  return awq_tmem_launch_t<32>(y, x, qw, qz, sc, bias, M, K, N, group, stream, dev,
+                               g_smem_awq_tmem[1]);
 }
 
 int awq_gemv_launch(__half* y, const __half* x, const int32_t* qw, const uint32_t* qz,
@@ -569,8 +629,12 @@ int fp8_gemm_launch(__nv_bfloat16* y, const uint8_t* xq, const float* sx, const 
 
 // The tile GEMM's epilogue stores 8 channels at a time (N % 8 == 0); the GEMV
 // and swap-AB kernels store single channels.
-bool fp8_uses_gemm(int M) {
-  return !(M <= g_tune.fp8_gemv_max_m && M <= 32) && !(M <= g_tune.fp8_swap_max_m && M <= 64);
+bool fp8_uses_gemv(int M, int K, int N) {
+  return M <= g_tune.fp8_gemv_max_m && M <= 32 &&
+         static_cast<int64_t>(K) * N <= static_cast<int64_t>(g_tune.fp8_gemv_max_kn);
+}
+bool fp8_uses_gemm(int M, int K, int N) {
+  return !fp8_uses_gemv(M, K, N) && !(M <= g_tune.fp8_swap_max_m && M <= 64);
 }
 
 int fp8_linear_prequant_impl(void* y, const uint8_t* xq, const float* x_scale, const uint8_t* wq,
@@ -578,7 +642,7 @@ int fp8_linear_prequant_impl(void* y, const uint8_t* xq, const float* x_scale, c
                              cudaStream_t stream, int dev) {
   auto* yb = static_cast<__nv_bfloat16*>(y);
   auto* bb = static_cast<const __nv_bfloat16*>(bias);
-  if (M <= g_tune.fp8_gemv_max_m && M <= 32)
+  if (fp8_uses_gemv(M, K, N))
     return fp8_gemv_launch(yb, xq, x_scale, wq, w_scale, bb, M, K, N, stream, dev);
   if (M <= g_tune.fp8_swap_max_m && M <= 64)
     return fp8_swap_launch(yb, xq, x_scale, wq, w_scale, bb, M, K, N, stream, dev);
@@ -646,6 +710,12 @@ int lmrs_set_tuning(const char* key, int value) {
   else if (!strcmp(key, "attn_ctas_per_sm")) g_tune.attn_ctas_per_sm = value;
   else if (!strcmp(key, "fp8_gemv_cluster")) g_tune.fp8_gemv_cluster = value;
   else if (!strcmp(key, "fp8_swap_max_m")) g_tune.fp8_swap_max_m = value;
+  else if (!strcmp(key, "fp8_gemv_max_kn")) g_tune.fp8_gemv_max_kn = value;
+  else if (!strcmp(key, "awq_tmem_max_m")) g_tune.awq_tmem_max_m = value;
+  else if (!strcmp(key, "awq_tmem_min_m")) g_tune.awq_tmem_min_m = value;
+  else if (!strcmp(key, "awq_tmem_wide_n")) g_tune.awq_tmem_wide_n = value;
+  else if (!strcmp(key, "awq_tmem_cluster")) g_tune.awq_tmem_cluster = value;
+  else if (!strcmp(key, "awq_tmem_ctas_per_sm")) g_tune.awq_tmem_ctas_per_sm = value;
   else if (!strcmp(key, "fp8_swap_cluster")) g_tune.fp8_swap_cluster = value;
   else return LMRS_ERR_SHAPE;
   return LMRS_OK;
@@ -714,6 +784,8 @@ int lmrs_awq_linear(void* y, const void* x, const int32_t* qweight, const int32_
   auto* xh = static_cast<const __half*>(x);
   auto* sh = static_cast<const __half*>(scales);
   auto* bh = static_cast<const __half*>(bias_or_null);
+  if (awq_use_tmem(M, N))
+    return awq_tmem_launch(yh, xh, qweight, qzeros, sh, bh, M, K, N, group, st, dev);
   if (M <= g_tune.awq_gemv_max_m && M <= 16)
     return awq_gemv_launch(yh, xh, qweight, reinterpret_cast<const uint32_t*>(qzeros), sh, bh, M,
                            K, N, group, st, dev);
@@ -753,7 +825,7 @@ int lmrs_fp8_linear_prequant(void* y, const uint8_t* xq, const float* x_scale, c
       (reinterpret_cast<uintptr_t>(x_scale) & 3u) || (reinterpret_cast<uintptr_t>(w_scale) & 3u) ||
       (reinterpret_cast<uintptr_t>(bias_or_null) & 1u))
     return LMRS_ERR_ALIGN;
-  if (N % 8 && fp8_uses_gemm(M)) return LMRS_ERR_SHAPE;  // GEMM epilogue stores
+  if (N % 8 && fp8_uses_gemm(M, K, N)) return LMRS_ERR_SHAPE;  // GEMM epilogue stores
   int dev = 0;
   int rc = check_device(&dev);
   if (rc) return rc;
@@ -773,7 +845,7 @@ int lmrs_fp8_linear(void* y, const void* x, const uint8_t* wq, const float* w_sc
       (reinterpret_cast<uintptr_t>(y) & 3u) || (reinterpret_cast<uintptr_t>(w_scale) & 3u) ||
       (reinterpret_cast<uintptr_t>(bias_or_null) & 1u))
     return LMRS_ERR_ALIGN;
-  if (N % 8 && fp8_uses_gemm(M)) return LMRS_ERR_SHAPE;
+  if (N % 8 && fp8_uses_gemm(M, K, N)) return LMRS_ERR_SHAPE;
   int dev = 0;
   int rc = check_device(&dev);
   if (rc) return rc;
@@ -822,7 +894,7 @@ extern "C" int lmrs_fp8_linear_noalloc(void* y, const void* x, const uint8_t* wq
       (reinterpret_cast<uintptr_t>(w_scale) & 3u) ||
       (reinterpret_cast<uintptr_t>(bias_or_null) & 1u))
     return LMRS_ERR_ALIGN;
-  if (N % 8 && fp8_uses_gemm(M)) return LMRS_ERR_SHAPE;
+  if (N % 8 && fp8_uses_gemm(M, K, N)) return LMRS_ERR_SHAPE;
   int dev = 0;
   int rc = check_device(&dev);
   if (rc) return rc;

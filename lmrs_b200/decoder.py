@@ -92,7 +92,10 @@ class QuantDecoder:
 
     def __init__(self, cfg: DecoderConfig, batch: int, ctx: int, device, rank: int = 0,
                  world: int = 1, seed: int = 0, group=None, fused: bool = True,
-                 allreduce: str = "peer"):
+                 allreduce: str = "peer", weights: Optional[dict] = None):
+        """Random (seeded) weights, or `weights` in the layout of state() without
+        the KV cache and tokens (e.g. checkpoint.load_decoder_weights for this
+        rank); the KV cache and token ids are random either way."""
         if cfg.heads % world or cfg.intermediate % world or cfg.kv_heads % world:
             raise ValueError(f"tensor parallelism {world} does not divide heads / kv heads / intermediate")
         if cfg.vocab % world:
@@ -115,7 +118,14 @@ class QuantDecoder:
         gen = torch.Generator(device=self.device).manual_seed(seed * 1000 + rank)
         rep = torch.Generator(device=self.device).manual_seed(seed * 1000 + 999)
 
-        def lin(K, N):
+        def lin(K, N, given=None):
+            if given is not None:
+                if cfg.quant == "awq":
+                    return ops.QuantLinearOp.awq(ops.LinearConfig(K, N), given["qweight"],
+                                                 given["qzeros"], given["scales"], None,
+                                                 ops.AwqConfig(cfg.group))
+                return ops.QuantLinearOp.fp8(ops.LinearConfig(K, N), given["weight_q"],
+                                             given["weight_scale"])
             if cfg.quant == "awq":
                 t = _awq_random(K, N, cfg.group, gen, self.device)
                 return ops.QuantLinearOp.awq(ops.LinearConfig(K, N), t["qweight"], t["qzeros"],
@@ -123,21 +133,34 @@ class QuantDecoder:
             t = _fp8_random(K, N, gen, self.device)
             return ops.QuantLinearOp.fp8(ops.LinearConfig(K, N), t["weight_q"], t["weight_scale"])
 
-        self.embed = (torch.randn((cfg.vocab, H), generator=rep, device=self.device) * 0.02).to(self.act)
-        self.layers = []
         shapes = cfg.projections(world)
-        for _ in range(cfg.layers):
-            self.layers.append(dict(
-                in_norm=(1.0 + 0.02 * torch.randn(H, generator=rep, device=self.device)).to(self.act),
-                post_norm=(1.0 + 0.02 * torch.randn(H, generator=rep, device=self.device)).to(self.act),
-                qkv=lin(*shapes[0]),        # column-parallel, q/k/v merged
-                o=lin(*shapes[1]),          # row-parallel
-                gate_up=lin(*shapes[2]),    # column-parallel, gate/up merged
-                down=lin(*shapes[3]),       # row-parallel
-            ))
-        self.final_norm = (1.0 + 0.02 * torch.randn(H, generator=rep, device=self.device)).to(self.act)
-        self.lm_head = (torch.randn((self.vocab_local, H), generator=gen, device=self.device)
-                        * 0.02).to(self.act)
+        self.layers = []
+        if weights is not None:
+            dev = self.device
+            self.embed = weights["embed"].to(dev, self.act)
+            self.final_norm = weights["final_norm"].to(dev, self.act)
+            self.lm_head = weights["lm_head"].to(dev, self.act)
+            if len(weights["layers"]) != cfg.layers:
+                raise ValueError(f"{len(weights['layers'])} layers given, config has {cfg.layers}")
+            for W in weights["layers"]:
+                self.layers.append(dict(
+                    in_norm=W["in_norm"].to(dev, self.act), post_norm=W["post_norm"].to(dev, self.act),
+                    **{k: lin(*shp, {n: t.to(dev) for n, t in W[k].items()})
+                       for k, shp in zip(("qkv", "o", "gate_up", "down"), shapes)}))
+        else:
+            self.embed = (torch.randn((cfg.vocab, H), generator=rep, device=self.device) * 0.02).to(self.act)
+            for _ in range(cfg.layers):
+                self.layers.append(dict(
+                    in_norm=(1.0 + 0.02 * torch.randn(H, generator=rep, device=self.device)).to(self.act),
+                    post_norm=(1.0 + 0.02 * torch.randn(H, generator=rep, device=self.device)).to(self.act),
+                    qkv=lin(*shapes[0]),        # column-parallel, q/k/v merged
+                    o=lin(*shapes[1]),          # row-parallel
+                    gate_up=lin(*shapes[2]),    # column-parallel, gate/up merged
+                    down=lin(*shapes[3]),       # row-parallel
+                ))
+            self.final_norm = (1.0 + 0.02 * torch.randn(H, generator=rep, device=self.device)).to(self.act)
+            self.lm_head = (torch.randn((self.vocab_local, H), generator=gen, device=self.device)
+                            * 0.02).to(self.act)
         pos = ctx - 1
         inv = 1.0 / (cfg.rope_theta ** (torch.arange(0, d, 2, device=self.device, dtype=torch.float32) / d))
         ang = pos * inv
@@ -145,6 +168,15 @@ class QuantDecoder:
         self.sin = torch.cat([ang.sin(), ang.sin()]).to(self.act)
         self.kv = None
         self.set_batch(batch, seed)
+
+    @classmethod
+    def from_checkpoint(cls, path: str, batch: int, ctx: int, device, rank: int = 0,
+                        world: int = 1, **kw) -> "QuantDecoder":
+        """This rank's decoder from a quantized (AWQ or FP8) safetensors
+        checkpoint directory (checkpoint.load_decoder_weights)."""
+        from .checkpoint import load_decoder_weights
+        cfg, weights = load_decoder_weights(path, rank, world, device)
+        return cls(cfg, batch, ctx, device, rank=rank, world=world, weights=weights, **kw)
 
     # ---------------------------------------------------------------- state
     def state(self) -> dict:

@@ -201,10 +201,12 @@ def test_status_codes(cuda):
                                            ("awq_gemv_cluster", 8, (1, 5, 16)),
                                            ("awq_gemv_slots", 8, (5, 16)),
                                            ("awq_gemv4_slots", 8, (1, 4)),
-                                           ("pdl", 0, (1, 8, 40, 300))])
+                                           ("awq_tmem_max_m", 0, (17, 24, 32)),
+                                           ("pdl", 0, (1, 8, 20, 40, 300))])
 def test_opt_in_paths(cuda, knob, value, Ms):
     """Kernels and launch shapes the default dispatch does not pick for these M
-    (CTA-pair GEMM, swap-AB below 17 or above 64 tokens, the general GEMV for
+    (CTA-pair GEMM, swap-AB below 17 or from 17 to 32 tokens (where the
+    TMEM-staged kernel is the default) or above 64, the general GEMV for
     M <= 4, 64-row boxes, other cluster sizes and ring depths, launches without
     programmatic dependent launch) stay correct and deterministic when selected."""
     import torch
@@ -212,7 +214,7 @@ def test_opt_in_paths(cuda, knob, value, Ms):
     from lmrs_b200 import _lib
     defaults = {"awq_gemm_pair": 0, "awq_gemv_max_m": 16, "awq_swap_max_m": 64, "gemm_bn": 256,
                 "awq_gemv4": 1, "gemv_box_rows": 128, "awq_gemv_cluster": 0, "awq_gemv_slots": 4,
-                "awq_gemv4_slots": 4, "pdl": 1}
+                "awq_gemv4_slots": 4, "awq_tmem_max_m": 32, "pdl": 1}
     K, N, g = 1024, 1280, 128
     try:
         L.set_tuning(knob, value)
@@ -227,3 +229,50 @@ def test_opt_in_paths(cuda, knob, value, Ms):
     finally:
         L.set_tuning(knob, defaults[knob])
     assert L.read_device_error() == 0
+
+
+def _awq_case(dev, M, K, N, g, seed, bias=True):
+    import lmrs_b200 as L
+    d = O.awq_inputs(M, K, N, g, seed=seed, with_bias=bias)
+    qw, qz, sc, x, b = _awq_dev(d, dev)
+    y = L.awq_linear(x, qw, qz, sc, b, g)
+    ref = O.c_awq_linear(d["x"], d["qweight"], d["qzeros"], d["scales"], d["bias"], M, K, N, g)
+    return O.max_rel_err(y.cpu().numpy(), ref), (x, qw, qz, sc, b, y)
+
+
+@pytest.mark.parametrize("M", [1, 3, 4, 5, 8, 15, 16, 17, 31, 32])
+@pytest.mark.parametrize("K,N,g", [(1024, 1280, 128), (2048, 1312, 64), (4096, 512, 128),
+                                   (3072, 768, 256)])
+def test_tmem_linear(cuda, M, K, N, g):
+    """AWQ linear with the weights dequantised into tensor memory (tcgen05 with
+    the A operand in TMEM), forced on for every M up to 32: both token-tile
+    widths (16/32), N not a multiple of the 256-channel strip, groups of 64,
+    128 and 256 rows, and deterministic across calls."""
+    import torch
+    import lmrs_b200 as L
+    try:
+        L.set_tuning("awq_tmem_min_m", 1)
+        err, (x, qw, qz, sc, b, y) = _awq_case(cuda, M, K, N, g, 300 + M + N)
+        for _ in range(2):
+            assert torch.equal(L.awq_linear(x, qw, qz, sc, b, g), y)
+    finally:
+        L.set_tuning("awq_tmem_min_m", 17)
+        L.set_tuning("awq_tmem_max_m", 32)
+    assert err < TIGHT, err
+    assert L.read_device_error() == 0
+
+
+@pytest.mark.parametrize("C", [1, 2, 4, 8])
+@pytest.mark.parametrize("M", [1, 12])
+def test_tmem_linear_clusters(cuda, C, M):
+    """Every split-K cluster size, with 17 boxes of 64 rows that do not divide
+    evenly over the cluster."""
+    import lmrs_b200 as L
+    try:
+        L.set_tuning("awq_tmem_min_m", 1)
+        L.set_tuning("awq_tmem_cluster", C)
+        err, _ = _awq_case(cuda, M, 17 * 64, 768, 64, 41 + C, bias=False)
+    finally:
+        L.set_tuning("awq_tmem_min_m", 17)
+        L.set_tuning("awq_tmem_cluster", 0)
+    assert err < TIGHT, err
