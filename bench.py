@@ -384,6 +384,17 @@ def run_case(case, launches=3):
         ws = DO.AttentionWorkspace()
         for _ in range(launches):
             DO.paged_attention_decode(q, kc, vc, tables, lens, ctx, 1 / math.sqrt(128), 1, ws)
+    elif kind == "decode":
+        # eager decode steps of a config-3/4 decoder cut to `layers` layers:
+        # decode:<8b-awq|70b-fp8>:<batch>:<layers>
+        import dataclasses
+        from lmrs_b200 import decoder as D
+        preset, B, nl = dims[0], int(dims[1]), int(dims[2])
+        attr, ctx, _, _ = DECODE_PRESETS[preset]
+        cfg = dataclasses.replace(getattr(D, attr), layers=nl)
+        dec = D.QuantDecoder(cfg, batch=B, ctx=ctx, device=dev, seed=0)
+        for _ in range(launches):
+            dec.logits()
     else:
         raise SystemExit(f"unknown case {case}")
     torch.cuda.synchronize()
@@ -606,7 +617,8 @@ def main():
     ap.add_argument("--case", default=None,
                     help="profiling mode: run a few launches of one case and exit, e.g. "
                          "awq:4096 (config-1 shape, M=4096), fp8:8192:4096:28672 (M:K:N) or "
-                         "attn:64:32:8:2048 (paged decode attention B:q heads:KV heads:ctx)")
+                         "attn:64:32:8:2048 (paged decode attention B:q heads:KV heads:ctx) or "
+                         "decode:8b-awq:16:2 (eager decode steps, preset:batch:layers)")
     ap.add_argument("--decode", choices=sorted(DECODE_PRESETS), default=None,
                     help="configs 3/4: decode tok/s of the 8B AWQ or 70B FP8 decoder "
                          "(tensor parallel over the torchrun ranks)")

@@ -17,7 +17,8 @@
 extern "C" {
 #endif
 
-/* RMSNorm over rows of H (H % 8 == 0), optionally fused with the residual add:
+/* RMSNorm over rows of H (H % 8 == 0, H <= 32768: a row is held in one CTA's
+ * registers), optionally fused with the residual add:
  *   if delta: residual[r] = round(residual[r] + delta[r])   (in place)
  *   out[r, c] = round(residual[r, c] * rsqrt(mean_c residual[r]^2 + eps) * weight[c])
  * The normalisation is the reference's rmsnorm_fwd (kernels/ffi/norm_ffi.cu:9-31,
@@ -40,7 +41,8 @@ LMRS_API int lmrs_rmsnorm_fp8(uint8_t* q_out, float* scale_out, void* residual,
 LMRS_API int lmrs_silu_mul(void* out, const void* gate_up, int rows, int inter, int dtype,
                            lmrs_stream_t stream);
 
-/* Same, leaving as FP8 activations (bytes [rows, inter] + per-row scales). */
+/* Same, leaving as FP8 activations (bytes [rows, inter] + per-row scales);
+ * inter <= 32768 (the row's absmax is taken in one CTA). */
 LMRS_API int lmrs_silu_mul_fp8(uint8_t* q_out, float* scale_out, const void* gate_up, int rows,
                                int inter, int dtype, lmrs_stream_t stream);
 
@@ -50,7 +52,9 @@ LMRS_API int lmrs_silu_mul_fp8(uint8_t* q_out, float* scale_out, const void* gat
  * cos/sin given for that position: head_size / 2 entries each):
  *   q_out[s, h, :] = rope(q);  k/v written into the paged cache at positions[s]
  *   (cache[block][kv_head][block_offset][head_size], block = block_tables[s,
- *   positions[s] / block_size], as paged_attention_v1 reads it).  head_size even. */
+ *   positions[s] / block_size], as paged_attention_v1 reads it).  head_size even
+ *   (16-byte vector path when head_size % 16 == 0 and every pointer is 16-byte
+ *   aligned). */
 LMRS_API int lmrs_rope_kv_write(void* q_out, void* key_cache, void* value_cache,
                                 const void* qkv, const void* cos, const void* sin,
                                 const int32_t* block_tables, const int32_t* positions,

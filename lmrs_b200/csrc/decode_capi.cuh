@@ -8,20 +8,56 @@ namespace {
 
 bool act_dtype(int dt) { return dt == LMRS_DTYPE_BF16 || dt == LMRS_DTYPE_F16; }
 
+// A whole row in one CTA's registers: the fewest vectors per thread (1, 2 or 4
+// of 8 columns) that fit 1024 threads, and the threads that covers.
+constexpr int kRowMaxCols = lmrs::kRowMaxThreads * lmrs::kRowMaxVecs * 8;
+
+void row_shape(int cols, int* vpt, int* threads) {
+  const int vecs = cols / 8;
+  int v = 1;
+  while (v < lmrs::kRowMaxVecs && vecs > lmrs::kRowMaxThreads * v) v *= 2;
+  int t = (vecs + v - 1) / v;
+  t = (t + 31) / 32 * 32;
+  *vpt = v;
+  *threads = clampi(t, lmrs::kNormThreads, lmrs::kRowMaxThreads);
+}
+
 template <typename T, bool FP8>
 int rmsnorm_launch(void* out, uint8_t* q, float* s, void* resid, const void* delta, const void* w,
                    int rows, int H, float eps, cudaStream_t st) {
-  int rc = launch_ex(lmrs::rmsnorm_kernel<T, FP8>, rows, 0, lmrs::kNormThreads, 0, st,
-                     static_cast<T*>(out), q, s, static_cast<T*>(resid),
-                     static_cast<const T*>(delta), static_cast<const T*>(w), H, eps);
+  int vpt, threads;
+  row_shape(H, &vpt, &threads);
+  auto go = [&](auto kern) {
+    return launch_ex_grid(kern, dim3(rows, 1, 1), threads, st, static_cast<T*>(out), q, s,
+                          static_cast<T*>(resid), static_cast<const T*>(delta),
+                          static_cast<const T*>(w), H, eps);
+  };
+  int rc = vpt == 1   ? go(lmrs::rmsnorm_kernel<T, FP8, 1>)
+           : vpt == 2 ? go(lmrs::rmsnorm_kernel<T, FP8, 2>)
+                      : go(lmrs::rmsnorm_kernel<T, FP8, 4>);
   return rc ? rc : after_launch();
 }
 
 template <typename T, bool FP8>
 int silu_launch(void* out, uint8_t* q, float* s, const void* gu, int rows, int inter,
                 cudaStream_t st) {
-  int rc = launch_ex(lmrs::silu_mul_kernel<T, FP8>, rows, 0, lmrs::kNormThreads, 0, st,
-                     static_cast<T*>(out), q, s, static_cast<const T*>(gu), inter);
+  int rc;
+  if (!FP8) {  // no row reduction: (row, chunk of 256 x 8 columns) CTAs
+    const int chunks = (inter + lmrs::kNormThreads * 8 - 1) / (lmrs::kNormThreads * 8);
+    rc = launch_ex_grid(lmrs::silu_mul_kernel<T, FP8, 1>, dim3(rows, chunks, 1),
+                        lmrs::kNormThreads, st, static_cast<T*>(out), q, s,
+                        static_cast<const T*>(gu), inter);
+  } else {
+    int vpt, threads;
+    row_shape(inter, &vpt, &threads);
+    auto go = [&](auto kern) {
+      return launch_ex_grid(kern, dim3(rows, 1, 1), threads, st, static_cast<T*>(out), q, s,
+                            static_cast<const T*>(gu), inter);
+    };
+    rc = vpt == 1   ? go(lmrs::silu_mul_kernel<T, FP8, 1>)
+         : vpt == 2 ? go(lmrs::silu_mul_kernel<T, FP8, 2>)
+                    : go(lmrs::silu_mul_kernel<T, FP8, 4>);
+  }
   return rc ? rc : after_launch();
 }
 
@@ -84,7 +120,7 @@ extern "C" {
 LMRS_API int lmrs_rmsnorm(void* out, void* residual, const void* delta_or_null, const void* weight,
                           int rows, int H, float eps, int dtype, lmrs_stream_t stream) {
   if (!act_dtype(dtype)) return LMRS_ERR_DTYPE;
-  if (rows < 0 || H <= 0 || H % 8) return LMRS_ERR_SHAPE;
+  if (rows < 0 || H <= 0 || H % 8 || H > kRowMaxCols) return LMRS_ERR_SHAPE;
   if (rows == 0) return LMRS_OK;
   if (!out || !residual || !weight) return LMRS_ERR_NULL;
   if (!aligned16(out) || !aligned16(residual) || !aligned16(weight) ||
@@ -104,7 +140,7 @@ LMRS_API int lmrs_rmsnorm_fp8(uint8_t* q_out, float* scale_out, void* residual,
                               const void* delta_or_null, const void* weight, int rows, int H,
                               float eps, int dtype, lmrs_stream_t stream) {
   if (!act_dtype(dtype)) return LMRS_ERR_DTYPE;
-  if (rows < 0 || H <= 0 || H % 8) return LMRS_ERR_SHAPE;
+  if (rows < 0 || H <= 0 || H % 8 || H > kRowMaxCols) return LMRS_ERR_SHAPE;
   if (rows == 0) return LMRS_OK;
   if (!q_out || !scale_out || !residual || !weight) return LMRS_ERR_NULL;
   if (!aligned16(q_out) || !aligned16(residual) || !aligned16(weight) ||
@@ -138,7 +174,7 @@ LMRS_API int lmrs_silu_mul(void* out, const void* gate_up, int rows, int inter, 
 LMRS_API int lmrs_silu_mul_fp8(uint8_t* q_out, float* scale_out, const void* gate_up, int rows,
                                int inter, int dtype, lmrs_stream_t stream) {
   if (!act_dtype(dtype)) return LMRS_ERR_DTYPE;
-  if (rows < 0 || inter <= 0 || inter % 8) return LMRS_ERR_SHAPE;
+  if (rows < 0 || inter <= 0 || inter % 8 || inter > kRowMaxCols) return LMRS_ERR_SHAPE;
   if (rows == 0) return LMRS_OK;
   if (!q_out || !scale_out || !gate_up) return LMRS_ERR_NULL;
   if (!aligned16(q_out) || !aligned16(gate_up)) return LMRS_ERR_ALIGN;
@@ -165,21 +201,25 @@ LMRS_API int lmrs_rope_kv_write(void* q_out, void* key_cache, void* value_cache,
   int rc = check_device(nullptr);
   if (rc) return rc;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  if (dtype == LMRS_DTYPE_BF16) {
-    using T = __nv_bfloat16;
-    rc = launch_ex(lmrs::rope_kv_kernel<T>, num_seqs, 0, 256, 0, st, static_cast<T*>(q_out),
-                   static_cast<T*>(key_cache), static_cast<T*>(value_cache),
-                   static_cast<const T*>(qkv), static_cast<const T*>(cos),
-                   static_cast<const T*>(sin), block_tables, positions, num_heads, num_kv_heads,
-                   head_size, block_size, max_blocks_per_seq);
-  } else {
-    using T = __half;
-    rc = launch_ex(lmrs::rope_kv_kernel<T>, num_seqs, 0, 256, 0, st, static_cast<T*>(q_out),
-                   static_cast<T*>(key_cache), static_cast<T*>(value_cache),
-                   static_cast<const T*>(qkv), static_cast<const T*>(cos),
-                   static_cast<const T*>(sin), block_tables, positions, num_heads, num_kv_heads,
-                   head_size, block_size, max_blocks_per_seq);
-  }
+  const bool vec = head_size % 16 == 0 && aligned16(q_out) && aligned16(key_cache) &&
+                   aligned16(value_cache) && aligned16(qkv) && aligned16(cos) && aligned16(sin);
+  const int items = (num_heads + num_kv_heads) * (head_size / 16) + num_kv_heads * (head_size / 8);
+  const dim3 vgrid(num_seqs, (items + 127) / 128, 1);
+  auto go = [&](auto tag) {
+    using T = decltype(tag);
+    if (vec)
+      return launch_ex_grid(lmrs::rope_kv_vec_kernel<T>, vgrid, 128, st, static_cast<T*>(q_out),
+                            static_cast<T*>(key_cache), static_cast<T*>(value_cache),
+                            static_cast<const T*>(qkv), static_cast<const T*>(cos),
+                            static_cast<const T*>(sin), block_tables, positions, num_heads,
+                            num_kv_heads, head_size, block_size, max_blocks_per_seq);
+    return launch_ex(lmrs::rope_kv_kernel<T>, num_seqs, 0, 256, 0, st, static_cast<T*>(q_out),
+                     static_cast<T*>(key_cache), static_cast<T*>(value_cache),
+                     static_cast<const T*>(qkv), static_cast<const T*>(cos),
+                     static_cast<const T*>(sin), block_tables, positions, num_heads, num_kv_heads,
+                     head_size, block_size, max_blocks_per_seq);
+  };
+  rc = dtype == LMRS_DTYPE_BF16 ? go(__nv_bfloat16()) : go(__half());
   return rc ? rc : after_launch();
 }
 

@@ -37,16 +37,18 @@ struct Act<__nv_bfloat16> {
   static __device__ __forceinline__ __nv_bfloat16 t(float v) { return __float2bfloat16_rn(v); }
 };
 
-constexpr int kNormThreads = 256;
+constexpr int kNormThreads = 256;     // smallest CTA of the row kernels
+constexpr int kRowMaxThreads = 1024;
+constexpr int kRowMaxVecs = 4;        // 8-element vectors per thread held in registers
 
+// Sum / max over the CTA (any multiple of 32 threads up to 1024).
 __device__ __forceinline__ float block_sum(float v, float* red) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
   __syncthreads();
   float s = 0.f;
-#pragma unroll
-  for (int w = 0; w < kNormThreads / 32; ++w) s += red[w];
+  for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) s += red[w];
   __syncthreads();
   return s;
 }
@@ -57,8 +59,7 @@ __device__ __forceinline__ float block_max(float v, float* red) {
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
   __syncthreads();
   float m = red[0];
-#pragma unroll
-  for (int w = 1; w < kNormThreads / 32; ++w) m = fmaxf(m, red[w]);
+  for (int w = 1; w < static_cast<int>(blockDim.x >> 5); ++w) m = fmaxf(m, red[w]);
   __syncthreads();
   return m;
 }
@@ -79,130 +80,179 @@ __device__ __forceinline__ uint2 e4m3x8(const float (&v)[8], float s) {
   return make_uint2(out[0], out[1]);
 }
 
-// residual (+)= delta, out = rmsnorm(residual) * w; one CTA per row, chunks of
-// 8 columns (H % 8 == 0).  FP8: out is replaced by its per-row e4m3 bytes and
-// scale (the rounded outputs are recomputed for each pass instead of stored).
-template <typename T, bool FP8>
-__global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(
+template <typename T>
+__device__ __forceinline__ void unpack8(const uint4& v, float (&f)[8]) {
+  const T* e = reinterpret_cast<const T*>(&v);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) f[i] = Act<T>::f(e[i]);
+}
+
+// residual (+)= delta, out = rmsnorm(residual) * w, one CTA per row.  Thread t
+// holds vectors v*blockDim + t (8 columns each, H % 8 == 0) of the row in
+// registers: one read pass, one write pass.  FP8: out is replaced by the
+// row's e4m3 bytes and scale, computed from the same rounded outputs.
+template <typename T, bool FP8, int VPT>
+__global__ void __launch_bounds__(kRowMaxThreads) rmsnorm_kernel(
     T* __restrict__ out, uint8_t* __restrict__ qout, float* __restrict__ qscale,
     T* __restrict__ resid, const T* __restrict__ delta, const T* __restrict__ w, int H, float eps) {
   pdl_wait();
   pdl_trigger();
-  __shared__ float red[kNormThreads / 32];
+  __shared__ float red[32];
   const int row = blockIdx.x;
   T* xr = resid + static_cast<int64_t>(row) * H;
+  float x[VPT][8];
   float ss = 0.f;
-  for (int c = threadIdx.x * 8; c < H; c += kNormThreads * 8) {
-    uint4 v = *reinterpret_cast<const uint4*>(xr + c);
-    if (delta != nullptr) {
-      const uint4 dv = *reinterpret_cast<const uint4*>(delta + static_cast<int64_t>(row) * H + c);
-      const T* e = reinterpret_cast<const T*>(&v);
-      const T* de = reinterpret_cast<const T*>(&dv);
-      uint4 sv;
-      T* se = reinterpret_cast<T*>(&sv);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) se[i] = Act<T>::t(Act<T>::f(e[i]) + Act<T>::f(de[i]));
-      *reinterpret_cast<uint4*>(xr + c) = sv;   // the updated residual stream
-      v = sv;
-    }
-    const T* e = reinterpret_cast<const T*>(&v);
+  for (int v = 0; v < VPT; ++v) {
+    const int c = (v * blockDim.x + threadIdx.x) * 8;
+    if (c < H) {
+      uint4 xv = *reinterpret_cast<const uint4*>(xr + c);
+      if (delta != nullptr) {
+        const uint4 dv = *reinterpret_cast<const uint4*>(delta + static_cast<int64_t>(row) * H + c);
+        const T* e = reinterpret_cast<const T*>(&xv);
+        const T* de = reinterpret_cast<const T*>(&dv);
+        uint4 sv;
+        T* se = reinterpret_cast<T*>(&sv);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float f = Act<T>::f(e[i]);
-      ss += f * f;
+        for (int i = 0; i < 8; ++i) se[i] = Act<T>::t(Act<T>::f(e[i]) + Act<T>::f(de[i]));
+        *reinterpret_cast<uint4*>(xr + c) = sv;  // the updated residual stream
+        xv = sv;
+      }
+      unpack8<T>(xv, x[v]);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) ss += x[v][i] * x[v][i];
     }
   }
   const float inv = rsqrtf(block_sum(ss, red) / H + eps);
-  auto normed = [&](int c, float (&y)[8], uint4& packed) {
-    const uint4 v = *reinterpret_cast<const uint4*>(xr + c);
-    const uint4 wv = *reinterpret_cast<const uint4*>(w + c);
-    const T* e = reinterpret_cast<const T*>(&v);
-    const T* we = reinterpret_cast<const T*>(&wv);
-    T* oe = reinterpret_cast<T*>(&packed);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      oe[i] = Act<T>::t(Act<T>::f(e[i]) * inv * Act<T>::f(we[i]));
-      y[i] = Act<T>::f(oe[i]);
-    }
-  };
-  if (!FP8) {
-    for (int c = threadIdx.x * 8; c < H; c += kNormThreads * 8) {
-      float y[8];
-      uint4 pk;
-      normed(c, y, pk);
-      *reinterpret_cast<uint4*>(out + static_cast<int64_t>(row) * H + c) = pk;
-    }
-    return;
-  }
   float amax = 0.f;
-  for (int c = threadIdx.x * 8; c < H; c += kNormThreads * 8) {
-    float y[8];
-    uint4 pk;
-    normed(c, y, pk);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(y[i]));
+  for (int v = 0; v < VPT; ++v) {
+    const int c = (v * blockDim.x + threadIdx.x) * 8;
+    if (c < H) {
+      float wf[8];
+      unpack8<T>(*reinterpret_cast<const uint4*>(w + c), wf);
+      uint4 pk;
+      T* oe = reinterpret_cast<T*>(&pk);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        oe[i] = Act<T>::t(x[v][i] * inv * wf[i]);
+        x[v][i] = Act<T>::f(oe[i]);
+        amax = fmaxf(amax, fabsf(x[v][i]));
+      }
+      if (!FP8) *reinterpret_cast<uint4*>(out + static_cast<int64_t>(row) * H + c) = pk;
+    }
   }
+  if (!FP8) return;
   const float sc = __fdiv_rn(block_max(amax, red), 448.0f);
   if (threadIdx.x == 0) qscale[row] = sc;
-  for (int c = threadIdx.x * 8; c < H; c += kNormThreads * 8) {
-    float y[8];
-    uint4 pk;
-    normed(c, y, pk);
-    *reinterpret_cast<uint2*>(qout + static_cast<int64_t>(row) * H + c) = e4m3x8(y, sc);
+#pragma unroll
+  for (int v = 0; v < VPT; ++v) {
+    const int c = (v * blockDim.x + threadIdx.x) * 8;
+    if (c < H) *reinterpret_cast<uint2*>(qout + static_cast<int64_t>(row) * H + c) = e4m3x8(x[v], sc);
   }
 }
 
-// out[r, i] = silu(gu[r, i]) * gu[r, I + i]  (I = inter, I % 8 == 0); FP8 as above.
-template <typename T, bool FP8>
-__global__ void __launch_bounds__(kNormThreads) silu_mul_kernel(
+// out[r, i] = silu(gu[r, i]) * gu[r, I + i]  (I = inter, I % 8 == 0).  Plain
+// form: CTA (row, chunk), one vector per thread (gridDim.y chunks per row).
+// FP8 form: one CTA per row with the row's VPT vectors per thread in
+// registers (row absmax, then e4m3 from the same rounded values).
+template <typename T, bool FP8, int VPT>
+__global__ void __launch_bounds__(kRowMaxThreads) silu_mul_kernel(
     T* __restrict__ out, uint8_t* __restrict__ qout, float* __restrict__ qscale,
     const T* __restrict__ gu, int I) {
   pdl_wait();
   pdl_trigger();
-  __shared__ float red[kNormThreads / 32];
+  __shared__ float red[32];
   const int row = blockIdx.x;
+  const int base = blockIdx.y * blockDim.x * 8 * VPT;
   const T* gr = gu + static_cast<int64_t>(row) * 2 * I;
-  auto act = [&](int c, float (&y)[8], uint4& packed) {
-    const uint4 gv = *reinterpret_cast<const uint4*>(gr + c);
-    const uint4 uv = *reinterpret_cast<const uint4*>(gr + I + c);
-    const T* ge = reinterpret_cast<const T*>(&gv);
-    const T* ue = reinterpret_cast<const T*>(&uv);
-    T* oe = reinterpret_cast<T*>(&packed);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float gval = Act<T>::f(ge[i]);
-      oe[i] = Act<T>::t((gval / (1.0f + expf(-gval))) * Act<T>::f(ue[i]));
-      y[i] = Act<T>::f(oe[i]);
-    }
-  };
-  if (!FP8) {
-    for (int c = threadIdx.x * 8; c < I; c += kNormThreads * 8) {
-      float y[8];
-      uint4 pk;
-      act(c, y, pk);
-      *reinterpret_cast<uint4*>(out + static_cast<int64_t>(row) * I + c) = pk;
-    }
-    return;
-  }
+  float y[VPT][8];
   float amax = 0.f;
-  for (int c = threadIdx.x * 8; c < I; c += kNormThreads * 8) {
-    float y[8];
-    uint4 pk;
-    act(c, y, pk);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(y[i]));
+  for (int v = 0; v < VPT; ++v) {
+    const int c = base + (v * blockDim.x + threadIdx.x) * 8;
+    if (c < I) {
+      float g[8], u[8];
+      unpack8<T>(*reinterpret_cast<const uint4*>(gr + c), g);
+      unpack8<T>(*reinterpret_cast<const uint4*>(gr + I + c), u);
+      uint4 pk;
+      T* oe = reinterpret_cast<T*>(&pk);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        oe[i] = Act<T>::t((g[i] / (1.0f + expf(-g[i]))) * u[i]);
+        y[v][i] = Act<T>::f(oe[i]);
+        amax = fmaxf(amax, fabsf(y[v][i]));
+      }
+      if (!FP8) *reinterpret_cast<uint4*>(out + static_cast<int64_t>(row) * I + c) = pk;
+    }
   }
+  if (!FP8) return;
   const float sc = __fdiv_rn(block_max(amax, red), 448.0f);
   if (threadIdx.x == 0) qscale[row] = sc;
-  for (int c = threadIdx.x * 8; c < I; c += kNormThreads * 8) {
-    float y[8];
-    uint4 pk;
-    act(c, y, pk);
-    *reinterpret_cast<uint2*>(qout + static_cast<int64_t>(row) * I + c) = e4m3x8(y, sc);
+#pragma unroll
+  for (int v = 0; v < VPT; ++v) {
+    const int c = (v * blockDim.x + threadIdx.x) * 8;
+    if (c < I) *reinterpret_cast<uint2*>(qout + static_cast<int64_t>(row) * I + c) = e4m3x8(y[v], sc);
   }
 }
 
-// One CTA per sequence.  qkv row: [q (hq*d) | k (hkv*d) | v (hkv*d)].
+// Vectorised RoPE + KV write for head sizes with 16-byte aligned half-rows
+// (d % 16 == 0): CTA (sequence, item block); an item is 8 columns of the first
+// half of one q / k head with the matching 8 of the second half (rotated), or
+// 8 columns of one v head (copied).
+template <typename T>
+__global__ void __launch_bounds__(128) rope_kv_vec_kernel(
+    T* __restrict__ q_out, T* __restrict__ k_cache, T* __restrict__ v_cache,
+    const T* __restrict__ qkv, const T* __restrict__ cosv, const T* __restrict__ sinv,
+    const int32_t* __restrict__ tables, const int32_t* __restrict__ positions, int hq, int hkv,
+    int d, int block_size, int max_blocks) {
+  pdl_wait();
+  pdl_trigger();
+  const int b = blockIdx.x;
+  const int half = d / 2, oct = half / 8, dv = d / 8;
+  const int rot = (hq + hkv) * oct;
+  const int it = blockIdx.y * blockDim.x + threadIdx.x;
+  if (it >= rot + hkv * dv) return;
+  const T* row = qkv + static_cast<int64_t>(b) * (hq + 2 * hkv) * d;
+  const int pos = positions[b];
+  const bool in_cache = pos >= 0 && pos < max_blocks * block_size;
+  const int blk = in_cache ? tables[static_cast<int64_t>(b) * max_blocks + pos / block_size] : 0;
+  const int off = in_cache ? pos % block_size : 0;
+  if (it < rot) {
+    const int h = it / oct, c = (it - h * oct) * 8;
+    float x0[8], x1[8], cs[8], sn[8];
+    unpack8<T>(*reinterpret_cast<const uint4*>(row + h * d + c), x0);
+    unpack8<T>(*reinterpret_cast<const uint4*>(row + h * d + half + c), x1);
+    unpack8<T>(*reinterpret_cast<const uint4*>(cosv + c), cs);
+    unpack8<T>(*reinterpret_cast<const uint4*>(sinv + c), sn);
+    uint4 p0, p1;
+    T* r0 = reinterpret_cast<T*>(&p0);
+    T* r1 = reinterpret_cast<T*>(&p1);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      r0[i] = Act<T>::t(x0[i] * cs[i] - x1[i] * sn[i]);  // rotate-half: first half
+      r1[i] = Act<T>::t(x1[i] * cs[i] + x0[i] * sn[i]);  // second half
+    }
+    T* dst;
+    if (h < hq) {
+      dst = q_out + (static_cast<int64_t>(b) * hq + h) * d;
+    } else if (in_cache) {
+      dst = k_cache + ((static_cast<int64_t>(blk) * hkv + (h - hq)) * block_size + off) * d;
+    } else {
+      return;
+    }
+    *reinterpret_cast<uint4*>(dst + c) = p0;
+    *reinterpret_cast<uint4*>(dst + half + c) = p1;
+  } else if (in_cache) {
+    const int e = it - rot;
+    const int kh = e / dv, c = (e - kh * dv) * 8;
+    *reinterpret_cast<uint4*>(v_cache + ((static_cast<int64_t>(blk) * hkv + kh) * block_size + off) * d + c) =
+        *reinterpret_cast<const uint4*>(row + (hq + hkv) * d + kh * d + c);
+  }
+}
+
+// General head sizes (d even): one CTA per sequence, scalar accesses.
+// qkv row: [q (hq*d) | k (hkv*d) | v (hkv*d)].
 // cos/sin: d/2 entries for this step's position.  Cache: paged, block table row
 // `tables[b]`, block_size positions per block.
 template <typename T>

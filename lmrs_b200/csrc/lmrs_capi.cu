@@ -203,6 +203,28 @@ int launch_ex(Kern kernel, int grid_x, int cluster, int threads, int smem, cudaS
   return LMRS_OK;
 }
 
+// 2-D/3-D grid, no cluster, programmatic dependent launch when enabled.
+template <typename Kern, typename... Args>
+int launch_ex_grid(Kern kernel, dim3 grid, int threads, cudaStream_t stream, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(threads, 1, 1);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  int n = 0;
+  if (g_tune.pdl) {
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    n = 1;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, args...);
+  if (e != cudaSuccess) return record(e);
+  return LMRS_OK;
+}
+
 template <typename Kern, typename... Args>
 int launch_cluster(Kern kernel, int grid_x, int cluster, int threads, int smem,
                    cudaStream_t stream, Args... args) {

@@ -26,7 +26,8 @@ def _ulp_close(got, ref, dtype):
 
 
 @pytest.mark.parametrize("dtype", DTS)
-@pytest.mark.parametrize("rows,H", [(1, 4096), (7, 8192), (64, 4096), (3, 1032)])
+@pytest.mark.parametrize("rows,H", [(1, 4096), (7, 8192), (64, 4096), (3, 1032), (2, 32768),
+                                    (5, 16392)])
 @pytest.mark.parametrize("with_delta", [False, True])
 def test_rmsnorm(cuda, dtype, rows, H, with_delta):
     from lmrs_b200 import decode_ops as DO
@@ -45,7 +46,7 @@ def test_rmsnorm(cuda, dtype, rows, H, with_delta):
 
 
 @pytest.mark.parametrize("dtype", DTS)
-@pytest.mark.parametrize("rows,H", [(1, 8192), (32, 4096), (5, 1040)])
+@pytest.mark.parametrize("rows,H", [(1, 8192), (32, 4096), (5, 1040), (2, 32768)])
 def test_rmsnorm_fp8_equals_unfused(cuda, dtype, rows, H):
     import lmrs_b200 as L
     from lmrs_b200 import decode_ops as DO
@@ -63,7 +64,8 @@ def test_rmsnorm_fp8_equals_unfused(cuda, dtype, rows, H):
 
 
 @pytest.mark.parametrize("dtype", DTS)
-@pytest.mark.parametrize("rows,inter", [(1, 14336), (16, 7168), (40, 1024), (3, 1032)])
+@pytest.mark.parametrize("rows,inter", [(1, 14336), (16, 7168), (40, 1024), (3, 1032), (2, 28672),
+                                        (1, 40000)])
 def test_silu_mul(cuda, dtype, rows, inter):
     import lmrs_b200 as L
     from lmrs_b200 import decode_ops as DO
@@ -74,8 +76,8 @@ def test_silu_mul(cuda, dtype, rows, inter):
     ref = ((g / (1 + torch.exp(-g))) * u).to(dtype)
     ok, worst = _ulp_close(y, ref, dtype)
     assert ok, worst
-    if inter % 16:
-        return  # the standalone quantiser takes K % 16 == 0
+    if inter % 16 or inter > 32768:
+        return  # the standalone quantiser takes K % 16 == 0; the fused form rows <= 32768
     q, s = DO.silu_mul_fp8(gu)
     q_ref, s_ref = L.fp8_quant_rows(y)
     assert torch.equal(s, s_ref) and torch.equal(q, q_ref)
@@ -137,9 +139,10 @@ def test_paged_attention_decode(cuda, dtype, seqs, hq, hkv, block_size, lens, kv
 
 
 @pytest.mark.parametrize("dtype", DTS)
-def test_rope_kv_write(cuda, dtype):
+@pytest.mark.parametrize("d", [128, 64, 72])  # 16-byte vector path (d % 16 == 0) and the general one
+def test_rope_kv_write(cuda, dtype, d):
     from lmrs_b200 import decode_ops as DO
-    seqs, hq, hkv, d, bs, mb = 5, 8, 2, 128, 16, 6
+    seqs, hq, hkv, bs, mb = 5, 8, 2, 16, 6
     kc, vc, tables = _paged_cache(seqs, hkv, d, bs, mb, dtype, cuda, 3)
     k0, v0 = kc.clone(), vc.clone()
     torch.manual_seed(3)
@@ -181,6 +184,8 @@ def test_decode_ops_status(cuda):
     assert lib.lmrs_rmsnorm(x.data_ptr(), x.data_ptr(), None, x.data_ptr(), 2, 64, 1e-5, 2,
                             s) == _lib.LMRS_ERR_DTYPE
     assert lib.lmrs_rmsnorm(x.data_ptr(), x.data_ptr(), None, x.data_ptr(), 2, 60, 1e-5, 0,
+                            s) == _lib.LMRS_ERR_SHAPE
+    assert lib.lmrs_rmsnorm(x.data_ptr(), x.data_ptr(), None, x.data_ptr(), 2, 32776, 1e-5, 0,
                             s) == _lib.LMRS_ERR_SHAPE
     assert lib.lmrs_paged_attention_decode(x.data_ptr(), x.data_ptr(), x.data_ptr(), x.data_ptr(),
                                            x.data_ptr(), x.data_ptr(), 1, 8, 8, 64, 16, 1, 16,
