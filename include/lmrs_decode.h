@@ -42,7 +42,8 @@ LMRS_API int lmrs_silu_mul(void* out, const void* gate_up, int rows, int inter, 
                            lmrs_stream_t stream);
 
 /* Same, leaving as FP8 activations (bytes [rows, inter] + per-row scales);
- * inter <= 32768 (the row's absmax is taken in one CTA). */
+ * inter <= 65536 (rows wider than 8192 are split over a thread-block cluster
+ * whose CTAs exchange the row absmax through distributed shared memory). */
 LMRS_API int lmrs_silu_mul_fp8(uint8_t* q_out, float* scale_out, const void* gate_up, int rows,
                                int inter, int dtype, lmrs_stream_t stream);
 

@@ -47,6 +47,12 @@ int silu_launch(void* out, uint8_t* q, float* s, const void* gu, int rows, int i
     rc = launch_ex_grid(lmrs::silu_mul_kernel<T, FP8, 1>, dim3(rows, chunks, 1),
                         lmrs::kNormThreads, st, static_cast<T*>(out), q, s,
                         static_cast<const T*>(gu), inter);
+  } else if (inter > lmrs::kSiluClusterThreads * lmrs::kSiluClusterVecs * 8) {
+    // long rows: a cluster of CTAs per row, absmax exchanged through DSMEM
+    const int per = lmrs::kSiluClusterThreads * lmrs::kSiluClusterVecs * 8;
+    const int C = (inter + per - 1) / per;
+    rc = launch_ex_cluster3(lmrs::silu_mul_fp8_cluster_kernel<T>, dim3(rows, C, 1), dim3(1, C, 1),
+                            lmrs::kSiluClusterThreads, st, q, s, static_cast<const T*>(gu), inter);
   } else {
     int vpt, threads;
     row_shape(inter, &vpt, &threads);
@@ -66,6 +72,7 @@ void attn_split(int seqs, int hkv, int max_ctx, int sms, int* splits, int* span)
   const int tiles = max_ctx > 0 ? (max_ctx + lmrs::kAttnTile - 1) / lmrs::kAttnTile : 1;  // 64-pos units
   const int work = seqs * hkv > 0 ? seqs * hkv : 1;
   int s = clampi((g_tune.attn_ctas_per_sm * sms + work - 1) / work, 1, tiles);
+  if (s > lmrs::kAttnMaxSplits) s = lmrs::kAttnMaxSplits;  // the combine's weight table
   const int per = (tiles + s - 1) / s;
   *span = per * lmrs::kAttnTile;
   *splits = (tiles + per - 1) / per;
@@ -174,7 +181,9 @@ LMRS_API int lmrs_silu_mul(void* out, const void* gate_up, int rows, int inter, 
 LMRS_API int lmrs_silu_mul_fp8(uint8_t* q_out, float* scale_out, const void* gate_up, int rows,
                                int inter, int dtype, lmrs_stream_t stream) {
   if (!act_dtype(dtype)) return LMRS_ERR_DTYPE;
-  if (rows < 0 || inter <= 0 || inter % 8 || inter > kRowMaxCols) return LMRS_ERR_SHAPE;
+  if (rows < 0 || inter <= 0 || inter % 8 ||
+      inter > lmrs::kSiluMaxCluster * lmrs::kSiluClusterThreads * lmrs::kSiluClusterVecs * 8)
+    return LMRS_ERR_SHAPE;
   if (rows == 0) return LMRS_OK;
   if (!q_out || !scale_out || !gate_up) return LMRS_ERR_NULL;
   if (!aligned16(q_out) || !aligned16(gate_up)) return LMRS_ERR_ALIGN;

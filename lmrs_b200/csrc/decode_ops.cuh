@@ -19,6 +19,7 @@
 // All are launched with programmatic dependent launch and call pdl_wait before
 // touching their inputs.
 #pragma once
+#include <cooperative_groups.h>
 #include "fp8_kernels.cuh"
 #include "lmrs_ptx.cuh"
 
@@ -192,6 +193,61 @@ __global__ void __launch_bounds__(kRowMaxThreads) silu_mul_kernel(
 #pragma unroll
   for (int v = 0; v < VPT; ++v) {
     const int c = (v * blockDim.x + threadIdx.x) * 8;
+    if (c < I) *reinterpret_cast<uint2*>(qout + static_cast<int64_t>(row) * I + c) = e4m3x8(y[v], sc);
+  }
+}
+
+// FP8 silu * up for long rows: a cluster of C CTAs per row (grid (rows, C)),
+// each CTA VPT vectors per thread of its column chunk in registers; the row
+// absmax is exchanged through distributed shared memory (every CTA stores its
+// maximum into slot [rank] of every CTA, then one cluster barrier).
+constexpr int kSiluClusterThreads = 256;
+constexpr int kSiluClusterVecs = 4;
+constexpr int kSiluMaxCluster = 8;
+
+template <typename T>
+__global__ void __launch_bounds__(kSiluClusterThreads) silu_mul_fp8_cluster_kernel(
+    uint8_t* __restrict__ qout, float* __restrict__ qscale, const T* __restrict__ gu, int I) {
+  constexpr int VPT = kSiluClusterVecs;
+  pdl_wait();
+  pdl_trigger();
+  __shared__ float red[32];
+  __shared__ float slot[kSiluMaxCluster];
+  namespace cg = cooperative_groups;
+  cg::cluster_group cluster = cg::this_cluster();
+  const int C = static_cast<int>(cluster.num_blocks());
+  const int rank = static_cast<int>(cluster.block_rank());
+  const int row = blockIdx.x;
+  const int base = rank * kSiluClusterThreads * 8 * VPT;
+  const T* gr = gu + static_cast<int64_t>(row) * 2 * I;
+  float y[VPT][8];
+  float amax = 0.f;
+#pragma unroll
+  for (int v = 0; v < VPT; ++v) {
+    const int c = base + (v * kSiluClusterThreads + threadIdx.x) * 8;
+    if (c < I) {
+      float g[8], u[8];
+      unpack8<T>(*reinterpret_cast<const uint4*>(gr + c), g);
+      unpack8<T>(*reinterpret_cast<const uint4*>(gr + I + c), u);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        y[v][i] = Act<T>::f(Act<T>::t((g[i] / (1.0f + expf(-g[i]))) * u[i]));
+        amax = fmaxf(amax, fabsf(y[v][i]));
+      }
+    }
+  }
+  const float local = block_max(amax, red);
+  if (threadIdx.x < C) {  // thread r stores this CTA's maximum into CTA r's slot[rank]
+    st_cluster_f32(mapa_shared(smem_u32(&slot[rank]), static_cast<uint32_t>(threadIdx.x)), local);
+  }
+  cluster_sync_all();
+  float rmax = slot[0];
+  for (int r = 1; r < C; ++r) rmax = fmaxf(rmax, slot[r]);
+  const float sc = __fdiv_rn(rmax, 448.0f);
+  if (rank == 0 && threadIdx.x == 0) qscale[row] = sc;
+#pragma unroll
+  for (int v = 0; v < VPT; ++v) {
+    const int c = base + (v * kSiluClusterThreads + threadIdx.x) * 8;
     if (c < I) *reinterpret_cast<uint2*>(qout + static_cast<int64_t>(row) * I + c) = e4m3x8(y[v], sc);
   }
 }
@@ -603,24 +659,36 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(
 }
 
 // out[seq, h, :] = sum_s 2^(m_s - M) O_s / sum_s 2^(m_s - M) l_s over the splits.
+constexpr int kAttnMaxSplits = 1024;
+
+// Split-context merge, one CTA per (sequence, head): the split maxima and
+// weights f_s = 2^(m_s - M) are computed once (cooperatively, into shared
+// memory), then each thread (one of the 128 columns) sums f_s * acc_s with
+// independent loads.
 template <typename T>
 __global__ void __launch_bounds__(128) decode_attn_combine_kernel(T* __restrict__ out,
                                                                   const float* __restrict__ ws,
                                                                   int splits) {
   pdl_wait();
   pdl_trigger();
+  __shared__ float fs[kAttnMaxSplits];
+  __shared__ float red[32];
   const int sh = blockIdx.x;  // seq * num_heads + h
   const float* p = ws + static_cast<int64_t>(sh) * splits * (kAttnD + 2);
-  float M = -INFINITY;
-  for (int s = 0; s < splits; ++s) M = fmaxf(M, p[s * (kAttnD + 2) + kAttnD]);
-  float L = 0.f, acc = 0.f;
-  const int d = threadIdx.x;
-  for (int s = 0; s < splits; ++s) {
-    const float* ps = p + s * (kAttnD + 2);
-    const float f = M == -INFINITY ? 0.f : exp2f(ps[kAttnD] - M);
-    L += f * ps[kAttnD + 1];
-    acc += f * ps[d];
+  float m = -INFINITY;
+  for (int s = threadIdx.x; s < splits; s += blockDim.x) m = fmaxf(m, p[s * (kAttnD + 2) + kAttnD]);
+  const float M = block_max(m, red);
+  float l = 0.f;
+  for (int s = threadIdx.x; s < splits; s += blockDim.x) {
+    const float f = M == -INFINITY ? 0.f : exp2f(p[s * (kAttnD + 2) + kAttnD] - M);
+    fs[s] = f;
+    l += f * p[s * (kAttnD + 2) + kAttnD + 1];
   }
+  const float L = block_sum(l, red);  // its barriers also publish fs
+  const int d = threadIdx.x;
+  float acc = 0.f;
+#pragma unroll 8
+  for (int s = 0; s < splits; ++s) acc += fs[s] * p[s * (kAttnD + 2) + d];
   out[static_cast<int64_t>(sh) * kAttnD + d] = Act<T>::t(L > 0.f ? acc / L : 0.f);
 }
 

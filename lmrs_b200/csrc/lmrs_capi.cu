@@ -225,6 +225,34 @@ int launch_ex_grid(Kern kernel, dim3 grid, int threads, cudaStream_t stream, Arg
   return LMRS_OK;
 }
 
+// 2-D/3-D grid with a thread-block cluster shape, PDL when enabled.
+template <typename Kern, typename... Args>
+int launch_ex_cluster3(Kern kernel, dim3 grid, dim3 cluster, int threads, cudaStream_t stream,
+                       Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(threads, 1, 1);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  int n = 0;
+  attr[n].id = cudaLaunchAttributeClusterDimension;
+  attr[n].val.clusterDim.x = cluster.x;
+  attr[n].val.clusterDim.y = cluster.y;
+  attr[n].val.clusterDim.z = cluster.z;
+  ++n;
+  if (g_tune.pdl) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, args...);
+  if (e != cudaSuccess) return record(e);
+  return LMRS_OK;
+}
+
 template <typename Kern, typename... Args>
 int launch_cluster(Kern kernel, int grid_x, int cluster, int threads, int smem,
                    cudaStream_t stream, Args... args) {
