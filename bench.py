@@ -60,9 +60,9 @@ FP8_MS = [1, 32, 512, 8192]
 # No FP8 figure in MEASURED_PEAKS.json: torch._scaled_mm e4m3 8192^3 measured on
 # this pool's B200s (dense, burst) stands in as the FP8 tensor denominator.
 FP8_PEAK_TFLOPS = 3008.0
-# DRAM bytes (read + write) of one awq_gemm_tc_kernel launch at M=4096, from the
-# ncu capture recorded in profiles/awq_gemm_tc_config1_M2048.md (update with the kernel).
-AWQ_GEMM_M4096_DRAM_BYTES = 74558464 + 74811136
+# DRAM bytes (read + write) of one awq_gemm_tmem_kernel<256> launch at M=4096, from the
+# ncu capture recorded in profiles/awq_gemm_tmem_config1_M2048.md (update with the kernel).
+AWQ_GEMM_M4096_DRAM_BYTES = 93_220_000 + 73_690_000
 
 
 def peaks():
@@ -278,7 +278,7 @@ def run_awq(args, device, dist_on, world, rank):
     dom = max(range(len(AWQ_MS)), key=lambda j: per_ms[j])
     Md = AWQ_MS[dom]
     ach = awq_flops(Md) / (per_ms[dom] * 1e-3) / 1e12
-    roof = {"bound": "tensor", "kernel": f"awq_gemm_tc_kernel (M={Md})", "achieved": round(ach, 2),
+    roof = {"bound": "tensor", "kernel": f"awq_gemm_tmem_kernel<256> (M={Md})", "achieved": round(ach, 2),
             "peak": pk["bf16_tflops"], "unit": "TFLOP/s", "frac": round(ach / pk["bf16_tflops"], 4),
             "peak_source": f"{pk_kind} bf16 dense (burst)",
             "traffic": AWQ_GEMM_M4096_DRAM_BYTES if Md == 4096 else None,

@@ -1,0 +1,303 @@
+// awq_gemm_tmem.cuh — AWQ W4A16 prefill GEMM with the dequantised weights as the
+// tcgen05 A operand in tensor memory (roles swapped: D[channel][token]).
+//
+// Why: the shared-memory-staged GEMM (awq_gemm_tc_kernel) moves per 64-deep
+// K-block the token tile (TMA write + UMMA read) and the dequantised fp16
+// weight tile (st.shared + UMMA read) through shared memory, ~137 B/cycle at
+// the tensor rate against ~128 available; it stalls at ~0.62 of the bf16 peak.
+// Here the weights go CUDA cores -> TMEM (tcgen05.st) and are read by the MMA
+// from TMEM; only the token tile crosses shared memory, and each dequantised
+// weight serves BT tokens.
+//
+// One persistent CTA per SM walks tiles of 128 output channels (UMMA M, TMEM
+// lanes) x BT tokens (UMMA N), K in blocks of 64:
+//   * warp 0: TMA ring — lane 0 the token tile [BT rows x 64 k] (128 B
+//     swizzle, K-major: x as stored), lane 1 the packed weight rows [64 k x 16
+//     words]; tile coordinates once per tile.  (One thread issuing four copies
+//     plus the index arithmetic per K-block was the bottleneck: ~900 cycles per
+//     K-block for the bare pipeline.)
+//   * warp 1: TMEM owner and MMA issuer — per K-block four UMMAs M=128, N=BT,
+//     K=16, A from the TMEM stage, B from the token stage, then one commit
+//     that frees the stage; accumulators double-buffered (2 x BT columns) up
+//     to BT = 192, single at BT = 256.
+//   * warps 2-5: epilogue — TMEM lane = channel, 16 token columns per
+//     tcgen05.ld, + bias, transposed through shared memory so each lane stores
+//     16 contiguous channels of one token (two 16-byte stores): one-channel
+//     2-byte stores stalled the single-buffered accumulator at BT = 256.
+//   * warps 6-13: dequant, two groups of four taking alternate K-blocks (one
+//     warp per TMEM lane quarter and group) — TMEM lane = channel c; for rows r, r+1 one prmt
+//     gathers the byte holding c's nibble from both packed words and one lop3
+//     makes the biased half2 (1024 + q or 64 + q); each thread loads its own
+//     scale and zero word (2 + 4 bytes) one K-block ahead; subtracting the same-biased
+//     zero is exact and the multiply by the scale rounds once, so A holds
+//     exactly fp16_rne((q - z) * s); 32 columns (64 k) per tcgen05.st.
+// Every mbarrier wait is bounded; on expiry the kernel records the site in the
+// device error word and unwinds; TMEM is always released.
+#pragma once
+#include "awq_gemv.cuh"
+#include "lmrs_ptx.cuh"
+#include "tc_gemm.cuh"
+
+namespace lmrs {
+
+constexpr int kAgtCh = 128;          // output channels per tile (UMMA M)
+constexpr int kAgtWords = kAgtCh / 8;
+constexpr int kAgtBK = 64;           // k rows per stage
+constexpr int kAgtEpiWarp0 = 2;
+constexpr int kAgtDqWarp0 = 6;
+constexpr int kAgtDqGroups = 4;      // dequant warp groups, alternating K-blocks
+constexpr int kAgtThreads = 32 * (kAgtDqWarp0 + 4 * kAgtDqGroups);  // 448
+
+// Shared-memory ring of S stages (token tile + packed weights) and a TMEM ring of
+// R stages (dequantised weights, 32 columns each), R <= S.  One tcgen05.commit
+// per K-block (on the shared-memory slot's barrier) frees both: the dequant
+// warps reuse TMEM stage kg % R after the commit of K-block kg - R.  (A commit
+// costs ~280 cycles in the issuing thread; two per K-block are too many.)
+// Accumulators: two BT-column buffers when they leave room for two A stages, one
+// for BT = 256 (the A ring then buffers 8 K-blocks while the epilogue drains).
+template <int BT>
+struct AgtLayout {
+  static constexpr int kAccBufs = 2 * BT + 64 <= 512 ? 2 : 1;
+  static constexpr int kStages = BT == 128 ? 10 : (BT == 192 ? 7 : 6);  // as deep as shared memory allows
+  static constexpr int kATmem = (512 - kAccBufs * BT) / 32;  // A stages TMEM has room for
+  static constexpr int kAStages = kATmem < kStages ? (kATmem < 8 ? kATmem : 8) : (kStages < 8 ? kStages : 8);
+  static constexpr int kX = BT * kAgtBK * 2;        // token stage (1024-aligned)
+  static constexpr int kW = kAgtBK * kAgtWords * 4; // packed weight rows, 4 KB
+  static constexpr int kSmall = kW;
+  static constexpr uint32_t kTx = kX + kW;
+  static constexpr uint32_t kTmemA = kAccBufs * BT; // A stages after the accumulators
+  static constexpr uint32_t kTmemCols = 512;
+  static constexpr int kEpiPitch = 40;               // halves per token row of a warp's chunk
+  static constexpr int kEpi = 4 * 16 * kEpiPitch * 2; // epilogue transpose, 16 tokens x 32 channels per warp
+  static constexpr int kSmem = 1024 + kStages * (kX + kSmall) + kEpi + 256;
+  static_assert(kSmem <= 227 * 1024, "shared memory per CTA");
+  static_assert(kX % 1024 == 0, "128B-swizzled token stages are 1024-byte aligned");
+  static_assert(kSmall % 128 == 0, "TMA destinations are 128-byte aligned");
+  static_assert(kAccBufs * BT + 32 * kAStages <= 512 && kAStages >= 2 && kAStages <= kStages,
+                "TMEM columns");
+  static_assert(BT % 16 == 0 && BT <= 256, "UMMA N");
+};
+
+// Tile t -> (first token m0, first channel n0): groups of kTcGroupM token tiles
+// walked channel tile by channel tile, tokens fastest (x and weights stay in L2).
+template <int BT>
+__device__ __forceinline__ void agt_coords(int t, int m_tiles, int n_tiles, int& m0, int& n0) {
+  const int per_group = kTcGroupM * n_tiles;
+  const int grp = t / per_group;
+  const int first_m = grp * kTcGroupM;
+  const int gm = min(m_tiles - first_m, kTcGroupM);
+  const int local = t - grp * per_group;
+  m0 = (first_m + local % gm) * BT;
+  n0 = (local / gm) * kAgtCh;
+}
+
+template <int BT>
+__global__ void __launch_bounds__(kAgtThreads, 1) awq_gemm_tmem_kernel(
+    const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_q,
+    const __half* __restrict__ scales, const uint32_t* __restrict__ qzeros,
+    __half* __restrict__ y, const __half* __restrict__ bias, int M, int K, int N, int group) {
+  using L = AgtLayout<BT>;
+  constexpr int S = L::kStages, R = L::kAStages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sx = align1024(smem_raw);
+  uint8_t* ssm = sx + S * L::kX;
+  __half* sepi = reinterpret_cast<__half*>(ssm + S * L::kSmall);
+  uint64_t* full = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(sepi) + L::kEpi);
+  uint64_t* empty = full + S;
+  uint64_t* afull = empty + S;  // TMEM stage's dequantised weights are written
+  AccBars* acc = reinterpret_cast<AccBars*>(afull + R);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int KB = K / kAgtBK;
+  const int n_tiles = (N + kAgtCh - 1) / kAgtCh;
+  const int m_tiles = (M + BT - 1) / BT;
+  const int tiles = n_tiles * m_tiles;
+  const int my_tiles = blockIdx.x < tiles ? (tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+  const int total = my_tiles * KB;  // K-blocks this CTA streams
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < R; ++a) mbar_init(&afull[a], 4);  // one arrive per dequant warp
+    acc_bars_init(acc);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, L::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  pdl_trigger();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- TMA ring
+    // lane 0 owns the stage's transaction count and the token tile, lane 1 the
+    // packed weights (which may land first: the count then dips below zero)
+    if (lane < 2) {
+      if (lane == 0) tma_prefetch_desc(&tm_x); else tma_prefetch_desc(&tm_q);
+      const uint64_t keep = policy_evict_last();  // token tiles are re-read by every channel tile
+      if (lane == 0) pdl_wait();  // the tokens are the previous kernel's output
+      int m0 = 0, n0 = 0;
+      for (uint32_t kg = 0; kg < static_cast<uint32_t>(total); ++kg) {
+        const int kb = static_cast<int>(kg % KB);
+        if (kb == 0)
+          agt_coords<BT>(blockIdx.x + static_cast<int>(kg / KB) * gridDim.x, m_tiles, n_tiles, m0, n0);
+        const int s = kg % S;
+        if (kg >= static_cast<uint32_t>(S) && !mbar_wait(&empty[s], ((kg / S) - 1) & 1, kErrWaitEmpty))
+          break;
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&full[s], L::kTx);
+          tma_load_2d_hint(&tm_x, &full[s], sx + s * L::kX, kb * kAgtBK, m0, keep);
+        } else {
+          tma_load_2d(&tm_q, &full[s], ssm + s * L::kSmall, n0 / 8, kb * kAgtBK);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA
+    if (lane == 0) {
+      constexpr uint32_t idesc = make_idesc(0, 0, 0, 0, kAgtCh, BT);  // f16 x f16, K-major
+      uint32_t kg = 0, it = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++it) {
+        const uint32_t a = it % L::kAccBufs, use = it / L::kAccBufs;
+        if (!(ok = mbar_wait(&acc->empty[a], (use & 1) ^ 1, kErrWaitAccum))) break;
+        tc_fence_after();
+        const uint32_t d = tmem + a * BT;
+        for (int kb = 0; kb < KB; ++kb, ++kg) {
+          const int s = kg % S, ar = kg % R;
+          ok = mbar_wait(&full[s], (kg / S) & 1, kErrWaitFull) &&
+               mbar_wait(&afull[ar], (kg / R) & 1, kErrWaitDequant);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t xs = smem_u32(sx + s * L::kX);
+          const uint32_t acol = tmem + L::kTmemA + ar * 32;
+#pragma unroll
+          for (int kk = 0; kk < kAgtBK / 16; ++kk)
+            umma_f16_tmem_a(d, acol + kk * 8, make_sdesc(xs + kk * 32, 16, 1024), idesc,
+                            (kb | kk) != 0 ? 1u : 0u);
+          umma_commit(&empty[s]);  // slot s and TMEM stage ar are free
+        }
+        if (ok) umma_commit(&acc->full[a]);
+      }
+    }
+  } else if (warp < kAgtDqWarp0) {
+    // ------------------------------------------- epilogue: lane = output channel
+    const int quarter = warp & 3;
+    const int c = quarter * 32 + lane;
+    const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
+    pdl_wait();  // y may still be read by the previous kernel
+    uint32_t it = 0;
+    for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++it) {
+      const uint32_t a = it % L::kAccBufs;
+      if (!mbar_wait(&acc->full[a], (it / L::kAccBufs) & 1, kErrWaitAccum)) break;
+      tc_fence_after();
+      int m0, n0;
+      agt_coords<BT>(t, m_tiles, n_tiles, m0, n0);
+      const int n = n0 + c;
+      const float bn = (bias != nullptr && n < N) ? __half2float(bias[n]) : 0.f;
+      __half* tw = sepi + quarter * 16 * L::kEpiPitch;
+      const int te = lane >> 1, th = lane & 1;          // read side: token, 16-channel half
+      const int nw = n0 + quarter * 32 + 16 * th;       // N % 32 == 0: whole 16-channel runs
+      for (int ch = 0; ch < BT / 16; ++ch) {
+        uint32_t r[16];
+        tmem_ld16(tmem + lane_addr + a * BT + ch * 16, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int e = 0; e < 16; ++e) tw[e * L::kEpiPitch + lane] = __float2half_rn(__uint_as_float(r[e]) + bn);
+        __syncwarp();
+        const int m = m0 + ch * 16 + te;
+        if (m < M && nw < N) {
+          const uint4* src = reinterpret_cast<const uint4*>(tw + te * L::kEpiPitch + 16 * th);
+          uint4* dst = reinterpret_cast<uint4*>(y + static_cast<int64_t>(m) * N + nw);
+          dst[0] = src[0];
+          dst[1] = src[1];
+        }
+        __syncwarp();
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc->empty[a]);
+    }
+  } else {
+    // ------------------------------------------- dequant: lane = output channel
+    const int quarter = warp & 3;
+    const int dgrp = (warp - kAgtDqWarp0) >> 2;
+    const int c = quarter * 32 + lane;
+    const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
+    const int w = c >> 3;
+    // nibble i of word w holds column 8w + ORDER[i], ORDER = {0,2,4,6,1,3,5,7}
+    const int j = c & 7;
+    const int i = (j >> 1) | ((j & 1) << 2);
+    const int byte = i >> 1, hi = i & 1;
+    const uint32_t sel = static_cast<uint32_t>(byte) | (static_cast<uint32_t>(4 + byte) << 8);
+    const uint32_t mask = hi ? 0x00F000F0u : 0x000F000Fu;
+    const uint32_t magic = hi ? 0x54005400u : 0x64006400u;
+    const int words = N / 8;
+    // this thread's scale (fp16 bits) and zero word for K-block kg
+    int ftile = -1, fm0 = 0, n0 = 0;
+    auto fetch = [&](uint32_t kg, uint32_t& sv, uint32_t& zv) {
+      sv = 0u;
+      zv = 0u;
+      if (kg >= static_cast<uint32_t>(total)) return;
+      const int tt = static_cast<int>(kg / KB);
+      if (tt != ftile) {
+        ftile = tt;
+        agt_coords<BT>(blockIdx.x + tt * gridDim.x, m_tiles, n_tiles, fm0, n0);
+      }
+      const int gi = static_cast<int>(kg % KB) * kAgtBK / group;
+      const int n = n0 + c;
+      if (n < N) {
+        sv = reinterpret_cast<const uint16_t*>(scales)[static_cast<int64_t>(gi) * N + n];
+        zv = qzeros[static_cast<int64_t>(gi) * words + (n >> 3)];
+      }
+    };
+    uint32_t s_nxt, z_nxt;
+    fetch(dgrp, s_nxt, z_nxt);
+    bool ok = true;
+    for (uint32_t kg = dgrp; kg < static_cast<uint32_t>(total) && ok; kg += kAgtDqGroups) {
+      const uint32_t s_cur = s_nxt, z_cur = z_nxt;
+      fetch(kg + kAgtDqGroups, s_nxt, z_nxt);
+      const int s = kg % S, ar = kg % R;
+      if (!(ok = mbar_wait(&full[s], (kg / S) & 1, kErrWaitFull))) break;
+      // TMEM stage ar was last read by the MMAs of K-block j = kg - R: wait for
+      // its commit (on slot j % S).  That phase cannot have been overtaken: the
+      // next commit on that slot is K-block j + S > kg, issued after kg's MMAs.
+      if (kg >= static_cast<uint32_t>(R)) {
+        const uint32_t j = kg - R;
+        if (!(ok = mbar_wait(&empty[j % S], (j / S) & 1, kErrWaitAccum))) break;
+      }
+      const uint8_t* sm = ssm + s * L::kSmall;
+      const uint32_t z = (z_cur >> (4 * i)) & 0xFu;
+      const uint32_t zz = (hi ? (0x5400u | (z << 4)) : (0x6400u | z)) * 0x00010001u;
+      const uint32_t ss = s_cur | (s_cur << 16);
+      const uint8_t* wb = sm + 4 * w;
+      uint32_t r[32];
+#pragma unroll
+      for (int p = 0; p < 32; ++p) {  // column p = k rows (2p, 2p+1)
+        const uint32_t wa = ld_s32(wb + (2 * p) * (kAgtWords * 4));
+        const uint32_t wc = ld_s32(wb + (2 * p + 1) * (kAgtWords * 4));
+        r[p] = dq_h2(lop3_and_or(prmt(wa, wc, sel), mask, magic), zz, ss);
+      }
+      tmem_st32(tmem + lane_addr + L::kTmemA + ar * 32, r);
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&afull[ar]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, L::kTmemCols);
+  }
+}
+
+}  // namespace lmrs

@@ -31,6 +31,7 @@
 #include "tc_gemm2.cuh"
 #include "fp8_swap.cuh"
 #include "awq_tmem.cuh"
+#include "awq_gemm_tmem.cuh"
 
 namespace {
 
@@ -64,6 +65,8 @@ struct Tuning {
   int awq_tmem_wide_n = 12288;  // ... and down to M = 9 when N is at least this
   int awq_tmem_cluster = 0;  // 0 = heuristic
   int awq_tmem_ctas_per_sm = 2;
+  int awq_gemm_tmem = 1;     // prefill: GEMM with the weights as the TMEM A operand (0: smem-staged)
+  int awq_gemm_tmem_bt = 256;  // its token tile (128, 192 or 256; 256 measured fastest at every M)
 };
 Tuning g_tune;
 
@@ -462,6 +465,44 @@ int awq_swap_launch(__half* y, const __half* x, const int32_t* qw, const int32_t
 
 std::atomic<int> g_smem_awq_gemm2[kMaxDevices];
 
+std::atomic<int> g_smem_awq_gemm_tmem[3][kMaxDevices];
+
+template <int BT>
+int awq_gemm_tmem_launch_t(__half* y, const __half* x, const int32_t* qw, const int32_t* qz,
+                           const __half* sc, const __half* bias, int M, int K, int N, int group,
+                           cudaStream_t stream, int dev, std::atomic<int>* done) {
+  using L = lmrs::AgtLayout<BT>;
+  CUtensorMap tx, tq;
+  int rc;
+  if ((rc = make_tmap(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, x, K, M, uint64_t(K) * 2, 64, BT,
+                      CU_TENSOR_MAP_SWIZZLE_128B)))
+    return rc;
+  if ((rc = make_tmap(&tq, CU_TENSOR_MAP_DATA_TYPE_INT32, qw, N / 8, K, uint64_t(N / 8) * 4,
+                      lmrs::kAgtWords, lmrs::kAgtBK, CU_TENSOR_MAP_SWIZZLE_NONE)))
+    return rc;
+  if ((rc = ensure_smem(lmrs::awq_gemm_tmem_kernel<BT>, L::kSmem, done, dev))) return rc;
+  const int tiles = ((N + lmrs::kAgtCh - 1) / lmrs::kAgtCh) * ((M + BT - 1) / BT);
+  const int grid = tiles < sm_count(dev) ? tiles : sm_count(dev);
+  rc = launch_ex(lmrs::awq_gemm_tmem_kernel<BT>, grid, 0, lmrs::kAgtThreads, L::kSmem, stream, tx,
+                 tq, sc, reinterpret_cast<const uint32_t*>(qz), y, bias, M, K, N, group);
+  return rc ? rc : after_launch();
+}
+
+int awq_gemm_tmem_launch(__half* y, const __half* x, const int32_t* qw, const int32_t* qz,
+                         const __half* sc, const __half* bias, int M, int K, int N, int group,
+                         cudaStream_t stream, int dev) {
+  const int f = g_tune.awq_gemm_tmem_bt;
+  const int bt = (f == 128 || f == 192) ? f : 256;
+  if (bt == 128)
+    return awq_gemm_tmem_launch_t<128>(y, x, qw, qz, sc, bias, M, K, N, group, stream, dev,
+                                       g_smem_awq_gemm_tmem[0]);
+  if (bt == 192)
+    return awq_gemm_tmem_launch_t<192>(y, x, qw, qz, sc, bias, M, K, N, group, stream, dev,
+                                       g_smem_awq_gemm_tmem[1]);
+  return awq_gemm_tmem_launch_t<256>(y, x, qw, qz, sc, bias, M, K, N, group, stream, dev,
+                                     g_smem_awq_gemm_tmem[2]);
+}
+
 int awq_gemm2_launch(__half* y, const __half* x, const int32_t* qw, const int32_t* qz,
                      const __half* sc, const __half* bias, int M, int K, int N, int group,
                      cudaStream_t stream, int dev) {
@@ -762,6 +803,8 @@ int lmrs_set_tuning(const char* key, int value) {
   else if (!strcmp(key, "fp8_swap_max_m")) g_tune.fp8_swap_max_m = value;
   else if (!strcmp(key, "fp8_gemv_max_kn")) g_tune.fp8_gemv_max_kn = value;
   else if (!strcmp(key, "awq_tmem_max_m")) g_tune.awq_tmem_max_m = value;
+  else if (!strcmp(key, "awq_gemm_tmem")) g_tune.awq_gemm_tmem = value ? 1 : 0;
+  else if (!strcmp(key, "awq_gemm_tmem_bt")) g_tune.awq_gemm_tmem_bt = value;
   else if (!strcmp(key, "awq_tmem_min_m")) g_tune.awq_tmem_min_m = value;
   else if (!strcmp(key, "awq_tmem_wide_n")) g_tune.awq_tmem_wide_n = value;
   else if (!strcmp(key, "awq_tmem_cluster")) g_tune.awq_tmem_cluster = value;
@@ -841,6 +884,10 @@ int lmrs_awq_linear(void* y, const void* x, const int32_t* qweight, const int32_
                            K, N, group, st, dev);
   if (M <= g_tune.awq_swap_max_m && M <= 128)
     return awq_swap_launch(yh, xh, qweight, qzeros, sh, bh, M, K, N, group, st, dev);
+  // up to one token tile, more 128-channel tiles than SMs leave a tail wave the
+  // 256-channel smem-staged tiles avoid
+  if (g_tune.awq_gemm_tmem && (M > 128 || (N + lmrs::kAgtCh - 1) / lmrs::kAgtCh <= sm_count(dev)))
+    return awq_gemm_tmem_launch(yh, xh, qweight, qzeros, sh, bh, M, K, N, group, st, dev);
   if (g_tune.awq_gemm_pair)
     return awq_gemm2_launch(yh, xh, qweight, qzeros, sh, bh, M, K, N, group, st, dev);
   return awq_gemm_launch(yh, xh, qweight, qzeros, sh, bh, M, K, N, group, st, dev);

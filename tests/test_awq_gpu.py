@@ -202,11 +202,12 @@ def test_status_codes(cuda):
                                            ("awq_gemv_slots", 8, (5, 16)),
                                            ("awq_gemv4_slots", 8, (1, 4)),
                                            ("awq_tmem_max_m", 0, (17, 24, 32)),
+                                           ("awq_gemm_tmem", 0, (100, 300, 512)),
                                            ("pdl", 0, (1, 8, 20, 40, 300))])
 def test_opt_in_paths(cuda, knob, value, Ms):
     """Kernels and launch shapes the default dispatch does not pick for these M
-    (CTA-pair GEMM, swap-AB below 17 or from 17 to 32 tokens (where the
-    TMEM-staged kernel is the default) or above 64, the general GEMV for
+    (CTA-pair GEMM, the shared-memory-staged GEMM, swap-AB below 17 or from 17
+    to 32 tokens (where the TMEM-staged kernel is the default) or above 64, the general GEMV for
     M <= 4, 64-row boxes, other cluster sizes and ring depths, launches without
     programmatic dependent launch) stay correct and deterministic when selected."""
     import torch
@@ -214,10 +215,14 @@ def test_opt_in_paths(cuda, knob, value, Ms):
     from lmrs_b200 import _lib
     defaults = {"awq_gemm_pair": 0, "awq_gemv_max_m": 16, "awq_swap_max_m": 64, "gemm_bn": 256,
                 "awq_gemv4": 1, "gemv_box_rows": 128, "awq_gemv_cluster": 0, "awq_gemv_slots": 4,
-                "awq_gemv4_slots": 4, "awq_tmem_max_m": 32, "pdl": 1}
+                "awq_gemv4_slots": 4, "awq_tmem_max_m": 32, "awq_gemm_tmem": 1, "pdl": 1}
     K, N, g = 1024, 1280, 128
+    # the smem-staged GEMM's own knobs are only reached with the TMEM GEMM off
+    also_off = knob in ("awq_gemm_pair", "gemm_bn")
     try:
         L.set_tuning(knob, value)
+        if also_off:
+            L.set_tuning("awq_gemm_tmem", 0)
         for M in Ms:
             d = O.awq_inputs(M, K, N, g, seed=M + 7, with_bias=True)
             qw, qz, sc, x, b = _awq_dev(d, cuda)
@@ -228,6 +233,7 @@ def test_opt_in_paths(cuda, knob, value, Ms):
                 assert torch.equal(L.awq_linear(x, qw, qz, sc, b, g), y), (knob, M, "nondeterministic")
     finally:
         L.set_tuning(knob, defaults[knob])
+        L.set_tuning("awq_gemm_tmem", 1)
     assert L.read_device_error() == 0
 
 
@@ -276,3 +282,22 @@ def test_tmem_linear_clusters(cuda, C, M):
         L.set_tuning("awq_tmem_min_m", 17)
         L.set_tuning("awq_tmem_cluster", 0)
     assert err < TIGHT, err
+
+
+@pytest.mark.parametrize("bt", [128, 192, 256])
+@pytest.mark.parametrize("M,K,N,g", [(65, 1024, 1280, 128), (128, 2048, 1312, 64), (200, 1024, 768, 128),
+                                     (513, 3072, 640, 256), (1000, 1024, 2048, 128)])
+def test_gemm_tmem_opt_in(cuda, bt, M, K, N, g):
+    """Prefill GEMM with the dequantised weights as the TMEM A operand (the
+    default above 64 tokens): ragged token and channel tiles, groups of
+    64/128/256 rows, every token-tile width, deterministic across calls."""
+    import torch
+    import lmrs_b200 as L
+    try:
+        L.set_tuning("awq_gemm_tmem_bt", bt)
+        err, (x, qw, qz, sc, b, y) = _awq_case(cuda, M, K, N, g, 900 + M + bt)
+        assert torch.equal(L.awq_linear(x, qw, qz, sc, b, g), y)
+    finally:
+        L.set_tuning("awq_gemm_tmem_bt", 256)
+    assert err < TIGHT, err
+    assert L.read_device_error() == 0
