@@ -24,6 +24,7 @@
 #include "awq_gemm_swap.cuh"
 #include "awq_gemv.cuh"
 #include "awq_gemv4.cuh"
+#include "awq_i8.cuh"
 #include "awq_pack.cuh"
 #include "fp8_kernels.cuh"
 #include "lmrs_ptx.cuh"
@@ -67,6 +68,11 @@ struct Tuning {
   int awq_tmem_ctas_per_sm = 2;
   int awq_gemm_tmem = 1;     // prefill: GEMM with the weights as the TMEM A operand (0: smem-staged)
   int awq_gemm_tmem_bt = 256;  // its token tile (128, 192 or 256; 256 measured fastest at every M)
+  int awq_i8_max_m = 1;      // M up to this (2 at most): packed bytes as integer MMA operands
+  int awq_i8_slots = 5;      // its ring slots at most (fewer when the grid fills the SMs)
+  int awq_i8_ctas_per_sm = 2;
+  int awq_i8_cluster = 0;    // 0 = heuristic (1..8)
+  int awq_i8_box_rows = 128; // its box height for groups of 128k rows (128 or 64)
 };
 Tuning g_tune;
 
@@ -367,9 +373,86 @@ int awq_tmem_launch(__half* y, const __half* x, const int32_t* qw, const int32_t
                                g_smem_awq_tmem[1]);
 }
 
+std::atomic<int> g_smem_awq_i8[4][kMaxDevices];
+
+template <int TOK, int BR>
+int awq_i8_launch_t(const CUtensorMap& tq, const CUtensorMap& ts, const CUtensorMap& tz,
+                    const __half* x, __half* y, const __half* bias, int M, int K, int N, int group,
+                    cudaStream_t stream, int dev, int strips, int C, int S, int nbmax,
+                    std::atomic<int>* done) {
+  using L = lmrs::AwqI8Layout<TOK, BR>;
+  // Slots: as many as asked (up to the CTA's box count) while the grid takes at
+  // most 80 % of the CTAs that fit per SM at that size, so that the next kernel
+  // can become resident early (programmatic dependent launch); at least 2.
+  const int ctas = strips * C;
+  auto fits = [&](int s) {
+    const int smem = L::smem_bytes(s);
+    const int per_sm = smem <= 227 * 1024 ? (228 * 1024) / (smem + 1024) : 0;
+    return per_sm > 0 && ctas * 5 <= per_sm * sm_count(dev) * 4;
+  };
+  if (S > nbmax) S = nbmax;
+  while (S > 2 && !fits(S)) --S;
+  while (S > 2 && L::smem_bytes(S) > 227 * 1024) --S;
+  const int smem = L::smem_bytes(S);
+  if (smem > 227 * 1024) return -1;
+  CUtensorMap tx;
+  int rc;
+  if ((rc = make_tmap(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, x, K, M, uint64_t(K) * 2, BR, TOK,
+                      CU_TENSOR_MAP_SWIZZLE_NONE)))
+    return rc;
+  if ((rc = ensure_smem(lmrs::awq_gemv_i8_kernel<TOK, BR>, smem, done, dev))) return rc;
+  rc = launch_ex(lmrs::awq_gemv_i8_kernel<TOK, BR>, ctas, C, lmrs::kI8Threads, smem, stream, tq,
+                 ts, tz, tx, y, bias, M, K, N, group, S);
+  return rc ? rc : after_launch();
+}
+
+// 1-2 tokens with the packed bytes as integer MMA operands.  Returns -1 when
+// the shape does not fit the kernel (the caller then takes the fp16 GEMV).
+int awq_i8_launch(__half* y, const __half* x, const int32_t* qw, const uint32_t* qz,
+                  const __half* sc, const __half* bias, int M, int K, int N, int group,
+                  cudaStream_t stream, int dev) {
+  const int BR = group % 128 == 0 && g_tune.awq_i8_box_rows != 64 ? 128 : 64;
+  if (M < 1 || M > 2 || K % BR) return -1;
+  const int strips = (N + lmrs::kI8Strip - 1) / lmrs::kI8Strip;
+  const int nb_all = K / BR;
+  int C = g_tune.awq_i8_cluster > 0
+              ? g_tune.awq_i8_cluster
+              : (sm_count(dev) * clampi(g_tune.awq_i8_ctas_per_sm, 1, 4)) / strips;
+  C = clampi(C, 1, lmrs::kI8MaxCluster);
+  if (C > nb_all) C = nb_all;
+  const int nbmax = (nb_all + C - 1) / C;
+  const int S = clampi(g_tune.awq_i8_slots, 2, 12);
+  CUtensorMap tq, ts, tz;
+  int rc;
+  if ((rc = make_tmap(&tq, CU_TENSOR_MAP_DATA_TYPE_INT32, qw, N / 8, K, uint64_t(N / 8) * 4,
+                      lmrs::kI8Words, BR, CU_TENSOR_MAP_SWIZZLE_128B)))
+    return rc;
+  if ((rc = make_tmap(&ts, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, sc, N, K / group, uint64_t(N) * 2,
+                      lmrs::kI8Strip, 1, CU_TENSOR_MAP_SWIZZLE_NONE)))
+    return rc;
+  if ((rc = make_tmap(&tz, CU_TENSOR_MAP_DATA_TYPE_INT32, qz, N / 8, K / group,
+                      uint64_t(N / 8) * 4, lmrs::kI8Words, 1, CU_TENSOR_MAP_SWIZZLE_NONE)))
+    return rc;
+  if (M == 1 && BR == 128)
+    return awq_i8_launch_t<1, 128>(tq, ts, tz, x, y, bias, M, K, N, group, stream, dev, strips, C,
+                                   S, nbmax, g_smem_awq_i8[0]);
+  if (M == 1)
+    return awq_i8_launch_t<1, 64>(tq, ts, tz, x, y, bias, M, K, N, group, stream, dev, strips, C,
+                                  S, nbmax, g_smem_awq_i8[1]);
+  if (BR == 128)
+    return awq_i8_launch_t<2, 128>(tq, ts, tz, x, y, bias, M, K, N, group, stream, dev, strips, C,
+                                   S, nbmax, g_smem_awq_i8[2]);
+  return awq_i8_launch_t<2, 64>(tq, ts, tz, x, y, bias, M, K, N, group, stream, dev, strips, C, S,
+                                nbmax, g_smem_awq_i8[3]);
+}
+
 int awq_gemv_launch(__half* y, const __half* x, const int32_t* qw, const uint32_t* qz,
                     const __half* sc, const __half* bias, int M, int K, int N, int group,
                     cudaStream_t stream, int dev) {
+  if (M <= g_tune.awq_i8_max_m) {
+    const int rc = awq_i8_launch(y, x, qw, qz, sc, bias, M, K, N, group, stream, dev);
+    if (rc >= 0) return rc;
+  }
   const int BR = (group % 128 == 0 && g_tune.gemv_box_rows != 64) ? 128 : 64;
   const int MT = M <= 8 ? 1 : 2;
   const int strips = (N + lmrs::kAwqGemvStrip - 1) / lmrs::kAwqGemvStrip;
@@ -810,6 +893,11 @@ int lmrs_set_tuning(const char* key, int value) {
   else if (!strcmp(key, "awq_tmem_cluster")) g_tune.awq_tmem_cluster = value;
   else if (!strcmp(key, "awq_tmem_ctas_per_sm")) g_tune.awq_tmem_ctas_per_sm = value;
   else if (!strcmp(key, "fp8_swap_cluster")) g_tune.fp8_swap_cluster = value;
+  else if (!strcmp(key, "awq_i8_max_m")) g_tune.awq_i8_max_m = value;
+  else if (!strcmp(key, "awq_i8_slots")) g_tune.awq_i8_slots = value;
+  else if (!strcmp(key, "awq_i8_ctas_per_sm")) g_tune.awq_i8_ctas_per_sm = value;
+  else if (!strcmp(key, "awq_i8_cluster")) g_tune.awq_i8_cluster = value;
+  else if (!strcmp(key, "awq_i8_box_rows")) g_tune.awq_i8_box_rows = value;
   else return LMRS_ERR_SHAPE;
   return LMRS_OK;
 }

@@ -220,6 +220,7 @@ def test_opt_in_paths(cuda, knob, value, Ms):
     # the smem-staged GEMM's own knobs are only reached with the TMEM GEMM off
     also_off = knob in ("awq_gemm_pair", "gemm_bn")
     try:
+        L.set_tuning("awq_i8_max_m", 0)   # 1-2 tokens: the fp16 GEMVs these knobs steer
         L.set_tuning(knob, value)
         if also_off:
             L.set_tuning("awq_gemm_tmem", 0)
@@ -234,6 +235,7 @@ def test_opt_in_paths(cuda, knob, value, Ms):
     finally:
         L.set_tuning(knob, defaults[knob])
         L.set_tuning("awq_gemm_tmem", 1)
+        L.set_tuning("awq_i8_max_m", 1)
     assert L.read_device_error() == 0
 
 
