@@ -63,8 +63,10 @@ LMRS_API int lmrs_rope_kv_write(void* q_out, void* key_cache, void* value_cache,
                                 int block_size, int max_blocks_per_seq, int dtype,
                                 lmrs_stream_t stream);
 
-/* Workspace for lmrs_paged_attention_decode (split-context partials); 0 when
- * the launch needs none. */
+/* Workspace for lmrs_paged_attention_decode: 0 (the context splits of one
+ * sequence and KV head form a thread-block cluster and merge their partials in
+ * distributed shared memory).  Kept so that bindings written against a scratch
+ * buffer keep working. */
 LMRS_API size_t lmrs_paged_attention_workspace_bytes(int num_seqs, int num_heads,
                                                      int num_kv_heads, int max_context);
 
@@ -74,7 +76,7 @@ LMRS_API size_t lmrs_paged_attention_workspace_bytes(int num_seqs, int num_heads
  *   max_context   an upper bound of context_lens (sizes the context split),
  *   kv_head_map   0: q head h reads KV head h % num_kv_heads (the reference's
  *                 kernel), 1: h / (num_heads / num_kv_heads) (grouped heads),
- *   workspace     lmrs_paged_attention_workspace_bytes(...) bytes.
+ *   workspace     unused (may be NULL).
  * head_size must be 128; num_heads / num_kv_heads <= 16.  out[s, h, :] =
  * softmax(scale * q . k) v over positions [0, context_lens[s]); context 0 gives 0. */
 LMRS_API int lmrs_paged_attention_decode(void* out, const void* query, const void* key_cache,

@@ -67,57 +67,57 @@ int silu_launch(void* out, uint8_t* q, float* s, const void* gu, int rows, int i
   return rc ? rc : after_launch();
 }
 
-// context split of the decode attention: ~2 CTAs per SM, whole 64-position tiles
+// context split of the decode attention: ~2 CTAs per SM, whole 64-position tiles,
+// at most one cluster's worth of splits (they merge in distributed shared memory)
 void attn_split(int seqs, int hkv, int max_ctx, int sms, int* splits, int* span) {
   const int tiles = max_ctx > 0 ? (max_ctx + lmrs::kAttnTile - 1) / lmrs::kAttnTile : 1;  // 64-pos units
   const int work = seqs * hkv > 0 ? seqs * hkv : 1;
   int s = clampi((g_tune.attn_ctas_per_sm * sms + work - 1) / work, 1, tiles);
-  if (s > lmrs::kAttnMaxSplits) s = lmrs::kAttnMaxSplits;  // the combine's weight table
+  if (s > lmrs::kAttnMaxCluster) s = lmrs::kAttnMaxCluster;
   const int per = (tiles + s - 1) / s;
   *span = per * lmrs::kAttnTile;
   *splits = (tiles + per - 1) / per;
 }
 
 std::atomic<int> g_smem_attn[2][3][kMaxDevices];
-// per warp: NS stages of 16 K rows + 16 V rows; at least the end-of-kernel merge buffer
-constexpr int attn_smem(int ns) {
-  return 4 * ns * 2 * 16 * lmrs::kAttnRowBytes > 4 * 16 * (lmrs::kAttnD + 2) * 4
-             ? 4 * ns * 2 * 16 * lmrs::kAttnRowBytes
-             : 4 * 16 * (lmrs::kAttnD + 2) * 4;
-}
 
 template <typename T, int NS>
-int attn_launch(void* out, void* ws, const void* q, const void* kc, const void* vc,
+int attn_launch(void* out, const void* q, const void* kc, const void* vc,
                 const int32_t* tables, const int32_t* lens, int seqs, int heads, int hkv,
                 int bs, int maxb, int splits, int span, float scale, int map, cudaStream_t st,
                 int dev, std::atomic<int>* done) {
   int rc;
-  if ((rc = ensure_smem(lmrs::decode_attn_kernel<T, NS>, attn_smem(NS), done, dev))) return rc;
+  if ((rc = ensure_smem(lmrs::decode_attn_kernel<T, NS>, lmrs::attn_smem_bytes(NS), done, dev)))
+    return rc;
   const float scale_log2 = scale * 1.4426950408889634f;
   // grid (seqs * hkv, splits): launch_ex is 1-D, so pack the split into y here
   cudaLaunchConfig_t c = {};
   c.gridDim = dim3(seqs * hkv, splits, 1);
   c.blockDim = dim3(lmrs::kAttnThreads, 1, 1);
-  c.dynamicSmemBytes = attn_smem(NS);
+  c.dynamicSmemBytes = lmrs::attn_smem_bytes(NS);
   c.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  c.attrs = attr;
-  c.numAttrs = g_tune.pdl ? 1 : 0;
-  cudaError_t e = cudaLaunchKernelEx(&c, lmrs::decode_attn_kernel<T, NS>, static_cast<T*>(out),
-                                     static_cast<float*>(ws), static_cast<const T*>(q),
-                                     static_cast<const T*>(kc), static_cast<const T*>(vc), tables,
-                                     lens, heads, hkv, bs, maxb, span, scale_log2, map);
-  if (e != cudaSuccess) return record(e);
-  if ((rc = after_launch())) return rc;
-  if (splits > 1) {
-    rc = launch_ex(lmrs::decode_attn_combine_kernel<T>, seqs * heads, 0, lmrs::kAttnD, 0, st,
-                   static_cast<T*>(out), static_cast<const float*>(ws), splits);
-    if (rc) return rc;
-    return after_launch();
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  if (splits > 1) {   // the splits of one (sequence, KV head) merge inside their cluster
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = 1;
+    attr[na].val.clusterDim.y = splits;
+    attr[na].val.clusterDim.z = 1;
+    ++na;
   }
-  return LMRS_OK;
+  if (g_tune.pdl) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  c.attrs = attr;
+  c.numAttrs = na;
+  cudaError_t e = cudaLaunchKernelEx(&c, lmrs::decode_attn_kernel<T, NS>, static_cast<T*>(out),
+                                     static_cast<const T*>(q), static_cast<const T*>(kc),
+                                     static_cast<const T*>(vc), tables, lens, heads, hkv, bs, maxb,
+                                     span, scale_log2, map);
+  if (e != cudaSuccess) return record(e);
+  return after_launch();
 }
 
 }  // namespace
@@ -234,11 +234,8 @@ LMRS_API int lmrs_rope_kv_write(void* q_out, void* key_cache, void* value_cache,
 
 LMRS_API size_t lmrs_paged_attention_workspace_bytes(int num_seqs, int num_heads,
                                                      int num_kv_heads, int max_context) {
-  if (num_seqs <= 0 || num_heads <= 0 || num_kv_heads <= 0) return 0;
-  int splits, span;
-  attn_split(num_seqs, num_kv_heads, max_context, sm_count_cached(), &splits, &span);
-  if (splits <= 1) return 0;
-  return static_cast<size_t>(num_seqs) * num_heads * splits * (lmrs::kAttnD + 2) * sizeof(float);
+  (void)num_seqs; (void)num_heads; (void)num_kv_heads; (void)max_context;
+  return 0;   // split partials merge in distributed shared memory
 }
 
 LMRS_API int lmrs_paged_attention_decode(void* out, const void* query, const void* key_cache,
@@ -263,15 +260,12 @@ LMRS_API int lmrs_paged_attention_decode(void* out, const void* query, const voi
   if (rc) return rc;
   int splits, span;
   attn_split(num_seqs, num_kv_heads, max_context, sm_count(dev), &splits, &span);
-  const size_t need = splits > 1 ? static_cast<size_t>(num_seqs) * num_heads * splits *
-                                       (lmrs::kAttnD + 2) * sizeof(float)
-                                 : 0;
-  if (need && (!workspace || workspace_bytes < need)) return LMRS_ERR_WORKSPACE;
-  if (need && !aligned16(workspace)) return LMRS_ERR_ALIGN;
+  (void)workspace;
+  (void)workspace_bytes;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const int ns = clampi(g_tune.attn_stages, 2, 4);
 #define LMRS_ATTN(T, I, NS)                                                                      \
-  return attn_launch<T, NS>(out, workspace, query, key_cache, value_cache, block_tables,        \
+  return attn_launch<T, NS>(out, query, key_cache, value_cache, block_tables,                   \
                             context_lens, num_seqs, num_heads, num_kv_heads, block_size,        \
                             max_blocks_per_seq, splits, span, scale, kv_head_map, st, dev,      \
                             g_smem_attn[I][NS - 2])

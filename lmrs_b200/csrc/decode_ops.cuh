@@ -361,6 +361,18 @@ constexpr int kAttnTile = 64;      // positions per CTA iteration (16 per warp)
 constexpr int kAttnThreads = 128;  // 4 warps
 constexpr int kAttnRowBytes = kAttnD * 2 + 16;  // padded smem row (conflict-free ldmatrix)
 constexpr int kAttnMaxBlocks = 512;  // block-table entries of one split cached in smem
+constexpr int kAttnMaxCluster = 8;   // context splits of one (sequence, KV head) = one cluster
+constexpr int kAttnPartStride = 132; // split partial row: O[128], m, l, pad (16-byte rows)
+// dynamic shared memory: per warp NS stages of 16 K + 16 V rows (at least the
+// end-of-kernel warp merge buffer), then the split partial [16 rows][132]
+__host__ __device__ constexpr int attn_main_smem(int ns) {
+  return 4 * ns * 2 * 16 * kAttnRowBytes > 4 * 16 * (kAttnD + 2) * 4
+             ? 4 * ns * 2 * 16 * kAttnRowBytes
+             : 4 * 16 * (kAttnD + 2) * 4;
+}
+__host__ __device__ constexpr int attn_smem_bytes(int ns) {
+  return attn_main_smem(ns) + 16 * kAttnPartStride * 4;
+}
 
 __device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], uint32_t addr) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
@@ -421,10 +433,14 @@ struct MmaT<__nv_bfloat16> {
 // that read this KV head (G <= 16; rows >= G are padding).
 // kv_map 0: q head h reads KV head h % num_kv_heads (the reference's paged
 // kernel); 1: h / G (grouped, as torch's enable_gqa).
-// splits == 1: writes out directly; otherwise writes (O, m, l) partials to ws.
+// splits == 1: writes out directly.  Otherwise the splits of one (sequence, KV
+// head) are one thread-block cluster (grid y = cluster y): each CTA leaves its
+// (O, m, l) partial in shared memory and, after a cluster barrier, the CTAs share
+// out the (row, 16-dim) items and merge all partials in split order through
+// distributed shared memory (deterministic; no global scratch, no second kernel).
 template <typename T, int NS>
 __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(
-    T* __restrict__ out, float* __restrict__ ws, const T* __restrict__ query,
+    T* __restrict__ out, const T* __restrict__ query,
     const T* __restrict__ k_cache, const T* __restrict__ v_cache,
     const int32_t* __restrict__ tables, const int32_t* __restrict__ ctx_lens, int num_heads,
     int num_kv_heads, int block_size, int max_blocks, int span, float scale_log2, int kv_map) {
@@ -604,6 +620,7 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(
   }
   float* mrg = reinterpret_cast<float*>(sm);  // [4 warps][16 rows][130] (O 128, m, l)
   constexpr int kStride = kAttnD + 2;
+  float* part = reinterpret_cast<float*>(sm + attn_main_smem(NS));  // this split's partial
   __syncthreads();
   {
     float* wp = mrg + warp * 16 * kStride;
@@ -647,7 +664,7 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(
       for (int i = 0; i < 16; ++i) dst[i] = Act<T>::t(acc[i] * inv);
     } else {
       // partial: O (unnormalised, fp32), then m, l
-      float* pw = ws + ((static_cast<int64_t>(seq) * num_heads + h) * splits + split) * (kAttnD + 2);
+      float* pw = part + r * kAttnPartStride;
 #pragma unroll
       for (int i = 0; i < 16; ++i) pw[d0 + i] = acc[i];
       if (d0 == 0) {
@@ -656,40 +673,41 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(
       }
     }
   }
-}
-
-// out[seq, h, :] = sum_s 2^(m_s - M) O_s / sum_s 2^(m_s - M) l_s over the splits.
-constexpr int kAttnMaxSplits = 1024;
-
-// Split-context merge, one CTA per (sequence, head): the split maxima and
-// weights f_s = 2^(m_s - M) are computed once (cooperatively, into shared
-// memory), then each thread (one of the 128 columns) sums f_s * acc_s with
-// independent loads.
-template <typename T>
-__global__ void __launch_bounds__(128) decode_attn_combine_kernel(T* __restrict__ out,
-                                                                  const float* __restrict__ ws,
-                                                                  int splits) {
-  pdl_wait();
-  pdl_trigger();
-  __shared__ float fs[kAttnMaxSplits];
-  __shared__ float red[32];
-  const int sh = blockIdx.x;  // seq * num_heads + h
-  const float* p = ws + static_cast<int64_t>(sh) * splits * (kAttnD + 2);
-  float m = -INFINITY;
-  for (int s = threadIdx.x; s < splits; s += blockDim.x) m = fmaxf(m, p[s * (kAttnD + 2) + kAttnD]);
-  const float M = block_max(m, red);
-  float l = 0.f;
-  for (int s = threadIdx.x; s < splits; s += blockDim.x) {
-    const float f = M == -INFINITY ? 0.f : exp2f(p[s * (kAttnD + 2) + kAttnD] - M);
-    fs[s] = f;
-    l += f * p[s * (kAttnD + 2) + kAttnD + 1];
+  if (splits > 1) {
+    cluster_sync_all();   // every split's partial is in its CTA's shared memory
+    const uint32_t part_u32 = smem_u32(part);
+    for (int e = threadIdx.x * splits + split; e < G * 8; e += kAttnThreads * splits) {
+      const int r = e >> 3, d0 = (e & 7) * 16;
+      const uint32_t row = part_u32 + static_cast<uint32_t>(r * kAttnPartStride) * 4u;
+      float M = -INFINITY;
+      for (int src = 0; src < splits; ++src) {
+        const float4 ml = ld_cluster_v4(mapa_shared(row + kAttnD * 4u, static_cast<uint32_t>(src)));
+        M = fmaxf(M, ml.x);
+      }
+      float L = 0.f, acc[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) acc[i] = 0.f;
+      for (int src = 0; src < splits; ++src) {
+        const uint32_t pr = mapa_shared(row, static_cast<uint32_t>(src));
+        const float4 ml = ld_cluster_v4(pr + kAttnD * 4u);
+        const float f = M == -INFINITY ? 0.f : exp2f(ml.x - M);
+        L += f * ml.y;
+#pragma unroll
+        for (int i = 0; i < 16; i += 4) {
+          const float4 o4 = ld_cluster_v4(pr + static_cast<uint32_t>(d0 + i) * 4u);
+          acc[i] += f * o4.x;
+          acc[i + 1] += f * o4.y;
+          acc[i + 2] += f * o4.z;
+          acc[i + 3] += f * o4.w;
+        }
+      }
+      T* dst = out + (static_cast<int64_t>(seq) * num_heads + qhead(r)) * kAttnD + d0;
+      const float inv = L > 0.f ? 1.f / L : 0.f;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) dst[i] = Act<T>::t(acc[i] * inv);
+    }
+    cluster_sync_all();   // no CTA leaves while a peer may read its partial
   }
-  const float L = block_sum(l, red);  // its barriers also publish fs
-  const int d = threadIdx.x;
-  float acc = 0.f;
-#pragma unroll 8
-  for (int s = 0; s < splits; ++s) acc += fs[s] * p[s * (kAttnD + 2) + d];
-  out[static_cast<int64_t>(sh) * kAttnD + d] = Act<T>::t(L > 0.f ? acc / L : 0.f);
 }
 
 }  // namespace lmrs

@@ -192,3 +192,40 @@ def test_decode_ops_status(cuda):
                                            0.1, 1, 0, None, 0, s) == _lib.LMRS_ERR_SHAPE
     import lmrs_b200 as L
     assert L.read_device_error() == 0
+
+
+@pytest.mark.parametrize("cps", [1, 2, 4, 16])
+def test_paged_attention_cluster_splits(cuda, cps):
+    """Context splits from 1 to 8 (one thread-block cluster per sequence and KV
+    head, merged in distributed shared memory), with a short and an empty
+    sequence among full ones; deterministic across calls."""
+    import lmrs_b200 as L
+    from lmrs_b200 import decode_ops as DO
+    d, hq, hkv, bs = 128, 32, 8, 16
+    lens = [2048, 37, 0, 1500]
+    seqs, max_ctx = len(lens), max(lens)
+    max_blocks = (max_ctx + bs - 1) // bs
+    kc, vc, tables = _paged_cache(seqs, hkv, d, bs, max_blocks, torch.float16, cuda, 99)
+    torch.manual_seed(3)
+    q = torch.randn(seqs, hq, d, device=cuda).half()
+    ctx = torch.tensor(lens, dtype=torch.int32, device=cuda)
+    scale = 1 / math.sqrt(d)
+    try:
+        L.set_tuning("attn_ctas_per_sm", cps)
+        out = DO.paged_attention_decode(q, kc, vc, tables, ctx, max_ctx, scale)
+        again = DO.paged_attention_decode(q, kc, vc, tables, ctx, max_ctx, scale)
+    finally:
+        L.set_tuning("attn_ctas_per_sm", 2)
+    assert torch.equal(out, again)
+    G = hq // hkv
+    for s in range(seqs):
+        n = lens[s]
+        for h in range(hq):
+            if n == 0:
+                assert torch.all(out[s, h] == 0)
+                continue
+            K = _gather(kc, tables, s, n, h // G).float()
+            V = _gather(vc, tables, s, n, h // G).float()
+            ref = torch.softmax(q[s, h].float() @ K.t() * scale, -1) @ V
+            assert (out[s, h].float() - ref).abs().max().item() < 2e-3
+    assert L.read_device_error() == 0
