@@ -337,7 +337,7 @@ int awq_tmem_launch_t(__half* y, const __half* x, const int32_t* qw, const int32
   CUtensorMap tq, tx, ts, tz;
   int rc;
   if ((rc = make_tmap(&tq, CU_TENSOR_MAP_DATA_TYPE_INT32, qw, N / 8, K, uint64_t(N / 8) * 4,
-                      lmrs::kAtWords, lmrs::kAtRows, CU_TENSOR_MAP_SWIZZLE_NONE)))
+                      lmrs::kAtWords, lmrs::kAtRows, CU_TENSOR_MAP_SWIZZLE_128B)))
     return rc;
   if ((rc = make_tmap(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, x, K, M, uint64_t(K) * 2, 64, NT,
                       CU_TENSOR_MAP_SWIZZLE_128B)))
