@@ -18,15 +18,19 @@
 //
 // Layout of one CTA: a strip of 32 packed words (256 output channels) and a
 // K range (clusters of C CTAs split K; C a power of two).
-//   * Weight ring (warp 0 lane 0, SW slots): boxes of 64 rows x 32 words
+//   * Weight ring (warp 0, SW slots): boxes of 64 rows x 32 words
 //     (8 KB) with the group's scale and zero rows.  A slot is free again as
 //     soon as the four dequant warps have read it (one arrive each), so the
 //     ring runs ahead of the MMAs.  None of it depends on the previous kernel:
 //     it is issued before griddepcontrol.wait.
-//   * Token / A-stage ring (warp 0 lane 1, R slots): the 64-k token tile of
-//     a box [NT rows x 128 B, 128-byte swizzle; rows >= M are the zero fill]
-//     and TMEM A stage b % R.  Both are released by the box's MMAs: one
-//     tcgen05.commit per issuer per box on mempty[b % R] (count 4).
+//   * Token ring (warp 9, SX slots): the 64-k token tile of a box
+//     [NT rows x 128 B, 128-byte swizzle; rows >= M are the zero fill].  TMEM
+//     A stage b % R is released by the box's MMAs (one tcgen05.commit per
+//     issuer per box on mempty[b % R], count 4); the token slot of box b is
+//     released by the dequant warps once they have seen that commit (at box
+//     b + R), so the token ring runs SX - R boxes ahead of the MMAs without a
+//     second commit (a commit costs the issuing thread about as much as an
+//     MMA).
 //   * Dequant (warps 1-4, one per TMEM lane quarter): the 128-row MMA group g
 //     is the word half 16g .. 16g+15 of the strip; warp qv takes the 16-byte
 //     chunk 4g + qv of each row with ldmatrix.trans (the weight box arrives
@@ -64,13 +68,16 @@ constexpr int kAtDqWarp0 = 1;
 constexpr int kAtDqWarps = 4;     // one per TMEM lane quarter
 constexpr int kAtMmaWarp0 = kAtDqWarp0 + kAtDqWarps;
 constexpr int kAtIssuers = 4;     // MMA warps, one accumulator each
-constexpr int kAtThreads = 32 * (kAtMmaWarp0 + kAtIssuers);  // 288
+constexpr int kAtXWarp = kAtMmaWarp0 + kAtIssuers;  // token-tile producer
+constexpr int kAtThreads = 32 * (kAtXWarp + 1);     // 320: the two producers wait on
+                                                    // different barriers, so each has a warp
 constexpr int kAtMaxCluster = 8;
 
 template <int NT>
 struct AtLayout {
-  static constexpr int kWStages = NT == 16 ? 8 : 7;  // weight ring depth
-  static constexpr int kAStages = NT == 16 ? 3 : 2;  // token tiles = TMEM A stages
+  static constexpr int kWStages = NT == 16 ? 8 : 5;  // weight ring depth
+  static constexpr int kXStages = NT == 16 ? 8 : 6;  // token ring depth
+  static constexpr int kAStages = NT == 16 ? 3 : 2;  // TMEM A stages
   static constexpr int kW = kAtRows * kAtWords * 4;  // 8 KB
   static constexpr int kX = NT * 128;                // 64 k x NT tokens, fp16, swizzled
   static constexpr int kS = kAtCols * 2;
@@ -82,11 +89,13 @@ struct AtLayout {
   static constexpr uint32_t kTmemA = kAtIssuers * NT;  // A stages after the accumulators
   static constexpr uint32_t kTmemCols = 256;
   static_assert(kAtIssuers * NT + 64 * kAStages <= 256, "TMEM columns");
+  static constexpr int kBars = 512;
   static constexpr int kSmem =
-      1024 + kWStages * kW + kAStages * kX + kWStages * kSZ + kRecv + 256;
+      1024 + kWStages * kW + kXStages * kX + kWStages * kSZ + kRecv + kBars;
   static_assert(kW % 1024 == 0 && kX % 1024 == 0, "swizzled token tiles are 1024-byte aligned");
   static_assert(kSZ % 128 == 0, "TMA destinations are 128-byte aligned");
-  static_assert((2 * kWStages + 3 * kAStages + 2) * 8 + 4 <= 256, "barrier area");
+  static_assert(kXStages >= kAStages, "token slots are released R boxes after their MMAs");
+  static_assert((2 * kWStages + 2 * kXStages + 2 * kAStages + 2) * 8 + 4 <= kBars, "barrier area");
   static_assert(2 * (kSmem + 1024) <= 228 * 1024, "two CTAs per SM");
 };
 
@@ -98,16 +107,18 @@ __global__ void __launch_bounds__(kAtThreads, 2) awq_tmem_kernel(
   using L = AtLayout<NT>;
   constexpr int SW = L::kWStages;
   constexpr int R = L::kAStages;
+  constexpr int SX = L::kXStages;
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte aligned by byte offset, so every access stays a shared-memory one
   uint8_t* wring = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint8_t* xring = wring + SW * L::kW;
-  uint8_t* sz = xring + R * L::kX;
+  uint8_t* sz = xring + SX * L::kX;
   float* recv = reinterpret_cast<float*>(sz + SW * L::kSZ);
   uint64_t* wfull = reinterpret_cast<uint64_t*>(recv + kAtCols * L::kPitch);
   uint64_t* wempty = wfull + SW;
   uint64_t* xfull = wempty + SW;
-  uint64_t* afull = xfull + R;
+  uint64_t* xempty = xfull + SX;
+  uint64_t* afull = xempty + SX;
   uint64_t* mempty = afull + R;
   uint64_t* dfull = mempty + R;
   uint64_t* recv_bar = dfull + 1;
@@ -129,8 +140,11 @@ __global__ void __launch_bounds__(kAtThreads, 2) awq_tmem_kernel(
       mbar_init(&wfull[i], 1);
       mbar_init(&wempty[i], kAtDqWarps);  // one arrive per dequant warp once read
     }
-    for (int i = 0; i < R; ++i) {
+    for (int i = 0; i < SX; ++i) {
       mbar_init(&xfull[i], 1);
+      mbar_init(&xempty[i], kAtDqWarps);  // the box's MMAs are known to be done
+    }
+    for (int i = 0; i < R; ++i) {
       mbar_init(&afull[i], kAtDqWarps);   // TMEM stage written
       mbar_init(&mempty[i], kAtIssuers);  // one commit per issuer: MMAs of the box done
     }
@@ -151,9 +165,7 @@ __global__ void __launch_bounds__(kAtThreads, 2) awq_tmem_kernel(
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
-    // ------------------------------------------------------------ TMA rings
-    // lane 0: weights, scales and zeros; lane 1: token tiles.  The two lanes
-    // wait on different barriers and proceed independently.
+    // ------------------------------------------------------ weight TMA ring
     if (lane == 0) {
       tma_prefetch_desc(&tm_q);
       tma_prefetch_desc(&tm_s);
@@ -169,35 +181,38 @@ __global__ void __launch_bounds__(kAtThreads, 2) awq_tmem_kernel(
         tma_load_2d(&tm_s, &wfull[s], sz + s * L::kSZ, strip * kAtCols, gi);
         tma_load_2d(&tm_z, &wfull[s], sz + s * L::kSZ + L::kS, c0, gi);
       }
-    } else if (lane == 1) {
+    }
+  } else if (warp == kAtXWarp) {
+    // ------------------------------------------------------- token TMA ring
+    if (lane == 0) {
       tma_prefetch_desc(&tm_x);
       pdl_wait();  // the tokens are the previous kernel's output
       for (int b = 0; b < nbox; ++b) {
-        const int a = b % R;
-        if (b >= R && !mbar_wait(&mempty[a], ((b / R) - 1) & 1, kErrWaitEmpty)) break;
-        mbar_arrive_expect_tx(&xfull[a], static_cast<uint32_t>(L::kX));
-        tma_load_2d(&tm_x, &xfull[a], xring + a * L::kX, (b_lo + b) * kAtRows, 0);
+        const int sx = b % SX;
+        if (b >= SX && !mbar_wait(&xempty[sx], ((b / SX) - 1) & 1, kErrWaitEmpty)) break;
+        mbar_arrive_expect_tx(&xfull[sx], static_cast<uint32_t>(L::kX));
+        tma_load_2d(&tm_x, &xfull[sx], xring + sx * L::kX, (b_lo + b) * kAtRows, 0);
       }
     }
   } else if (warp >= kAtMmaWarp0) {
-    // ---------------------------------------------------------------- MMA
+    // ---------------------------------------------------------- MMA (warps 5-8)
     if (lane == 0) {
       constexpr uint32_t idesc = make_idesc(0, 0, 0, 0, 128, NT);  // f16 x f16, K-major
       const int p = warp - kAtMmaWarp0;
       const int jj = p & 1, st0 = 2 * (p >> 1);
       const uint32_t d = tmem + static_cast<uint32_t>(p * NT);
       for (int b = 0; b < nbox; ++b) {
-        const int a = b % R;
-        if (!mbar_wait(&xfull[a], (b / R) & 1, kErrWaitFull)) break;
+        const int a = b % R, sx = b % SX;
+        if (!mbar_wait(&xfull[sx], (b / SX) & 1, kErrWaitFull)) break;
         if (!mbar_wait(&afull[a], (b / R) & 1, kErrWaitDequant)) break;
         tc_fence_after();
-        const uint32_t xs_addr = smem_u32(xring + a * L::kX);
+        const uint32_t xs_addr = smem_u32(xring + sx * L::kX);
         const uint32_t acol = tmem + L::kTmemA + a * 64;
 #pragma unroll
         for (int st = st0; st < st0 + 2; ++st)
           umma_f16_tmem_a(d, acol + 32 * jj + 8 * st, make_sdesc(xs_addr + st * 32, 16, 1024),
                           idesc, (b | (st - st0)) != 0 ? 1u : 0u);
-        umma_commit(&mempty[a]);  // token tile a and TMEM stage a are free
+        umma_commit(&mempty[a]);  // TMEM stage a (and, via the dequant, token slot sx) free
       }
       umma_commit(dfull);  // also fires (over no MMAs) if a wait gave up
     }
@@ -241,7 +256,10 @@ __global__ void __launch_bounds__(kAtThreads, 2) awq_tmem_kernel(
       }
       // TMEM stage a was last read by the MMAs of box b - R (mempty[a] phase
       // (b - R) / R; the next phase needs this box's own afull arrive)
-      if (b >= R && !(ok = mbar_wait(&mempty[a], ((b / R) - 1) & 1, kErrWaitAccum))) break;
+      if (b >= R) {
+        if (!(ok = mbar_wait(&mempty[a], ((b / R) - 1) & 1, kErrWaitAccum))) break;
+        if (lane == 0) mbar_arrive(&xempty[(b - R) % SX]);  // box b - R's token slot
+      }
       const uint32_t acol = tmem + lane_addr + L::kTmemA + a * 64;
 #pragma unroll
       for (int g = 0; g < 2; ++g) {
