@@ -20,17 +20,20 @@
 //     K=16, A from the TMEM stage, B from the token stage, then one commit
 //     that frees the stage; accumulators double-buffered (2 x BT columns) up
 //     to BT = 192, single at BT = 256.
-//   * warps 2-5: epilogue — TMEM lane = channel, 16 token columns per
+//   * warps 2-5: epilogue — TMEM lane = channel (in the dequant's lane order), 16 token columns per
 //     tcgen05.ld, + bias, transposed through shared memory so each lane stores
 //     16 contiguous channels of one token (two 16-byte stores): one-channel
 //     2-byte stores stalled the single-buffered accumulator at BT = 256.
-//   * warps 6-13: dequant, two groups of four taking alternate K-blocks (one
-//     warp per TMEM lane quarter and group) — TMEM lane = channel c; for rows r, r+1 one prmt
-//     gathers the byte holding c's nibble from both packed words and one lop3
-//     makes the biased half2 (1024 + q or 64 + q); each thread loads its own
-//     scale and zero word (2 + 4 bytes) one K-block ahead; subtracting the same-biased
-//     zero is exact and the multiply by the scale rounds once, so A holds
-//     exactly fp16_rne((q - z) * s); 32 columns (64 k) per tcgen05.st.
+//   * warps 6-21: dequant, four groups of four taking alternate K-blocks (one
+//     warp per TMEM lane quarter and group) — quarter q takes the 16-byte
+//     chunk q of each packed row with ldmatrix.trans (64-byte swizzled box),
+//     whose registers pair rows r, r+1 of a half-word: one lop3 per nibble
+//     makes the biased half2 (1024 + q or 64 + q); each thread loads its
+//     word's 8 scales (16 bytes) and zero word one K-block ahead; subtracting
+//     the same-biased zero is exact and the multiply by the scale rounds once,
+//     so A holds exactly fp16_rne((q - z) * s); tcgen05.st 16x128b lays each
+//     channel along one TMEM lane (lane L of a quarter: channel
+//     8 ((L & 7) >> 1) + 2 (L >> 3) + (L & 1)).
 // Every mbarrier wait is bounded; on expiry the kernel records the site in the
 // device error word and unwinds; TMEM is always released.
 #pragma once
@@ -46,7 +49,7 @@ constexpr int kAgtBK = 64;           // k rows per stage
 constexpr int kAgtEpiWarp0 = 2;
 constexpr int kAgtDqWarp0 = 6;
 constexpr int kAgtDqGroups = 4;      // dequant warp groups, alternating K-blocks
-constexpr int kAgtThreads = 32 * (kAgtDqWarp0 + 4 * kAgtDqGroups);  // 448
+constexpr int kAgtThreads = 32 * (kAgtDqWarp0 + 4 * kAgtDqGroups);  // 704
 
 // Shared-memory ring of S stages (token tile + packed weights) and a TMEM ring of
 // R stages (dequantised weights, 32 columns each), R <= S.  One tcgen05.commit
@@ -190,7 +193,10 @@ __global__ void __launch_bounds__(kAgtThreads, 1) awq_gemm_tmem_kernel(
   } else if (warp < kAgtDqWarp0) {
     // ------------------------------------------- epilogue: lane = output channel
     const int quarter = warp & 3;
-    const int c = quarter * 32 + lane;
+    // TMEM lane L of a quarter holds channel 8 ((L & 7) >> 1) + 2 (L >> 3) + (L & 1)
+    // of the quarter's 32 (the dequant's ldmatrix / 16x128b layout)
+    const int cq = 8 * ((lane & 7) >> 1) + 2 * (lane >> 3) + (lane & 1);
+    const int c = quarter * 32 + cq;
     const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
     pdl_wait();  // y may still be read by the previous kernel
     uint32_t it = 0;
@@ -210,7 +216,7 @@ __global__ void __launch_bounds__(kAgtThreads, 1) awq_gemm_tmem_kernel(
         tmem_ld16(tmem + lane_addr + a * BT + ch * 16, r);
         tmem_ld_wait();
 #pragma unroll
-        for (int e = 0; e < 16; ++e) tw[e * L::kEpiPitch + lane] = __float2half_rn(__uint_as_float(r[e]) + bn);
+        for (int e = 0; e < 16; ++e) tw[e * L::kEpiPitch + cq] = __float2half_rn(__uint_as_float(r[e]) + bn);
         __syncwarp();
         const int m = m0 + ch * 16 + te;
         if (m < M && nw < N) {
@@ -226,24 +232,30 @@ __global__ void __launch_bounds__(kAgtThreads, 1) awq_gemm_tmem_kernel(
       if (lane == 0) mbar_arrive(&acc->empty[a]);
     }
   } else {
-    // ------------------------------------------- dequant: lane = output channel
+    // ------------------------------------------- dequant
+    // Quarter q's 32 TMEM lanes take the 16-byte chunk q (words 4q .. 4q+3, 32
+    // channels) of every 64-byte packed row.  ldmatrix.trans of 32 rows gives
+    // thread t = 4hc + pp, register i, half-word hc of the chunk for rows
+    // 8i + 2pp (low half) and 8i + 2pp + 1 (high half): each of its four
+    // nibbles already has its row pair in the two halves, so one lop3 (after
+    // one shift for the upper byte) makes the biased half2.  tcgen05.st
+    // 16x128b puts register 2j at lane hc, column 4j + pp, and 2j + 1 at lane
+    // hc + 8: nibbles 0, 1 go to lanes hc, hc + 8, nibbles 2, 3 to 16 + hc,
+    // 24 + hc, each lane one channel with k-pair kp in column kp.  The weight
+    // box arrives with the 64-byte swizzle, so the 8-row reads are
+    // conflict-free: 8 wavefronts per warp and K-block.
     const int quarter = warp & 3;
     const int dgrp = (warp - kAgtDqWarp0) >> 2;
-    const int c = quarter * 32 + lane;
     const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
-    const int w = c >> 3;
-    // nibble i of word w holds column 8w + ORDER[i], ORDER = {0,2,4,6,1,3,5,7}
-    const int j = c & 7;
-    const int i = (j >> 1) | ((j & 1) << 2);
-    const int byte = i >> 1, hi = i & 1;
-    const uint32_t sel = static_cast<uint32_t>(byte) | (static_cast<uint32_t>(4 + byte) << 8);
-    const uint32_t mask = hi ? 0x00F000F0u : 0x000F000Fu;
-    const uint32_t magic = hi ? 0x54005400u : 0x64006400u;
+    const int hc = lane >> 2;                 // half-word of the chunk
+    const int wt = 4 * quarter + (hc >> 1);   // word of the tile
+    const int codd = hc & 1;                  // nibbles 4 codd .. 4 codd + 3 of the word
+    const uint32_t sdup = codd ? 0x3232u : 0x1010u;  // prmt: duplicate the high / low half
     const int words = N / 8;
-    // this thread's scale (fp16 bits) and zero word for K-block kg
+    // scales of the word's 8 channels and its zero word for K-block kg
     int ftile = -1, fm0 = 0, n0 = 0;
-    auto fetch = [&](uint32_t kg, uint32_t& sv, uint32_t& zv) {
-      sv = 0u;
+    auto fetch = [&](uint32_t kg, uint4& sv, uint32_t& zv) {
+      sv = make_uint4(0u, 0u, 0u, 0u);
       zv = 0u;
       if (kg >= static_cast<uint32_t>(total)) return;
       const int tt = static_cast<int>(kg / KB);
@@ -252,17 +264,19 @@ __global__ void __launch_bounds__(kAgtThreads, 1) awq_gemm_tmem_kernel(
         agt_coords<BT>(blockIdx.x + tt * gridDim.x, m_tiles, n_tiles, fm0, n0);
       }
       const int gi = static_cast<int>(kg % KB) * kAgtBK / group;
-      const int n = n0 + c;
-      if (n < N) {
-        sv = reinterpret_cast<const uint16_t*>(scales)[static_cast<int64_t>(gi) * N + n];
+      const int n = n0 + 8 * wt;
+      if (n < N) {  // N % 8 == 0: the whole word is in range
+        sv = *reinterpret_cast<const uint4*>(scales + static_cast<int64_t>(gi) * N + n);
         zv = qzeros[static_cast<int64_t>(gi) * words + (n >> 3)];
       }
     };
-    uint32_t s_nxt, z_nxt;
+    uint4 s_nxt;
+    uint32_t z_nxt;
     fetch(dgrp, s_nxt, z_nxt);
     bool ok = true;
     for (uint32_t kg = dgrp; kg < static_cast<uint32_t>(total) && ok; kg += kAgtDqGroups) {
-      const uint32_t s_cur = s_nxt, z_cur = z_nxt;
+      const uint4 s_cur = s_nxt;
+      const uint32_t z_cur = z_nxt >> (16 * codd);
       fetch(kg + kAgtDqGroups, s_nxt, z_nxt);
       const int s = kg % S, ar = kg % R;
       if (!(ok = mbar_wait(&full[s], (kg / S) & 1, kErrWaitFull))) break;
@@ -273,19 +287,33 @@ __global__ void __launch_bounds__(kAgtThreads, 1) awq_gemm_tmem_kernel(
         const uint32_t j = kg - R;
         if (!(ok = mbar_wait(&empty[j % S], (j / S) & 1, kErrWaitAccum))) break;
       }
-      const uint8_t* sm = ssm + s * L::kSmall;
-      const uint32_t z = (z_cur >> (4 * i)) & 0xFu;
-      const uint32_t zz = (hi ? (0x5400u | (z << 4)) : (0x6400u | z)) * 0x00010001u;
-      const uint32_t ss = s_cur | (s_cur << 16);
-      const uint8_t* wb = sm + 4 * w;
-      uint32_t r[32];
+      const uint32_t s4[4] = {s_cur.x, s_cur.y, s_cur.z, s_cur.w};
+      uint32_t zz[4], ss[4];
 #pragma unroll
-      for (int p = 0; p < 32; ++p) {  // column p = k rows (2p, 2p+1)
-        const uint32_t wa = ld_s32(wb + (2 * p) * (kAgtWords * 4));
-        const uint32_t wc = ld_s32(wb + (2 * p + 1) * (kAgtWords * 4));
-        r[p] = dq_h2(lop3_and_or(prmt(wa, wc, sel), mask, magic), zz, ss);
+      for (int n = 0; n < 4; ++n) {
+        const uint32_t z = (z_cur >> (4 * n)) & 0xFu;
+        zz[n] = ((n & 1) ? (0x5400u | (z << 4)) : (0x6400u | z)) * 0x00010001u;
+        ss[n] = prmt(s4[n], s4[n], sdup);  // channel 8 wt + 2n + codd
       }
-      tmem_st32(tmem + lane_addr + L::kTmemA + ar * 32, r);
+      const uint8_t* sm = ssm + s * L::kSmall;
+      const uint32_t acol = tmem + lane_addr + L::kTmemA + ar * 32;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int r = 32 * h + lane;  // row this lane addresses for ldmatrix
+        uint32_t d[4];
+        ldsm_x4_t(d, smem_u32(sm + r * (kAgtWords * 4) + ((quarter ^ ((r >> 1) & 3)) << 4)));
+        uint32_t lo[8], hi[8];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const uint32_t v = d[i], v8 = d[i] >> 8;
+          lo[2 * i] = dq_h2(lop3_and_or(v, 0x000F000Fu, 0x64006400u), zz[0], ss[0]);
+          lo[2 * i + 1] = dq_h2(lop3_and_or(v, 0x00F000F0u, 0x54005400u), zz[1], ss[1]);
+          hi[2 * i] = dq_h2(lop3_and_or(v8, 0x000F000Fu, 0x64006400u), zz[2], ss[2]);
+          hi[2 * i + 1] = dq_h2(lop3_and_or(v8, 0x00F000F0u, 0x54005400u), zz[3], ss[3]);
+        }
+        tmem_st16x128b_x4(acol + 16 * h, lo);
+        tmem_st16x128b_x4(acol + (16u << 16) + 16 * h, hi);
+      }
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();

@@ -561,7 +561,7 @@ int awq_gemm_tmem_launch_t(__half* y, const __half* x, const int32_t* qw, const 
                       CU_TENSOR_MAP_SWIZZLE_128B)))
     return rc;
   if ((rc = make_tmap(&tq, CU_TENSOR_MAP_DATA_TYPE_INT32, qw, N / 8, K, uint64_t(N / 8) * 4,
-                      lmrs::kAgtWords, lmrs::kAgtBK, CU_TENSOR_MAP_SWIZZLE_NONE)))
+                      lmrs::kAgtWords, lmrs::kAgtBK, CU_TENSOR_MAP_SWIZZLE_64B)))
     return rc;
   if ((rc = ensure_smem(lmrs::awq_gemm_tmem_kernel<BT>, L::kSmem, done, dev))) return rc;
   const int tiles = ((N + lmrs::kAgtCh - 1) / lmrs::kAgtCh) * ((M + BT - 1) / BT);
