@@ -84,10 +84,10 @@ LMRS_API int lmrs_version(void);
  * "awq_swap_cluster", "awq_gemm_pair", "gemm_bn", "fp8_gemv_max_m",
  * "gemv_ctas_per_sm", "awq_gemv_cluster", "fp8_gemv_cluster", "fp8_gemv_max_kn",
  * "fp8_swap_max_m", "fp8_swap_cluster", "awq_tmem_min_m", "awq_tmem_max_m",
- * "awq_tmem_wide_n", "awq_tmem_cluster", "awq_tmem_ctas_per_sm", "awq_gemm_tmem",
+ * "awq_tmem_min_m_wide", "awq_tmem_cluster", "awq_tmem_ctas_per_sm", "awq_gemm_tmem",
  * "awq_gemm_tmem_bt", "awq_gemv4", "awq_gemv_slots", "awq_gemv4_slots",
  * "gemv_box_rows", "attn_stages", "attn_ctas_per_sm", "awq_i8_max_m" (1-2 token
- * AWQ on the integer MMA path up to this M, default 2; 0 = fp16 GEMV),
+ * AWQ on the integer MMA path up to this M, default 1; 0 = fp16 GEMV),
  * "awq_i8_slots", "awq_i8_ctas_per_sm", "awq_i8_cluster", "awq_i8_box_rows", "pdl" (programmatic
  * dependent launch on every kernel, default 1).
  * Process-wide, not thread-safe against concurrent launches. */

@@ -61,9 +61,9 @@ struct Tuning {
   int awq_gemv4_slots = 4;   // its ring slots (4 or 8)
   int attn_stages = 3;       // decode attention cp.async ring depth (2..4)
   int attn_ctas_per_sm = 2;  // decode attention context split target
-  int awq_tmem_min_m = 17;   // TMEM-staged tcgen05 AWQ linear for M in [min, max];
+  int awq_tmem_min_m = 9;    // TMEM-staged tcgen05 AWQ linear for M in [min, max];
   int awq_tmem_max_m = 32;   // its cost is flat in M (32 at most)
-  int awq_tmem_wide_n = 12288;  // ... and down to M = 9 when N is at least this
+  int awq_tmem_min_m_wide = 5;  // ... and down to this M when N >= K (0 = off)
   int awq_tmem_cluster = 0;  // 0 = heuristic
   int awq_tmem_ctas_per_sm = 2;
   int awq_gemm_tmem = 1;     // prefill: GEMM with the weights as the TMEM A operand (0: smem-staged)
@@ -357,10 +357,14 @@ int awq_tmem_launch_t(__half* y, const __half* x, const int32_t* qw, const int32
 
 // 9..16 tokens: the register-fed GEMV is faster unless N is wide; 17..32: the
 // TMEM-staged kernel (flat in M) beats both the GEMV and the swap-AB kernel.
-bool awq_use_tmem(int M, int N) {
+// Measured graph-timed on the 8B/config-1 shapes: from 9 tokens the TMEM kernel
+// beats the register-fed GEMV on every shape (4096 x 4096 at 16: 7.7 vs 9.2 us);
+// at 5..8 it wins where N >= K and loses on deep-K, narrow-N shapes (14336 x
+// 4096: 20.5 vs 19.5 us); at 3..4 the four-token GEMV is ahead everywhere.
+bool awq_use_tmem(int M, int K, int N) {
   if (M > g_tune.awq_tmem_max_m || M > 32) return false;
   if (M >= g_tune.awq_tmem_min_m) return true;
-  return M >= 9 && g_tune.awq_tmem_wide_n > 0 && N >= g_tune.awq_tmem_wide_n;
+  return g_tune.awq_tmem_min_m_wide > 0 && M >= g_tune.awq_tmem_min_m_wide && N >= K;
 }
 
 int awq_tmem_launch(__half* y, const __half* x, const int32_t* qw, const int32_t* qz,
@@ -889,7 +893,7 @@ int lmrs_set_tuning(const char* key, int value) {
   else if (!strcmp(key, "awq_gemm_tmem")) g_tune.awq_gemm_tmem = value ? 1 : 0;
   else if (!strcmp(key, "awq_gemm_tmem_bt")) g_tune.awq_gemm_tmem_bt = value;
   else if (!strcmp(key, "awq_tmem_min_m")) g_tune.awq_tmem_min_m = value;
-  else if (!strcmp(key, "awq_tmem_wide_n")) g_tune.awq_tmem_wide_n = value;
+  else if (!strcmp(key, "awq_tmem_min_m_wide")) g_tune.awq_tmem_min_m_wide = value;
   else if (!strcmp(key, "awq_tmem_cluster")) g_tune.awq_tmem_cluster = value;
   else if (!strcmp(key, "awq_tmem_ctas_per_sm")) g_tune.awq_tmem_ctas_per_sm = value;
   else if (!strcmp(key, "fp8_swap_cluster")) g_tune.fp8_swap_cluster = value;
@@ -965,7 +969,7 @@ int lmrs_awq_linear(void* y, const void* x, const int32_t* qweight, const int32_
   auto* xh = static_cast<const __half*>(x);
   auto* sh = static_cast<const __half*>(scales);
   auto* bh = static_cast<const __half*>(bias_or_null);
-  if (awq_use_tmem(M, N))
+  if (awq_use_tmem(M, K, N))
     return awq_tmem_launch(yh, xh, qweight, qzeros, sh, bh, M, K, N, group, st, dev);
   if (M <= g_tune.awq_gemv_max_m && M <= 16)
     return awq_gemv_launch(yh, xh, qweight, reinterpret_cast<const uint32_t*>(qzeros), sh, bh, M,

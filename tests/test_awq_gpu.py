@@ -72,14 +72,21 @@ def test_dequant_extremes(cuda):
 @pytest.mark.parametrize("M", [1, 2, 7, 8, 9, 16])
 @pytest.mark.parametrize("bias", [False, True])
 def test_linear_gemv_small(cuda, M, bias):
+    """Default dispatch, and the register-fed GEMV with the TMEM-staged kernel
+    switched off (it takes 9..16 tokens by default)."""
     import lmrs_b200 as L
     K, N, g = 1024, 512, 128
     d = O.awq_inputs(M, K, N, g, seed=M, with_bias=bias)
     qw, qz, sc, x, b = _awq_dev(d, cuda)
-    y = L.awq_linear(x, qw, qz, sc, b, g)
     ref = O.c_awq_linear(d["x"], d["qweight"], d["qzeros"], d["scales"], d["bias"], M, K, N, g)
-    err = O.max_rel_err(y.cpu().numpy(), ref)
-    assert err < TIGHT, err
+    for tmem_max in (32, 0):
+        try:
+            L.set_tuning("awq_tmem_max_m", tmem_max)
+            y = L.awq_linear(x, qw, qz, sc, b, g)
+        finally:
+            L.set_tuning("awq_tmem_max_m", 32)
+        err = O.max_rel_err(y.cpu().numpy(), ref)
+        assert err < TIGHT, (tmem_max, err)
 
 
 @pytest.mark.parametrize("M", [17, 100, 128, 129, 300, 512])
@@ -219,8 +226,12 @@ def test_opt_in_paths(cuda, knob, value, Ms):
     K, N, g = 1024, 1280, 128
     # the smem-staged GEMM's own knobs are only reached with the TMEM GEMM off
     also_off = knob in ("awq_gemm_pair", "gemm_bn")
+    gemv_knob = knob in ("awq_gemv_cluster", "awq_gemv_slots", "gemv_box_rows", "awq_gemv4",
+                         "awq_gemv4_slots")
     try:
         L.set_tuning("awq_i8_max_m", 0)   # 1-2 tokens: the fp16 GEMVs these knobs steer
+        if gemv_knob:
+            L.set_tuning("awq_tmem_max_m", 0)  # 5..16 tokens go to the TMEM kernel by default
         L.set_tuning(knob, value)
         if also_off:
             L.set_tuning("awq_gemm_tmem", 0)
@@ -236,6 +247,7 @@ def test_opt_in_paths(cuda, knob, value, Ms):
         L.set_tuning(knob, defaults[knob])
         L.set_tuning("awq_gemm_tmem", 1)
         L.set_tuning("awq_i8_max_m", 1)
+        L.set_tuning("awq_tmem_max_m", 32)
     assert L.read_device_error() == 0
 
 
@@ -264,7 +276,7 @@ def test_tmem_linear(cuda, M, K, N, g):
         for _ in range(2):
             assert torch.equal(L.awq_linear(x, qw, qz, sc, b, g), y)
     finally:
-        L.set_tuning("awq_tmem_min_m", 17)
+        L.set_tuning("awq_tmem_min_m", 9)
         L.set_tuning("awq_tmem_max_m", 32)
     assert err < TIGHT, err
     assert L.read_device_error() == 0
@@ -281,7 +293,7 @@ def test_tmem_linear_clusters(cuda, C, M):
         L.set_tuning("awq_tmem_cluster", C)
         err, _ = _awq_case(cuda, M, 17 * 64, 768, 64, 41 + C, bias=False)
     finally:
-        L.set_tuning("awq_tmem_min_m", 17)
+        L.set_tuning("awq_tmem_min_m", 9)
         L.set_tuning("awq_tmem_cluster", 0)
     assert err < TIGHT, err
 
