@@ -43,7 +43,8 @@ thread_local int t_last_cuda_error = 0;
 // ---- tuning knobs (lmrs_set_tuning); defaults chosen from B200 measurements
 struct Tuning {
   int awq_gemv_max_m = 16;   // M up to this -> register-dequant GEMV (16 at most)
-  int awq_swap_max_m = 64;   // M up to this -> swap-AB split-K tcgen05; above -> tile GEMM
+  int awq_swap_max_m = 64;   // M up to this -> swap-AB split-K tcgen05 while N/128 < SMs; above -> tile GEMM
+  int awq_swap_deep_k = 2;   // ... and up to 128 tokens on any N when K >= this x N (0 = off)
   int fp8_gemv_max_m = 8;    // M up to this (and K*N up to fp8_gemv_max_kn) -> register-fed FP8 GEMV
   int fp8_gemv_max_kn = 1 << 25;  // larger weights: the swap-AB kernel streams faster
   int fp8_swap_max_m = 64;   // M up to this -> swap-AB tcgen05 FP8 (64 at most)
@@ -365,6 +366,20 @@ bool awq_use_tmem(int M, int K, int N) {
   if (M > g_tune.awq_tmem_max_m || M > 32) return false;
   if (M >= g_tune.awq_tmem_min_m) return true;
   return g_tune.awq_tmem_min_m_wide > 0 && M >= g_tune.awq_tmem_min_m_wide && N >= K;
+}
+
+// 33..128 tokens, measured graph-timed: the split-K swap-AB kernel wins while the
+// prefill GEMM has few 128-channel tiles and a deep K to walk per tile (14336 x
+// 4096 at 96 tokens: 60 vs 92 us; 28672 x 8192: 122 vs 180), the GEMM once the
+// tiles fill the SMs (4096 x 28672 at 40..64 tokens: 44 vs 51-54 us; 8192 x
+// 57344: 156 vs 172) or the tokens pass 64 on shallow K (4096 x 14336 at 96: 33
+// vs 54 us).
+bool awq_use_swap(int M, int K, int N, int sms) {
+  if (M > 128) return false;
+  if (g_tune.awq_swap_deep_k > 0 &&
+      static_cast<long long>(K) >= static_cast<long long>(g_tune.awq_swap_deep_k) * N)
+    return true;
+  return M <= g_tune.awq_swap_max_m && (N + lmrs::kAgtCh - 1) / lmrs::kAgtCh < sms;
 }
 
 int awq_tmem_launch(__half* y, const __half* x, const int32_t* qw, const int32_t* qz,
@@ -873,6 +888,7 @@ int lmrs_set_tuning(const char* key, int value) {
   if (!key) return LMRS_ERR_NULL;
   if (!strcmp(key, "awq_gemv_max_m")) g_tune.awq_gemv_max_m = value;
   else if (!strcmp(key, "awq_swap_max_m")) g_tune.awq_swap_max_m = value;
+  else if (!strcmp(key, "awq_swap_deep_k")) g_tune.awq_swap_deep_k = value;
   else if (!strcmp(key, "awq_swap_cluster")) g_tune.awq_swap_cluster = value;
   else if (!strcmp(key, "awq_gemm_pair")) g_tune.awq_gemm_pair = value;
   else if (!strcmp(key, "gemm_bn")) g_tune.gemm_bn = value;
@@ -974,7 +990,7 @@ int lmrs_awq_linear(void* y, const void* x, const int32_t* qweight, const int32_
   if (M <= g_tune.awq_gemv_max_m && M <= 16)
     return awq_gemv_launch(yh, xh, qweight, reinterpret_cast<const uint32_t*>(qzeros), sh, bh, M,
                            K, N, group, st, dev);
-  if (M <= g_tune.awq_swap_max_m && M <= 128)
+  if (awq_use_swap(M, K, N, sm_count(dev)))
     return awq_swap_launch(yh, xh, qweight, qzeros, sh, bh, M, K, N, group, st, dev);
   // up to one token tile, more 128-channel tiles than SMs leave a tail wave the
   // 256-channel smem-staged tiles avoid
