@@ -81,7 +81,7 @@ LMRS_API int lmrs_read_device_error(int* out_flags);
 LMRS_API int lmrs_version(void);
 /* Measurement knobs (dispatch thresholds, split-K shape, launch mode); 0 on a
  * known key, LMRS_ERR_SHAPE otherwise.  Keys: "awq_gemv_max_m", "awq_swap_max_m",
- * "awq_swap_deep_k",
+ * "awq_swap_deep_k" (swap-AB up to 128 tokens when 4K >= value x N, default 5; 0 = off),
  * "awq_swap_cluster", "awq_gemm_pair", "gemm_bn", "fp8_gemv_max_m",
  * "gemv_ctas_per_sm", "awq_gemv_cluster", "fp8_gemv_cluster", "fp8_gemv_max_kn",
  * "fp8_swap_max_m", "fp8_swap_cluster", "awq_tmem_min_m", "awq_tmem_max_m",

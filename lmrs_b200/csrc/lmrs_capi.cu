@@ -44,7 +44,7 @@ thread_local int t_last_cuda_error = 0;
 struct Tuning {
   int awq_gemv_max_m = 16;   // M up to this -> register-dequant GEMV (16 at most)
   int awq_swap_max_m = 64;   // M up to this -> swap-AB split-K tcgen05 while N/128 < SMs; above -> tile GEMM
-  int awq_swap_deep_k = 2;   // ... and up to 128 tokens on any N when K >= this x N (0 = off)
+  int awq_swap_deep_k = 5;   // ... and up to 128 tokens on any N when 4K >= this x N (0 = off)
   int fp8_gemv_max_m = 8;    // M up to this (and K*N up to fp8_gemv_max_kn) -> register-fed FP8 GEMV
   int fp8_gemv_max_kn = 1 << 25;  // larger weights: the swap-AB kernel streams faster
   int fp8_swap_max_m = 64;   // M up to this -> swap-AB tcgen05 FP8 (64 at most)
@@ -373,11 +373,13 @@ bool awq_use_tmem(int M, int K, int N) {
 // 4096 at 96 tokens: 60 vs 92 us; 28672 x 8192: 122 vs 180), the GEMM once the
 // tiles fill the SMs (4096 x 28672 at 40..64 tokens: 44 vs 51-54 us; 8192 x
 // 57344: 156 vs 172) or the tokens pass 64 on shallow K (4096 x 14336 at 96: 33
-// vs 54 us).
+// vs 54 us).  The crossover in K / N at 96-128 tokens lies between 1 (4096 x
+// 4096: GEMM 30.7 vs 31.4 us) and 1.33 (4096 x 3072: swap 21.6 vs 30.6 us), so
+// swap from K >= 1.25 N.
 bool awq_use_swap(int M, int K, int N, int sms) {
   if (M > 128) return false;
   if (g_tune.awq_swap_deep_k > 0 &&
-      static_cast<long long>(K) >= static_cast<long long>(g_tune.awq_swap_deep_k) * N)
+      4LL * K >= static_cast<long long>(g_tune.awq_swap_deep_k) * N)
     return true;
   return M <= g_tune.awq_swap_max_m && (N + lmrs::kAgtCh - 1) / lmrs::kAgtCh < sms;
 }

@@ -309,9 +309,11 @@ def test_gemm_tmem_opt_in(cuda, bt, M, K, N, g):
     import lmrs_b200 as L
     try:
         L.set_tuning("awq_gemm_tmem_bt", bt)
+        L.set_tuning("awq_swap_deep_k", 0)  # deep-K shapes up to 128 tokens go to swap-AB by default
         err, (x, qw, qz, sc, b, y) = _awq_case(cuda, M, K, N, g, 900 + M + bt)
         assert torch.equal(L.awq_linear(x, qw, qz, sc, b, g), y)
     finally:
         L.set_tuning("awq_gemm_tmem_bt", 256)
+        L.set_tuning("awq_swap_deep_k", 5)
     assert err < TIGHT, err
     assert L.read_device_error() == 0
