@@ -13,7 +13,7 @@ streamed between two uses of a copy exceeds 2x the 126 MB L2.
 The line also carries ``fp8_sweep``: BASELINE config 2 (FP8 W8A8, (K, N) in
 {(4096,4096), (4096,28672), (14336,4096)} x M in {1, 32, 512, 8192}), device
 time per quant+GEMM call, as context (``--no-fp8`` skips it).  ``--case`` runs
-a few launches of one shape for ncu captures (see profiles/).
+a few launches of one shape for ncu captures.
 
 ``--impl reference`` times the reference side on the same workload: the
 reference has no CPU implementation of this path, so the CPU restatement in
@@ -55,14 +55,17 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 
 AWQ_K, AWQ_N, AWQ_G = 4096, 14336, 128
 AWQ_MS = [1, 16, 128, 1024, 4096]
+AWQ_WORKLOAD = "config1: AWQ W4A16 K=4096 N=14336 g=128, M in {1,16,128,1024,4096}"
 FP8_K, FP8_N = 4096, 28672
 FP8_MS = [1, 32, 512, 8192]
-# No FP8 figure in MEASURED_PEAKS.json: torch._scaled_mm e4m3 8192^3 measured on
-# this pool's B200s (dense, burst) stands in as the FP8 tensor denominator.
-FP8_PEAK_TFLOPS = 3008.0
-# DRAM bytes (read + write) of one awq_gemm_tmem_kernel<256> launch at M=4096, from the
-# ncu capture recorded in profiles/awq_gemm_tmem_config1_M2048.md (update with the kernel).
+# DRAM bytes (read + write) of one awq_gemm_tmem_kernel<256> launch at M=4096 and
+# how they were captured (ncu cannot run inside the timed bench; the figure is
+# re-captured whenever the kernel changes and printed with its source).
 AWQ_GEMM_M4096_DRAM_BYTES = 93_220_000 + 73_690_000
+AWQ_GEMM_M4096_TRAFFIC_SOURCE = (
+    "ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum,gpu__time_duration.sum "
+    "--clock-control none -k regex:awq_gemm_tmem -s 1 -c 1 python bench.py --case awq:4096 "
+    "(93.22 MB read + 73.69 MB written)")
 
 
 def peaks():
@@ -282,12 +285,13 @@ def run_awq(args, device, dist_on, world, rank):
             "peak": pk["bf16_tflops"], "unit": "TFLOP/s", "frac": round(ach / pk["bf16_tflops"], 4),
             "peak_source": f"{pk_kind} bf16 dense (burst)",
             "traffic": AWQ_GEMM_M4096_DRAM_BYTES if Md == 4096 else None,
+            "traffic_source": AWQ_GEMM_M4096_TRAFFIC_SOURCE if Md == 4096 else None,
             "traffic_unit": "bytes per launch (ncu dram__bytes_read.sum + dram__bytes_write.sum)",
             "algorithmic_bytes": awq_bytes(Md), "algorithmic_flops": awq_flops(Md)}
     return dict(
         metric="awq_w4a16_linear_throughput_config1_sweep", value=round(value, 3), unit="TFLOP/s",
         ms_per_step=round(ms_step, 4), dtype="f16 (int4 weights, fp32 accumulate)",
-        config={"workload": "config1: AWQ W4A16 K=4096 N=14336 g=128, M in {1,16,128,1024,4096}",
+        config={"workload": AWQ_WORKLOAD,
                 "global_batch": sum(AWQ_MS), "parallelism": f"replicas{world}",
                 "l2": f"rotating {copies} weight copies ({copies * awq_bytes(0) / 1e6:.0f} MB > 2x L2)"},
         roofline=roof, sweep=sweep, clocks=clocks,
@@ -297,41 +301,75 @@ def run_awq(args, device, dist_on, world, rank):
         _peaks=pk, _weights=W)
 
 
-def cpu_baseline_awq(nthreads, ms=(1, 16, 128, 1024)):
-    """Oracle (CPU restatement, OpenMP) over a bounded sample of the sweep."""
+# Columns of the config-1 weight the CPU arm computes per step: every M of the
+# sweep, full K, this many of the N = 14336 output channels (the work per output
+# is the same K-long dot product, so the TFLOP/s of the slice is the sweep's).
+CPU_SAMPLE_COLS = 1024
+
+
+def cpu_sweep(nthreads, steps, warmup, ncols=CPU_SAMPLE_COLS):
+    """The config-1 sweep on the host cores through the oracle's OpenMP C
+    restatement (dequant + fp32-FMA linear, the reference's linear_kernel
+    arithmetic): each step is one call at every M in the sweep on the first
+    `ncols` output channels of the seeded config-1 weights.  Returns the
+    cpu_baseline dict (value in TFLOP/s)."""
     from oracle import oracle as O
-    d = O.awq_inputs(max(ms), AWQ_K, AWQ_N, AWQ_G, seed=0)
-    t = 0.0
-    fl = 0.0
-    for M in ms:
-        x = np.ascontiguousarray(d["x"][:M])
-        t0 = time.perf_counter()
-        O.c_awq_linear(x, d["qweight"], d["qzeros"], d["scales"], None, M, AWQ_K, AWQ_N, AWQ_G,
-                       nthreads=nthreads)
-        t += time.perf_counter() - t0
-        fl += awq_flops(M)
+    K, N, g = AWQ_K, AWQ_N, AWQ_G
+    d = O.awq_inputs(max(AWQ_MS), K, N, g, seed=0)
+    qw = np.ascontiguousarray(d["qweight"][:, :ncols // 8])
+    qz = np.ascontiguousarray(d["qzeros"][:, :ncols // 8])
+    sc = np.ascontiguousarray(d["scales"][:, :ncols])
+    xs = {M: np.ascontiguousarray(d["x"][:M]) for M in AWQ_MS}
+
+    def step():
+        for M in AWQ_MS:
+            O.c_awq_linear(xs[M], qw, qz, sc, None, M, K, ncols, g, nthreads=nthreads)
+
+    for _ in range(warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        step()
+    t = time.perf_counter() - t0
+    fl = steps * sum(2.0 * M * K * ncols for M in AWQ_MS)
+    # config 0 (M=8, K=N=4096, g=128), the reference's CPU-runnable case, whole
+    d0 = O.awq_inputs(8, 4096, 4096, 128, seed=0)
+    reps, t0c = 5, time.perf_counter()
+    for _ in range(reps):
+        O.c_awq_linear(d0["x"], d0["qweight"], d0["qzeros"], d0["scales"], None, 8, 4096, 4096,
+                       128, nthreads=nthreads)
+    c0_ms = (time.perf_counter() - t0c) / reps * 1e3
     return {"value": round(fl / t / 1e12, 5), "unit": "TFLOP/s", "cores": nthreads, "kind": "port",
-            "sample": f"one AWQ linear (dequant + fp32-FMA GEMM) at each M in {list(ms)}, "
-                      f"K=4096 N=14336; M=4096 omitted to bound CPU time ({t:.1f} s)"}
+            "steps": steps, "warmup": warmup, "ms_per_step": round(t / steps * 1e3, 2),
+            "sample": f"every M in {AWQ_MS} of the config-1 sweep, K=4096, the first {ncols} of "
+                      f"the 14336 output channels per step (dequant + fp32-FMA linear, "
+                      f"oracle/lmrs_oracle.c, OpenMP over {nthreads} host threads)",
+            "config0": {"M": 8, "K": 4096, "N": 4096, "group": 128, "ms": round(c0_ms, 2),
+                        "TFLOP_s": round(2.0 * 8 * 4096 * 4096 / (c0_ms * 1e-3) / 1e12, 5),
+                        "what": "whole config-0 AWQ linear, median-free mean of 5 calls"}}
 
 
-def ref_gpu_linear_fwd(device, W, steps=2):
-    """The reference's own linear_fwd (oracle/_ref) on the dequantised config-1 weights."""
+def ref_gpu_linear_fwd(device, steps=2):
+    """The reference's own linear_fwd (oracle/_ref, its kernels/ffi/tensor_ffi.cu
+    built unchanged) on the config-1 weights dequantised on the host by the
+    oracle; loads nothing of this package."""
     import ctypes
     so = ROOT / "oracle" / "_ref" / "libref_ffi.so"
     if not so.exists():
         return None
-    import lmrs_b200 as L
+    from oracle import oracle as O
     lib = ctypes.CDLL(str(so))
     P, I = ctypes.c_void_p, ctypes.c_int
     lib.linear_fwd.argtypes = [P, P, P, P, I, I, I, I, P]
-    qw, qz, sc = W[0]
-    w_nk = L.awq_dequant(qw, qz, sc, AWQ_G).t().contiguous()
+    d = O.awq_inputs(max(AWQ_MS), AWQ_K, AWQ_N, AWQ_G, seed=0)
+    w_kn = O.c_awq_dequant(d["qweight"], d["qzeros"], d["scales"], AWQ_K, AWQ_N, AWQ_G)
+    w_nk = torch.from_numpy(np.ascontiguousarray(w_kn.T)).to(device)
+    xall = torch.from_numpy(d["x"]).to(device)
     stream = torch.cuda.current_stream(device)
     res = []
     tot_fl, tot_ms = 0.0, 0.0
     for M in AWQ_MS:
-        x = torch.randn(M, AWQ_K, device=device).half()
+        x = xall[:M].contiguous()
         y = torch.empty(M, AWQ_N, dtype=torch.float16, device=device)
         call = lambda: lib.linear_fwd(P(y.data_ptr()), P(x.data_ptr()), P(w_nk.data_ptr()), None,
                                       M, AWQ_K, AWQ_N, 1, P(stream.cuda_stream))
@@ -425,12 +463,42 @@ def graph_time(fn, steps):
     return a.elapsed_time(b) / steps * 1e3
 
 
+def measure_fp8_peak(device, n=8192, reps=10):
+    """FP8 dense denominator measured in this run, the way the driver measures
+    the bf16 one: a library e4m3 GEMM (torch._scaled_mm, cuBLASLt) at n^3, best
+    of `reps` event-timed calls.  MEASURED_PEAKS.json holds no FP8 figure."""
+    try:
+        a = torch.randn(n, n, device=device).to(torch.float8_e4m3fn)
+        b = torch.randn(n, n, device=device).to(torch.float8_e4m3fn).t()
+        one = torch.ones((), device=device)
+        for _ in range(3):
+            torch._scaled_mm(a, b, scale_a=one, scale_b=one, out_dtype=torch.bfloat16)
+        torch.cuda.synchronize()
+        best = None
+        for _ in range(reps):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            torch._scaled_mm(a, b, scale_a=one, scale_b=one, out_dtype=torch.bfloat16)
+            e1.record()
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1)
+            best = ms if best is None else min(best, ms)
+        del a, b
+        torch.cuda.empty_cache()
+        return (round(2.0 * n ** 3 / (best * 1e-3) / 1e12, 1),
+                f"measured in this run: torch._scaled_mm e4m3 {n}^3 -> bf16, best of {reps}")
+    except Exception as e:  # an older torch without this signature
+        return None, f"unavailable: {type(e).__name__}"
+
+
 def fp8_sweep(device, steps=5):
     """Config 2: FP8 W8A8 (K, N) x M, device time per call (context for the line)."""
     import lmrs_b200 as L
     out = []
     pk, _ = peaks()
-    fp8_peak = pk.get("fp8_tflops", FP8_PEAK_TFLOPS)
+    fp8_peak, fp8_src = measure_fp8_peak(device)
+    if fp8_peak is None:
+        fp8_peak, fp8_src = 2 * pk["bf16_tflops"], "2 x the bf16 dense burst (scaled_mm unavailable)"
     for K, N in ((4096, 4096), (4096, 28672), (14336, 4096)):
         copies = max(2, int(3e8 // (N * K)))
         w = (torch.randn(N, K, device=device) * 0.02).bfloat16()
@@ -453,7 +521,8 @@ def fp8_sweep(device, steps=5):
         torch.cuda.empty_cache()
     return {"config": "config2: FP8 W8A8, quant + GEMM per call, bf16 in/out; device time per "
                       "call from a CUDA-graph replay (host launch overhead excluded)",
-            "fp8_peak_tflops": fp8_peak, "fp8_peak_source": "torch._scaled_mm e4m3 8192^3 on this pool",
+            "fp8_peak_tflops": fp8_peak, "fp8_peak_source": fp8_src,
+            "fp8_peak_2x_bf16": 2 * pk["bf16_tflops"],
             "points": out}
 
 
@@ -577,6 +646,7 @@ def run_decode(args, device, dist_on, world, rank, preset=None, batches=None, ct
             "batch": B, "ms_per_step": round(step_ms, 4), "ms_median": round(step_med, 4),
             "tok_s": round(B / (step_med * 1e-3), 1),
             "e2e_tok_s": round(B / (e2e_ms * 1e-3), 1), "e2e_ms_per_step": round(e2e_ms, 4),
+            "own_launches_per_step": dec.own_launches_per_step(),
             "linear_ms": round(lin_ms, 4), "linear_share": round(lin_ms / step_med, 4),
             "linear_GB_s": round(lin_b / (lin_ms * 1e-3) / 1e9, 1),
             "linear_frac_hbm": round(lin_b / (lin_ms * 1e-3) / 1e9 / pk["hbm_gbs"], 4),
@@ -651,15 +721,17 @@ def main():
             if dist_on:
                 torch.distributed.destroy_process_group()
             return
-        cb = cpu_baseline_awq(nthreads)
-        W = awq_weights(device, 1)
-        rg = ref_gpu_linear_fwd(device, W)
+        cb = cpu_sweep(nthreads, args.steps, args.warmup)
+        rg = ref_gpu_linear_fwd(device)
         line = {"metric": "awq_w4a16_linear_throughput_config1_sweep", "value": cb["value"],
-                "unit": "TFLOP/s", "impl": "reference", "n_gpus": args.gpus, "steps": 1,
-                "warmup": 0, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-                "dtype": "f16 (int4 weights, fp32 accumulate)", "data": "synthetic (seed 0)",
-                "config": {"workload": "config1: AWQ W4A16 K=4096 N=14336 g=128, "
-                                       "M in {1,16,128,1024,4096}", "parallelism": "cpu"},
+                "unit": "TFLOP/s", "impl": "reference", "n_gpus": args.gpus,
+                "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": cb["ms_per_step"], "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "f16 (int4 weights, fp32 accumulate)",
+                "data": "synthetic (seeded AWQ weights/activations, config-1 distributions)",
+                "config": {"workload": AWQ_WORKLOAD, "global_batch": sum(AWQ_MS),
+                           "parallelism": f"host threads ({nthreads})",
+                           "sample": cb["sample"]},
                 "cpu_baseline": cb,
                 "e2e": {"value": cb["value"], "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": 0},
@@ -706,11 +778,37 @@ def main():
                 "data": "synthetic (seeded AWQ weights/activations, config-1 distributions)"}
         line.update(res)
         if world == 1 and not args.no_cpu_baseline:
-            line["cpu_baseline"] = cpu_baseline_awq(nthreads)
+            line["cpu_baseline"] = cpu_sweep(nthreads, steps=3, warmup=1)
         if world == 1 and not args.no_fp8:
             line["fp8_sweep"] = fp8_sweep(device)
         if decode:
             line["decode"] = decode
+        c4 = decode.get("decode_tok_s_config4", {})
+        p1 = next((p for p in c4.get("points", []) if p.get("batch") == 1 and "tok_s" in p), None)
+        if world > 1 and p1 is not None:
+            # N > 1: the headline is the tensor-parallel config-4 decode at batch 1
+            # (strong scaling of one fixed step over the N GPUs); the per-rank
+            # config-1 replicas move to `replica_sweep`.  The TP=1 figure is the
+            # same point of the N=1 line's decode block.
+            keys = ("metric", "value", "unit", "ms_per_step", "scaling", "dtype", "config",
+                    "e2e", "roofline", "sweep")
+            line["replica_sweep"] = {k: line.pop(k) for k in keys if k in line}
+            line.update(
+                metric="decode_tok_s_config4_batch1", value=p1["tok_s"], unit="tok/s",
+                ms_per_step=p1["ms_median"], scaling="strong",
+                dtype="bf16 act, e4m3 W8A8 (fp32 accumulate)",
+                data="synthetic (random-init Llama-3-70B-shaped FP8 weights, random KV cache "
+                     "and token ids)",
+                config={"workload": "config4: Llama-3-70B FP8 decoder, one decode step at batch 1, "
+                                    "ctx 4096, tensor parallel", "global_batch": 1,
+                        "seq_len": 4096, "parallelism": f"tp{world}",
+                        "l2": "weights + KV per step >> L2"},
+                e2e={"value": p1["e2e_tok_s"], "unit": "tok/s",
+                     "ms_per_step": p1["e2e_ms_per_step"],
+                     "h2d_bytes_per_step": p1["h2d_bytes_per_step"],
+                     "d2h_bytes_per_step": p1["d2h_bytes_per_step"]},
+                allreduce_ms=p1.get("allreduce_ms"), clocks=c4.get("clocks"),
+                gpu_launches=args.steps * p1["own_launches_per_step"])
         print(json.dumps(line), flush=True)
     if dist_on:
         torch.distributed.barrier()

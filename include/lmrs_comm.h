@@ -40,7 +40,9 @@ LMRS_API int lmrs_ipc_close(void* ptr);
  * max_elems) bytes each, peers' mapped through lmrs_ipc_open), in rank order.
  * Every rank must issue the same sequence of calls (same n) on its stream;
  * results are bit-identical on all ranks.  A wait for a peer that never
- * arrives gives up after ~2 s and flags lmrs_read_device_error. */
+ * arrives gives up after ~2 s (lmrs_set_tuning "wait_limit_kcycles"), flags
+ * kErrWaitPeer (bit 5) in lmrs_read_device_error and leaves NaN in every
+ * output element that source's packets did not reach. */
 LMRS_API int lmrs_allreduce_sum(void* out, const void* in, size_t n, int dtype, int rank,
                                 int world, void* const* buffers, size_t max_elems,
                                 lmrs_stream_t stream);

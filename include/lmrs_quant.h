@@ -90,8 +90,12 @@ LMRS_API int lmrs_version(void);
  * "gemv_box_rows", "attn_stages", "attn_ctas_per_sm", "awq_i8_max_m" (1-2 token
  * AWQ on the integer MMA path up to this M, default 1; 0 = fp16 GEMV),
  * "awq_i8_slots", "awq_i8_ctas_per_sm", "awq_i8_cluster", "awq_i8_box_rows", "pdl" (programmatic
- * dependent launch on every kernel, default 1).
- * Process-wide, not thread-safe against concurrent launches. */
+ * dependent launch on every kernel, default 1), "wait_limit_kcycles" (how long a
+ * kernel's bounded wait spins before it gives up and flags the device error
+ * word, in thousands of SM cycles, on the CURRENT device only; <= 0 restores the
+ * default of ~2 s; synchronous).
+ * Process-wide, not thread-safe against concurrent launches: for measurement and
+ * tests, not for a host's hot path. */
 LMRS_API int lmrs_set_tuning(const char* key, int value);
 
 /* ---- AWQ W4A16 ----------------------------------------------------------- */

@@ -13,9 +13,10 @@ that path to the quantized formats this package runs:
   "zero_point": true, "version": "gemm"}``.
 * FP8 W8A8: ``weight`` F8_E4M3 [N, K] with ``weight_scale`` fp32 per output
   channel ([N] or [N, 1]) or per tensor ([] or [1], expanded to [N]);
-  ``quantization_config = {"quant_method": "fp8", ...}``.  Activations are
-  always quantized per token at run time (a checkpoint's static
-  ``input_scale``, if present, is not used).
+  ``quantization_config = {"quant_method": "fp8", "activation_scheme":
+  "dynamic"}``.  Activations are always quantized per token at run time: a
+  static scheme and block-wise weight scales (``weight_block_size``) are
+  rejected, and a stray ``input_scale`` tensor is ignored with a warning.
 * Single-file or sharded checkpoints (``model.safetensors.index.json`` with a
   ``weight_map`` from tensor name to file), read through memory maps so a
   tensor-parallel rank only copies its own slices.
@@ -35,6 +36,7 @@ from __future__ import annotations
 import json
 import os
 import struct
+import warnings
 from dataclasses import dataclass
 from typing import Dict, Iterable, List, Optional, Tuple
 
@@ -194,6 +196,9 @@ class Checkpoint:
     def has(self, name: str) -> bool:
         return name in self.where
 
+    def names(self) -> List[str]:
+        return list(self.where)
+
     def file(self, name: str) -> SafetensorsFile:
         if name not in self.where:
             raise CheckpointError(f"{self.path}: missing tensor {name}")
@@ -263,7 +268,16 @@ def quant_spec(config: dict) -> QuantSpec:
             raise CheckpointError(f"AWQ group size {group}: must be a positive multiple of 64")
         return QuantSpec("awq", group=group)
     if method == "fp8":
-        return QuantSpec("fp8", activation_scheme=str(qc.get("activation_scheme", "dynamic")))
+        if qc.get("weight_block_size") is not None:
+            raise CheckpointError(
+                f"FP8 with weight_block_size {qc['weight_block_size']}: only per-channel or "
+                "per-tensor weight scales are supported, not block-wise scales")
+        scheme = str(qc.get("activation_scheme", "dynamic")).lower()
+        if scheme != "dynamic":
+            raise CheckpointError(
+                f"FP8 activation_scheme {scheme!r}: activations are quantized per token at run "
+                "time ('dynamic'); static input scales are not supported")
+        return QuantSpec("fp8", activation_scheme=scheme)
     raise CheckpointError(f"quant_method {method!r}: expected 'awq' or 'fp8'")
 
 
@@ -271,6 +285,14 @@ def decoder_config(config: dict):
     """DecoderConfig from the hyper-parameters of a Llama / Qwen3 config.json."""
     from .decoder import DecoderConfig
     spec = quant_spec(config)
+    # The decoder is the reference's qwen3 block with use_qk_norm = false and
+    # plain RoPE (crates/model/src/models/qwen3.rs:35-67); a checkpoint that
+    # needs per-head q/k norms or scaled RoPE would load and give wrong outputs.
+    if config.get("use_qk_norm"):
+        raise CheckpointError("use_qk_norm: per-head q/k RMSNorm is not implemented")
+    if config.get("rope_scaling") is not None:
+        raise CheckpointError(f"rope_scaling {config['rope_scaling']!r}: only plain RoPE "
+                              "(rope_theta) is implemented")
     H = int(config["hidden_size"])
     heads = int(config["num_attention_heads"])
     return DecoderConfig(
@@ -332,6 +354,9 @@ def _load_fp8(ck: Checkpoint, base: str, nrows: Optional[Tuple[int, int]] = None
         raise CheckpointError(f"{base}.weight: dtype {ck.dtype(f'{base}.weight')}, expected F8_E4M3")
     if ck.has(f"{base}.bias"):
         raise CheckpointError(f"{base}.bias: projection biases are not part of this decoder")
+    if ck.has(f"{base}.input_scale"):
+        warnings.warn(f"{base}.input_scale is ignored: activations are quantized per token "
+                      "at run time", stacklevel=2)
     N, K = ck.shape(f"{base}.weight")
     rs = slice(*nrows) if nrows is not None else None
     cs = slice(*kcols) if kcols is not None else None
@@ -363,6 +388,10 @@ def load_decoder_weights(path_or_ck, rank: int = 0, world: int = 1, device="cpu"
     ck = path_or_ck if isinstance(path_or_ck, Checkpoint) else Checkpoint(path_or_ck)
     cfg = decoder_config(ck.config)
     spec = quant_spec(ck.config)
+    qk = [n for n in ck.names() if n.endswith((".q_norm.weight", ".k_norm.weight"))]
+    if qk:
+        raise CheckpointError(f"{qk[0]}: per-head q/k RMSNorm (Qwen3 use_qk_norm) is not "
+                              "implemented by this decoder")
     R, r = world, rank
     if cfg.heads % R or cfg.kv_heads % R or cfg.intermediate % R or cfg.vocab % R:
         raise CheckpointError(f"tensor parallelism {R} does not divide heads / kv heads / "

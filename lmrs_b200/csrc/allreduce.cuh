@@ -15,7 +15,9 @@
 // reading it (each call needs every peer's packets of the call before).  The
 // epoch lives in device memory next to the buffer and advances at the end of
 // each call (last CTA), so the kernel is CUDA-graph replayable.
-// Every wait is bounded: on expiry the kernel sets kErrWaitPeer and moves on.
+// Every wait is bounded: on expiry the kernel sets kErrWaitPeer, stops waiting
+// for the rest of the call and writes NaN wherever a source's packet was
+// missing, so a lost peer cannot pass for a valid sum downstream.
 #pragma once
 #include "lmrs_ptx.cuh"
 
@@ -70,12 +72,17 @@ __global__ void __launch_bounds__(kArThreads) allreduce_ll_kernel(T* out,
       uint64_t pkt = ld_sys_b64(src);
       if ((pkt & 0xFFFFFFFF00000000ull) != flag) {
         const long long t0 = clock64();
+        const long long limit = *static_cast<volatile long long*>(&g_wait_limit_cycles);
         while (ok && ((pkt = ld_sys_b64(src)) & 0xFFFFFFFF00000000ull) != flag) {
-          if (clock64() - t0 > kWaitLimitCycles) {
+          if (clock64() - t0 > limit) {
             atomicOr(&g_device_error, kErrWaitPeer);
             ok = false;
           }
         }
+      }
+      if ((pkt & 0xFFFFFFFF00000000ull) != flag) {  // gave up on this source
+        a0 = a1 = __int_as_float(0x7fc00000);
+        continue;
       }
       const uint32_t v = static_cast<uint32_t>(pkt);
       T pair[2];

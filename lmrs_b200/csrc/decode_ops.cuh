@@ -15,7 +15,9 @@
 //     [block_offset][head_size], block table per sequence), GQA with the q heads
 //     of one KV head in one CTA: S = Q K^T and O += P V on mma.sync (16 q-head
 //     rows, 16 positions per warp step, fp32 accumulate), online softmax,
-//     split over the context with a combine kernel when a split has peers.
+//     split over the context; the splits of one (sequence, KV head) form a
+//     thread-block cluster and merge their (O, m, l) partials in split order
+//     through distributed shared memory (no second kernel, no global scratch).
 // All are launched with programmatic dependent launch and call pdl_wait before
 // touching their inputs.
 #pragma once

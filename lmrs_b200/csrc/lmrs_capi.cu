@@ -550,7 +550,10 @@ int awq_swap_launch_nt(__half* y, const __half* x, const int32_t* qw, const int3
   if ((rc = ensure_smem(lmrs::awq_gemm_swap_kernel<NT>, smem, g_smem_awq_swap[slot], dev))) return rc;
   const int tiles = (N + lmrs::kSwBN - 1) / lmrs::kSwBN;
   const int KB = K / lmrs::kSwBK;
-  int C = g_tune.awq_swap_cluster > 0 ? g_tune.awq_swap_cluster : (2 * sm_count(dev)) / tiles;
+  // CTAs resident per SM at this tile width (launch bounds allow 2; the
+  // 128-token tile's ~117 KB of shared memory leaves room for one)
+  constexpr int per_sm = (228 * 1024) / (smem + 1024) < 2 ? 1 : 2;
+  int C = g_tune.awq_swap_cluster > 0 ? g_tune.awq_swap_cluster : (per_sm * sm_count(dev)) / tiles;
   C = clampi(C, 1, 8);
   if (C > KB) C = KB;
   rc = launch_cluster(lmrs::awq_gemm_swap_kernel<NT>, tiles * C, C, lmrs::kSwThreads, smem, stream,
@@ -920,6 +923,15 @@ int lmrs_set_tuning(const char* key, int value) {
   else if (!strcmp(key, "awq_i8_ctas_per_sm")) g_tune.awq_i8_ctas_per_sm = value;
   else if (!strcmp(key, "awq_i8_cluster")) g_tune.awq_i8_cluster = value;
   else if (!strcmp(key, "awq_i8_box_rows")) g_tune.awq_i8_box_rows = value;
+  else if (!strcmp(key, "wait_limit_kcycles")) {
+    // bounded-wait limit of the current device, in thousands of SM cycles
+    // (<= 0 restores the default of ~2 s); a device variable, so set per device
+    int rc = check_device(nullptr);
+    if (rc) return rc;
+    const long long v = value > 0 ? 1000LL * value : lmrs::kWaitLimitCycles;
+    cudaError_t e = cudaMemcpyToSymbol(lmrs::g_wait_limit_cycles, &v, sizeof(v));
+    if (e != cudaSuccess) return record(e);
+  }
   else return LMRS_ERR_SHAPE;
   return LMRS_OK;
 }

@@ -29,6 +29,11 @@ __device__ uint32_t g_device_error;
 
 // ~2 s at 1.9 GHz: far above any legitimate wait in these kernels.
 constexpr long long kWaitLimitCycles = 4000000000LL;
+// The limit every bounded wait uses, per device; kWaitLimitCycles unless a
+// host lowers it (lmrs_set_tuning "wait_limit_kcycles", e.g. to make a test's
+// wait on an arrival that never comes give up within a millisecond).  Read
+// only once a wait has already failed its first try.
+__device__ long long g_wait_limit_cycles = kWaitLimitCycles;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -68,12 +73,13 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Wait for the phase with the given parity to complete.  Bounded: after
-// kWaitLimitCycles it records `site` in the device error word and returns false.
+// g_wait_limit_cycles it records `site` in the device error word and returns false.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t site) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
+  const long long limit = *static_cast<volatile long long*>(&g_wait_limit_cycles);
   while (!mbar_try_wait(bar, parity)) {
-    if (clock64() - t0 > kWaitLimitCycles) {
+    if (clock64() - t0 > limit) {
       atomicOr(&g_device_error, site);
       return false;
     }
@@ -368,6 +374,7 @@ __device__ __forceinline__ void st_async_v4(uint32_t cluster_addr, float4 v, uin
 // CTA's shared memory by peer CTAs before their release-arrive).
 __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, uint32_t site) {
   const long long t0 = clock64();
+  long long limit = -1;
   while (true) {
     uint32_t ok;
     asm volatile(
@@ -378,7 +385,8 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity
         : "r"(smem_u32(bar)), "r"(parity), "r"(1000000u)
         : "memory");
     if (ok) return true;
-    if (clock64() - t0 > kWaitLimitCycles) {
+    if (limit < 0) limit = *static_cast<volatile long long*>(&g_wait_limit_cycles);
+    if (clock64() - t0 > limit) {
       atomicOr(&g_device_error, site);
       return false;
     }

@@ -351,6 +351,15 @@ class QuantDecoder:
             L["gate_up"].forward(x)
             L["down"].forward(m)
 
+    def own_launches_per_step(self) -> int:
+        """Kernels of this package one fused decode step launches: per layer the
+        norm, qkv projection, RoPE + KV write, attention, o projection (FP8: its
+        per-token quantisation is a second kernel), norm, gate/up, SiLU * up and
+        down, plus one all-reduce after o and after down when tensor parallel;
+        then the final norm (the embedding gather and the LM head are torch)."""
+        per = 9 + (1 if self.cfg.quant == "fp8" else 0) + (2 if self.world > 1 else 0)
+        return per * self.cfg.layers + 1
+
     def weight_bytes(self) -> int:
         n = 0
         for L in self.layers:

@@ -134,9 +134,12 @@ def test_config0_vs_reference_linear_fwd(cuda, ref_ffi):
 
 
 @pytest.mark.slow
-@pytest.mark.parametrize("M", [1, 16, 128, 1024])
+@pytest.mark.parametrize("M", [1, 16, 128, 1024, 4096])
 def test_config1_full_size(cuda, ref_ffi, M):
-    """Config 1 shape (K=4096, N=14336, g=128) against the reference's linear_fwd."""
+    """Config 1 shape (K=4096, N=14336, g=128) at every M of the sweep against the
+    reference's linear_fwd on the dequantised weights, over all M x N outputs.
+    M=4096 is the bench line's dominant kernel, where each persistent CTA of the
+    prefill GEMM walks several 128-channel x 256-token tiles."""
     import lmrs_b200 as L
     K, N, g = 4096, 14336, 128
     d = O.awq_inputs(M, K, N, g, seed=0)
@@ -316,4 +319,18 @@ def test_gemm_tmem_opt_in(cuda, bt, M, K, N, g):
         L.set_tuning("awq_gemm_tmem_bt", 256)
         L.set_tuning("awq_swap_deep_k", 5)
     assert err < TIGHT, err
+    assert L.read_device_error() == 0
+
+
+@pytest.mark.parametrize("M", [65, 96, 128])
+@pytest.mark.parametrize("K,N", [(4096, 3072), (6144, 4096)])
+def test_default_dispatch_deep_k_band(cuda, M, K, N):
+    """Default dispatch in the 1.25 <= K/N < 2 band at 65-128 tokens, where the
+    split-K swap-AB kernel is picked over the prefill GEMM (4K >= 5N), against
+    the C oracle."""
+    import torch
+    import lmrs_b200 as L
+    err, (x, qw, qz, sc, b, y) = _awq_case(cuda, M, K, N, 128, 77 + M + N)
+    assert err < TIGHT, err
+    assert torch.equal(L.awq_linear(x, qw, qz, sc, b, 128), y)
     assert L.read_device_error() == 0

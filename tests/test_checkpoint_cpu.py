@@ -88,6 +88,10 @@ def test_sharded_index(tmp_path):
     ({"quant_method": "awq", "bits": 4, "group_size": 128, "version": "gemv"}, None),
     ({"quant_method": "awq", "bits": 4, "group_size": 128, "zero_point": False}, None),
     ({"quant_method": "fp8", "activation_scheme": "dynamic"}, "fp8"),
+    ({"quant_method": "fp8"}, "fp8"),
+    ({"quant_method": "fp8", "activation_scheme": "static"}, None),
+    ({"quant_method": "fp8", "activation_scheme": "dynamic", "weight_block_size": [128, 128]},
+     None),
     ({"quant_method": "gptq", "bits": 4}, None),
 ])
 def test_quant_spec(qc, ok):
@@ -190,3 +194,36 @@ def test_awq_split_must_keep_groups(tmp_path):
     C.load_decoder_weights(str(tmp_path), rank=0, world=1)
     with pytest.raises(C.CheckpointError):   # down: 768 / 2 = 384 rows cut a 256-row group
         C.load_decoder_weights(str(tmp_path), rank=0, world=2)
+
+
+def test_rejects_qk_norm_tensors(tmp_path):
+    """A Qwen3 checkpoint carries per-head q/k norms (use_qk_norm); the decoder
+    does not implement them, so loading must fail instead of giving wrong
+    attention outputs."""
+    cfg = _cfg("awq")
+    t = _write_model(tmp_path / "a", cfg)
+    t["model.layers.0.self_attn.q_norm.weight"] = torch.ones(cfg.head_dim).half()
+    t["model.layers.0.self_attn.k_norm.weight"] = torch.ones(cfg.head_dim).half()
+    C.save_sharded(str(tmp_path / "b"), t, shards=1, config=C.hf_config(cfg))
+    with pytest.raises(C.CheckpointError, match="q_norm|k_norm"):
+        C.load_decoder_weights(str(tmp_path / "b"))
+
+
+@pytest.mark.parametrize("extra", [{"use_qk_norm": True},
+                                   {"rope_scaling": {"rope_type": "llama3", "factor": 8.0}}])
+def test_rejects_unimplemented_config(tmp_path, extra):
+    cfg = _cfg("fp8")
+    t = _write_model(tmp_path, cfg)
+    hf = dict(C.hf_config(cfg), **extra)
+    C.save_sharded(str(tmp_path / "c"), t, shards=1, config=hf)
+    with pytest.raises(C.CheckpointError):
+        C.load_decoder_weights(str(tmp_path / "c"))
+
+
+def test_fp8_input_scale_warns(tmp_path):
+    cfg = _cfg("fp8")
+    t = _write_model(tmp_path, cfg)
+    t["model.layers.0.self_attn.q_proj.input_scale"] = torch.tensor(0.5)
+    C.save_sharded(str(tmp_path / "d"), t, shards=1, config=C.hf_config(cfg))
+    with pytest.warns(UserWarning, match="input_scale"):
+        C.load_decoder_weights(str(tmp_path / "d"))

@@ -80,6 +80,64 @@ def _worker(rank, world, port, out_path):
         dist.destroy_process_group()
 
 
+def test_wait_gives_up_without_peer():
+    """The all-reduce's bounded wait, made to run out on one GPU: a 2-rank call
+    whose second rank is only a local buffer nobody writes into.  With the wait
+    limit lowered to ~1 ms the call must return, flag kErrWaitPeer in the device
+    error word and leave NaN where the missing rank's packets belong; after the
+    limit and the buffers are reset, the next call is clean.  No kernel waits on
+    another launch: rank 1's packets simply never come."""
+    import ctypes
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    import lmrs_b200 as L
+    from lmrs_b200 import _lib
+    lib = _lib.load()
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    n, world = 4096, 2
+    nbytes = lib.lmrs_allreduce_buffer_bytes(world, n)
+    bufs = (ctypes.c_void_p * world)()
+
+    def alloc():  # zero-filled receive buffers (epoch 0)
+        for r in range(world):
+            p = ctypes.c_void_p()
+            _lib.check("lmrs_comm_alloc", lib.lmrs_comm_alloc(ctypes.byref(p), nbytes))
+            bufs[r] = p
+
+    def free():
+        torch.cuda.synchronize()
+        for r in range(world):
+            lib.lmrs_comm_free(bufs[r])
+            bufs[r] = None
+
+    alloc()
+    stream = torch.cuda.current_stream().cuda_stream
+    x = torch.ones(n, dtype=torch.bfloat16, device=dev)
+    y = torch.zeros_like(x)
+    try:
+        assert L.read_device_error() == 0
+        L.set_tuning("wait_limit_kcycles", 2000)  # ~1 ms at 1.9 GHz
+        _lib.check("lmrs_allreduce_sum", lib.lmrs_allreduce_sum(
+            y.data_ptr(), x.data_ptr(), n, _lib.DTYPE_BF16, 0, world, bufs, n, stream))
+        torch.cuda.synchronize()
+        assert L.read_device_error() & (1 << 5), "kErrWaitPeer not flagged"
+        assert bool(torch.isnan(y.float()).all()), "a missing peer must not yield a sum"
+        # reset: default limit, fresh buffers; a single-rank call is then exact and clean
+        L.set_tuning("wait_limit_kcycles", 0)
+        free()
+        alloc()
+        y2 = torch.empty_like(x)
+        _lib.check("lmrs_allreduce_sum", lib.lmrs_allreduce_sum(
+            y2.data_ptr(), x.data_ptr(), n, _lib.DTYPE_BF16, 0, 1, bufs, n, stream))
+        torch.cuda.synchronize()
+        assert torch.equal(y2, x)
+        assert L.read_device_error() == 0
+    finally:
+        L.set_tuning("wait_limit_kcycles", 0)
+        free()
+
+
 def test_peer_allreduce_2gpu(tmp_path):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")

@@ -92,10 +92,11 @@ def test_linear_gemm_small(cuda, M, bias):
 
 
 @pytest.mark.parametrize("K,N", [(4096, 4096), (4096, 28672), (14336, 4096)])
-@pytest.mark.parametrize("M", [1, 32, 512])
+@pytest.mark.parametrize("M", [1, 32, 512, 8192])
 def test_config2_shapes_vs_reference(cuda, ref_ffi, K, N, M):
-    """Config 2 shapes: CUDA W8A8 vs the reference's linear_fwd (f32 variant) run on
-    the dequantised operands xq*s_x and wq*s_w."""
+    """Config 2, every (K, N) at every M of the sweep (M=8192 is the FP8 GEMM's
+    headline point): CUDA W8A8 vs the reference's linear_fwd (f32 variant) run on
+    the dequantised operands xq*s_x and wq*s_w, over all M x N outputs."""
     import torch
     import lmrs_b200 as L
     f = O.fp8_inputs(M, K, N, seed=0)
