@@ -25,8 +25,10 @@
  *   AWQ W4A16: qweight int32 [K, N/8]; word j of row k holds columns 8j..8j+7,
  *     nibble i (bits 4i..4i+3) = column 8j + ORDER[i], ORDER = {0,2,4,6,1,3,5,7}.
  *     qzeros int32 [K/g, N/8] packed the same way; scales fp16 [K/g, N].
- *     w[k,n] = fp16_rne((q[k,n] - z[k/g,n]) * s[k/g,n])   (one rounding);
- *     y[m,n] = fp16(sum_k x[m,k] * w[k,n] (+ bias[n])), fp32 accumulation.
+ *     Activations x, y, bias are fp16 or bf16 (act_dtype); the dequantised
+ *     weight has the activation type and is the exact product rounded once:
+ *     w[k,n] = T_rne((q[k,n] - z[k/g,n]) * s[k/g,n]), T = fp16 or bf16;
+ *     y[m,n] = T(sum_k x[m,k] * w[k,n] (+ bias[n])), fp32 accumulation.
  *   FP8 W8A8: wq e4m3 [N, K] (same [out, in] layout as LinearOp's weight,
  *     crates/ops/src/linear/linear.rs:48-66), w_scale fp32 [N];
  *     s_x[m] = absmax_k |x[m,k]| / 448, xq = e4m3_rne_satfinite(x / s_x)
@@ -116,12 +118,23 @@ LMRS_API int lmrs_awq_dequant(void* w_out, const int32_t* qweight, const int32_t
                      const void* scales, int K, int N, int group,
                      lmrs_stream_t stream);
 
+/* The same dequant to the activation type out_dtype: LMRS_DTYPE_F16 (as
+ * lmrs_awq_dequant) or LMRS_DTYPE_BF16, w = bf16_rne((q - z) * s) with the
+ * fp16 scale as stored (one rounding of the exact product), bit-exact.  These
+ * are the weights the bf16 lmrs_awq_linear multiplies by (the GEMV regimes
+ * apply the scale to integer sums instead and round nothing per weight). */
+LMRS_API int lmrs_awq_dequant_dtype(void* w_out, const int32_t* qweight,
+                                    const int32_t* qzeros, const void* scales, int K,
+                                    int N, int group, int out_dtype, lmrs_stream_t stream);
+
 /* Workspace for lmrs_awq_linear.  Returns 0: the AWQ linear keeps its split-K
  * partial sums in thread-block-cluster shared memory and needs no scratch. */
 LMRS_API size_t lmrs_awq_linear_workspace_bytes(int M, int K, int N, int group);
 
 /* y[M,N] = x[M,K] @ dequant(qweight, qzeros, scales) (+ bias[N]).
- * act_dtype must be LMRS_DTYPE_F16 (x, y, bias fp16).  Requirements:
+ * act_dtype is the type of x, y and bias: LMRS_DTYPE_BF16 (the reference
+ * model's dtype, crates/kernels/src/raw.rs:9-13) or LMRS_DTYPE_F16; scales are
+ * fp16 either way.  Requirements:
  * K % group == 0, group % 64 == 0, N % 32 == 0, 16-byte aligned pointers.
  * M <= 8 runs a register-dequant tensor-core GEMV (HBM bound); M <= 64 a
  * swap-AB split-K tcgen05 kernel; larger M a persistent tcgen05 GEMM (one SM

@@ -48,6 +48,7 @@ SIGNATURES = {
     "lmrs_set_tuning": (I, [ctypes.c_char_p, I]),
     "lmrs_awq_unpack": (I, [P, P, I, I, P]),
     "lmrs_awq_dequant": (I, [P, P, P, P, I, I, I, P]),
+    "lmrs_awq_dequant_dtype": (I, [P, P, P, P, I, I, I, I, P]),
     "lmrs_awq_linear_workspace_bytes": (SZ, [I, I, I, I]),
     "lmrs_awq_linear": (I, [P, P, P, P, P, P, I, I, I, I, I, P, SZ, P]),
     "lmrs_fp8_quant_rows": (I, [P, P, P, I, I, I, P]),

@@ -72,9 +72,9 @@ __global__ void __launch_bounds__(kArThreads) allreduce_ll_kernel(T* out,
       uint64_t pkt = ld_sys_b64(src);
       if ((pkt & 0xFFFFFFFF00000000ull) != flag) {
         const long long t0 = clock64();
-        const long long limit = *static_cast<volatile long long*>(&g_wait_limit_cycles);
+        long long limit = -1;
         while (ok && ((pkt = ld_sys_b64(src)) & 0xFFFFFFFF00000000ull) != flag) {
-          if (clock64() - t0 > limit) {
+          if (wait_expired(t0, limit)) {
             atomicOr(&g_device_error, kErrWaitPeer);
             ok = false;
           }

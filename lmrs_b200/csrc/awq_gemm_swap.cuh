@@ -9,8 +9,9 @@
 //     "N" side is the padded token count NT in {16, 32, 64, 128} (operand B =
 //     the x tile, K-major, TMA with 128-byte swizzle);
 //   * dequant warps turn TMA-staged packed int4 (16 words x 64 k rows) plus the
-//     group's zeros/scales into fp16 A stages in the UMMA MN-major SW128 layout
-//     (canonical fp16 (q - z) * s, bit-identical to lmrs_awq_dequant);
+//     group's zeros/scales into A stages of the activation type (fp16 or
+//     bf16) in the UMMA MN-major SW128 layout (canonical T_rne((q - z) * s),
+//     bit-identical to lmrs_awq_dequant_dtype);
 //   * K is split over a cluster of C CTAs (grid = N/128 tiles x C, about two CTAs
 //     per SM); each CTA's 128 x NT fp32 accumulator goes TMEM -> shared memory
 //     and the cluster sums the C partials through distributed shared memory.
@@ -30,7 +31,7 @@ constexpr int kSwSB = 2;         // dequantised A stages
 constexpr int kSwDqWarps = 8;
 constexpr int kSwThreads = 32 * (2 + kSwDqWarps);  // 320
 constexpr int kSwPBytes = kSwBK * (kSwBN / 8) * 4;  // 4 KB packed
-constexpr int kSwABytes = kSwBN * kSwBK * 2;        // 16 KB fp16 A stage
+constexpr int kSwABytes = kSwBN * kSwBK * 2;        // 16 KB 16-bit A stage
 constexpr int kSwSBytes = kSwBN * 2;                // 256 B scales
 constexpr int kSwZBytes = (kSwBN / 8) * 4;          // 64 B zeros
 
@@ -42,13 +43,13 @@ __host__ __device__ constexpr int sw_smem_bytes(int nt) {
   return 1024 + kSwSA * ((sw_stage_bytes(nt) + 1023) / 1024 * 1024) + kSwSB * kSwABytes + 256;
 }
 
-template <int NT>
+template <int NT, typename T>
 __global__ void __launch_bounds__(kSwThreads, 2)
     awq_gemm_swap_kernel(const __grid_constant__ CUtensorMap tm_x,
                          const __grid_constant__ CUtensorMap tm_q,
                          const __grid_constant__ CUtensorMap tm_s,
-                         const __grid_constant__ CUtensorMap tm_z, __half* __restrict__ y,
-                         const __half* __restrict__ bias, int M, int K, int N, int group) {
+                         const __grid_constant__ CUtensorMap tm_z, T* __restrict__ y,
+                         const T* __restrict__ bias, int M, int K, int N, int group) {
   pdl_wait();     // activations are the previous kernel's output
   pdl_trigger();
   namespace cg = cooperative_groups;
@@ -123,7 +124,8 @@ __global__ void __launch_bounds__(kSwThreads, 2)
   } else if (warp == 1) {
     if (lane == 0) {
       // A = W^T tile (MN-major), B = x tile (K-major), D[n][m] in TMEM
-      constexpr uint32_t idesc = make_idesc(0, 0, /*a MN-major*/ 1, /*b K-major*/ 0, kSwBN, NT);
+      constexpr uint32_t fmt = Act<T>::kUmmaFmt;  // both operands f16, or both bf16
+      constexpr uint32_t idesc = make_idesc(fmt, fmt, /*a MN-major*/ 1, /*b K-major*/ 0, kSwBN, NT);
       bool ok = true;
       for (int i = 0; i < nkb && ok; ++i) {
         const int s = i % kSwSA, sa = i % kSwSB;
@@ -160,7 +162,9 @@ __global__ void __launch_bounds__(kSwThreads, 2)
       const uint4 sv = reinterpret_cast<const uint4*>(st + kX + kSwPBytes)[j];
       const uint32_t zw = reinterpret_cast<const uint32_t*>(st + kX + kSwPBytes + kSwSBytes)[j];
       uint32_t zb[4];
-      awq_word_to_h2_biased(zw, zb);
+      awq_word_biased<T>(zw, zb);
+      const AwqScale2 sp[4] = {awq_scale2<T>(sv.x), awq_scale2<T>(sv.y), awq_scale2<T>(sv.z),
+                               awq_scale2<T>(sv.w)};
       const uint32_t abase = smem_u32(sA + sa * kSwABytes) + blk * 8192;
       uint32_t w[4];
 #pragma unroll
@@ -169,12 +173,12 @@ __global__ void __launch_bounds__(kSwThreads, 2)
       for (int it = 0; it < 4; ++it) {
         const int r = dw * 8 + 2 * it + half;
         uint32_t qb[4];
-        awq_word_to_h2_biased(w[it], qb);
+        awq_word_biased<T>(w[it], qb);
         uint4 o;
-        o.x = dq_h2(qb[0], zb[0], sv.x);
-        o.y = dq_h2(qb[1], zb[1], sv.y);
-        o.z = dq_h2(qb[2], zb[2], sv.z);
-        o.w = dq_h2(qb[3], zb[3], sv.w);
+        o.x = awq_dq<T>(qb[0], zb[0], sp[0]);
+        o.y = awq_dq<T>(qb[1], zb[1], sp[1]);
+        o.z = awq_dq<T>(qb[2], zb[2], sp[2]);
+        o.w = awq_dq<T>(qb[3], zb[3], sp[3]);
         st_shared_v4(abase + (r >> 3) * 1024 + (r & 7) * 128 + ((chunk ^ (r & 7)) << 4), o);
       }
       fence_proxy_async_smem();
@@ -218,8 +222,8 @@ __global__ void __launch_bounds__(kSwThreads, 2)
     float v = 0.f;
     for (int r = 0; r < C; ++r) v += cluster.map_shared_rank(red, r)[m * kSwBN + f];
     if (n < N) {
-      if (bias != nullptr) v += __half2float(bias[n]);
-      y[static_cast<int64_t>(m) * N + n] = __float2half_rn(v);
+      if (bias != nullptr) v += Act<T>::to_float(bias[n]);
+      y[static_cast<int64_t>(m) * N + n] = Act<T>::from_float(v);
     }
   }
   cluster.sync();

@@ -28,10 +28,11 @@
 //     warp per TMEM lane quarter and group) — quarter q takes the 16-byte
 //     chunk q of each packed row with ldmatrix.trans (64-byte swizzled box),
 //     whose registers pair rows r, r+1 of a half-word: one lop3 per nibble
-//     makes the biased half2 (1024 + q or 64 + q); each thread loads its
-//     word's 8 scales (16 bytes) and zero word one K-block ahead; subtracting
-//     the same-biased zero is exact and the multiply by the scale rounds once,
-//     so A holds exactly fp16_rne((q - z) * s); tcgen05.st 16x128b lays each
+//     makes the biased pair (fp16: 1024 + q or 64 + q; bf16: 128 + q after a
+//     shift); each thread loads its word's 8 scales (16 bytes) and zero word
+//     one K-block ahead; subtracting the same-biased zero is exact and the
+//     scale product rounds once, so A holds exactly T_rne((q - z) * s) in the
+//     activation type T (fp16 or bf16, lmrs_ptx.cuh Act<T>); tcgen05.st 16x128b lays each
 //     channel along one TMEM lane (lane L of a quarter: channel
 //     8 ((L & 7) >> 1) + 2 (L >> 3) + (L & 1)).
 // Every mbarrier wait is bounded; on expiry the kernel records the site in the
@@ -94,17 +95,17 @@ __device__ __forceinline__ void agt_coords(int t, int m_tiles, int n_tiles, int&
   n0 = (local / gm) * kAgtCh;
 }
 
-template <int BT>
+template <int BT, typename T>
 __global__ void __launch_bounds__(kAgtThreads, 1) awq_gemm_tmem_kernel(
     const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_q,
     const __half* __restrict__ scales, const uint32_t* __restrict__ qzeros,
-    __half* __restrict__ y, const __half* __restrict__ bias, int M, int K, int N, int group) {
+    T* __restrict__ y, const T* __restrict__ bias, int M, int K, int N, int group) {
   using L = AgtLayout<BT>;
   constexpr int S = L::kStages, R = L::kAStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sx = align1024(smem_raw);
   uint8_t* ssm = sx + S * L::kX;
-  __half* sepi = reinterpret_cast<__half*>(ssm + S * L::kSmall);
+  T* sepi = reinterpret_cast<T*>(ssm + S * L::kSmall);
   uint64_t* full = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(sepi) + L::kEpi);
   uint64_t* empty = full + S;
   uint64_t* afull = empty + S;  // TMEM stage's dequantised weights are written
@@ -165,7 +166,8 @@ __global__ void __launch_bounds__(kAgtThreads, 1) awq_gemm_tmem_kernel(
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA
     if (lane == 0) {
-      constexpr uint32_t idesc = make_idesc(0, 0, 0, 0, kAgtCh, BT);  // f16 x f16, K-major
+      constexpr uint32_t fmt = Act<T>::kUmmaFmt;  // both operands f16, or both bf16
+      constexpr uint32_t idesc = make_idesc(fmt, fmt, 0, 0, kAgtCh, BT);  // K-major
       uint32_t kg = 0, it = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++it) {
@@ -207,8 +209,8 @@ __global__ void __launch_bounds__(kAgtThreads, 1) awq_gemm_tmem_kernel(
       int m0, n0;
       agt_coords<BT>(t, m_tiles, n_tiles, m0, n0);
       const int n = n0 + c;
-      const float bn = (bias != nullptr && n < N) ? __half2float(bias[n]) : 0.f;
-      __half* tw = sepi + quarter * 16 * L::kEpiPitch;
+      const float bn = (bias != nullptr && n < N) ? Act<T>::to_float(bias[n]) : 0.f;
+      T* tw = sepi + quarter * 16 * L::kEpiPitch;
       const int te = lane >> 1, th = lane & 1;          // read side: token, 16-channel half
       const int nw = n0 + quarter * 32 + 16 * th;       // N % 32 == 0: whole 16-channel runs
       for (int ch = 0; ch < BT / 16; ++ch) {
@@ -216,7 +218,7 @@ __global__ void __launch_bounds__(kAgtThreads, 1) awq_gemm_tmem_kernel(
         tmem_ld16(tmem + lane_addr + a * BT + ch * 16, r);
         tmem_ld_wait();
 #pragma unroll
-        for (int e = 0; e < 16; ++e) tw[e * L::kEpiPitch + cq] = __float2half_rn(__uint_as_float(r[e]) + bn);
+        for (int e = 0; e < 16; ++e) tw[e * L::kEpiPitch + cq] = Act<T>::from_float(__uint_as_float(r[e]) + bn);
         __syncwarp();
         const int m = m0 + ch * 16 + te;
         if (m < M && nw < N) {
@@ -288,12 +290,12 @@ __global__ void __launch_bounds__(kAgtThreads, 1) awq_gemm_tmem_kernel(
         if (!(ok = mbar_wait(&empty[j % S], (j / S) & 1, kErrWaitAccum))) break;
       }
       const uint32_t s4[4] = {s_cur.x, s_cur.y, s_cur.z, s_cur.w};
-      uint32_t zz[4], ss[4];
+      uint32_t zz[4];
+      AwqScale2 ss[4];
 #pragma unroll
       for (int n = 0; n < 4; ++n) {
-        const uint32_t z = (z_cur >> (4 * n)) & 0xFu;
-        zz[n] = ((n & 1) ? (0x5400u | (z << 4)) : (0x6400u | z)) * 0x00010001u;
-        ss[n] = prmt(s4[n], s4[n], sdup);  // channel 8 wt + 2n + codd
+        zz[n] = awq_zero_pair<T>((z_cur >> (4 * n)) & 0xFu, n);
+        ss[n] = awq_scale2<T>(prmt(s4[n], s4[n], sdup));  // channel 8 wt + 2n + codd
       }
       const uint8_t* sm = ssm + s * L::kSmall;
       const uint32_t acol = tmem + lane_addr + L::kTmemA + ar * 32;
@@ -305,11 +307,11 @@ __global__ void __launch_bounds__(kAgtThreads, 1) awq_gemm_tmem_kernel(
         uint32_t lo[8], hi[8];
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          const uint32_t v = d[i], v8 = d[i] >> 8;
-          lo[2 * i] = dq_h2(lop3_and_or(v, 0x000F000Fu, 0x64006400u), zz[0], ss[0]);
-          lo[2 * i + 1] = dq_h2(lop3_and_or(v, 0x00F000F0u, 0x54005400u), zz[1], ss[1]);
-          hi[2 * i] = dq_h2(lop3_and_or(v8, 0x000F000Fu, 0x64006400u), zz[2], ss[2]);
-          hi[2 * i + 1] = dq_h2(lop3_and_or(v8, 0x00F000F0u, 0x54005400u), zz[3], ss[3]);
+          // nibble j of each half: j = 0, 1 -> lanes hc, hc + 8; j = 2, 3 -> 16 + hc, 24 + hc
+          lo[2 * i] = awq_dq<T>(awq_nib_pair<T>(d[i], 0), zz[0], ss[0]);
+          lo[2 * i + 1] = awq_dq<T>(awq_nib_pair<T>(d[i], 1), zz[1], ss[1]);
+          hi[2 * i] = awq_dq<T>(awq_nib_pair<T>(d[i], 2), zz[2], ss[2]);
+          hi[2 * i + 1] = awq_dq<T>(awq_nib_pair<T>(d[i], 3), zz[3], ss[3]);
         }
         tmem_st16x128b_x4(acol + 16 * h, lo);
         tmem_st16x128b_x4(acol + (16u << 16) + 16 * h, hi);

@@ -23,7 +23,8 @@
 //     64-byte swizzle makes the 32-bit LDS conflict-free).  prmt pairs rows
 //     (k, k+1); since AWQ stores columns (2i, 2i+1) in nibbles (i, i+4), one
 //     lop3 turns a nibble pair into the half2 (B + q[k][c], B + q[k+1][c]),
-//     B = 1024 (bits 0-3 of a half) or 64 (bits 4-7).  Output columns are the
+//     B = 1024 (bits 0-3 of a half) or 64 (bits 4-7); with bf16 activations
+//     (bf16 MMA operands) every nibble is shifted to bits 0-3, B = 128.  Output columns are the
 //     MMA "M" (16 per m16n8k16 tile), tokens the "N" (8 per tile, MT tiles).
 //   * Zero point and scale are applied once per box, not per weight: the MMAs
 //     accumulate D = sum_k (B + q) x and, with an all-ones A tile, X = sum_k x;
@@ -69,6 +70,22 @@ __device__ __forceinline__ void mma_f16_16816(float (&d)[4], const uint32_t (&a)
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
+__device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a)[4],
+                                               uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// m16n8k16 with both operands of the activation type T, fp32 accumulate.
+template <typename T>
+__device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                          uint32_t b1) {
+  if constexpr (Act<T>::kUmmaFmt == 0) mma_f16_16816(d, a, b0, b1);
+  else mma_bf16_16816(d, a, b0, b1);
+}
+
 __device__ __forceinline__ void named_bar_sync(int id, int threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
@@ -109,11 +126,11 @@ __device__ __forceinline__ uint32_t sw64(int r, int j) {
   return off ^ (((off >> 7) & 3u) << 4);
 }
 
-template <int MT, int BR>
+template <int MT, int BR, typename T>
 __global__ void __launch_bounds__(kAwqGemvThreads, (MT == 1 ? 4 : 3)) awq_gemv_kernel(
     const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_x,
     const __grid_constant__ CUtensorMap tm_s, const __grid_constant__ CUtensorMap tm_z,
-    __half* __restrict__ y, const __half* __restrict__ bias, int M, int K, int N, int group,
+    T* __restrict__ y, const T* __restrict__ bias, int M, int K, int N, int group,
     int S) {
   using L = AwqGemvLayout<MT, BR>;
   constexpr int MP = 8 * MT;  // padded token count
@@ -209,7 +226,7 @@ __global__ void __launch_bounds__(kAwqGemvThreads, (MT == 1 ? 4 : 3)) awq_gemv_k
     // row pairs so each LDS hits 32 distinct banks
     const uint32_t o0 = sw64(2 * t + odd, jj), o1 = sw64(2 * t + 1 - odd, jj);
     const uint32_t o8 = sw64(2 * t + 8 + odd, jj), o9 = sw64(2 * t + 9 - odd, jj);
-    const uint32_t ones[4] = {0x3C003C00u, 0x3C003C00u, 0x3C003C00u, 0x3C003C00u};  // fp16 1.0
+    const uint32_t ones[4] = {Act<T>::kOne2, Act<T>::kOne2, Act<T>::kOne2, Act<T>::kOne2};
     int s = p;
     uint32_t ph = 0;
     for (int b = p; b < nbox; b += 2) {
@@ -243,33 +260,26 @@ __global__ void __launch_bounds__(kAwqGemvThreads, (MT == 1 ? 4 : 3)) awq_gemv_k
           bx[mt][0] = ld_s32(xs + mt * 1024 + ((c2 ^ g) << 4));
           bx[mt][1] = ld_s32(xs + mt * 1024 + (((c2 + 1) ^ g) << 4));
         }
-        uint32_t pk[2][4];  // [row pair 01 / 89][lo 16 bits, hi 16 bits, and the same >> 8]
+        uint32_t pk[2][2];  // [row pair 01 / 89][lo 16 bits (nibbles 0-3), hi 16 bits (4-7)]
         pk[0][0] = prmt(w0, w1, 0x5410);
         pk[0][1] = prmt(w0, w1, 0x7632);
         pk[1][0] = prmt(w8, w9, 0x5410);
         pk[1][1] = prmt(w8, w9, 0x7632);
 #pragma unroll
-        for (int r = 0; r < 2; ++r) {
-          pk[r][2] = pk[r][0] >> 8;
-          pk[r][3] = pk[r][1] >> 8;
-        }
-#pragma unroll
         for (int i = 0; i < 4; ++i) {
-          const uint32_t mask = (i & 1) ? 0x00F000F0u : 0x000F000Fu;
-          const uint32_t magic = (i & 1) ? 0x54005400u : 0x64006400u;
-          const int sh = (i >> 1) * 2;
+          // nibble i of each half-word: column 2i (low half-word) and 2i+1 (high)
           uint32_t a[4];
-          a[0] = lop3_and_or(pk[0][sh + 0], mask, magic);
-          a[1] = lop3_and_or(pk[0][sh + 1], mask, magic);
-          a[2] = lop3_and_or(pk[1][sh + 0], mask, magic);
-          a[3] = lop3_and_or(pk[1][sh + 1], mask, magic);
+          a[0] = awq_nib_pair<T>(pk[0][0], i);
+          a[1] = awq_nib_pair<T>(pk[0][1], i);
+          a[2] = awq_nib_pair<T>(pk[1][0], i);
+          a[3] = awq_nib_pair<T>(pk[1][1], i);
 #pragma unroll
-          for (int mt = 0; mt < MT; ++mt) mma_f16_16816(D[mt][i], a, bx[mt][0], bx[mt][1]);
+          for (int mt = 0; mt < MT; ++mt) mma_16816<T>(D[mt][i], a, bx[mt][0], bx[mt][1]);
         }
 #pragma unroll
         for (int mt = 0; mt < MT; ++mt) {
           float xsum[4] = {X[mt][0], X[mt][1], 0.f, 0.f};
-          mma_f16_16816(xsum, ones, bx[mt][0], bx[mt][1]);
+          mma_16816<T>(xsum, ones, bx[mt][0], bx[mt][1]);
           X[mt][0] = xsum[0];
           X[mt][1] = xsum[1];
         }
@@ -285,7 +295,7 @@ __global__ void __launch_bounds__(kAwqGemvThreads, (MT == 1 ? 4 : 3)) awq_gemv_k
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         // nibble pair i of the zero word holds columns (2i, 2i+1)
-        const float bias_i = (i & 1) ? 64.f : 1024.f;  // the magic each tile's A carries
+        const float bias_i = awq_nib_bias<T>(i);  // the magic each tile's A carries
         const float za = bias_i + static_cast<float>((zw >> (4 * i)) & 0xFu);
         const float zb = bias_i + static_cast<float>((zw >> (4 * i + 16)) & 0xFu);
         const float2 sp = __half22float2(u32_as_h2(sv[i]));
@@ -351,8 +361,8 @@ __global__ void __launch_bounds__(kAwqGemvThreads, (MT == 1 ? 4 : 3)) awq_gemv_k
         float v = 0.f;
         for (int q = 0; q < C; ++q) v += recv[(q * cw + cl) * MP + m];
         if (n < N) {
-          if (bias != nullptr) v += __half2float(bias[n]);
-          y[static_cast<int64_t>(m) * N + n] = __float2half_rn(v);
+          if (bias != nullptr) v += Act<T>::to_float(bias[n]);
+          y[static_cast<int64_t>(m) * N + n] = Act<T>::from_float(v);
         }
       }
     }

@@ -50,11 +50,11 @@ struct AwqGemv4Layout {
   }
 };
 
-template <int BR>
+template <int BR, typename T>
 __global__ void __launch_bounds__(kAwqGemv4Threads, 4) awq_gemv4_kernel(
     const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_x,
     const __grid_constant__ CUtensorMap tm_s, const __grid_constant__ CUtensorMap tm_z,
-    __half* __restrict__ y, const __half* __restrict__ bias, int M, int K, int N, int group,
+    T* __restrict__ y, const T* __restrict__ bias, int M, int K, int N, int group,
     int S) {
   using L = AwqGemv4Layout<BR>;
   constexpr int kTok = 4;
@@ -154,7 +154,7 @@ __global__ void __launch_bounds__(kAwqGemv4Threads, 4) awq_gemv4_kernel(
     const uint32_t v0 = odd ? hi_v : lo_v, v1 = odd ? lo_v : hi_v;  // rows R, R'
     const uint32_t sel0 = (g & 1) ? (0x44u | (v0 << 8)) : (v0 | 0x4400u);
     const uint32_t sel1 = (g & 1) ? (0x44u | (v1 << 8)) : (v1 | 0x4400u);
-    const uint32_t ones[4] = {0x3C003C00u, 0x3C003C00u, 0x3C003C00u, 0x3C003C00u};
+    const uint32_t ones[4] = {Act<T>::kOne2, Act<T>::kOne2, Act<T>::kOne2, Act<T>::kOne2};
     int s = p;
     uint32_t ph = 0;
     for (int b = p; b < nbox; b += 4) {
@@ -173,20 +173,15 @@ __global__ void __launch_bounds__(kAwqGemv4Threads, 4) awq_gemv4_kernel(
         const uint32_t xv = ld_s32(sbase + L::kW + sub * L::kXSub + xo + ((c16 ^ tok) << 4));
         const uint32_t b0 = prmt(xv, 0u, sel0), b1 = prmt(xv, 0u, sel1);
         const uint32_t ra[4] = {pa.x, pa.y, pb.x, pb.y};
-        uint32_t rs[4];
-#pragma unroll
-        for (int r = 0; r < 4; ++r) rs[r] = ra[r] >> 8;
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          const uint32_t mask = (i & 1) ? 0x00F000F0u : 0x000F000Fu;
-          const uint32_t magic = (i & 1) ? 0x54005400u : 0x64006400u;
           uint32_t a[4];
 #pragma unroll
-          for (int r = 0; r < 4; ++r) a[r] = lop3_and_or(i < 2 ? ra[r] : rs[r], mask, magic);
-          mma_f16_16816(D[i], a, b0, b1);
+          for (int r = 0; r < 4; ++r) a[r] = awq_nib_pair<T>(ra[r], i);  // nibbles i, i + 4
+          mma_16816<T>(D[i], a, b0, b1);
         }
         float xs[4] = {X0, X1, 0.f, 0.f};
-        mma_f16_16816(xs, ones, b0, b1);
+        mma_16816<T>(xs, ones, b0, b1);
         X0 = xs[0];
         X1 = xs[1];
       }
@@ -200,7 +195,7 @@ __global__ void __launch_bounds__(kAwqGemv4Threads, 4) awq_gemv4_kernel(
       const uint32_t sva[4] = {sa.x, sa.y, sa.z, sa.w}, svb[4] = {sb.x, sb.y, sb.z, sb.w};
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        const float bias_i = (i & 1) ? 64.f : 1024.f;
+        const float bias_i = awq_nib_bias<T>(i);
         const float za0 = bias_i + static_cast<float>((zw.x >> (4 * i)) & 0xFu);
         const float za1 = bias_i + static_cast<float>((zw.x >> (4 * i + 16)) & 0xFu);
         const float zb0 = bias_i + static_cast<float>((zw.y >> (4 * i)) & 0xFu);
@@ -260,8 +255,8 @@ __global__ void __launch_bounds__(kAwqGemv4Threads, 4) awq_gemv4_kernel(
         float v = 0.f;
         for (int q = 0; q < C; ++q) v += recv[(q * cw + cl) * kTok + m];
         if (n < N) {
-          if (bias != nullptr) v += __half2float(bias[n]);
-          y[static_cast<int64_t>(m) * N + n] = __float2half_rn(v);
+          if (bias != nullptr) v += Act<T>::to_float(bias[n]);
+          y[static_cast<int64_t>(m) * N + n] = Act<T>::from_float(v);
         }
       }
     }

@@ -13,8 +13,9 @@
 //     integers.
 //   * The activations become integers without loss that matters: per box of
 //     BR rows and per token, X = rint(x * 2^sh) with sh chosen so |X| < 2^22
-//     (every fp16 value within 2^11 of the box maximum is exact; the rest are
-//     rounded at 2^-22 of the maximum, below fp32 accumulation noise), split
+//     (every fp16 value within 2^11 of the box maximum is exact, every bf16
+//     one within 2^14; the rest are rounded at 2^-22 of the maximum, below
+//     fp32 accumulation noise), split
 //     into three balanced signed bytes X = d0 + 256 d1 + 65536 d2.  Each limb
 //     is one MMA column, so a box's integer sums are exact.
 //   * No byte transposes: the K slots of an A register are the four bytes of
@@ -92,11 +93,11 @@ __device__ __forceinline__ void mma_u8s8_16832(int (&d)[4], const uint32_t (&a)[
 // a power of two).
 __device__ __forceinline__ int i8_col_lo(int r, int C) { return (r * kI8Strip) / C; }
 
-template <int TOK, int BR>
+template <int TOK, int BR, typename T>
 __global__ void __launch_bounds__(kI8Threads, 1) awq_gemv_i8_kernel(
     const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_s,
     const __grid_constant__ CUtensorMap tm_z, const __grid_constant__ CUtensorMap tm_x,
-    __half* __restrict__ y, const __half* __restrict__ bias, int M, int K, int N, int group,
+    T* __restrict__ y, const T* __restrict__ bias, int M, int K, int N, int group,
     int S) {
   using L = AwqI8Layout<TOK, BR>;
   constexpr int V = L::kVar;
@@ -201,10 +202,10 @@ __global__ void __launch_bounds__(kI8Threads, 1) awq_gemv_i8_kernel(
         float v[RPL];
         if constexpr (RPL == 4) {
           const uint2 raw = ld_s64(xp);
-          const float2 f0 = __half22float2(u32_as_h2(raw.x)), f1 = __half22float2(u32_as_h2(raw.y));
+          const float2 f0 = Act<T>::unpack2(raw.x), f1 = Act<T>::unpack2(raw.y);
           v[0] = f0.x; v[1] = f0.y; v[2] = f1.x; v[3] = f1.y;
         } else {
-          const float2 f0 = __half22float2(u32_as_h2(ld_s32(xp)));
+          const float2 f0 = Act<T>::unpack2(ld_s32(xp));
           v[0] = f0.x; v[1] = f0.y;
         }
         float m = 0.f;
@@ -212,15 +213,18 @@ __global__ void __launch_bounds__(kI8Threads, 1) awq_gemv_i8_kernel(
 #pragma unroll
         for (int i = 0; i < RPL; ++i) {
           const float a = fabsf(v[i]);
-          bad |= !(a <= 65504.f);   // NaN or Inf
+          bad |= !(a <= Act<T>::kMaxFinite);   // NaN or Inf
           m = fmaxf(m, a);
         }
 #pragma unroll
         for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
         bad = __any_sync(0xffffffffu, bad);
-        // m is a normal fp32 number (fp16 values are); |X| < 2^(e+1) * 2^(21-e) = 2^22
+        // |X| < 2^(e+1) * 2^(21-e) = 2^22.  fp16 values are normal fp32 numbers
+        // (sh <= 45); bf16 ones span the fp32 range, so sh is capped at 126 to
+        // keep 2^sh and 2^-sh normal (a box whose maximum is below 2^-105 then
+        // keeps fewer than 22 bits: values that small vanish in fp32 sums anyway)
         const int e = m > 0.f ? ((__float_as_int(m) >> 23) & 255) - 127 : 0;
-        const int sh = m > 0.f ? 21 - e : 0;
+        const int sh = m > 0.f ? min(21 - e, 126) : 0;
         const float scl = __int_as_float((sh + 127) << 23);
         int sx0 = 0, sx1 = 0, sx2 = 0;
         uint8_t* xr = slot + L::kOffLimb + lane * RPL * L::kXRow + 4 * tok;
@@ -256,9 +260,9 @@ __global__ void __launch_bounds__(kI8Threads, 1) awq_gemv_i8_kernel(
       }
     }
   } else {
-    // ---------------- consumers: warp (p, T) takes the 16-word tile T of boxes
+    // ---------------- consumers: warp (p, tl) takes the 16-word tile tl of boxes
     // p, p+2, ...
-    const int p = warp >> 1, T = warp & 1;
+    const int p = warp >> 1, tl = warp & 1;
     // Rows of the 8-row step: a0/a1 and b0 use row rho, a2/a3 and b1 row rho + 2;
     // rho = 0,1,4,5 for t = 0..3 keeps each 64-bit LDS at two addresses per bank
     // under the 128-byte swizzle (chunk ^= row).
@@ -267,7 +271,7 @@ __global__ void __launch_bounds__(kI8Threads, 1) awq_gemv_i8_kernel(
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       const int r = rho + 2 * h;
-      offA[h] = static_cast<uint32_t>(r * 128 + ((((4 * T + (g >> 1)) ^ r) & 7) << 4) +
+      offA[h] = static_cast<uint32_t>(r * 128 + ((((4 * tl + (g >> 1)) ^ r) & 7) << 4) +
                                       8 * (g & 1));
     }
     // B selectors: column n = g carries entry e = 2v + (g & 1) (token e / 3, limb
@@ -283,7 +287,7 @@ __global__ void __launch_bounds__(kI8Threads, 1) awq_gemv_i8_kernel(
     const bool odd = (g & 1) != 0;
     // this lane's columns: byte t of word w holds columns 8w + ORDER[2t], 8w + ORDER[2t+1]
     const int clo = (t >> 1) | ((t & 1) << 2);
-    const int w0 = 16 * T + 2 * g;   // this lane's words w0, w0 + 1
+    const int w0 = 16 * tl + 2 * g;   // this lane's words w0, w0 + 1
     int s = p;
     uint32_t ph = 0;
     for (int b = p; b < nbox; b += kI8Streams) {
@@ -377,13 +381,13 @@ __global__ void __launch_bounds__(kI8Threads, 1) awq_gemv_i8_kernel(
   __syncthreads();
   float* red = reinterpret_cast<float*>(ring);  // [stream][token][256 columns]
   if (warp < kI8Consumers) {
-    const int p = warp >> 1, T = warp & 1;
+    const int p = warp >> 1, tl = warp & 1;
     const int clo = (t >> 1) | ((t & 1) << 2);
 #pragma unroll
     for (int m = 0; m < TOK; ++m)
 #pragma unroll
       for (int w = 0; w < 2; ++w) {
-        float* rp = red + (p * TOK + m) * kI8Strip + 8 * (16 * T + 2 * g + w) + clo;
+        float* rp = red + (p * TOK + m) * kI8Strip + 8 * (16 * tl + 2 * g + w) + clo;
         rp[0] = acc[w][m][0];
         rp[2] = acc[w][m][1];
       }
@@ -413,8 +417,8 @@ __global__ void __launch_bounds__(kI8Threads, 1) awq_gemv_i8_kernel(
         v += m == 0 ? r4.x : r4.y;
       }
       if (n < N) {
-        if (bias != nullptr) v += __half2float(bias[n]);
-        y[static_cast<int64_t>(m) * N + n] = __float2half_rn(v);
+        if (bias != nullptr) v += Act<T>::to_float(bias[n]);
+        y[static_cast<int64_t>(m) * N + n] = Act<T>::from_float(v);
       }
     }
   }

@@ -25,9 +25,10 @@ __global__ void __launch_bounds__(256) awq_unpack_kernel(int8_t* __restrict__ q_
   reinterpret_cast<uint2*>(q_out)[idx] = make_uint2(lo, hi);
 }
 
-// w_out[k, n] = fp16_rne((q[k,n] - z[k/g, n]) * s[k/g, n]).
+// w_out[k, n] = T_rne((q[k,n] - z[k/g, n]) * s[k/g, n]), T = fp16 or bf16.
+template <typename T>
 __global__ void __launch_bounds__(256) awq_dequant_kernel(
-    __half* __restrict__ w_out, const uint32_t* __restrict__ qweight,
+    T* __restrict__ w_out, const uint32_t* __restrict__ qweight,
     const uint32_t* __restrict__ qzeros, const __half* __restrict__ scales, int K, int words_n,
     int group) {
   pdl_wait();     // activations are the previous kernel's output
@@ -42,13 +43,13 @@ __global__ void __launch_bounds__(256) awq_dequant_kernel(
   const uint32_t zw = __ldg(qzeros + static_cast<int64_t>(gi) * words_n + j);
   const uint4 s = __ldg(reinterpret_cast<const uint4*>(scales + (static_cast<int64_t>(gi) * words_n + j) * 8));
   uint32_t qb[4], zb[4];
-  awq_word_to_h2_biased(w, qb);
-  awq_word_to_h2_biased(zw, zb);
+  awq_word_biased<T>(w, qb);
+  awq_word_biased<T>(zw, zb);
   uint4 out;
-  out.x = dq_h2(qb[0], zb[0], s.x);
-  out.y = dq_h2(qb[1], zb[1], s.y);
-  out.z = dq_h2(qb[2], zb[2], s.z);
-  out.w = dq_h2(qb[3], zb[3], s.w);
+  out.x = awq_dq<T>(qb[0], zb[0], awq_scale2<T>(s.x));
+  out.y = awq_dq<T>(qb[1], zb[1], awq_scale2<T>(s.y));
+  out.z = awq_dq<T>(qb[2], zb[2], awq_scale2<T>(s.z));
+  out.w = awq_dq<T>(qb[3], zb[3], awq_scale2<T>(s.w));
   reinterpret_cast<uint4*>(w_out)[idx] = out;
 }
 

@@ -37,9 +37,10 @@
 //     with the 128-byte swizzle, so its 8-row reads are conflict-free) and
 //     finds rows r, r+1 of each nibble in the two halves of one register: one
 //     lop3 per nibble makes the half2 (1024 + q_r, 1024 + q_r+1) (nibbles 0,
-//     2) or (64 + q_r, 64 + q_r+1) (nibbles 1, 3: magic 64, ulp 1/16).
-//     Subtracting the same-biased zero is exact and the multiply by the scale
-//     rounds once: bit for bit the fp16 dequant fp16_rne((q - z) * s).
+//     2) or (64 + q_r, 64 + q_r+1) (nibbles 1, 3: magic 64, ulp 1/16); with
+//     bf16 activations each nibble is shifted to bits 0-3 first (128 + q).
+//     Subtracting the same-biased zero is exact and the scale product rounds
+//     once: bit for bit the dequant T_rne((q - z) * s) of the activation type.
 //     tcgen05.st 16x128b lays each channel along one TMEM lane.  A TMEM stage
 //     holds a whole 64-row box (64 columns: group g, k-pair kp at column
 //     32g + kp) and is handed over with one arrive per warp.
@@ -99,11 +100,11 @@ struct AtLayout {
   static_assert(2 * (kSmem + 1024) <= 228 * 1024, "two CTAs per SM");
 };
 
-template <int NT>
+template <int NT, typename T>
 __global__ void __launch_bounds__(kAtThreads, 2) awq_tmem_kernel(
     const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_x,
     const __grid_constant__ CUtensorMap tm_s, const __grid_constant__ CUtensorMap tm_z,
-    __half* __restrict__ y, const __half* __restrict__ bias, int M, int K, int N, int group) {
+    T* __restrict__ y, const T* __restrict__ bias, int M, int K, int N, int group) {
   using L = AtLayout<NT>;
   constexpr int SW = L::kWStages;
   constexpr int R = L::kAStages;
@@ -197,7 +198,8 @@ __global__ void __launch_bounds__(kAtThreads, 2) awq_tmem_kernel(
   } else if (warp >= kAtMmaWarp0) {
     // ---------------------------------------------------------- MMA (warps 5-8)
     if (lane == 0) {
-      constexpr uint32_t idesc = make_idesc(0, 0, 0, 0, 128, NT);  // f16 x f16, K-major
+      constexpr uint32_t fmt = Act<T>::kUmmaFmt;  // both operands f16, or both bf16
+      constexpr uint32_t idesc = make_idesc(fmt, fmt, 0, 0, 128, NT);  // K-major
       const int p = warp - kAtMmaWarp0;
       const int jj = p & 1, st0 = 2 * (p >> 1);
       const uint32_t d = tmem + static_cast<uint32_t>(p * NT);
@@ -240,7 +242,8 @@ __global__ void __launch_bounds__(kAtThreads, 2) awq_tmem_kernel(
       if (!(ok = mbar_wait(&wfull[s], (b / SW) & 1, kErrWaitFull))) break;
       const uint8_t* wsl = wring + s * L::kW;
       const uint8_t* szb = sz + s * L::kSZ;
-      uint32_t zz[2][4], ss[2][4];
+      uint32_t zz[2][4];
+      AwqScale2 ss[2][4];
 #pragma unroll
       for (int g = 0; g < 2; ++g) {
         const int word = 16 * g + 4 * qv + (c >> 1);
@@ -249,9 +252,8 @@ __global__ void __launch_bounds__(kAtThreads, 2) awq_tmem_kernel(
         const uint32_t s4[4] = {sv.x, sv.y, sv.z, sv.w};
 #pragma unroll
         for (int n = 0; n < 4; ++n) {
-          const uint32_t z = (zw >> (4 * n)) & 0xFu;
-          zz[g][n] = ((n & 1) ? (0x5400u | (z << 4)) : (0x6400u | z)) * 0x00010001u;
-          ss[g][n] = prmt(s4[n], s4[n], sdup);  // channel 8 word + 2n + codd
+          zz[g][n] = awq_zero_pair<T>((zw >> (4 * n)) & 0xFu, n);
+          ss[g][n] = awq_scale2<T>(prmt(s4[n], s4[n], sdup));  // channel 8 word + 2n + codd
         }
       }
       // TMEM stage a was last read by the MMAs of box b - R (mempty[a] phase
@@ -271,11 +273,10 @@ __global__ void __launch_bounds__(kAtThreads, 2) awq_tmem_kernel(
           uint32_t lo[8], hi[8];
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
-            const uint32_t v = d[i], v8 = d[i] >> 8;
-            lo[2 * i] = dq_h2(lop3_and_or(v, 0x000F000Fu, 0x64006400u), zz[g][0], ss[g][0]);
-            lo[2 * i + 1] = dq_h2(lop3_and_or(v, 0x00F000F0u, 0x54005400u), zz[g][1], ss[g][1]);
-            hi[2 * i] = dq_h2(lop3_and_or(v8, 0x000F000Fu, 0x64006400u), zz[g][2], ss[g][2]);
-            hi[2 * i + 1] = dq_h2(lop3_and_or(v8, 0x00F000F0u, 0x54005400u), zz[g][3], ss[g][3]);
+            lo[2 * i] = awq_dq<T>(awq_nib_pair<T>(d[i], 0), zz[g][0], ss[g][0]);
+            lo[2 * i + 1] = awq_dq<T>(awq_nib_pair<T>(d[i], 1), zz[g][1], ss[g][1]);
+            hi[2 * i] = awq_dq<T>(awq_nib_pair<T>(d[i], 2), zz[g][2], ss[g][2]);
+            hi[2 * i + 1] = awq_dq<T>(awq_nib_pair<T>(d[i], 3), zz[g][3], ss[g][3]);
           }
           tmem_st16x128b_x4(acol + 32 * g + 16 * h, lo);
           tmem_st16x128b_x4(acol + (16u << 16) + 32 * g + 16 * h, hi);
@@ -358,11 +359,11 @@ __global__ void __launch_bounds__(kAtThreads, 2) awq_tmem_kernel(
         }
         if (n < N) {
           const float a4[4] = {acc.x, acc.y, acc.z, acc.w};
-          const float bn = bias != nullptr ? __half2float(bias[n]) : 0.f;
+          const float bn = bias != nullptr ? Act<T>::to_float(bias[n]) : 0.f;
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
             const int m = 4 * m4 + j;
-            if (m < M) y[static_cast<int64_t>(m) * N + n] = __float2half_rn(a4[j] + bn);
+            if (m < M) y[static_cast<int64_t>(m) * N + n] = Act<T>::from_float(a4[j] + bn);
           }
         }
       }

@@ -27,19 +27,6 @@
 
 namespace lmrs {
 
-template <typename T>
-struct Act;
-template <>
-struct Act<__half> {
-  static __device__ __forceinline__ float f(__half v) { return __half2float(v); }
-  static __device__ __forceinline__ __half t(float v) { return __float2half_rn(v); }
-};
-template <>
-struct Act<__nv_bfloat16> {
-  static __device__ __forceinline__ float f(__nv_bfloat16 v) { return __bfloat162float(v); }
-  static __device__ __forceinline__ __nv_bfloat16 t(float v) { return __float2bfloat16_rn(v); }
-};
-
 constexpr int kNormThreads = 256;     // smallest CTA of the row kernels
 constexpr int kRowMaxThreads = 1024;
 constexpr int kRowMaxVecs = 4;        // 8-element vectors per thread held in registers
@@ -87,7 +74,7 @@ template <typename T>
 __device__ __forceinline__ void unpack8(const uint4& v, float (&f)[8]) {
   const T* e = reinterpret_cast<const T*>(&v);
 #pragma unroll
-  for (int i = 0; i < 8; ++i) f[i] = Act<T>::f(e[i]);
+  for (int i = 0; i < 8; ++i) f[i] = Act<T>::to_float(e[i]);
 }
 
 // residual (+)= delta, out = rmsnorm(residual) * w, one CTA per row.  Thread t
@@ -117,7 +104,7 @@ __global__ void __launch_bounds__(kRowMaxThreads) rmsnorm_kernel(
         uint4 sv;
         T* se = reinterpret_cast<T*>(&sv);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) se[i] = Act<T>::t(Act<T>::f(e[i]) + Act<T>::f(de[i]));
+        for (int i = 0; i < 8; ++i) se[i] = Act<T>::from_float(Act<T>::to_float(e[i]) + Act<T>::to_float(de[i]));
         *reinterpret_cast<uint4*>(xr + c) = sv;  // the updated residual stream
         xv = sv;
       }
@@ -138,8 +125,8 @@ __global__ void __launch_bounds__(kRowMaxThreads) rmsnorm_kernel(
       T* oe = reinterpret_cast<T*>(&pk);
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        oe[i] = Act<T>::t(x[v][i] * inv * wf[i]);
-        x[v][i] = Act<T>::f(oe[i]);
+        oe[i] = Act<T>::from_float(x[v][i] * inv * wf[i]);
+        x[v][i] = Act<T>::to_float(oe[i]);
         amax = fmaxf(amax, fabsf(x[v][i]));
       }
       if (!FP8) *reinterpret_cast<uint4*>(out + static_cast<int64_t>(row) * H + c) = pk;
@@ -182,8 +169,8 @@ __global__ void __launch_bounds__(kRowMaxThreads) silu_mul_kernel(
       T* oe = reinterpret_cast<T*>(&pk);
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        oe[i] = Act<T>::t((g[i] / (1.0f + expf(-g[i]))) * u[i]);
-        y[v][i] = Act<T>::f(oe[i]);
+        oe[i] = Act<T>::from_float((g[i] / (1.0f + expf(-g[i]))) * u[i]);
+        y[v][i] = Act<T>::to_float(oe[i]);
         amax = fmaxf(amax, fabsf(y[v][i]));
       }
       if (!FP8) *reinterpret_cast<uint4*>(out + static_cast<int64_t>(row) * I + c) = pk;
@@ -233,7 +220,7 @@ __global__ void __launch_bounds__(kSiluClusterThreads) silu_mul_fp8_cluster_kern
       unpack8<T>(*reinterpret_cast<const uint4*>(gr + I + c), u);
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        y[v][i] = Act<T>::f(Act<T>::t((g[i] / (1.0f + expf(-g[i]))) * u[i]));
+        y[v][i] = Act<T>::to_float(Act<T>::from_float((g[i] / (1.0f + expf(-g[i]))) * u[i]));
         amax = fmaxf(amax, fabsf(y[v][i]));
       }
     }
@@ -288,8 +275,8 @@ __global__ void __launch_bounds__(128) rope_kv_vec_kernel(
     T* r1 = reinterpret_cast<T*>(&p1);
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      r0[i] = Act<T>::t(x0[i] * cs[i] - x1[i] * sn[i]);  // rotate-half: first half
-      r1[i] = Act<T>::t(x1[i] * cs[i] + x0[i] * sn[i]);  // second half
+      r0[i] = Act<T>::from_float(x0[i] * cs[i] - x1[i] * sn[i]);  // rotate-half: first half
+      r1[i] = Act<T>::from_float(x1[i] * cs[i] + x0[i] * sn[i]);  // second half
     }
     T* dst;
     if (h < hq) {
@@ -334,10 +321,10 @@ __global__ void __launch_bounds__(256) rope_kv_kernel(
     if (e < pairs) {
       const int h = e / half, c = e - h * half;
       const T* src = row + h * d;
-      const float x0 = Act<T>::f(src[c]), x1 = Act<T>::f(src[c + half]);
-      const float cs = Act<T>::f(cosv[c]), sn = Act<T>::f(sinv[c]);
-      const T r0 = Act<T>::t(x0 * cs - x1 * sn);   // rotate-half: first half
-      const T r1 = Act<T>::t(x1 * cs + x0 * sn);   // second half
+      const float x0 = Act<T>::to_float(src[c]), x1 = Act<T>::to_float(src[c + half]);
+      const float cs = Act<T>::to_float(cosv[c]), sn = Act<T>::to_float(sinv[c]);
+      const T r0 = Act<T>::from_float(x0 * cs - x1 * sn);   // rotate-half: first half
+      const T r1 = Act<T>::from_float(x1 * cs + x0 * sn);   // second half
       if (h < hq) {
         T* dst = q_out + (static_cast<int64_t>(b) * hq + h) * d;
         dst[c] = r0;
@@ -653,7 +640,7 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(
       T* dst = out + (static_cast<int64_t>(seq) * num_heads + h) * kAttnD + d0;
       const float inv = L > 0.f ? 1.f / L : 0.f;
 #pragma unroll
-      for (int i = 0; i < 16; ++i) dst[i] = Act<T>::t(acc[i] * inv);
+      for (int i = 0; i < 16; ++i) dst[i] = Act<T>::from_float(acc[i] * inv);
     } else {
       // partial: O (unnormalised, fp32), then m, l
       float* pw = part + r * kAttnPartStride;
@@ -696,7 +683,7 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(
       T* dst = out + (static_cast<int64_t>(seq) * num_heads + qhead(r)) * kAttnD + d0;
       const float inv = L > 0.f ? 1.f / L : 0.f;
 #pragma unroll
-      for (int i = 0; i < 16; ++i) dst[i] = Act<T>::t(acc[i] * inv);
+      for (int i = 0; i < 16; ++i) dst[i] = Act<T>::from_float(acc[i] * inv);
     }
     cluster_sync_all();   // no CTA leaves while a peer may read its partial
   }

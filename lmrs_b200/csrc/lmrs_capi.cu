@@ -133,6 +133,14 @@ int ensure_smem(K kernel, int bytes, std::atomic<int>* done, int dev) {
   return LMRS_OK;
 }
 
+// The same with the per-device record kept per kernel instantiation (Kern is
+// the kernel itself, so every template instance has its own).
+template <auto Kern>
+int ensure_smem_of(int bytes, int dev) {
+  static std::atomic<int> done[kMaxDevices];
+  return ensure_smem(Kern, bytes, done, dev);
+}
+
 // ---- TMA descriptors
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
                                    const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
@@ -269,12 +277,14 @@ int launch_cluster(Kern kernel, int grid_x, int cluster, int threads, int smem,
   return launch_ex(kernel, grid_x, cluster, threads, smem, stream, args...);
 }
 
-std::atomic<int> g_smem_awq_gemm[kMaxDevices];
 std::atomic<int> g_smem_f8_gemm[kMaxDevices];
-std::atomic<int> g_smem_awq_gemv[4][kMaxDevices];
 std::atomic<int> g_smem_f8_gemv[3][kMaxDevices];
 
 // ------------------------------------------------------------------ AWQ
+// Every AWQ launcher is a template on the activation type T (__half for
+// LMRS_DTYPE_F16, __nv_bfloat16 for LMRS_DTYPE_BF16): x, y and bias are T, the
+// scales stay fp16, and the kernels dequantise to T (lmrs_ptx.cuh, Act<T>).
+
 // Cluster size for a TMA-fed GEMV: split K over C CTAs so that every CTA of
 // the grid is resident at once (~4 per SM), C <= 8 and C <= K units.
 int gemv_cluster(int strips, int units, int forced) {
@@ -292,41 +302,35 @@ int pow2_floor(int v) {
   return r;
 }
 
-template <int MT, int BR>
+template <int MT, int BR, typename T>
 int awq_gemv_launch_t(const CUtensorMap& tq, const CUtensorMap& tx, const CUtensorMap& ts,
-                      const CUtensorMap& tz, __half* y, const __half* bias, int M, int K, int N,
-                      int group, cudaStream_t stream, int dev, int strips, int C, int S,
-                      std::atomic<int>* done) {
+                      const CUtensorMap& tz, T* y, const T* bias, int M, int K, int N, int group,
+                      cudaStream_t stream, int dev, int strips, int C, int S) {
   using L = lmrs::AwqGemvLayout<MT, BR>;
   const int smem = L::smem_bytes(S);
   int rc;
-  if ((rc = ensure_smem(lmrs::awq_gemv_kernel<MT, BR>, smem, done, dev))) return rc;
-  rc = launch_ex(lmrs::awq_gemv_kernel<MT, BR>, strips * C, C, lmrs::kAwqGemvThreads, smem, stream,
-                 tq, tx, ts, tz, y, bias, M, K, N, group, S);
+  if ((rc = ensure_smem_of<lmrs::awq_gemv_kernel<MT, BR, T>>(smem, dev))) return rc;
+  rc = launch_ex(lmrs::awq_gemv_kernel<MT, BR, T>, strips * C, C, lmrs::kAwqGemvThreads, smem,
+                 stream, tq, tx, ts, tz, y, bias, M, K, N, group, S);
   return rc ? rc : after_launch();
 }
 
-std::atomic<int> g_smem_awq_gemv4[2][kMaxDevices];
-
-template <int BR>
+template <int BR, typename T>
 int awq_gemv4_launch_t(const CUtensorMap& tq, const CUtensorMap& tx, const CUtensorMap& ts,
-                       const CUtensorMap& tz, __half* y, const __half* bias, int M, int K, int N,
-                       int group, cudaStream_t stream, int dev, int strips, int C, int S,
-                       std::atomic<int>* done) {
+                       const CUtensorMap& tz, T* y, const T* bias, int M, int K, int N, int group,
+                       cudaStream_t stream, int dev, int strips, int C, int S) {
   const int smem = lmrs::AwqGemv4Layout<BR>::smem_bytes(S);
   int rc;
-  if ((rc = ensure_smem(lmrs::awq_gemv4_kernel<BR>, smem, done, dev))) return rc;
-  rc = launch_ex(lmrs::awq_gemv4_kernel<BR>, strips * C, C, lmrs::kAwqGemv4Threads, smem, stream,
-                 tq, tx, ts, tz, y, bias, M, K, N, group, S);
+  if ((rc = ensure_smem_of<lmrs::awq_gemv4_kernel<BR, T>>(smem, dev))) return rc;
+  rc = launch_ex(lmrs::awq_gemv4_kernel<BR, T>, strips * C, C, lmrs::kAwqGemv4Threads, smem,
+                 stream, tq, tx, ts, tz, y, bias, M, K, N, group, S);
   return rc ? rc : after_launch();
 }
 
-std::atomic<int> g_smem_awq_tmem[3][kMaxDevices];
-
-template <int NT>
-int awq_tmem_launch_t(__half* y, const __half* x, const int32_t* qw, const int32_t* qz,
-                      const __half* sc, const __half* bias, int M, int K, int N, int group,
-                      cudaStream_t stream, int dev, std::atomic<int>* done) {
+template <int NT, typename T>
+int awq_tmem_launch_t(T* y, const T* x, const int32_t* qw, const int32_t* qz, const __half* sc,
+                      const T* bias, int M, int K, int N, int group, cudaStream_t stream,
+                      int dev) {
   using L = lmrs::AtLayout<NT>;
   const int strips = (N + lmrs::kAtCols - 1) / lmrs::kAtCols;
   const int nb_all = K / lmrs::kAtRows;
@@ -340,7 +344,7 @@ int awq_tmem_launch_t(__half* y, const __half* x, const int32_t* qw, const int32
   if ((rc = make_tmap(&tq, CU_TENSOR_MAP_DATA_TYPE_INT32, qw, N / 8, K, uint64_t(N / 8) * 4,
                       lmrs::kAtWords, lmrs::kAtRows, CU_TENSOR_MAP_SWIZZLE_128B)))
     return rc;
-  if ((rc = make_tmap(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, x, K, M, uint64_t(K) * 2, 64, NT,
+  if ((rc = make_tmap(&tx, lmrs::Act<T>::kTma, x, K, M, uint64_t(K) * 2, 64, NT,
                       CU_TENSOR_MAP_SWIZZLE_128B)))
     return rc;
   if ((rc = make_tmap(&ts, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, sc, N, K / group, uint64_t(N) * 2,
@@ -350,9 +354,9 @@ int awq_tmem_launch_t(__half* y, const __half* x, const int32_t* qw, const int32
                       uint64_t(N / 8) * 4, lmrs::kAtWords, 1, CU_TENSOR_MAP_SWIZZLE_NONE)))
     return rc;
   constexpr int smem = L::kSmem;
-  if ((rc = ensure_smem(lmrs::awq_tmem_kernel<NT>, smem, done, dev))) return rc;
-  rc = launch_ex(lmrs::awq_tmem_kernel<NT>, strips * C, C, lmrs::kAtThreads, smem, stream, tq, tx,
-                 ts, tz, y, bias, M, K, N, group);
+  if ((rc = ensure_smem_of<lmrs::awq_tmem_kernel<NT, T>>(smem, dev))) return rc;
+  rc = launch_ex(lmrs::awq_tmem_kernel<NT, T>, strips * C, C, lmrs::kAtThreads, smem, stream, tq,
+                 tx, ts, tz, y, bias, M, K, N, group);
   return rc ? rc : after_launch();
 }
 
@@ -384,23 +388,17 @@ bool awq_use_swap(int M, int K, int N, int sms) {
   return M <= g_tune.awq_swap_max_m && (N + lmrs::kAgtCh - 1) / lmrs::kAgtCh < sms;
 }
 
-int awq_tmem_launch(__half* y, const __half* x, const int32_t* qw, const int32_t* qz,
-                    const __half* sc, const __half* bias, int M, int K, int N, int group,
-                    cudaStream_t stream, int dev) {
-  if (M <= 16)
-    return awq_tmem_launch_t<16>(y, x, qw, qz, sc, bias, M, K, N, group, stream, dev,
-                                 g_smem_awq_tmem[0]);
-  return awq_tmem_launch_t<32>(y, x, qw, qz, sc, bias, M, K, N, group, stream, dev,
-                               g_smem_awq_tmem[1]);
+template <typename T>
+int awq_tmem_launch(T* y, const T* x, const int32_t* qw, const int32_t* qz, const __half* sc,
+                    const T* bias, int M, int K, int N, int group, cudaStream_t stream, int dev) {
+  if (M <= 16) return awq_tmem_launch_t<16, T>(y, x, qw, qz, sc, bias, M, K, N, group, stream, dev);
+  return awq_tmem_launch_t<32, T>(y, x, qw, qz, sc, bias, M, K, N, group, stream, dev);
 }
 
-std::atomic<int> g_smem_awq_i8[4][kMaxDevices];
-
-template <int TOK, int BR>
+template <int TOK, int BR, typename T>
 int awq_i8_launch_t(const CUtensorMap& tq, const CUtensorMap& ts, const CUtensorMap& tz,
-                    const __half* x, __half* y, const __half* bias, int M, int K, int N, int group,
-                    cudaStream_t stream, int dev, int strips, int C, int S, int nbmax,
-                    std::atomic<int>* done) {
+                    const T* x, T* y, const T* bias, int M, int K, int N, int group,
+                    cudaStream_t stream, int dev, int strips, int C, int S, int nbmax) {
   using L = lmrs::AwqI8Layout<TOK, BR>;
   // Slots: as many as asked (up to the CTA's box count) while the grid takes at
   // most 80 % of the CTAs that fit per SM at that size, so that the next kernel
@@ -418,20 +416,20 @@ int awq_i8_launch_t(const CUtensorMap& tq, const CUtensorMap& ts, const CUtensor
   if (smem > 227 * 1024) return -1;
   CUtensorMap tx;
   int rc;
-  if ((rc = make_tmap(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, x, K, M, uint64_t(K) * 2, BR, TOK,
+  if ((rc = make_tmap(&tx, lmrs::Act<T>::kTma, x, K, M, uint64_t(K) * 2, BR, TOK,
                       CU_TENSOR_MAP_SWIZZLE_NONE)))
     return rc;
-  if ((rc = ensure_smem(lmrs::awq_gemv_i8_kernel<TOK, BR>, smem, done, dev))) return rc;
-  rc = launch_ex(lmrs::awq_gemv_i8_kernel<TOK, BR>, ctas, C, lmrs::kI8Threads, smem, stream, tq,
+  if ((rc = ensure_smem_of<lmrs::awq_gemv_i8_kernel<TOK, BR, T>>(smem, dev))) return rc;
+  rc = launch_ex(lmrs::awq_gemv_i8_kernel<TOK, BR, T>, ctas, C, lmrs::kI8Threads, smem, stream, tq,
                  ts, tz, tx, y, bias, M, K, N, group, S);
   return rc ? rc : after_launch();
 }
 
 // 1-2 tokens with the packed bytes as integer MMA operands.  Returns -1 when
-// the shape does not fit the kernel (the caller then takes the fp16 GEMV).
-int awq_i8_launch(__half* y, const __half* x, const int32_t* qw, const uint32_t* qz,
-                  const __half* sc, const __half* bias, int M, int K, int N, int group,
-                  cudaStream_t stream, int dev) {
+// the shape does not fit the kernel (the caller then takes the 16-bit GEMV).
+template <typename T>
+int awq_i8_launch(T* y, const T* x, const int32_t* qw, const uint32_t* qz, const __half* sc,
+                  const T* bias, int M, int K, int N, int group, cudaStream_t stream, int dev) {
   const int BR = group % 128 == 0 && g_tune.awq_i8_box_rows != 64 ? 128 : 64;
   if (M < 1 || M > 2 || K % BR) return -1;
   const int strips = (N + lmrs::kI8Strip - 1) / lmrs::kI8Strip;
@@ -455,23 +453,23 @@ int awq_i8_launch(__half* y, const __half* x, const int32_t* qw, const uint32_t*
                       uint64_t(N / 8) * 4, lmrs::kI8Words, 1, CU_TENSOR_MAP_SWIZZLE_NONE)))
     return rc;
   if (M == 1 && BR == 128)
-    return awq_i8_launch_t<1, 128>(tq, ts, tz, x, y, bias, M, K, N, group, stream, dev, strips, C,
-                                   S, nbmax, g_smem_awq_i8[0]);
+    return awq_i8_launch_t<1, 128, T>(tq, ts, tz, x, y, bias, M, K, N, group, stream, dev, strips,
+                                      C, S, nbmax);
   if (M == 1)
-    return awq_i8_launch_t<1, 64>(tq, ts, tz, x, y, bias, M, K, N, group, stream, dev, strips, C,
-                                  S, nbmax, g_smem_awq_i8[1]);
+    return awq_i8_launch_t<1, 64, T>(tq, ts, tz, x, y, bias, M, K, N, group, stream, dev, strips,
+                                     C, S, nbmax);
   if (BR == 128)
-    return awq_i8_launch_t<2, 128>(tq, ts, tz, x, y, bias, M, K, N, group, stream, dev, strips, C,
-                                   S, nbmax, g_smem_awq_i8[2]);
-  return awq_i8_launch_t<2, 64>(tq, ts, tz, x, y, bias, M, K, N, group, stream, dev, strips, C, S,
-                                nbmax, g_smem_awq_i8[3]);
+    return awq_i8_launch_t<2, 128, T>(tq, ts, tz, x, y, bias, M, K, N, group, stream, dev, strips,
+                                      C, S, nbmax);
+  return awq_i8_launch_t<2, 64, T>(tq, ts, tz, x, y, bias, M, K, N, group, stream, dev, strips, C,
+                                   S, nbmax);
 }
 
-int awq_gemv_launch(__half* y, const __half* x, const int32_t* qw, const uint32_t* qz,
-                    const __half* sc, const __half* bias, int M, int K, int N, int group,
-                    cudaStream_t stream, int dev) {
+template <typename T>
+int awq_gemv_launch(T* y, const T* x, const int32_t* qw, const uint32_t* qz, const __half* sc,
+                    const T* bias, int M, int K, int N, int group, cudaStream_t stream, int dev) {
   if (M <= g_tune.awq_i8_max_m) {
-    const int rc = awq_i8_launch(y, x, qw, qz, sc, bias, M, K, N, group, stream, dev);
+    const int rc = awq_i8_launch<T>(y, x, qw, qz, sc, bias, M, K, N, group, stream, dev);
     if (rc >= 0) return rc;
   }
   const int BR = (group % 128 == 0 && g_tune.gemv_box_rows != 64) ? 128 : 64;
@@ -495,7 +493,7 @@ int awq_gemv_launch(__half* y, const __half* x, const int32_t* qw, const uint32_
   if ((rc = make_tmap(&tq, CU_TENSOR_MAP_DATA_TYPE_INT32, qw, N / 8, K, uint64_t(N / 8) * 4,
                       lmrs::kAwqGemvWords, BR, CU_TENSOR_MAP_SWIZZLE_64B)))
     return rc;
-  if ((rc = make_tmap(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, x, K, M, uint64_t(K) * 2, 64, 8 * MT,
+  if ((rc = make_tmap(&tx, lmrs::Act<T>::kTma, x, K, M, uint64_t(K) * 2, 64, 8 * MT,
                       CU_TENSOR_MAP_SWIZZLE_128B)))
     return rc;
   if ((rc = make_tmap(&ts, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, sc, N, K / group, uint64_t(N) * 2,
@@ -508,34 +506,32 @@ int awq_gemv_launch(__half* y, const __half* x, const int32_t* qw, const uint32_
     int S4 = g_tune.awq_gemv4_slots >= 16 ? 16 : (g_tune.awq_gemv4_slots >= 8 ? 8 : 4);
     while (S4 > 4 && per_cta <= S4 / 2) S4 /= 2;
     if (BR == 128)
-      return awq_gemv4_launch_t<128>(tq, tx, ts, tz, y, bias, M, K, N, group, stream, dev, strips,
-                                     C, S4, g_smem_awq_gemv4[0]);
-    return awq_gemv4_launch_t<64>(tq, tx, ts, tz, y, bias, M, K, N, group, stream, dev, strips, C,
-                                  S4, g_smem_awq_gemv4[1]);
+      return awq_gemv4_launch_t<128, T>(tq, tx, ts, tz, y, bias, M, K, N, group, stream, dev,
+                                        strips, C, S4);
+    return awq_gemv4_launch_t<64, T>(tq, tx, ts, tz, y, bias, M, K, N, group, stream, dev, strips,
+                                     C, S4);
   }
   if (MT == 1 && BR == 128)
-    return awq_gemv_launch_t<1, 128>(tq, tx, ts, tz, y, bias, M, K, N, group, stream, dev, strips,
-                                     C, S, g_smem_awq_gemv[0]);
+    return awq_gemv_launch_t<1, 128, T>(tq, tx, ts, tz, y, bias, M, K, N, group, stream, dev,
+                                        strips, C, S);
   if (MT == 2 && BR == 128)
-    return awq_gemv_launch_t<2, 128>(tq, tx, ts, tz, y, bias, M, K, N, group, stream, dev, strips,
-                                     C, S, g_smem_awq_gemv[1]);
+    return awq_gemv_launch_t<2, 128, T>(tq, tx, ts, tz, y, bias, M, K, N, group, stream, dev,
+                                        strips, C, S);
   if (MT == 1)
-    return awq_gemv_launch_t<1, 64>(tq, tx, ts, tz, y, bias, M, K, N, group, stream, dev, strips,
-                                    C, S, g_smem_awq_gemv[2]);
-  return awq_gemv_launch_t<2, 64>(tq, tx, ts, tz, y, bias, M, K, N, group, stream, dev, strips, C,
-                                  S, g_smem_awq_gemv[3]);
+    return awq_gemv_launch_t<1, 64, T>(tq, tx, ts, tz, y, bias, M, K, N, group, stream, dev,
+                                       strips, C, S);
+  return awq_gemv_launch_t<2, 64, T>(tq, tx, ts, tz, y, bias, M, K, N, group, stream, dev, strips,
+                                     C, S);
 }
 
-std::atomic<int> g_smem_awq_swap[4][kMaxDevices];
-
-template <int NT>
-int awq_swap_launch_nt(__half* y, const __half* x, const int32_t* qw, const int32_t* qz,
-                       const __half* sc, const __half* bias, int M, int K, int N, int group,
-                       cudaStream_t stream, int dev, int slot) {
+template <int NT, typename T>
+int awq_swap_launch_nt(T* y, const T* x, const int32_t* qw, const int32_t* qz, const __half* sc,
+                       const T* bias, int M, int K, int N, int group, cudaStream_t stream,
+                       int dev) {
   CUtensorMap tx, tq, ts, tz;
   int rc;
-  if ((rc = make_tmap(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, x, K, M, uint64_t(K) * 2, lmrs::kSwBK,
-                      NT, CU_TENSOR_MAP_SWIZZLE_128B)))
+  if ((rc = make_tmap(&tx, lmrs::Act<T>::kTma, x, K, M, uint64_t(K) * 2, lmrs::kSwBK, NT,
+                      CU_TENSOR_MAP_SWIZZLE_128B)))
     return rc;
   if ((rc = make_tmap(&tq, CU_TENSOR_MAP_DATA_TYPE_INT32, qw, N / 8, K, uint64_t(N / 8) * 4,
                       lmrs::kSwBN / 8, lmrs::kSwBK, CU_TENSOR_MAP_SWIZZLE_NONE)))
@@ -547,7 +543,7 @@ int awq_swap_launch_nt(__half* y, const __half* x, const int32_t* qw, const int3
                       uint64_t(N / 8) * 4, lmrs::kSwBN / 8, 1, CU_TENSOR_MAP_SWIZZLE_NONE)))
     return rc;
   constexpr int smem = lmrs::sw_smem_bytes(NT);
-  if ((rc = ensure_smem(lmrs::awq_gemm_swap_kernel<NT>, smem, g_smem_awq_swap[slot], dev))) return rc;
+  if ((rc = ensure_smem_of<lmrs::awq_gemm_swap_kernel<NT, T>>(smem, dev))) return rc;
   const int tiles = (N + lmrs::kSwBN - 1) / lmrs::kSwBN;
   const int KB = K / lmrs::kSwBK;
   // CTAs resident per SM at this tile width (launch bounds allow 2; the
@@ -556,66 +552,60 @@ int awq_swap_launch_nt(__half* y, const __half* x, const int32_t* qw, const int3
   int C = g_tune.awq_swap_cluster > 0 ? g_tune.awq_swap_cluster : (per_sm * sm_count(dev)) / tiles;
   C = clampi(C, 1, 8);
   if (C > KB) C = KB;
-  rc = launch_cluster(lmrs::awq_gemm_swap_kernel<NT>, tiles * C, C, lmrs::kSwThreads, smem, stream,
-                      tx, tq, ts, tz, y, bias, M, K, N, group);
+  rc = launch_cluster(lmrs::awq_gemm_swap_kernel<NT, T>, tiles * C, C, lmrs::kSwThreads, smem,
+                      stream, tx, tq, ts, tz, y, bias, M, K, N, group);
   return rc ? rc : after_launch();
 }
 
-int awq_swap_launch(__half* y, const __half* x, const int32_t* qw, const int32_t* qz,
-                    const __half* sc, const __half* bias, int M, int K, int N, int group,
-                    cudaStream_t stream, int dev) {
-  if (M <= 16) return awq_swap_launch_nt<16>(y, x, qw, qz, sc, bias, M, K, N, group, stream, dev, 0);
-  if (M <= 32) return awq_swap_launch_nt<32>(y, x, qw, qz, sc, bias, M, K, N, group, stream, dev, 1);
-  if (M <= 64) return awq_swap_launch_nt<64>(y, x, qw, qz, sc, bias, M, K, N, group, stream, dev, 2);
-  return awq_swap_launch_nt<128>(y, x, qw, qz, sc, bias, M, K, N, group, stream, dev, 3);
+template <typename T>
+int awq_swap_launch(T* y, const T* x, const int32_t* qw, const int32_t* qz, const __half* sc,
+                    const T* bias, int M, int K, int N, int group, cudaStream_t stream, int dev) {
+  if (M <= 16) return awq_swap_launch_nt<16, T>(y, x, qw, qz, sc, bias, M, K, N, group, stream, dev);
+  if (M <= 32) return awq_swap_launch_nt<32, T>(y, x, qw, qz, sc, bias, M, K, N, group, stream, dev);
+  if (M <= 64) return awq_swap_launch_nt<64, T>(y, x, qw, qz, sc, bias, M, K, N, group, stream, dev);
+  return awq_swap_launch_nt<128, T>(y, x, qw, qz, sc, bias, M, K, N, group, stream, dev);
 }
 
-std::atomic<int> g_smem_awq_gemm2[kMaxDevices];
-
-std::atomic<int> g_smem_awq_gemm_tmem[3][kMaxDevices];
-
-template <int BT>
-int awq_gemm_tmem_launch_t(__half* y, const __half* x, const int32_t* qw, const int32_t* qz,
-                           const __half* sc, const __half* bias, int M, int K, int N, int group,
-                           cudaStream_t stream, int dev, std::atomic<int>* done) {
+template <int BT, typename T>
+int awq_gemm_tmem_launch_t(T* y, const T* x, const int32_t* qw, const int32_t* qz,
+                           const __half* sc, const T* bias, int M, int K, int N, int group,
+                           cudaStream_t stream, int dev) {
   using L = lmrs::AgtLayout<BT>;
   CUtensorMap tx, tq;
   int rc;
-  if ((rc = make_tmap(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, x, K, M, uint64_t(K) * 2, 64, BT,
+  if ((rc = make_tmap(&tx, lmrs::Act<T>::kTma, x, K, M, uint64_t(K) * 2, 64, BT,
                       CU_TENSOR_MAP_SWIZZLE_128B)))
     return rc;
   if ((rc = make_tmap(&tq, CU_TENSOR_MAP_DATA_TYPE_INT32, qw, N / 8, K, uint64_t(N / 8) * 4,
                       lmrs::kAgtWords, lmrs::kAgtBK, CU_TENSOR_MAP_SWIZZLE_64B)))
     return rc;
-  if ((rc = ensure_smem(lmrs::awq_gemm_tmem_kernel<BT>, L::kSmem, done, dev))) return rc;
+  if ((rc = ensure_smem_of<lmrs::awq_gemm_tmem_kernel<BT, T>>(L::kSmem, dev))) return rc;
   const int tiles = ((N + lmrs::kAgtCh - 1) / lmrs::kAgtCh) * ((M + BT - 1) / BT);
   const int grid = tiles < sm_count(dev) ? tiles : sm_count(dev);
-  rc = launch_ex(lmrs::awq_gemm_tmem_kernel<BT>, grid, 0, lmrs::kAgtThreads, L::kSmem, stream, tx,
-                 tq, sc, reinterpret_cast<const uint32_t*>(qz), y, bias, M, K, N, group);
+  rc = launch_ex(lmrs::awq_gemm_tmem_kernel<BT, T>, grid, 0, lmrs::kAgtThreads, L::kSmem, stream,
+                 tx, tq, sc, reinterpret_cast<const uint32_t*>(qz), y, bias, M, K, N, group);
   return rc ? rc : after_launch();
 }
 
-int awq_gemm_tmem_launch(__half* y, const __half* x, const int32_t* qw, const int32_t* qz,
-                         const __half* sc, const __half* bias, int M, int K, int N, int group,
-                         cudaStream_t stream, int dev) {
+template <typename T>
+int awq_gemm_tmem_launch(T* y, const T* x, const int32_t* qw, const int32_t* qz, const __half* sc,
+                         const T* bias, int M, int K, int N, int group, cudaStream_t stream,
+                         int dev) {
   const int f = g_tune.awq_gemm_tmem_bt;
   const int bt = (f == 128 || f == 192) ? f : 256;
   if (bt == 128)
-    return awq_gemm_tmem_launch_t<128>(y, x, qw, qz, sc, bias, M, K, N, group, stream, dev,
-                                       g_smem_awq_gemm_tmem[0]);
+    return awq_gemm_tmem_launch_t<128, T>(y, x, qw, qz, sc, bias, M, K, N, group, stream, dev);
   if (bt == 192)
-    return awq_gemm_tmem_launch_t<192>(y, x, qw, qz, sc, bias, M, K, N, group, stream, dev,
-                                       g_smem_awq_gemm_tmem[1]);
-  return awq_gemm_tmem_launch_t<256>(y, x, qw, qz, sc, bias, M, K, N, group, stream, dev,
-                                     g_smem_awq_gemm_tmem[2]);
+    return awq_gemm_tmem_launch_t<192, T>(y, x, qw, qz, sc, bias, M, K, N, group, stream, dev);
+  return awq_gemm_tmem_launch_t<256, T>(y, x, qw, qz, sc, bias, M, K, N, group, stream, dev);
 }
 
-int awq_gemm2_launch(__half* y, const __half* x, const int32_t* qw, const int32_t* qz,
-                     const __half* sc, const __half* bias, int M, int K, int N, int group,
-                     cudaStream_t stream, int dev) {
+template <typename T>
+int awq_gemm2_launch(T* y, const T* x, const int32_t* qw, const int32_t* qz, const __half* sc,
+                     const T* bias, int M, int K, int N, int group, cudaStream_t stream, int dev) {
   CUtensorMap tx, tq, ts, tz;
   int rc;
-  if ((rc = make_tmap(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, x, K, M, uint64_t(K) * 2, 64, 128,
+  if ((rc = make_tmap(&tx, lmrs::Act<T>::kTma, x, K, M, uint64_t(K) * 2, 64, 128,
                       CU_TENSOR_MAP_SWIZZLE_128B)))
     return rc;
   if ((rc = make_tmap(&tq, CU_TENSOR_MAP_DATA_TYPE_INT32, qw, N / 8, K, uint64_t(N / 8) * 4, 16,
@@ -627,11 +617,10 @@ int awq_gemm2_launch(__half* y, const __half* x, const int32_t* qw, const int32_
   if ((rc = make_tmap(&tz, CU_TENSOR_MAP_DATA_TYPE_INT32, qz, N / 8, K / group,
                       uint64_t(N / 8) * 4, 16, 1, CU_TENSOR_MAP_SWIZZLE_NONE)))
     return rc;
-  if ((rc = ensure_smem(lmrs::awq_gemm_tc2_kernel, lmrs::kP2SmemBytes, g_smem_awq_gemm2, dev)))
-    return rc;
+  if ((rc = ensure_smem_of<lmrs::awq_gemm_tc2_kernel<T>>(lmrs::kP2SmemBytes, dev))) return rc;
   const int tiles = ((N + lmrs::kP2BN - 1) / lmrs::kP2BN) * ((M + lmrs::kP2BM - 1) / lmrs::kP2BM);
   const int pairs = tiles < sm_count(dev) / 2 ? tiles : sm_count(dev) / 2;
-  rc = launch_cluster(lmrs::awq_gemm_tc2_kernel, 2 * pairs, 2, lmrs::kP2Threads,
+  rc = launch_cluster(lmrs::awq_gemm_tc2_kernel<T>, 2 * pairs, 2, lmrs::kP2Threads,
                       lmrs::kP2SmemBytes, stream, tx, tq, ts, tz, y, bias, M, K, N, group);
   return rc ? rc : after_launch();
 }
@@ -656,15 +645,13 @@ int pick_bn(int M, int N, int sms) {
   return best;
 }
 
-std::atomic<int> g_smem_awq_gemm224[kMaxDevices];
-
-template <int BN>
-int awq_gemm_launch_bn(__half* y, const __half* x, const int32_t* qw, const int32_t* qz,
-                       const __half* sc, const __half* bias, int M, int K, int N, int group,
-                       cudaStream_t stream, int dev, std::atomic<int>* smem_done) {
+template <int BN, typename T>
+int awq_gemm_launch_bn(T* y, const T* x, const int32_t* qw, const int32_t* qz, const __half* sc,
+                       const T* bias, int M, int K, int N, int group, cudaStream_t stream,
+                       int dev) {
   CUtensorMap tx, tq, ts, tz;
   int rc;
-  if ((rc = make_tmap(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, x, K, M, uint64_t(K) * 2, 64, 128,
+  if ((rc = make_tmap(&tx, lmrs::Act<T>::kTma, x, K, M, uint64_t(K) * 2, 64, 128,
                       CU_TENSOR_MAP_SWIZZLE_128B)))
     return rc;
   if ((rc = make_tmap(&tq, CU_TENSOR_MAP_DATA_TYPE_INT32, qw, N / 8, K, uint64_t(N / 8) * 4,
@@ -677,22 +664,41 @@ int awq_gemm_launch_bn(__half* y, const __half* x, const int32_t* qw, const int3
                       uint64_t(N / 8) * 4, BN / 8, 1, CU_TENSOR_MAP_SWIZZLE_NONE)))
     return rc;
   constexpr int smem = lmrs::AwqTile<BN>::kSmem;
-  if ((rc = ensure_smem(lmrs::awq_gemm_tc_kernel<BN>, smem, smem_done, dev))) return rc;
+  if ((rc = ensure_smem_of<lmrs::awq_gemm_tc_kernel<BN, T>>(smem, dev))) return rc;
   const int tiles = ((N + BN - 1) / BN) * ((M + lmrs::kTcBM - 1) / lmrs::kTcBM);
   const int grid = tiles < sm_count(dev) ? tiles : sm_count(dev);
-  rc = launch_ex(lmrs::awq_gemm_tc_kernel<BN>, grid, 0, lmrs::kAwqGemmThreads, smem, stream, tx, tq,
-                 ts, tz, y, bias, M, K, N, group);
+  rc = launch_ex(lmrs::awq_gemm_tc_kernel<BN, T>, grid, 0, lmrs::kAwqGemmThreads, smem, stream,
+                 tx, tq, ts, tz, y, bias, M, K, N, group);
   return rc ? rc : after_launch();
 }
 
-int awq_gemm_launch(__half* y, const __half* x, const int32_t* qw, const int32_t* qz,
-                    const __half* sc, const __half* bias, int M, int K, int N, int group,
-                    cudaStream_t stream, int dev) {
+template <typename T>
+int awq_gemm_launch(T* y, const T* x, const int32_t* qw, const int32_t* qz, const __half* sc,
+                    const T* bias, int M, int K, int N, int group, cudaStream_t stream, int dev) {
   if (pick_bn(M, N, sm_count(dev)) == 224)
-    return awq_gemm_launch_bn<224>(y, x, qw, qz, sc, bias, M, K, N, group, stream, dev,
-                                   g_smem_awq_gemm224);
-  return awq_gemm_launch_bn<256>(y, x, qw, qz, sc, bias, M, K, N, group, stream, dev,
-                                 g_smem_awq_gemm);
+    return awq_gemm_launch_bn<224, T>(y, x, qw, qz, sc, bias, M, K, N, group, stream, dev);
+  return awq_gemm_launch_bn<256, T>(y, x, qw, qz, sc, bias, M, K, N, group, stream, dev);
+}
+
+// Dispatch by M (every regime for both activation types).
+template <typename T>
+int awq_linear_dispatch(T* y, const T* x, const int32_t* qweight, const int32_t* qzeros,
+                        const __half* sc, const T* bias, int M, int K, int N, int group,
+                        cudaStream_t st, int dev) {
+  if (awq_use_tmem(M, K, N))
+    return awq_tmem_launch<T>(y, x, qweight, qzeros, sc, bias, M, K, N, group, st, dev);
+  if (M <= g_tune.awq_gemv_max_m && M <= 16)
+    return awq_gemv_launch<T>(y, x, qweight, reinterpret_cast<const uint32_t*>(qzeros), sc, bias,
+                              M, K, N, group, st, dev);
+  if (awq_use_swap(M, K, N, sm_count(dev)))
+    return awq_swap_launch<T>(y, x, qweight, qzeros, sc, bias, M, K, N, group, st, dev);
+  // up to one token tile, more 128-channel tiles than SMs leave a tail wave the
+  // 256-channel smem-staged tiles avoid
+  if (g_tune.awq_gemm_tmem && (M > 128 || (N + lmrs::kAgtCh - 1) / lmrs::kAgtCh <= sm_count(dev)))
+    return awq_gemm_tmem_launch<T>(y, x, qweight, qzeros, sc, bias, M, K, N, group, st, dev);
+  if (g_tune.awq_gemm_pair)
+    return awq_gemm2_launch<T>(y, x, qweight, qzeros, sc, bias, M, K, N, group, st, dev);
+  return awq_gemm_launch<T>(y, x, qweight, qzeros, sc, bias, M, K, N, group, st, dev);
 }
 
 // ------------------------------------------------------------------ FP8
@@ -965,9 +971,33 @@ int lmrs_awq_dequant(void* w_out, const int32_t* qweight, const int32_t* qzeros,
   int rc = check_device(nullptr);
   if (rc) return rc;
   const int64_t words = int64_t(K) * (N / 8);
-  lmrs::awq_dequant_kernel<<<static_cast<unsigned>((words + 255) / 256), 256, 0,
-                             reinterpret_cast<cudaStream_t>(stream)>>>(
+  lmrs::awq_dequant_kernel<__half><<<static_cast<unsigned>((words + 255) / 256), 256, 0,
+                                     reinterpret_cast<cudaStream_t>(stream)>>>(
       static_cast<__half*>(w_out), reinterpret_cast<const uint32_t*>(qweight),
+      reinterpret_cast<const uint32_t*>(qzeros), static_cast<const __half*>(scales), K, N / 8,
+      group);
+  return after_launch();
+}
+
+int lmrs_awq_dequant_dtype(void* w_out, const int32_t* qweight, const int32_t* qzeros,
+                           const void* scales, int K, int N, int group, int out_dtype,
+                           lmrs_stream_t stream) {
+  if (out_dtype == LMRS_DTYPE_F16)
+    return lmrs_awq_dequant(w_out, qweight, qzeros, scales, K, N, group, stream);
+  if (out_dtype != LMRS_DTYPE_BF16) return LMRS_ERR_DTYPE;
+  if (K < 0 || N < 0 || N % 8) return LMRS_ERR_SHAPE;
+  if (group <= 0 || K % group) return LMRS_ERR_GROUP;
+  if (K == 0 || N == 0) return LMRS_OK;
+  if (!w_out || !qweight || !qzeros || !scales) return LMRS_ERR_NULL;
+  if (!aligned16(w_out) || !aligned16(scales) || (reinterpret_cast<uintptr_t>(qweight) & 3u) ||
+      (reinterpret_cast<uintptr_t>(qzeros) & 3u))
+    return LMRS_ERR_ALIGN;
+  int rc = check_device(nullptr);
+  if (rc) return rc;
+  const int64_t words = int64_t(K) * (N / 8);
+  lmrs::awq_dequant_kernel<__nv_bfloat16><<<static_cast<unsigned>((words + 255) / 256), 256, 0,
+                                            reinterpret_cast<cudaStream_t>(stream)>>>(
+      static_cast<__nv_bfloat16*>(w_out), reinterpret_cast<const uint32_t*>(qweight),
       reinterpret_cast<const uint32_t*>(qzeros), static_cast<const __half*>(scales), K, N / 8,
       group);
   return after_launch();
@@ -983,7 +1013,7 @@ int lmrs_awq_linear(void* y, const void* x, const int32_t* qweight, const int32_
                     int act_dtype, void* workspace, size_t workspace_bytes,
                     lmrs_stream_t stream) {
   (void)workspace; (void)workspace_bytes;
-  if (act_dtype != LMRS_DTYPE_F16) return LMRS_ERR_DTYPE;
+  if (act_dtype != LMRS_DTYPE_F16 && act_dtype != LMRS_DTYPE_BF16) return LMRS_ERR_DTYPE;
   if (M < 0 || K <= 0 || N <= 0 || N % 32) return LMRS_ERR_SHAPE;
   if (group <= 0 || group % 64 || K % group) return LMRS_ERR_GROUP;
   if (M == 0) return LMRS_OK;
@@ -995,24 +1025,14 @@ int lmrs_awq_linear(void* y, const void* x, const int32_t* qweight, const int32_
   int rc = check_device(&dev);
   if (rc) return rc;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  auto* yh = static_cast<__half*>(y);
-  auto* xh = static_cast<const __half*>(x);
   auto* sh = static_cast<const __half*>(scales);
-  auto* bh = static_cast<const __half*>(bias_or_null);
-  if (awq_use_tmem(M, K, N))
-    return awq_tmem_launch(yh, xh, qweight, qzeros, sh, bh, M, K, N, group, st, dev);
-  if (M <= g_tune.awq_gemv_max_m && M <= 16)
-    return awq_gemv_launch(yh, xh, qweight, reinterpret_cast<const uint32_t*>(qzeros), sh, bh, M,
-                           K, N, group, st, dev);
-  if (awq_use_swap(M, K, N, sm_count(dev)))
-    return awq_swap_launch(yh, xh, qweight, qzeros, sh, bh, M, K, N, group, st, dev);
-  // up to one token tile, more 128-channel tiles than SMs leave a tail wave the
-  // 256-channel smem-staged tiles avoid
-  if (g_tune.awq_gemm_tmem && (M > 128 || (N + lmrs::kAgtCh - 1) / lmrs::kAgtCh <= sm_count(dev)))
-    return awq_gemm_tmem_launch(yh, xh, qweight, qzeros, sh, bh, M, K, N, group, st, dev);
-  if (g_tune.awq_gemm_pair)
-    return awq_gemm2_launch(yh, xh, qweight, qzeros, sh, bh, M, K, N, group, st, dev);
-  return awq_gemm_launch(yh, xh, qweight, qzeros, sh, bh, M, K, N, group, st, dev);
+  if (act_dtype == LMRS_DTYPE_BF16)
+    return awq_linear_dispatch<__nv_bfloat16>(
+        static_cast<__nv_bfloat16*>(y), static_cast<const __nv_bfloat16*>(x), qweight, qzeros, sh,
+        static_cast<const __nv_bfloat16*>(bias_or_null), M, K, N, group, st, dev);
+  return awq_linear_dispatch<__half>(static_cast<__half*>(y), static_cast<const __half*>(x),
+                                     qweight, qzeros, sh, static_cast<const __half*>(bias_or_null),
+                                     M, K, N, group, st, dev);
 }
 
 int lmrs_fp8_quant_rows(uint8_t* q, float* scale, const void* x, int rows, int K, int x_dtype,

@@ -31,9 +31,20 @@ __device__ uint32_t g_device_error;
 constexpr long long kWaitLimitCycles = 4000000000LL;
 // The limit every bounded wait uses, per device; kWaitLimitCycles unless a
 // host lowers it (lmrs_set_tuning "wait_limit_kcycles", e.g. to make a test's
-// wait on an arrival that never comes give up within a millisecond).  Read
-// only once a wait has already failed its first try.
+// wait on an arrival that never comes give up within a millisecond).  A wait
+// reads it only once it has lasted kWaitCheckCycles (~0.5 ms): a global load
+// on every wait that misses its first try put L2 latency on the critical path
+// of the GEMM pipelines.  Limits below kWaitCheckCycles act as kWaitCheckCycles.
 __device__ long long g_wait_limit_cycles = kWaitLimitCycles;
+constexpr long long kWaitCheckCycles = 1LL << 20;
+
+// True once a wait that started at t0 has outlived the device's limit.
+__device__ __forceinline__ bool wait_expired(long long t0, long long& limit) {
+  const long long el = clock64() - t0;
+  if (el < kWaitCheckCycles) return false;
+  if (limit < 0) limit = *static_cast<volatile long long*>(&g_wait_limit_cycles);
+  return el > limit;
+}
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -77,9 +88,9 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t site) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
-  const long long limit = *static_cast<volatile long long*>(&g_wait_limit_cycles);
+  long long limit = -1;
   while (!mbar_try_wait(bar, parity)) {
-    if (clock64() - t0 > limit) {
+    if (wait_expired(t0, limit)) {
       atomicOr(&g_device_error, site);
       return false;
     }
@@ -385,8 +396,7 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity
         : "r"(smem_u32(bar)), "r"(parity), "r"(1000000u)
         : "memory");
     if (ok) return true;
-    if (limit < 0) limit = *static_cast<volatile long long*>(&g_wait_limit_cycles);
-    if (clock64() - t0 > limit) {
+    if (wait_expired(t0, limit)) {
       atomicOr(&g_device_error, site);
       return false;
     }
@@ -478,6 +488,129 @@ __device__ __forceinline__ __half2 u32_as_h2(uint32_t v) {
 // fp16_rne((q - z) * s): (1024+q) - (1024+z) is exact, the fp16 multiply rounds once.
 __device__ __forceinline__ uint32_t dq_h2(uint32_t qb, uint32_t zb, uint32_t s) {
   return h2_as_u32(__hmul2(__hsub2(u32_as_h2(qb), u32_as_h2(zb)), u32_as_h2(s)));
+}
+
+// ------------------------------------------- activation types of the AWQ path
+// Every AWQ kernel runs with fp16 (LMRS_DTYPE_F16) or bf16 (LMRS_DTYPE_BF16)
+// activations; x, y, bias and the dequantised weight share that type, the
+// scales stay fp16 as stored.  The dequantised weight is always the exact
+// product (q - z) * s rounded once to the activation type.  What differs:
+//   * the magic-number bias: fp16 has 10 mantissa bits, so a nibble in bits
+//     0-3 of a half gives 1024 + q (0x6400) and one in bits 4-7 gives 64 + q
+//     (0x5400, ulp 1/16); bf16 has 7, so every nibble is first shifted to bits
+//     0-3 and gives 128 + q (0x4300, ulp 1);
+//   * the product: the fp16 multiply of (q - z) (exact) by s rounds once.  A
+//     bf16 multiply cannot take the fp16 scale, so s is split into
+//     s_hi = bf16_rne(s) and s_lo = s - s_hi (at most 3 significant bits,
+//     exact in bf16); d * s_lo is exact (|d| <= 15), and one
+//     fma.rn.bf16x2(d, s_hi, d * s_lo) rounds d * s once;
+//   * the UMMA / mma.sync operand format.
+template <typename T>
+struct Act;
+template <>
+struct Act<__half> {
+  static constexpr uint32_t kUmmaFmt = 0;          // kind::f16 operand format: f16
+  static constexpr uint32_t kOne2 = 0x3C003C00u;   // (1, 1)
+  static constexpr CUtensorMapDataType kTma = CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  static constexpr float kMaxFinite = 65504.f;
+  __device__ __forceinline__ static float to_float(__half v) { return __half2float(v); }
+  __device__ __forceinline__ static __half from_float(float v) { return __float2half_rn(v); }
+  __device__ __forceinline__ static float2 unpack2(uint32_t v) {
+    return __half22float2(u32_as_h2(v));
+  }
+  __device__ __forceinline__ static uint32_t pack2(float a, float b) {
+    return h2_as_u32(__floats2half2_rn(a, b));
+  }
+};
+template <>
+struct Act<__nv_bfloat16> {
+  static constexpr uint32_t kUmmaFmt = 1;          // kind::f16 operand format: bf16
+  static constexpr uint32_t kOne2 = 0x3F803F80u;
+  static constexpr CUtensorMapDataType kTma = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  static constexpr float kMaxFinite = 3.38953139e38f;
+  __device__ __forceinline__ static float to_float(__nv_bfloat16 v) { return __bfloat162float(v); }
+  __device__ __forceinline__ static float2 unpack2(uint32_t v) {
+    return make_float2(__uint_as_float(v << 16), __uint_as_float(v & 0xFFFF0000u));
+  }
+  __device__ __forceinline__ static __nv_bfloat16 from_float(float v) {
+    return __float2bfloat16_rn(v);
+  }
+  __device__ __forceinline__ static uint32_t pack2(float a, float b) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&v);
+  }
+};
+
+// Biased pair (B + q_lo, B + q_hi) of nibble j (bits 4j .. 4j+3) of each
+// 16-bit half of v; B = awq_nib_bias<T>(j).
+template <typename T>
+__device__ __forceinline__ uint32_t awq_nib_pair(uint32_t v, int j) {
+  if constexpr (Act<T>::kUmmaFmt == 0) {
+    const uint32_t u = (j & 2) ? v >> 8 : v;
+    return (j & 1) ? lop3_and_or(u, 0x00F000F0u, 0x54005400u)
+                   : lop3_and_or(u, 0x000F000Fu, 0x64006400u);
+  } else {
+    return lop3_and_or(v >> (4 * j), 0x000F000Fu, 0x43004300u);
+  }
+}
+template <typename T>
+__host__ __device__ constexpr float awq_nib_bias(int j) {
+  return Act<T>::kUmmaFmt == 0 ? ((j & 1) ? 64.f : 1024.f) : 128.f;
+}
+// The zero point z (0..15) biased like nibble j, in both halves.
+template <typename T>
+__device__ __forceinline__ uint32_t awq_zero_pair(uint32_t z, int j) {
+  if constexpr (Act<T>::kUmmaFmt == 0)
+    return ((j & 1) ? (0x5400u | (z << 4)) : (0x6400u | z)) * 0x00010001u;
+  else
+    return (0x4300u | z) * 0x00010001u;
+}
+
+// Four biased pairs for columns (0,1),(2,3),(4,5),(6,7) of one packed word
+// (every nibble shifted to bits 0-3: bias 1024 for fp16, 128 for bf16).
+template <typename T>
+__device__ __forceinline__ void awq_word_biased(uint32_t w, uint32_t (&h)[4]) {
+  constexpr uint32_t magic = Act<T>::kUmmaFmt == 0 ? 0x64006400u : 0x43004300u;
+  h[0] = lop3_and_or(w, 0x000F000Fu, magic);
+  h[1] = lop3_and_or(w >> 4, 0x000F000Fu, magic);
+  h[2] = lop3_and_or(w >> 8, 0x000F000Fu, magic);
+  h[3] = lop3_and_or(w >> 12, 0x000F000Fu, magic);
+}
+
+// The scale operand of a pair of channels (two fp16 scales in s16x2): fp16
+// keeps the pair as is; bf16 keeps (s_hi pair, s_lo pair).
+struct AwqScale2 {
+  uint32_t hi, lo;
+};
+template <typename T>
+__device__ __forceinline__ AwqScale2 awq_scale2(uint32_t s16x2) {
+  if constexpr (Act<T>::kUmmaFmt == 0) {
+    return {s16x2, 0u};
+  } else {
+    const float2 f = __half22float2(u32_as_h2(s16x2));
+    const __nv_bfloat162 hi = __floats2bfloat162_rn(f.x, f.y);
+    const float2 fh = __bfloat1622float2(hi);
+    // s - s_hi is exact in fp32; an infinite scale keeps s_lo = 0 so that
+    // d * s stays +-inf (NaN for d = 0) as in the exact product
+    const float lx = isinf(fh.x) ? 0.f : f.x - fh.x;
+    const float ly = isinf(fh.y) ? 0.f : f.y - fh.y;
+    const __nv_bfloat162 lo = __floats2bfloat162_rn(lx, ly);
+    return {*reinterpret_cast<const uint32_t*>(&hi), *reinterpret_cast<const uint32_t*>(&lo)};
+  }
+}
+
+// T_rne((q - z) * s) for a pair from biased q and z pairs.
+template <typename T>
+__device__ __forceinline__ uint32_t awq_dq(uint32_t qb, uint32_t zb, AwqScale2 s) {
+  if constexpr (Act<T>::kUmmaFmt == 0) {
+    return dq_h2(qb, zb, s.hi);
+  } else {
+    uint32_t d, t, w;
+    asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(qb), "r"(zb));      // exact
+    asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(t) : "r"(d), "r"(s.lo));     // exact
+    asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(w) : "r"(d), "r"(s.hi), "r"(t));
+    return w;
+  }
 }
 
 }  // namespace lmrs

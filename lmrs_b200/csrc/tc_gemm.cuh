@@ -101,24 +101,24 @@ template <int BN> struct AwqTile {
 };
 constexpr int kAwqSmemBytes = AwqTile<256>::kSmem;
 
-template <int BN>
+template <int BN, typename T>
 __global__ void __launch_bounds__(kAwqGemmThreads, 1)
     awq_gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x,
                        const __grid_constant__ CUtensorMap tm_q,
                        const __grid_constant__ CUtensorMap tm_s,
-                       const __grid_constant__ CUtensorMap tm_z, __half* __restrict__ y,
-                       const __half* __restrict__ bias, int M, int K, int N, int group) {
+                       const __grid_constant__ CUtensorMap tm_z, T* __restrict__ y,
+                       const T* __restrict__ bias, int M, int K, int N, int group) {
   pdl_wait();     // activations are the previous kernel's output
   pdl_trigger();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   uint8_t* sA = smem;
   uint8_t* sB = sA + kAwqSA * kAwqABytes;
-  using T = AwqTile<BN>;
+  using TL = AwqTile<BN>;
   uint8_t* sP = sB + kAwqSB * kAwqBBytes;
-  uint8_t* sS = sP + kAwqSA * T::kP;
-  uint8_t* sZ = sS + kAwqSA * T::kS;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sZ + kAwqSA * T::kZ);
+  uint8_t* sS = sP + kAwqSA * TL::kP;
+  uint8_t* sZ = sS + kAwqSA * TL::kS;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sZ + kAwqSA * TL::kZ);
   uint64_t* empty = full + kAwqSA;
   uint64_t* bfull = empty + kAwqSA;
   uint64_t* bempty = bfull + kAwqSB;
@@ -169,19 +169,20 @@ __global__ void __launch_bounds__(kAwqGemmThreads, 1)
         for (int kb = 0; kb < KB; ++kb, ++kg) {
           const int s = kg % kAwqSA;
           if (!(ok = mbar_wait(&empty[s], ((kg / kAwqSA) & 1) ^ 1, kErrWaitEmpty))) break;
-          mbar_arrive_expect_tx(&full[s], T::kTx);
+          mbar_arrive_expect_tx(&full[s], TL::kTx);
           const int k = kb * kAwqBK;
           const int gi = k / group;
           tma_load_2d_hint(&tm_x, &full[s], sA + s * kAwqABytes, k, m0, keep);
-          tma_load_2d(&tm_q, &full[s], sP + s * T::kP, n0 / 8, k);
-          tma_load_2d(&tm_s, &full[s], sS + s * T::kS, n0, gi);
-          tma_load_2d(&tm_z, &full[s], sZ + s * T::kZ, n0 / 8, gi);
+          tma_load_2d(&tm_q, &full[s], sP + s * TL::kP, n0 / 8, k);
+          tma_load_2d(&tm_s, &full[s], sS + s * TL::kS, n0, gi);
+          tma_load_2d(&tm_z, &full[s], sZ + s * TL::kZ, n0 / 8, gi);
         }
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t idesc = make_idesc(0, 0, /*a K-major*/ 0, /*b MN-major*/ 1, kTcBM, BN);
+      constexpr uint32_t fmt = Act<T>::kUmmaFmt;  // both operands f16, or both bf16
+      constexpr uint32_t idesc = make_idesc(fmt, fmt, /*a K-major*/ 0, /*b MN-major*/ 1, kTcBM, BN);
       uint32_t kg = 0, it = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++it) {
@@ -232,10 +233,10 @@ __global__ void __launch_bounds__(kAwqGemmThreads, 1)
           for (int e = 0; e < 8; ++e) {
             float v0 = __uint_as_float(r[2 * e]), v1 = __uint_as_float(r[2 * e + 1]);
             if (bias != nullptr) {
-              v0 += __half2float(bias[n + 2 * e]);
-              v1 += __half2float(bias[n + 2 * e + 1]);
+              v0 += Act<T>::to_float(bias[n + 2 * e]);
+              v1 += Act<T>::to_float(bias[n + 2 * e + 1]);
             }
-            packed[e] = h2_as_u32(__floats2half2_rn(v0, v1));
+            packed[e] = Act<T>::pack2(v0, v1);
           }
           uint4* dst = reinterpret_cast<uint4*>(y + static_cast<int64_t>(row) * N + n);
           dst[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
@@ -247,7 +248,7 @@ __global__ void __launch_bounds__(kAwqGemmThreads, 1)
       if (lane == 0) mbar_arrive(&acc->empty[a]);
     }
   } else {
-    // ---------------- dequant warps: packed int4 stage -> fp16 MN-major SW128 B stage
+    // ---------------- dequant warps: packed int4 stage -> MN-major SW128 B stage (fp16 or bf16)
     // two groups of 8 warps take alternate K-blocks, so two K-blocks are being
     // dequantised while the tensor core consumes a third
     const int dwa = warp - kAwqDqWarp0;
@@ -263,27 +264,29 @@ __global__ void __launch_bounds__(kAwqGemmThreads, 1)
              mbar_wait(&bempty[sb], ((kg / kAwqSB) & 1) ^ 1, kErrWaitEmpty);
         if (!ok) break;
         // lane = word column of the tile (BN/8 words; a 224-wide tile idles lanes 28..31)
-        const bool live = lane < T::kWords;
-        const uint32_t zw = live ? reinterpret_cast<const uint32_t*>(sZ + s * T::kZ)[lane] : 0u;
-        const uint4 sv = live ? reinterpret_cast<const uint4*>(sS + s * T::kS)[lane] : make_uint4(0u, 0u, 0u, 0u);
+        const bool live = lane < TL::kWords;
+        const uint32_t zw = live ? reinterpret_cast<const uint32_t*>(sZ + s * TL::kZ)[lane] : 0u;
+        const uint4 sv = live ? reinterpret_cast<const uint4*>(sS + s * TL::kS)[lane] : make_uint4(0u, 0u, 0u, 0u);
         uint32_t zb[4];
-        awq_word_to_h2_biased(zw, zb);
-        const uint32_t* prow = reinterpret_cast<const uint32_t*>(sP + s * T::kP);
+        awq_word_biased<T>(zw, zb);
+        const AwqScale2 sp[4] = {awq_scale2<T>(sv.x), awq_scale2<T>(sv.y), awq_scale2<T>(sv.z),
+                                 awq_scale2<T>(sv.w)};
+        const uint32_t* prow = reinterpret_cast<const uint32_t*>(sP + s * TL::kP);
         const uint32_t bbase = smem_u32(sB + sb * kAwqBBytes) + bblk * 8192;
         uint32_t w[kAwqBK / kAwqDqWarps];
 #pragma unroll
         for (int rr = 0; rr < kAwqBK / kAwqDqWarps; ++rr)
-          w[rr] = live ? prow[(dw * (kAwqBK / kAwqDqWarps) + rr) * T::kWords + lane] : 0u;
+          w[rr] = live ? prow[(dw * (kAwqBK / kAwqDqWarps) + rr) * TL::kWords + lane] : 0u;
 #pragma unroll
         for (int rr = 0; rr < kAwqBK / kAwqDqWarps; ++rr) {
           const int r = dw * (kAwqBK / kAwqDqWarps) + rr;
           uint32_t qb[4];
-          awq_word_to_h2_biased(w[rr], qb);
+          awq_word_biased<T>(w[rr], qb);
           uint4 o;
-          o.x = dq_h2(qb[0], zb[0], sv.x);
-          o.y = dq_h2(qb[1], zb[1], sv.y);
-          o.z = dq_h2(qb[2], zb[2], sv.z);
-          o.w = dq_h2(qb[3], zb[3], sv.w);
+          o.x = awq_dq<T>(qb[0], zb[0], sp[0]);
+          o.y = awq_dq<T>(qb[1], zb[1], sp[1]);
+          o.z = awq_dq<T>(qb[2], zb[2], sp[2]);
+          o.w = awq_dq<T>(qb[3], zb[3], sp[3]);
           const uint32_t addr = bbase + (r >> 3) * 1024 + (r & 7) * 128 + ((chunk ^ (r & 7)) << 4);
           if (live) st_shared_v4(addr, o);
         }

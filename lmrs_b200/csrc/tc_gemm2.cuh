@@ -51,12 +51,13 @@ constexpr int kP2StageAl = (kP2Stage + 1023) / 1024 * 1024;
 constexpr int kP2BBytes = 128 * kP2BK * 2;       // dequantised half-tile: 16 KB
 constexpr int kP2SmemBytes = 1024 + kP2SA * kP2StageAl + kP2SB * kP2BBytes + 512;
 
+template <typename T>
 __global__ void __launch_bounds__(kP2Threads, 1)
     awq_gemm_tc2_kernel(const __grid_constant__ CUtensorMap tm_x,
                         const __grid_constant__ CUtensorMap tm_q,
                         const __grid_constant__ CUtensorMap tm_s,
-                        const __grid_constant__ CUtensorMap tm_z, __half* __restrict__ y,
-                        const __half* __restrict__ bias, int M, int K, int N, int group) {
+                        const __grid_constant__ CUtensorMap tm_z, T* __restrict__ y,
+                        const T* __restrict__ bias, int M, int K, int N, int group) {
   pdl_wait();     // activations are the previous kernel's output
   pdl_trigger();
   extern __shared__ uint8_t smem_raw[];
@@ -175,7 +176,8 @@ __global__ void __launch_bounds__(kP2Threads, 1)
   } else if (warp == 1) {
     if (rank == 0 && lane == 0) {
       // M = 256 across the pair, N = 256; A K-major, B MN-major
-      constexpr uint32_t idesc = make_idesc(0, 0, 0, 1, kP2BM, kP2BN);
+      constexpr uint32_t fmt = Act<T>::kUmmaFmt;  // both operands f16, or both bf16
+      constexpr uint32_t idesc = make_idesc(fmt, fmt, 0, 1, kP2BM, kP2BN);
       uint32_t kg = 0, it = 0;
       bool ok = true;
       for (int t = pair; t < tiles && ok; t += npairs, ++it) {
@@ -227,10 +229,10 @@ __global__ void __launch_bounds__(kP2Threads, 1)
           for (int e = 0; e < 8; ++e) {
             float v0 = __uint_as_float(r[2 * e]), v1 = __uint_as_float(r[2 * e + 1]);
             if (bias != nullptr) {
-              v0 += __half2float(bias[n + 2 * e]);
-              v1 += __half2float(bias[n + 2 * e + 1]);
+              v0 += Act<T>::to_float(bias[n + 2 * e]);
+              v1 += Act<T>::to_float(bias[n + 2 * e + 1]);
             }
-            packed[e] = h2_as_u32(__floats2half2_rn(v0, v1));
+            packed[e] = Act<T>::pack2(v0, v1);
           }
           uint4* dst = reinterpret_cast<uint4*>(y + static_cast<int64_t>(row) * N + n);
           dst[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
@@ -263,7 +265,9 @@ __global__ void __launch_bounds__(kP2Threads, 1)
         const uint32_t zw =
             reinterpret_cast<const uint32_t*>(st + kP2ABytes + kP2PBytes + kP2SBytes)[j];
         uint32_t zb[4];
-        awq_word_to_h2_biased(zw, zb);
+        awq_word_biased<T>(zw, zb);
+        const AwqScale2 sp[4] = {awq_scale2<T>(sv.x), awq_scale2<T>(sv.y), awq_scale2<T>(sv.z),
+                                 awq_scale2<T>(sv.w)};
         const uint32_t bbase = smem_u32(sB + sb * kP2BBytes) + blk * 8192;
         uint32_t w[4];
 #pragma unroll
@@ -272,12 +276,12 @@ __global__ void __launch_bounds__(kP2Threads, 1)
         for (int i2 = 0; i2 < 4; ++i2) {
           const int r = dw * 8 + 2 * i2 + half;
           uint32_t qb[4];
-          awq_word_to_h2_biased(w[i2], qb);
+          awq_word_biased<T>(w[i2], qb);
           uint4 o;
-          o.x = dq_h2(qb[0], zb[0], sv.x);
-          o.y = dq_h2(qb[1], zb[1], sv.y);
-          o.z = dq_h2(qb[2], zb[2], sv.z);
-          o.w = dq_h2(qb[3], zb[3], sv.w);
+          o.x = awq_dq<T>(qb[0], zb[0], sp[0]);
+          o.y = awq_dq<T>(qb[1], zb[1], sp[1]);
+          o.z = awq_dq<T>(qb[2], zb[2], sp[2]);
+          o.w = awq_dq<T>(qb[3], zb[3], sp[3]);
           st_shared_v4(bbase + (r >> 3) * 1024 + (r & 7) * 128 + ((chunk ^ (r & 7)) << 4), o);
         }
         fence_proxy_async_smem();

@@ -79,25 +79,34 @@ def awq_unpack(packed: torch.Tensor, cols: Optional[int] = None) -> torch.Tensor
     return out
 
 
-def awq_dequant(qweight, qzeros, scales, group_size: int) -> torch.Tensor:
-    """fp16 [K, N] = fp16((q - z) * s), bit-exact."""
+# activation dtypes of the AWQ linear -> KernelDType code (crates/kernels/src/raw.rs:9-13)
+AWQ_ACT_DTYPES = {torch.bfloat16: _lib.DTYPE_BF16, torch.float16: _lib.DTYPE_F16}
+
+
+def awq_dequant(qweight, qzeros, scales, group_size: int,
+                dtype: torch.dtype = torch.float16) -> torch.Tensor:
+    """[K, N] = dtype_rne((q - z) * s) (fp16 or bf16; scales fp16), bit-exact."""
     for t, n in ((qweight, "qweight"), (qzeros, "qzeros"), (scales, "scales")):
         _require_cuda(t, "awq_dequant " + n)
+    if dtype not in AWQ_ACT_DTYPES:
+        raise DTypeMismatch(f"awq_dequant: dtype must be fp16 or bf16, got {dtype}")
     K, words = qweight.shape
     N = words * AWQ_PACK_FACTOR
-    out = torch.empty((K, N), dtype=torch.float16, device=qweight.device)
-    _lib.check("lmrs_awq_dequant", _lib.load().lmrs_awq_dequant(
+    out = torch.empty((K, N), dtype=dtype, device=qweight.device)
+    _lib.check("lmrs_awq_dequant_dtype", _lib.load().lmrs_awq_dequant_dtype(
         _ptr(out), _ptr(qweight), _ptr(qzeros), _ptr(scales), K, N, group_size,
-        _stream(qweight)))
+        AWQ_ACT_DTYPES[dtype], _stream(qweight)))
     return out
 
 
 def awq_linear(x: torch.Tensor, qweight: torch.Tensor, qzeros: torch.Tensor,
                scales: torch.Tensor, bias: Optional[torch.Tensor], group_size: int,
                out: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """y[..., N] = x[..., K] @ dequant(AWQ) (+ bias); x, y fp16."""
+    """y[..., N] = x[..., K] @ dequant(AWQ) (+ bias); x, y and bias share one
+    dtype, bf16 (the reference model's) or fp16; scales fp16."""
     _require_cuda(x, "awq_linear")
-    _require_dtype(x, torch.float16, "awq_linear input")
+    if x.dtype not in AWQ_ACT_DTYPES:
+        raise DTypeMismatch(f"awq_linear input: expected bf16 or fp16, got {x.dtype}")
     for t, n in ((qweight, "qweight"), (qzeros, "qzeros")):
         _require_cuda(t, "awq_linear " + n)
         _require_dtype(t, torch.int32, "awq_linear " + n)
@@ -111,16 +120,17 @@ def awq_linear(x: torch.Tensor, qweight: torch.Tensor, qzeros: torch.Tensor,
     N = qweight.shape[1] * AWQ_PACK_FACTOR
     rows = x.numel() // K if K else 0
     if out is None:
-        out = torch.empty((*x.shape[:-1], N), dtype=torch.float16, device=x.device)
+        out = torch.empty((*x.shape[:-1], N), dtype=x.dtype, device=x.device)
+    _require_dtype(out, x.dtype, "awq_linear output")
     if bias is not None:
         _require_cuda(bias, "awq_linear bias")
-        _require_dtype(bias, torch.float16, "awq_linear bias")
+        _require_dtype(bias, x.dtype, "awq_linear bias")
     L = _lib.load()
     ws_bytes = L.lmrs_awq_linear_workspace_bytes(rows, K, N, group_size)
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=x.device) if ws_bytes else None
     _lib.check("lmrs_awq_linear", L.lmrs_awq_linear(
         _ptr(out), _ptr(x), _ptr(qweight), _ptr(qzeros), _ptr(scales), _ptr(bias),
-        rows, K, N, group_size, _lib.DTYPE_F16, _ptr(ws), ws_bytes, _stream(x)))
+        rows, K, N, group_size, AWQ_ACT_DTYPES[x.dtype], _ptr(ws), ws_bytes, _stream(x)))
     return out
 
 

@@ -16,7 +16,9 @@
  *   - AWQ W4A16 pack/unpack/dequant.  The reference has no AWQ code; the format
  *     is the one the task's configs define (qweight int32 [K,N/8], nibble i of
  *     word j = column 8j + ORDER[i], ORDER = {0,2,4,6,1,3,5,7}); dequant is
- *     fp16_rne(float(q - z) * float(s)), whose fp32 product is exact.
+ *     the exact fp32 product float(q - z) * float(s) rounded once to the
+ *     activation type: fp16_rne(...) for fp16 activations, bf16_rne(...) for
+ *     bf16 ones (scales are fp16 either way).
  *   - FP8 e4m3 (OCP "e4m3fn": bias 7, no infinities, 0x7f/0xff NaN, max 448)
  *     per-row quantization, s = absmax / 448, q = e4m3_rne_satfinite(x / s),
  *     and the scaled GEMM y = bf16(acc * s_x * s_w (+ bias)).
@@ -168,10 +170,12 @@ static inline int awq_nib(const int32_t* packed, int words, int64_t r, int c) {
   return (int)((w >> (4 * inv[c & 7])) & 0xfu);
 }
 
-/* w_out fp16 bits [K, N] */
-void oracle_awq_dequant(const int32_t* qweight, const int32_t* qzeros,
-                        const uint16_t* scales, int K, int N, int group,
-                        uint16_t* w_out, int nthreads) {
+/* w_out [K, N] in `dtype` (1 = fp16, 0 = bf16) bits: the exact fp32 product
+ * float(q - z) * float(s) (a 5-bit integer times an 11-bit fp16 scale) rounded
+ * once, to nearest even, to the activation type. */
+void oracle_awq_dequant_dt(const int32_t* qweight, const int32_t* qzeros,
+                           const uint16_t* scales, int K, int N, int group, int dtype,
+                           uint16_t* w_out, int nthreads) {
   int words = N / 8;
 #ifdef _OPENMP
 #pragma omp parallel for num_threads(nthreads > 0 ? nthreads : 1) schedule(static)
@@ -182,10 +186,18 @@ void oracle_awq_dequant(const int32_t* qweight, const int32_t* qzeros,
       int q = awq_nib(qweight, words, k, n);
       int z = awq_nib(qzeros, words, g, n);
       float s = oracle_half_to_float(scales[(int64_t)g * N + n]);
-      w_out[(int64_t)k * N + n] = oracle_float_to_half((float)(q - z) * s);
+      float p = (float)(q - z) * s;
+      w_out[(int64_t)k * N + n] = dtype == 0 ? oracle_float_to_bf16(p) : oracle_float_to_half(p);
     }
   }
   (void)nthreads;
+}
+
+/* w_out fp16 bits [K, N] */
+void oracle_awq_dequant(const int32_t* qweight, const int32_t* qzeros,
+                        const uint16_t* scales, int K, int N, int group,
+                        uint16_t* w_out, int nthreads) {
+  oracle_awq_dequant_dt(qweight, qzeros, scales, K, N, group, 1, w_out, nthreads);
 }
 
 /* fp32 core of the dense linear: acc[m,n] = fmaf-chain over k (in order) of
@@ -214,10 +226,14 @@ static void linear_kn_f32(const float* x, const float* w, const float* bias, int
   (void)nthreads;
 }
 
-static float* to_f32(const void* p, int64_t n, int dtype) {
+static float* to_f32(const void* p, int64_t n, int dtype, int nthreads) {
   float* f = (float*)malloc((size_t)n * sizeof(float));
   if (!f) return NULL;
+#ifdef _OPENMP
+#pragma omp parallel for num_threads(nthreads > 0 ? nthreads : 1) schedule(static)
+#endif
   for (int64_t i = 0; i < n; ++i) f[i] = load_io(p, i, dtype);
+  (void)nthreads;
   return f;
 }
 
@@ -227,9 +243,9 @@ static float* to_f32(const void* p, int64_t n, int dtype) {
  * All buffers share `dtype`.  Returns nonzero on allocation failure. */
 int oracle_linear_kn(const void* x, const void* w_kn, const void* bias, int M,
                      int K, int N, int dtype, void* y, int nthreads) {
-  float* xf = to_f32(x, (int64_t)M * K, dtype);
-  float* wf = to_f32(w_kn, (int64_t)K * N, dtype);
-  float* bf = bias ? to_f32(bias, N, dtype) : NULL;
+  float* xf = to_f32(x, (int64_t)M * K, dtype, nthreads);
+  float* wf = to_f32(w_kn, (int64_t)K * N, dtype, nthreads);
+  float* bf = bias ? to_f32(bias, N, dtype, nthreads) : NULL;
   float* of = (float*)malloc((size_t)M * N * sizeof(float));
   int rc = (!xf || !wf || !of || (bias && !bf)) ? 1 : 0;
   if (!rc) {
@@ -257,17 +273,25 @@ void oracle_linear_nk(const void* x, const void* w_nk, const void* bias, int M,
   (void)nthreads;
 }
 
-/* AWQ linear: dequant (bit-exact fp16) then the reference's fp16 linear arithmetic.
- * x, bias, y: fp16 bits.  `wbuf` (K*N fp16) may be NULL (allocated here). */
+/* AWQ linear in activation type `dtype` (1 = fp16, 0 = bf16): the dequantised
+ * weight in that type, then the reference's linear arithmetic in that type
+ * (linear_fwd's dtype 1 / 0 variants).  x, bias, y: `dtype` bits; scales fp16. */
+int oracle_awq_linear_dt(const uint16_t* x, const int32_t* qweight, const int32_t* qzeros,
+                         const uint16_t* scales, const uint16_t* bias, int M, int K,
+                         int N, int group, int dtype, uint16_t* y, int nthreads) {
+  uint16_t* w = (uint16_t*)malloc((size_t)K * N * sizeof(uint16_t));
+  if (!w) return 1;
+  oracle_awq_dequant_dt(qweight, qzeros, scales, K, N, group, dtype, w, nthreads);
+  int rc = oracle_linear_kn(x, w, bias, M, K, N, dtype, y, nthreads);
+  free(w);
+  return rc;
+}
+
+/* AWQ linear with fp16 activations (the task's configs 0 and 1). */
 int oracle_awq_linear(const uint16_t* x, const int32_t* qweight, const int32_t* qzeros,
                       const uint16_t* scales, const uint16_t* bias, int M, int K,
                       int N, int group, uint16_t* y, int nthreads) {
-  uint16_t* w = (uint16_t*)malloc((size_t)K * N * sizeof(uint16_t));
-  if (!w) return 1;
-  oracle_awq_dequant(qweight, qzeros, scales, K, N, group, w, nthreads);
-  int rc = oracle_linear_kn(x, w, bias, M, K, N, 1, y, nthreads);
-  free(w);
-  return rc;
+  return oracle_awq_linear_dt(x, qweight, qzeros, scales, bias, M, K, N, group, 1, y, nthreads);
 }
 
 /* ------------------------------------------------------------------- FP8 */

@@ -32,20 +32,28 @@ E4M3_MAX = 448.0
 
 
 # ----------------------------------------------------------------- generators
-def awq_inputs(M, K, N, group=128, seed=0, with_bias=False):
+def awq_inputs(M, K, N, group=128, seed=0, with_bias=False, act="f16"):
     """Seeded AWQ inputs with the config-0 distributions.
 
     Draw order (recorded convention): q, then z, then s, then x (then bias).
-    q, z ~ U{0..15}; s ~ U[0.001, 0.02] as fp16; x ~ N(0, 1) as fp16.
+    q, z ~ U{0..15}; s ~ U[0.001, 0.02] as fp16; x ~ N(0, 1) in the activation
+    type: fp16 (act="f16"), or bf16 bit patterns as uint16 (act="bf16", the
+    same draws rounded to bf16 instead).
     """
     rng = np.random.default_rng(seed)
     q = rng.integers(0, 16, size=(K, N), dtype=np.int64).astype(np.int8)
     z = rng.integers(0, 16, size=(K // group, N), dtype=np.int64).astype(np.int8)
     s = rng.uniform(0.001, 0.02, size=(K // group, N)).astype(np.float16)
-    x = rng.standard_normal((M, K)).astype(np.float16)
-    bias = rng.standard_normal(N).astype(np.float16) if with_bias else None
+    xd = rng.standard_normal((M, K))
+    bd = rng.standard_normal(N) if with_bias else None
+    if act == "bf16":
+        x = f32_to_bf16_bits(xd.astype(np.float32))
+        bias = None if bd is None else f32_to_bf16_bits(bd.astype(np.float32))
+    else:
+        x = xd.astype(np.float16)
+        bias = None if bd is None else bd.astype(np.float16)
     return dict(q=q, z=z, qweight=np_awq_pack(q), qzeros=np_awq_pack(z), scales=s,
-                x=x, bias=bias, M=M, K=K, N=N, group=group)
+                x=x, bias=bias, M=M, K=K, N=N, group=group, act=act)
 
 
 def fp8_inputs(M, K, N, seed=0, with_bias=False):
@@ -91,13 +99,15 @@ def np_awq_unpack(packed):
     return nib[:, :, AWQ_INV].reshape(R, W * 8).astype(np.int8)
 
 
-def np_awq_dequant(qweight, qzeros, scales, group):
-    """fp16 [K, N] = fp16_rne(float32(q - z) * float32(s)); the fp32 product is exact."""
+def np_awq_dequant(qweight, qzeros, scales, group, act="f16"):
+    """[K, N] = T_rne(float32(q - z) * float32(s)); the fp32 product is exact.
+    act="f16": fp16 array; act="bf16": bf16 bit patterns (uint16)."""
     q = np_awq_unpack(qweight).astype(np.int32)
     z = np_awq_unpack(qzeros).astype(np.int32)
     zk = np.repeat(z, group, axis=0)
     sk = np.repeat(np.asarray(scales, dtype=np.float16).astype(np.float32), group, axis=0)
-    return ((q - zk).astype(np.float32) * sk).astype(np.float16)
+    p = (q - zk).astype(np.float32) * sk
+    return f32_to_bf16_bits(p) if act == "bf16" else p.astype(np.float16)
 
 
 def np_linear_f64(x, w_kn, bias=None):
@@ -175,8 +185,11 @@ def lib():
     L.oracle_awq_pack.argtypes = [P, I, I, P]
     L.oracle_awq_unpack.argtypes = [P, I, I, P]
     L.oracle_awq_dequant.argtypes = [P, P, P, I, I, I, P, I]
+    L.oracle_awq_dequant_dt.argtypes = [P, P, P, I, I, I, I, P, I]
     L.oracle_awq_linear.argtypes = [P, P, P, P, P, I, I, I, I, P, I]
     L.oracle_awq_linear.restype = I
+    L.oracle_awq_linear_dt.argtypes = [P, P, P, P, P, I, I, I, I, I, P, I]
+    L.oracle_awq_linear_dt.restype = I
     L.oracle_linear_kn.argtypes = [P, P, P, I, I, I, I, P, I]
     L.oracle_linear_kn.restype = I
     L.oracle_linear_nk.argtypes = [P, P, P, I, I, I, I, P, I]
@@ -219,27 +232,39 @@ def c_awq_unpack(packed, cols):
     return out
 
 
-def c_awq_dequant(qweight, qzeros, scales, K, N, group, nthreads=0):
-    out = np.empty((K, N), dtype=np.float16)
-    lib().oracle_awq_dequant(_p(np.ascontiguousarray(qweight, np.int32)),
-                             _p(np.ascontiguousarray(qzeros, np.int32)),
-                             _p(np.ascontiguousarray(scales, np.float16)),
-                             K, N, group, _p(out), _nt(nthreads))
+_ACT = {"f16": (1, np.float16), "bf16": (0, np.uint16)}  # dtype code, numpy storage
+
+
+def c_awq_dequant(qweight, qzeros, scales, K, N, group, nthreads=0, act="f16"):
+    """[K, N] dequantised weights: fp16 (act="f16") or bf16 bits as uint16 (act="bf16")."""
+    code, st = _ACT[act]
+    out = np.empty((K, N), dtype=st)
+    lib().oracle_awq_dequant_dt(_p(np.ascontiguousarray(qweight, np.int32)),
+                                _p(np.ascontiguousarray(qzeros, np.int32)),
+                                _p(np.ascontiguousarray(scales, np.float16)),
+                                K, N, group, code, _p(out), _nt(nthreads))
     return out
 
 
-def c_awq_linear(x, qweight, qzeros, scales, bias, M, K, N, group, nthreads=0):
-    """fp16 [M, N]: bit-exact restatement of dequant + the reference's fp16 linear."""
-    y = np.empty((M, N), dtype=np.float16)
-    b = None if bias is None else np.ascontiguousarray(bias, np.float16)
-    rc = lib().oracle_awq_linear(_p(np.ascontiguousarray(x, np.float16)),
-                                 _p(np.ascontiguousarray(qweight, np.int32)),
-                                 _p(np.ascontiguousarray(qzeros, np.int32)),
-                                 _p(np.ascontiguousarray(scales, np.float16)),
-                                 _p(b), M, K, N, group, _p(y), _nt(nthreads))
+def c_awq_linear(x, qweight, qzeros, scales, bias, M, K, N, group, nthreads=0, act="f16"):
+    """[M, N] in the activation type (fp16, or bf16 bits as uint16): bit-exact
+    restatement of dequant + the reference's linear in that type."""
+    code, st = _ACT[act]
+    y = np.empty((M, N), dtype=st)
+    b = None if bias is None else np.ascontiguousarray(bias, st)
+    rc = lib().oracle_awq_linear_dt(_p(np.ascontiguousarray(x, st)),
+                                    _p(np.ascontiguousarray(qweight, np.int32)),
+                                    _p(np.ascontiguousarray(qzeros, np.int32)),
+                                    _p(np.ascontiguousarray(scales, np.float16)),
+                                    _p(b), M, K, N, group, code, _p(y), _nt(nthreads))
     if rc:
-        raise MemoryError("oracle_awq_linear: allocation failed")
+        raise MemoryError("oracle_awq_linear_dt: allocation failed")
     return y
+
+
+def as_f32(a, act="f16"):
+    """Values of an activation-type array (fp16, or bf16 bits) as float32."""
+    return bf16_bits_to_f32(a) if act == "bf16" else np.asarray(a, np.float32)
 
 
 def c_linear_nk(x, w_nk, bias, dtype_code, nthreads=0):

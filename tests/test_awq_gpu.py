@@ -189,9 +189,9 @@ def test_status_codes(cuda):
                              torch.cuda.current_stream().cuda_stream)
     assert rc == _lib.LMRS_ERR_ALIGN
     rc = lib.lmrs_awq_linear(y.data_ptr(), x.data_ptr(), qw.data_ptr(), qz.data_ptr(),
-                             sc.data_ptr(), None, 2, 256, 64, 128, 0, None, 0,
+                             sc.data_ptr(), None, 2, 256, 64, 128, 2, None, 0,
                              torch.cuda.current_stream().cuda_stream)
-    assert rc == _lib.LMRS_ERR_DTYPE
+    assert rc == _lib.LMRS_ERR_DTYPE   # f32 activations are not an AWQ type
     # M == 0 is a no-op
     rc = lib.lmrs_awq_linear(y.data_ptr(), x.data_ptr(), qw.data_ptr(), qz.data_ptr(),
                              sc.data_ptr(), None, 0, 256, 64, 128, 1, None, 0,
@@ -334,3 +334,175 @@ def test_default_dispatch_deep_k_band(cuda, M, K, N):
     assert err < TIGHT, err
     assert torch.equal(L.awq_linear(x, qw, qz, sc, b, 128), y)
     assert L.read_device_error() == 0
+
+
+# ------------------------------------------------------------ bf16 activations
+# The reference model runs bf16 end to end (KernelDType::Bf16 = 0,
+# crates/kernels/src/raw.rs:9-13), so lmrs_awq_linear takes bf16 x / y / bias as
+# well; scales stay fp16.  The dequantised weight is bf16_rne((q - z) * s), one
+# rounding of the exact product.  bf16 keeps 8 significant bits, so one output
+# ulp is 2^-8 = 3.9e-3 of the element: the bf16 linears are held to 8e-3 (the
+# bound the FP8 tests use for their bf16 outputs) and to the north star's 1e-2.
+TIGHT_BF16 = 8e-3
+
+
+def _bf16_dev(a, dev):
+    import torch
+    return to_dev(np.asarray(a, np.uint16), dev, torch.bfloat16)
+
+
+def _awq_case_bf16(dev, M, K, N, g, seed, bias=True):
+    import lmrs_b200 as L
+    d = O.awq_inputs(M, K, N, g, seed=seed, with_bias=bias, act="bf16")
+    qw, qz, sc = to_dev(d["qweight"], dev), to_dev(d["qzeros"], dev), to_dev(d["scales"], dev)
+    x = _bf16_dev(d["x"], dev)
+    b = None if d["bias"] is None else _bf16_dev(d["bias"], dev)
+    y = L.awq_linear(x, qw, qz, sc, b, g)
+    assert y.dtype == x.dtype
+    ref = O.c_awq_linear(d["x"], d["qweight"], d["qzeros"], d["scales"], d["bias"], M, K, N, g,
+                         act="bf16")
+    err = O.max_rel_err(O.bf16_bits_to_f32(bits16(y)), O.bf16_bits_to_f32(ref))
+    return err, (x, qw, qz, sc, b, y)
+
+
+@pytest.mark.parametrize("K,N,g", [(128, 8, 128), (256, 40, 64), (4096, 4096, 128),
+                                   (512, 14336, 128)])
+def test_dequant_bf16_bit_exact(cuda, K, N, g):
+    import torch
+    import lmrs_b200 as L
+    d = O.awq_inputs(1, K, N, g, seed=K + N + 1)
+    w = L.awq_dequant(to_dev(d["qweight"], cuda), to_dev(d["qzeros"], cuda),
+                      to_dev(d["scales"], cuda), g, dtype=torch.bfloat16)
+    ref = O.c_awq_dequant(d["qweight"], d["qzeros"], d["scales"], K, N, g, act="bf16")
+    assert np.array_equal(bits16(w), ref)
+    assert np.array_equal(ref, O.np_awq_dequant(d["qweight"], d["qzeros"], d["scales"], g,
+                                                act="bf16"))
+
+
+def test_dequant_bf16_extremes(cuda):
+    """The fp16 extremes of test_dequant_extremes in bf16: q == z, +-15 * s, the
+    largest fp16 scale (finite in bf16: 15 x 65504 does not overflow), fp16
+    subnormal scales, and every fp16 scale whose bf16 rounding carries into the
+    next binade (the s_hi + s_lo split at its edge)."""
+    import torch
+    import lmrs_b200 as L
+    K, N, g = 128, 96, 128
+    q = np.zeros((K, N), np.int8)
+    z = np.zeros((1, N), np.int8)
+    q[:, 0:8] = 7; z[:, 0:8] = 7
+    q[:, 8:16] = 0; z[:, 8:16] = 15
+    q[:, 16:24] = 15; z[:, 16:24] = 0
+    q[:, 24:] = np.arange(K)[:, None] % 16
+    z[:, 24:] = np.arange(N - 24) % 16
+    s = np.full((1, N), 0.02, np.float16)
+    s[:, 32:] = np.float16(0.001)
+    s[:, 40:48] = np.float16(65504.0)
+    s[:, 48:56] = np.float16(6e-8)
+    s[:, 56:64] = np.float16(1.0) - np.float16(2.0 ** -11)          # rounds up to 1.0 in bf16
+    s[:, 64:72] = (np.arange(8) + 1017).astype(np.float16) / 1024    # near-ties of the split
+    s[:, 72:80] = np.float16(-0.0137)                                # negative scales
+    s[:, 80:96] = np.random.default_rng(5).uniform(1e-4, 4.0, (1, 16)).astype(np.float16)
+    qw, qz = O.np_awq_pack(q), O.np_awq_pack(z)
+    w = L.awq_dequant(to_dev(qw, cuda), to_dev(qz, cuda), to_dev(s, cuda), g, dtype=torch.bfloat16)
+    ref = O.c_awq_dequant(qw, qz, s, K, N, g, act="bf16")
+    assert np.array_equal(bits16(w), ref)
+
+
+def test_config0_bf16_vs_reference_linear_fwd(cuda, ref_ffi):
+    """Config 0 shapes in bf16: the oracle equals the reference's own linear_fwd
+    (dtype 0 = bf16) on the bf16-dequantised weights bit for bit, and the CUDA
+    path is within TIGHT_BF16 of both."""
+    import torch
+    import lmrs_b200 as L
+    M, K, N, g = 8, 4096, 4096, 128
+    d = O.awq_inputs(M, K, N, g, seed=0, act="bf16")
+    qw, qz, sc = to_dev(d["qweight"], cuda), to_dev(d["qzeros"], cuda), to_dev(d["scales"], cuda)
+    x = _bf16_dev(d["x"], cuda)
+    w_nk = L.awq_dequant(qw, qz, sc, g, dtype=torch.bfloat16).t().contiguous()
+    y_ref = ref_linear(ref_ffi, x, w_nk, None, 0)
+    y_oracle = O.c_awq_linear(d["x"], d["qweight"], d["qzeros"], d["scales"], None, M, K, N, g,
+                              act="bf16")
+    assert np.array_equal(bits16(y_ref), y_oracle), "oracle != reference linear_fwd (bf16)"
+    y = L.awq_linear(x, qw, qz, sc, None, g)
+    err = O.max_rel_err(O.bf16_bits_to_f32(bits16(y)), O.bf16_bits_to_f32(y_oracle))
+    assert err < TIGHT_BF16, err
+
+
+# (M, K, N, g): default dispatch through every regime — integer GEMV (1), the
+# 2-4 token GEMV (3), the general GEMV (5..8 on deep K), the TMEM-staged kernel
+# (5..8 wide, 9..32), swap-AB (33..64 and deep-K up to 128), the prefill GEMM
+# (shallow K above 64, and above 128) with ragged token and channel tiles
+BF16_CASES = [(1, 1024, 1280, 128), (2, 2048, 768, 64), (3, 1024, 1280, 128),
+              (4, 4096, 512, 128), (7, 4096, 512, 128), (8, 1024, 2048, 128),
+              (12, 1024, 1280, 128), (16, 2048, 1312, 64), (31, 1024, 768, 256),
+              (40, 1024, 1280, 128), (64, 2048, 512, 128), (96, 4096, 3072, 128),
+              (100, 1024, 1280, 128), (200, 1024, 768, 128), (513, 3072, 640, 256)]
+
+
+@pytest.mark.parametrize("M,K,N,g", BF16_CASES)
+def test_linear_bf16_default_dispatch(cuda, M, K, N, g):
+    import torch
+    import lmrs_b200 as L
+    err, (x, qw, qz, sc, b, y) = _awq_case_bf16(cuda, M, K, N, g, 4000 + M + N)
+    assert err < TIGHT_BF16 and err < TOL, err
+    assert torch.equal(L.awq_linear(x, qw, qz, sc, b, g), y), "nondeterministic"
+    assert L.read_device_error() == 0
+
+
+@pytest.mark.parametrize("knob,value,Ms", [("awq_gemm_pair", 1, (129, 300)),
+                                           ("awq_gemm_tmem", 0, (100, 300)),
+                                           ("gemm_bn", 224, (100, 300)),
+                                           ("awq_gemv4", 0, (1, 3)),
+                                           ("awq_i8_max_m", 2, (1, 2)),
+                                           ("awq_i8_max_m", 0, (1, 2)),
+                                           ("awq_tmem_max_m", 0, (9, 16, 24)),
+                                           ("awq_swap_max_m", 128, (65, 128)),
+                                           ("awq_gemm_tmem_bt", 128, (65, 200)),
+                                           ("awq_gemm_tmem_bt", 192, (65, 200)),
+                                           ("gemv_box_rows", 64, (1, 4, 8))])
+def test_linear_bf16_opt_in_paths(cuda, knob, value, Ms):
+    """Every kernel variant the knobs reach, in bf16, against the C oracle."""
+    import lmrs_b200 as L
+    defaults = {"awq_gemm_pair": 0, "awq_gemm_tmem": 1, "gemm_bn": 256, "awq_gemv4": 1,
+                "awq_i8_max_m": 1, "awq_tmem_max_m": 32, "awq_swap_max_m": 64,
+                "awq_gemm_tmem_bt": 256, "gemv_box_rows": 128}
+    K, N, g = 1024, 1280, 128
+    try:
+        if knob in ("awq_gemm_pair", "gemm_bn"):
+            L.set_tuning("awq_gemm_tmem", 0)
+        if knob in ("awq_gemv4", "gemv_box_rows"):
+            L.set_tuning("awq_i8_max_m", 0)
+            L.set_tuning("awq_tmem_max_m", 0)
+        if knob == "awq_gemm_tmem_bt":
+            L.set_tuning("awq_swap_deep_k", 0)
+        L.set_tuning(knob, value)
+        for M in Ms:
+            err, _ = _awq_case_bf16(cuda, M, K, N, g, 5000 + M + len(knob))
+            assert err < TIGHT_BF16, (knob, value, M, err)
+    finally:
+        for k, v in defaults.items():
+            L.set_tuning(k, v)
+        L.set_tuning("awq_swap_deep_k", 5)
+    assert L.read_device_error() == 0
+
+
+def test_linear_bf16_large_values(cuda):
+    """bf16 has fp32's range: activations far outside fp16's (1e6 .. 1e-20) stay
+    finite and accurate on every regime's path (the integer GEMV rescales each
+    box by a power of two chosen from its maximum)."""
+    import torch
+    import lmrs_b200 as L
+    K, N, g = 1024, 512, 128
+    d = O.awq_inputs(40, K, N, g, seed=77, act="bf16")
+    xf = O.bf16_bits_to_f32(d["x"]).copy()
+    xf[:, :512] *= 1e6
+    xf[1::2, 512:] *= 1e-20
+    xb = O.f32_to_bf16_bits(xf)
+    qw, qz, sc = to_dev(d["qweight"], cuda), to_dev(d["qzeros"], cuda), to_dev(d["scales"], cuda)
+    for M in (1, 2, 4, 8, 16, 40):
+        y = L.awq_linear(_bf16_dev(xb[:M], cuda), qw, qz, sc, None, g)
+        ref = O.c_awq_linear(xb[:M], d["qweight"], d["qzeros"], d["scales"], None, M, K, N, g,
+                             act="bf16")
+        yf, rf = O.bf16_bits_to_f32(bits16(y)), O.bf16_bits_to_f32(ref)
+        assert np.isfinite(yf).all()
+        assert O.max_rel_err(yf, rf) < TIGHT_BF16, M

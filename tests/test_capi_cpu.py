@@ -41,10 +41,18 @@ FAKE = ctypes.c_void_p(0x10000)  # 16-byte aligned, never dereferenced
 def test_awq_validation_codes():
     lib = _lib.load()
     f = lib.lmrs_awq_linear
-    # act dtype must be fp16
-    assert f(FAKE, FAKE, FAKE, FAKE, FAKE, None, 4, 256, 64, 128, 0, None, 0, None) == _lib.LMRS_ERR_DTYPE
-    # N % 32
-    assert f(FAKE, FAKE, FAKE, FAKE, FAKE, None, 4, 256, 40, 128, 1, None, 0, None) == _lib.LMRS_ERR_SHAPE
+    # act dtype must be bf16 (0) or fp16 (1); f32 (2) and unknown codes are rejected
+    assert f(FAKE, FAKE, FAKE, FAKE, FAKE, None, 4, 256, 64, 128, 2, None, 0, None) == _lib.LMRS_ERR_DTYPE
+    assert f(FAKE, FAKE, FAKE, FAKE, FAKE, None, 4, 256, 64, 128, 7, None, 0, None) == _lib.LMRS_ERR_DTYPE
+    # N % 32, for both activation types
+    for act in (0, 1):
+        assert f(FAKE, FAKE, FAKE, FAKE, FAKE, None, 4, 256, 40, 128, act, None, 0,
+                 None) == _lib.LMRS_ERR_SHAPE
+    # the bf16 dequant rejects f32 output and the same shape errors
+    d = lib.lmrs_awq_dequant_dtype
+    assert d(FAKE, FAKE, FAKE, FAKE, 256, 64, 128, 2, None) == _lib.LMRS_ERR_DTYPE
+    assert d(FAKE, FAKE, FAKE, FAKE, 256, 60, 128, 0, None) == _lib.LMRS_ERR_SHAPE
+    assert d(FAKE, FAKE, FAKE, FAKE, 200, 64, 128, 0, None) == _lib.LMRS_ERR_GROUP
     # group must divide K and be a multiple of 64
     assert f(FAKE, FAKE, FAKE, FAKE, FAKE, None, 4, 256, 64, 96, 1, None, 0, None) == _lib.LMRS_ERR_GROUP
     assert f(FAKE, FAKE, FAKE, FAKE, FAKE, None, 4, 192, 64, 128, 1, None, 0, None) == _lib.LMRS_ERR_GROUP
