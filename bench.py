@@ -567,6 +567,9 @@ def run_decode(args, device, dist_on, world, rank, preset=None, batches=None, ct
     preset = preset or args.decode
     attr, ctx0, batches0, cname = DECODE_PRESETS[preset]
     cfg = getattr(D, attr)
+    if getattr(args, "act", None) and cfg.quant == "awq":
+        import dataclasses
+        cfg = dataclasses.replace(cfg, act=args.act)
     ctx = ctx or args.ctx or ctx0
     if batches is None:
         batches = tuple(int(b) for b in args.batch.split(",")) if args.batch else batches0
@@ -661,7 +664,7 @@ def run_decode(args, device, dist_on, world, rank, preset=None, batches=None, ct
             "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": best["ms_median"] if best else None, "higher_is_better": True,
             "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
-            "dtype": "f16 act, int4 weights" if cfg.quant == "awq" else "bf16 act, e4m3 W8A8",
+            "dtype": f"{cfg.act} act, int4 weights" if cfg.quant == "awq" else "bf16 act, e4m3 W8A8",
             "data": "synthetic (random-init weights, random KV cache and token ids)",
             "config": {"workload": f"{cname}: {preset} decoder, one decode step at ctx {ctx}, "
                                    f"value = largest batch that fits",
@@ -694,6 +697,8 @@ def main():
                          "(tensor parallel over the torchrun ranks)")
     ap.add_argument("--batch", default=None, help="decode batches, comma separated")
     ap.add_argument("--ctx", type=int, default=None, help="decode context length")
+    ap.add_argument("--act", choices=["bf16", "f16"], default=None,
+                    help="activation dtype of the AWQ decoder (default bf16, config 3's)")
     ap.add_argument("--no-decode", action="store_true",
                     help="skip the configs 3/4 decode blocks of the default line")
     args = ap.parse_args()

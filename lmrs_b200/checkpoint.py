@@ -295,6 +295,9 @@ def decoder_config(config: dict):
                               "(rope_theta) is implemented")
     H = int(config["hidden_size"])
     heads = int(config["num_attention_heads"])
+    # activations follow the checkpoint's torch_dtype: fp16 for an AWQ model
+    # saved in fp16, bf16 otherwise (the FP8 linear always takes bf16)
+    f16 = str(config.get("torch_dtype", "")).lower() in ("float16", "fp16", "half")
     return DecoderConfig(
         layers=int(config["num_hidden_layers"]), hidden=H, heads=heads,
         kv_heads=int(config.get("num_key_value_heads", heads)),
@@ -302,7 +305,8 @@ def decoder_config(config: dict):
         intermediate=int(config["intermediate_size"]), vocab=int(config["vocab_size"]),
         quant=spec.method, group=spec.group,
         rope_theta=float(config.get("rope_theta", 10000.0)),
-        eps=float(config.get("rms_norm_eps", 1e-6)))
+        eps=float(config.get("rms_norm_eps", 1e-6)),
+        act="f16" if (f16 and spec.method == "awq") else "bf16")
 
 
 # ------------------------------------------------------------ decoder weights
@@ -396,7 +400,7 @@ def load_decoder_weights(path_or_ck, rank: int = 0, world: int = 1, device="cpu"
     if cfg.heads % R or cfg.kv_heads % R or cfg.intermediate % R or cfg.vocab % R:
         raise CheckpointError(f"tensor parallelism {R} does not divide heads / kv heads / "
                               "intermediate / vocab")
-    act = torch.float16 if spec.method == "awq" else torch.bfloat16
+    act = cfg.act_dtype
     d, hq, hkv, I = cfg.head_dim, cfg.heads // R, cfg.kv_heads // R, cfg.intermediate // R
     dev = torch.device(device)
 
@@ -487,7 +491,7 @@ def hf_config(cfg) -> dict:
             "num_attention_heads": cfg.heads, "num_key_value_heads": cfg.kv_heads,
             "head_dim": cfg.head_dim, "intermediate_size": cfg.intermediate,
             "vocab_size": cfg.vocab, "rope_theta": cfg.rope_theta, "rms_norm_eps": cfg.eps,
-            "torch_dtype": "float16" if cfg.quant == "awq" else "bfloat16",
+            "torch_dtype": "float16" if cfg.act == "f16" else "bfloat16",
             "tie_word_embeddings": False, "quantization_config": qc}
 
 

@@ -40,10 +40,23 @@ class DecoderConfig:
     head_dim: int
     intermediate: int
     vocab: int
-    quant: str            # "awq" (W4A16, fp16 activations) or "fp8" (W8A8, bf16 activations)
+    quant: str            # "awq" (W4A16) or "fp8" (W8A8)
     group: int = 128
     rope_theta: float = 500000.0
     eps: float = 1e-5
+    # activation / embedding / norm / KV dtype: "bf16" (the reference model's,
+    # crates/model/src/loader/safetensors.rs:274) or "f16" (AWQ only; the FP8
+    # linear takes bf16)
+    act: str = "bf16"
+
+    def __post_init__(self):
+        if self.act not in ("bf16", "f16") or (self.quant == "fp8" and self.act != "bf16"):
+            raise ValueError(f"activation dtype {self.act!r} with {self.quant}: AWQ takes bf16 "
+                             "or f16, FP8 bf16")
+
+    @property
+    def act_dtype(self) -> torch.dtype:
+        return torch.bfloat16 if self.act == "bf16" else torch.float16
 
     def projections(self, world: int = 1):
         """(K, N) of one rank's qkv, o, gate_up, down projections."""
@@ -111,7 +124,7 @@ class QuantDecoder:
         self.hq, self.hkv = cfg.heads // world, cfg.kv_heads // world
         self.inter = cfg.intermediate // world
         self.vocab_local = cfg.vocab // world
-        self.act = torch.float16 if cfg.quant == "awq" else torch.bfloat16
+        self.act = cfg.act_dtype
         d, H = cfg.head_dim, cfg.hidden
         # shard-local weights from a per-rank stream; replicated tensors (embedding,
         # norms) from one stream shared by all ranks

@@ -123,7 +123,7 @@ def _fp8(K, N, gen, per_tensor=False):
 
 def _write_model(path, cfg, per_tensor=False):
     gen = torch.Generator().manual_seed(1)
-    act = torch.float16 if cfg.quant == "awq" else torch.bfloat16
+    act = cfg.act_dtype
     d, H, I = cfg.head_dim, cfg.hidden, cfg.intermediate
     shapes = {"q": (H, cfg.heads * d), "k": (H, cfg.kv_heads * d), "v": (H, cfg.kv_heads * d),
               "o": (cfg.heads * d, H), "gate": (H, I), "up": (H, I), "down": (I, H)}
