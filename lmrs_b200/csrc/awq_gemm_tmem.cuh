@@ -46,27 +46,40 @@ namespace lmrs {
 
 constexpr int kAgtCh = 128;          // output channels per tile (UMMA M)
 constexpr int kAgtWords = kAgtCh / 8;
-constexpr int kAgtBK = 64;           // k rows per stage
+constexpr int kAgtBK = 64;           // k rows of one TMA box / UMMA sub-tile
 constexpr int kAgtEpiWarp0 = 2;
 constexpr int kAgtDqWarp0 = 6;
 constexpr int kAgtDqGroups = 4;      // dequant warp groups, alternating K-blocks
 constexpr int kAgtThreads = 32 * (kAgtDqWarp0 + 4 * kAgtDqGroups);  // 704
 
-// Shared-memory ring of S stages (token tile + packed weights) and a TMEM ring of
-// R stages (dequantised weights, 32 columns each), R <= S.  One tcgen05.commit
-// per K-block (on the shared-memory slot's barrier) frees both: the dequant
-// warps reuse TMEM stage kg % R after the commit of K-block kg - R.  (A commit
-// costs ~280 cycles in the issuing thread; two per K-block are too many.)
+// Shared-memory ring of S stages (token tile + packed weights of one BK-deep
+// K-block) and a TMEM ring of R stages (dequantised weights, BK / 2 columns
+// each), R <= S.  One tcgen05.commit per K-block (on the shared-memory slot's
+// barrier) frees both: the dequant warps reuse TMEM stage kg % R after the
+// commit of K-block kg - R.  The MMA thread's own work per K-block bounds the
+// kernel: measured with a clock64 trace of a copy of the kernel (config 1,
+// M = 4096), four UMMA issues take ~330 cycles, a commit ~200 and a check of an
+// mbarrier that completed long before ~130, against ~660 cycles of tensor work
+// per 64-deep K-block; so BK = 128 (eight UMMAs per commit and per wait) where
+// K and the quantisation group allow it.
 // Accumulators: two BT-column buffers when they leave room for two A stages, one
-// for BT = 256 (the A ring then buffers 8 K-blocks while the epilogue drains).
-template <int BT>
+// for BT = 256 (the A ring then keeps filling while the epilogue drains).
+template <int BT, int BK = 64>
 struct AgtLayout {
+  static constexpr int kSub = BK / kAgtBK;           // 64-deep token boxes per K-block
   static constexpr int kAccBufs = 2 * BT + 64 <= 512 ? 2 : 1;
-  static constexpr int kStages = BT == 128 ? 10 : (BT == 192 ? 7 : 6);  // as deep as shared memory allows
-  static constexpr int kATmem = (512 - kAccBufs * BT) / 32;  // A stages TMEM has room for
+  static constexpr int kStages = (BT == 128 ? 10 : (BT == 192 ? 7 : 6)) / kSub;  // as deep as smem allows
+  static constexpr int kACols = BK / 2;              // TMEM columns of one A stage
+  static constexpr int kATmem = (512 - kAccBufs * BT) / kACols;  // A stages TMEM has room for
   static constexpr int kAStages = kATmem < kStages ? (kATmem < 8 ? kATmem : 8) : (kStages < 8 ? kStages : 8);
-  static constexpr int kX = BT * kAgtBK * 2;        // token stage (1024-aligned)
-  static constexpr int kW = kAgtBK * kAgtWords * 4; // packed weight rows, 4 KB
+  // Dequant warp groups (four warps each, one per TMEM lane quarter) taking
+  // K-blocks round robin: no more groups than ring stages (see the dequant
+  // loop for why), and enough that each has several K-blocks of time.
+  static constexpr int kGroups = kStages < kAgtDqGroups ? kStages : kAgtDqGroups;
+  static constexpr int kThreads = 32 * (kAgtDqWarp0 + 4 * kGroups);
+  static constexpr int kXSub = BT * kAgtBK * 2;      // one 64-deep token box
+  static constexpr int kX = kSub * kXSub;            // token stage (1024-aligned)
+  static constexpr int kW = BK * kAgtWords * 4;      // packed weight rows, 4 / 8 KB
   static constexpr int kSmall = kW;
   static constexpr uint32_t kTx = kX + kW;
   static constexpr uint32_t kTmemA = kAccBufs * BT; // A stages after the accumulators
@@ -77,9 +90,11 @@ struct AgtLayout {
   static_assert(kSmem <= 227 * 1024, "shared memory per CTA");
   static_assert(kX % 1024 == 0, "128B-swizzled token stages are 1024-byte aligned");
   static_assert(kSmall % 128 == 0, "TMA destinations are 128-byte aligned");
-  static_assert(kAccBufs * BT + 32 * kAStages <= 512 && kAStages >= 2 && kAStages <= kStages,
+  static_assert(kAccBufs * BT + kACols * kAStages <= 512 && kAStages >= 2 && kAStages <= kStages,
                 "TMEM columns");
   static_assert(BT % 16 == 0 && BT <= 256, "UMMA N");
+  static_assert(BK == 64 || BK == 128, "K-block depth");
+  static_assert(kGroups >= 3 && kGroups <= kStages && kAStages <= kStages, "wait ordering");
 };
 
 // Tile t -> (first token m0, first channel n0): groups of kTcGroupM token tiles
@@ -95,12 +110,12 @@ __device__ __forceinline__ void agt_coords(int t, int m_tiles, int n_tiles, int&
   n0 = (local / gm) * kAgtCh;
 }
 
-template <int BT, typename T>
-__global__ void __launch_bounds__(kAgtThreads, 1) awq_gemm_tmem_kernel(
+template <int BT, int BK, typename T>
+__global__ void __launch_bounds__(AgtLayout<BT, BK>::kThreads, 1) awq_gemm_tmem_kernel(
     const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_q,
     const __half* __restrict__ scales, const uint32_t* __restrict__ qzeros,
     T* __restrict__ y, const T* __restrict__ bias, int M, int K, int N, int group) {
-  using L = AgtLayout<BT>;
+  using L = AgtLayout<BT, BK>;
   constexpr int S = L::kStages, R = L::kAStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sx = align1024(smem_raw);
@@ -113,7 +128,7 @@ __global__ void __launch_bounds__(kAgtThreads, 1) awq_gemm_tmem_kernel(
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int KB = K / kAgtBK;
+  const int KB = K / BK;   // K % BK == 0 (BK = 128 only when K and the group allow it)
   const int n_tiles = (N + kAgtCh - 1) / kAgtCh;
   const int m_tiles = (M + BT - 1) / BT;
   const int tiles = n_tiles * m_tiles;
@@ -157,9 +172,12 @@ __global__ void __launch_bounds__(kAgtThreads, 1) awq_gemm_tmem_kernel(
           break;
         if (lane == 0) {
           mbar_arrive_expect_tx(&full[s], L::kTx);
-          tma_load_2d_hint(&tm_x, &full[s], sx + s * L::kX, kb * kAgtBK, m0, keep);
+#pragma unroll
+          for (int sub = 0; sub < L::kSub; ++sub)
+            tma_load_2d_hint(&tm_x, &full[s], sx + s * L::kX + sub * L::kXSub,
+                             kb * BK + sub * kAgtBK, m0, keep);
         } else {
-          tma_load_2d(&tm_q, &full[s], ssm + s * L::kSmall, n0 / 8, kb * kAgtBK);
+          tma_load_2d(&tm_q, &full[s], ssm + s * L::kSmall, n0 / 8, kb * BK);
         }
       }
     }
@@ -177,16 +195,20 @@ __global__ void __launch_bounds__(kAgtThreads, 1) awq_gemm_tmem_kernel(
         const uint32_t d = tmem + a * BT;
         for (int kb = 0; kb < KB; ++kb, ++kg) {
           const int s = kg % S, ar = kg % R;
-          ok = mbar_wait(&full[s], (kg / S) & 1, kErrWaitFull) &&
-               mbar_wait(&afull[ar], (kg / R) & 1, kErrWaitDequant);
+          // The MMA reads the token tile through the async proxy: this thread
+          // observes full[s] itself rather than relying on the dequant warps'
+          // afull arrival to order the TMA writes for the tensor core.
+          ok = mbar_wait_fast(&full[s], (kg / S) & 1, kErrWaitFull) &&
+               mbar_wait_fast(&afull[ar], (kg / R) & 1, kErrWaitDequant);
           if (!ok) break;
           tc_fence_after();
           const uint32_t xs = smem_u32(sx + s * L::kX);
-          const uint32_t acol = tmem + L::kTmemA + ar * 32;
+          const uint32_t acol = tmem + L::kTmemA + ar * L::kACols;
 #pragma unroll
-          for (int kk = 0; kk < kAgtBK / 16; ++kk)
-            umma_f16_tmem_a(d, acol + kk * 8, make_sdesc(xs + kk * 32, 16, 1024), idesc,
-                            (kb | kk) != 0 ? 1u : 0u);
+          for (int kk = 0; kk < BK / 16; ++kk)
+            umma_f16_tmem_a(d, acol + kk * 8,
+                            make_sdesc(xs + (kk >> 2) * L::kXSub + (kk & 3) * 32, 16, 1024),
+                            idesc, (kb | kk) != 0 ? 1u : 0u);
           umma_commit(&empty[s]);  // slot s and TMEM stage ar are free
         }
         if (ok) umma_commit(&acc->full[a]);
@@ -246,6 +268,7 @@ __global__ void __launch_bounds__(kAgtThreads, 1) awq_gemm_tmem_kernel(
     // 24 + hc, each lane one channel with k-pair kp in column kp.  The weight
     // box arrives with the 64-byte swizzle, so the 8-row reads are
     // conflict-free: 8 wavefronts per warp and K-block.
+    constexpr int G = L::kGroups;
     const int quarter = warp & 3;
     const int dgrp = (warp - kAgtDqWarp0) >> 2;
     const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
@@ -265,7 +288,7 @@ __global__ void __launch_bounds__(kAgtThreads, 1) awq_gemm_tmem_kernel(
         ftile = tt;
         agt_coords<BT>(blockIdx.x + tt * gridDim.x, m_tiles, n_tiles, fm0, n0);
       }
-      const int gi = static_cast<int>(kg % KB) * kAgtBK / group;
+      const int gi = static_cast<int>(kg % KB) * BK / group;  // BK <= group or BK == 64
       const int n = n0 + 8 * wt;
       if (n < N) {  // N % 8 == 0: the whole word is in range
         sv = *reinterpret_cast<const uint4*>(scales + static_cast<int64_t>(gi) * N + n);
@@ -276,19 +299,26 @@ __global__ void __launch_bounds__(kAgtThreads, 1) awq_gemm_tmem_kernel(
     uint32_t z_nxt;
     fetch(dgrp, s_nxt, z_nxt);
     bool ok = true;
-    for (uint32_t kg = dgrp; kg < static_cast<uint32_t>(total) && ok; kg += kAgtDqGroups) {
+    for (uint32_t kg = dgrp; kg < static_cast<uint32_t>(total) && ok; kg += G) {
       const uint4 s_cur = s_nxt;
       const uint32_t z_cur = z_nxt >> (16 * codd);
-      fetch(kg + kAgtDqGroups, s_nxt, z_nxt);
+      fetch(kg + G, s_nxt, z_nxt);
       const int s = kg % S, ar = kg % R;
-      if (!(ok = mbar_wait(&full[s], (kg / S) & 1, kErrWaitFull))) break;
-      // TMEM stage ar was last read by the MMAs of K-block j = kg - R: wait for
-      // its commit (on slot j % S).  That phase cannot have been overtaken: the
-      // next commit on that slot is K-block j + S > kg, issued after kg's MMAs.
+      // A parity wait for phase P of a barrier is only sound once phase P - 1
+      // has completed (in phase P - 1 the parity test reads "done").  Several
+      // groups share these barriers, so the order of the two waits carries it:
+      //  1. TMEM stage ar was last read by the MMAs of K-block j = kg - R: wait
+      //     for their commit (phase j / S of empty[j % S]).  Its phase before,
+      //     the commit of j - S, is covered by this group's previous wait here
+      //     (the commit of kg - G - R >= j - S since G <= S; commits complete
+      //     in order); the phase after needs K-block j + S >= kg.
+      //  2. Then slot s (phase kg / S of full[s]): its phase before belongs to
+      //     K-block kg - S <= j, whose tokens the MMAs of step 1 consumed.
       if (kg >= static_cast<uint32_t>(R)) {
         const uint32_t j = kg - R;
         if (!(ok = mbar_wait(&empty[j % S], (j / S) & 1, kErrWaitAccum))) break;
       }
+      if (!(ok = mbar_wait(&full[s], (kg / S) & 1, kErrWaitFull))) break;
       const uint32_t s4[4] = {s_cur.x, s_cur.y, s_cur.z, s_cur.w};
       uint32_t zz[4];
       AwqScale2 ss[4];
@@ -298,9 +328,9 @@ __global__ void __launch_bounds__(kAgtThreads, 1) awq_gemm_tmem_kernel(
         ss[n] = awq_scale2<T>(prmt(s4[n], s4[n], sdup));  // channel 8 wt + 2n + codd
       }
       const uint8_t* sm = ssm + s * L::kSmall;
-      const uint32_t acol = tmem + lane_addr + L::kTmemA + ar * 32;
+      const uint32_t acol = tmem + lane_addr + L::kTmemA + ar * L::kACols;
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
+      for (int h = 0; h < BK / 32; ++h) {
         const int r = 32 * h + lane;  // row this lane addresses for ldmatrix
         uint32_t d[4];
         ldsm_x4_t(d, smem_u32(sm + r * (kAgtWords * 4) + ((quarter ^ ((r >> 1) & 3)) << 4)));

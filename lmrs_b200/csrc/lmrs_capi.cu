@@ -33,6 +33,7 @@
 #include "fp8_swap.cuh"
 #include "awq_tmem.cuh"
 #include "awq_gemm_tmem.cuh"
+#include "awq_gemm_pair.cuh"
 
 namespace {
 
@@ -69,6 +70,8 @@ struct Tuning {
   int awq_tmem_ctas_per_sm = 2;
   int awq_gemm_tmem = 1;     // prefill: GEMM with the weights as the TMEM A operand (0: smem-staged)
   int awq_gemm_tmem_bt = 256;  // its token tile (128, 192 or 256; 256 measured fastest at every M)
+  int awq_gemm_tmem_bk = 128;  // its K-block depth at 256 tokens (128 where K and the group allow; 64)
+  int awq_gemm_tmem_pair = 0;  // above 128 tokens, N % 256 == 0: the CTA-pair (cta_group::2) form
   int awq_i8_max_m = 1;      // M up to this (2 at most): packed bytes as integer MMA operands
   int awq_i8_slots = 5;      // its ring slots at most (fewer when the grid fills the SMs)
   int awq_i8_ctas_per_sm = 2;
@@ -566,24 +569,25 @@ int awq_swap_launch(T* y, const T* x, const int32_t* qw, const int32_t* qz, cons
   return awq_swap_launch_nt<128, T>(y, x, qw, qz, sc, bias, M, K, N, group, stream, dev);
 }
 
-template <int BT, typename T>
+template <int BT, int BK, typename T>
 int awq_gemm_tmem_launch_t(T* y, const T* x, const int32_t* qw, const int32_t* qz,
                            const __half* sc, const T* bias, int M, int K, int N, int group,
                            cudaStream_t stream, int dev) {
-  using L = lmrs::AgtLayout<BT>;
+  using L = lmrs::AgtLayout<BT, BK>;
   CUtensorMap tx, tq;
   int rc;
   if ((rc = make_tmap(&tx, lmrs::Act<T>::kTma, x, K, M, uint64_t(K) * 2, 64, BT,
                       CU_TENSOR_MAP_SWIZZLE_128B)))
     return rc;
   if ((rc = make_tmap(&tq, CU_TENSOR_MAP_DATA_TYPE_INT32, qw, N / 8, K, uint64_t(N / 8) * 4,
-                      lmrs::kAgtWords, lmrs::kAgtBK, CU_TENSOR_MAP_SWIZZLE_64B)))
+                      lmrs::kAgtWords, BK, CU_TENSOR_MAP_SWIZZLE_64B)))
     return rc;
-  if ((rc = ensure_smem_of<lmrs::awq_gemm_tmem_kernel<BT, T>>(L::kSmem, dev))) return rc;
+  if ((rc = ensure_smem_of<lmrs::awq_gemm_tmem_kernel<BT, BK, T>>(L::kSmem, dev))) return rc;
   const int tiles = ((N + lmrs::kAgtCh - 1) / lmrs::kAgtCh) * ((M + BT - 1) / BT);
   const int grid = tiles < sm_count(dev) ? tiles : sm_count(dev);
-  rc = launch_ex(lmrs::awq_gemm_tmem_kernel<BT, T>, grid, 0, lmrs::kAgtThreads, L::kSmem, stream,
-                 tx, tq, sc, reinterpret_cast<const uint32_t*>(qz), y, bias, M, K, N, group);
+  rc = launch_ex(lmrs::awq_gemm_tmem_kernel<BT, BK, T>, grid, 0, L::kThreads, L::kSmem,
+                 stream, tx, tq, sc, reinterpret_cast<const uint32_t*>(qz), y, bias, M, K, N,
+                 group);
   return rc ? rc : after_launch();
 }
 
@@ -594,10 +598,37 @@ int awq_gemm_tmem_launch(T* y, const T* x, const int32_t* qw, const int32_t* qz,
   const int f = g_tune.awq_gemm_tmem_bt;
   const int bt = (f == 128 || f == 192) ? f : 256;
   if (bt == 128)
-    return awq_gemm_tmem_launch_t<128, T>(y, x, qw, qz, sc, bias, M, K, N, group, stream, dev);
+    return awq_gemm_tmem_launch_t<128, 64, T>(y, x, qw, qz, sc, bias, M, K, N, group, stream, dev);
   if (bt == 192)
-    return awq_gemm_tmem_launch_t<192, T>(y, x, qw, qz, sc, bias, M, K, N, group, stream, dev);
-  return awq_gemm_tmem_launch_t<256, T>(y, x, qw, qz, sc, bias, M, K, N, group, stream, dev);
+    return awq_gemm_tmem_launch_t<192, 64, T>(y, x, qw, qz, sc, bias, M, K, N, group, stream, dev);
+  // 128-deep K-blocks where every K-block lies in one quantisation group
+  if (g_tune.awq_gemm_tmem_bk != 64 && K % 128 == 0 && group % 128 == 0)
+    return awq_gemm_tmem_launch_t<256, 128, T>(y, x, qw, qz, sc, bias, M, K, N, group, stream, dev);
+  return awq_gemm_tmem_launch_t<256, 64, T>(y, x, qw, qz, sc, bias, M, K, N, group, stream, dev);
+}
+
+// CTA-pair version of the prefill GEMM (256 channels x 256 tokens per pair).
+template <typename T>
+int awq_gemm_pair_launch(T* y, const T* x, const int32_t* qw, const int32_t* qz, const __half* sc,
+                         const T* bias, int M, int K, int N, int group, cudaStream_t stream,
+                         int dev) {
+  using L = lmrs::ApLayout;
+  CUtensorMap tx, tq;
+  int rc;
+  if ((rc = make_tmap(&tx, lmrs::Act<T>::kTma, x, K, M, uint64_t(K) * 2, 64, 128,
+                      CU_TENSOR_MAP_SWIZZLE_128B)))
+    return rc;
+  if ((rc = make_tmap(&tq, CU_TENSOR_MAP_DATA_TYPE_INT32, qw, N / 8, K, uint64_t(N / 8) * 4,
+                      lmrs::kAgtWords, lmrs::kAgtBK, CU_TENSOR_MAP_SWIZZLE_64B)))
+    return rc;
+  if ((rc = ensure_smem_of<lmrs::awq_gemm_pair_kernel<T>>(L::kSmem, dev))) return rc;
+  const int tiles = ((N + lmrs::kApCh - 1) / lmrs::kApCh) * ((M + lmrs::kApBT - 1) / lmrs::kApBT);
+  const int max_pairs = sm_count(dev) / 2;
+  const int pairs = tiles < max_pairs ? tiles : max_pairs;
+  rc = launch_cluster(lmrs::awq_gemm_pair_kernel<T>, 2 * pairs, 2, lmrs::kApThreads, L::kSmem,
+                      stream, tx, tq, sc, reinterpret_cast<const uint32_t*>(qz), y, bias, M, K, N,
+                      group);
+  return rc ? rc : after_launch();
 }
 
 template <typename T>
@@ -694,8 +725,11 @@ int awq_linear_dispatch(T* y, const T* x, const int32_t* qweight, const int32_t*
     return awq_swap_launch<T>(y, x, qweight, qzeros, sc, bias, M, K, N, group, st, dev);
   // up to one token tile, more 128-channel tiles than SMs leave a tail wave the
   // 256-channel smem-staged tiles avoid
-  if (g_tune.awq_gemm_tmem && (M > 128 || (N + lmrs::kAgtCh - 1) / lmrs::kAgtCh <= sm_count(dev)))
+  if (g_tune.awq_gemm_tmem && (M > 128 || (N + lmrs::kAgtCh - 1) / lmrs::kAgtCh <= sm_count(dev))) {
+    if (g_tune.awq_gemm_tmem_pair && M > 128 && N % lmrs::kApCh == 0)
+      return awq_gemm_pair_launch<T>(y, x, qweight, qzeros, sc, bias, M, K, N, group, st, dev);
     return awq_gemm_tmem_launch<T>(y, x, qweight, qzeros, sc, bias, M, K, N, group, st, dev);
+  }
   if (g_tune.awq_gemm_pair)
     return awq_gemm2_launch<T>(y, x, qweight, qzeros, sc, bias, M, K, N, group, st, dev);
   return awq_gemm_launch<T>(y, x, qweight, qzeros, sc, bias, M, K, N, group, st, dev);
@@ -919,6 +953,8 @@ int lmrs_set_tuning(const char* key, int value) {
   else if (!strcmp(key, "awq_tmem_max_m")) g_tune.awq_tmem_max_m = value;
   else if (!strcmp(key, "awq_gemm_tmem")) g_tune.awq_gemm_tmem = value ? 1 : 0;
   else if (!strcmp(key, "awq_gemm_tmem_bt")) g_tune.awq_gemm_tmem_bt = value;
+  else if (!strcmp(key, "awq_gemm_tmem_pair")) g_tune.awq_gemm_tmem_pair = value ? 1 : 0;
+  else if (!strcmp(key, "awq_gemm_tmem_bk")) g_tune.awq_gemm_tmem_bk = value;
   else if (!strcmp(key, "awq_tmem_min_m")) g_tune.awq_tmem_min_m = value;
   else if (!strcmp(key, "awq_tmem_min_m_wide")) g_tune.awq_tmem_min_m_wide = value;
   else if (!strcmp(key, "awq_tmem_cluster")) g_tune.awq_tmem_cluster = value;

@@ -506,3 +506,49 @@ def test_linear_bf16_large_values(cuda):
         yf, rf = O.bf16_bits_to_f32(bits16(y)), O.bf16_bits_to_f32(ref)
         assert np.isfinite(yf).all()
         assert O.max_rel_err(yf, rf) < TIGHT_BF16, M
+
+
+@pytest.mark.parametrize("act", ["f16", "bf16"])
+@pytest.mark.parametrize("M,K,N,g", [(129, 1024, 768, 128), (256, 2048, 512, 64),
+                                     (300, 3072, 1280, 256), (1000, 1024, 2048, 128),
+                                     (2100, 4096, 1024, 128)])
+def test_gemm_pair(cuda, act, M, K, N, g):
+    """The CTA-pair prefill GEMM (cta_group::2, 256 channels x 256 tokens per
+    pair, weights dequantised into each CTA's TMEM): ragged token tiles, groups
+    of 64/128/256 rows, several tiles per pair, both activation types,
+    deterministic across calls."""
+    import torch
+    import lmrs_b200 as L
+    try:
+        L.set_tuning("awq_gemm_tmem_pair", 1)
+        if act == "bf16":
+            err, (x, qw, qz, sc, b, y) = _awq_case_bf16(cuda, M, K, N, g, 7000 + M)
+            tol = TIGHT_BF16
+        else:
+            err, (x, qw, qz, sc, b, y) = _awq_case(cuda, M, K, N, g, 7000 + M)
+            tol = TIGHT
+        assert torch.equal(L.awq_linear(x, qw, qz, sc, b, g), y), "nondeterministic"
+    finally:
+        L.set_tuning("awq_gemm_tmem_pair", 0)
+    assert err < tol, err
+    assert L.read_device_error() == 0
+
+
+@pytest.mark.slow
+def test_gemm_pair_config1_vs_reference(cuda, ref_ffi):
+    """Config 1 (K=4096, N=14336) at M=4096 on the CTA-pair GEMM against the
+    reference's linear_fwd on the dequantised weights, every output."""
+    import lmrs_b200 as L
+    M, K, N, g = 4096, 4096, 14336, 128
+    d = O.awq_inputs(M, K, N, g, seed=0)
+    qw, qz, sc, x, _ = _awq_dev(d, cuda)
+    w_nk = L.awq_dequant(qw, qz, sc, g).t().contiguous()
+    y_ref = ref_linear(ref_ffi, x, w_nk, None, 1)
+    try:
+        L.set_tuning("awq_gemm_tmem_pair", 1)
+        y = L.awq_linear(x, qw, qz, sc, None, g)
+    finally:
+        L.set_tuning("awq_gemm_tmem_pair", 0)
+    err = O.max_rel_err(y.cpu().numpy(), y_ref.cpu().numpy())
+    assert err < TIGHT, err
+    assert L.read_device_error() == 0
