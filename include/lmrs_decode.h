@@ -63,10 +63,14 @@ LMRS_API int lmrs_rope_kv_write(void* q_out, void* key_cache, void* value_cache,
                                 int block_size, int max_blocks_per_seq, int dtype,
                                 lmrs_stream_t stream);
 
-/* Workspace for lmrs_paged_attention_decode: 0 (the context splits of one
- * sequence and KV head form a thread-block cluster and merge their partials in
- * distributed shared memory).  Kept so that bindings written against a scratch
- * buffer keep working. */
+/* Workspace for lmrs_paged_attention_decode with these sizes on the current
+ * device: 0 when the context splits of each sequence and KV head are few enough
+ * (<= 8) to merge their partials in a thread-block cluster's distributed shared
+ * memory; otherwise (small batches, long contexts) room for every split's
+ * fp32 (O, m, l) partial plus one arrival counter per sequence and KV head.
+ * The workspace must be zero-filled before its first use; every call leaves
+ * the counters at zero again.  Calls that overlap on the GPU need separate
+ * workspaces. */
 LMRS_API size_t lmrs_paged_attention_workspace_bytes(int num_seqs, int num_heads,
                                                      int num_kv_heads, int max_context);
 
@@ -76,7 +80,9 @@ LMRS_API size_t lmrs_paged_attention_workspace_bytes(int num_seqs, int num_heads
  *   max_context   an upper bound of context_lens (sizes the context split),
  *   kv_head_map   0: q head h reads KV head h % num_kv_heads (the reference's
  *                 kernel), 1: h / (num_heads / num_kv_heads) (grouped heads),
- *   workspace     unused (may be NULL).
+ *   workspace     lmrs_paged_attention_workspace_bytes() bytes, 16-byte aligned,
+ *                 zero-filled before first use (NULL when that size is 0);
+ *                 LMRS_ERR_WORKSPACE if missing or smaller.
  * head_size must be 128; num_heads / num_kv_heads <= 16.  out[s, h, :] =
  * softmax(scale * q . k) v over positions [0, context_lens[s]); context 0 gives 0. */
 LMRS_API int lmrs_paged_attention_decode(void* out, const void* query, const void* key_cache,

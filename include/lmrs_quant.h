@@ -89,7 +89,10 @@ LMRS_API int lmrs_version(void);
  * "fp8_swap_max_m", "fp8_swap_cluster", "awq_tmem_min_m", "awq_tmem_max_m",
  * "awq_tmem_min_m_wide", "awq_tmem_cluster", "awq_tmem_ctas_per_sm", "awq_gemm_tmem",
  * "awq_gemm_tmem_bt", "awq_gemv4", "awq_gemv_slots", "awq_gemv4_slots",
- * "gemv_box_rows", "attn_stages", "attn_ctas_per_sm", "awq_i8_max_m" (1-2 token
+ * "gemv_box_rows", "attn_stages", "attn_ctas_per_sm", "attn_global_merge" (small
+ * batches split the context over several 8-CTA clusters merged through the
+ * attention workspace, default 1), "attn_multi_min_ctx" (... only when
+ * max_context exceeds it, default 2048), "awq_i8_max_m" (1-2 token
  * AWQ on the integer MMA path up to this M, default 1; 0 = fp16 GEMV),
  * "awq_i8_slots", "awq_i8_ctas_per_sm", "awq_i8_cluster", "awq_i8_box_rows", "pdl" (programmatic
  * dependent launch on every kernel, default 1), "wait_limit_kcycles" (how long a

@@ -70,16 +70,45 @@ int silu_launch(void* out, uint8_t* q, float* s, const void* gu, int rows, int i
 // context split of the decode attention: as many splits as keep the grid within
 // one wave of ~2 CTAs per SM (rounded down: 128 (sequence, KV head) pairs at
 // batch 16 run 2 splits in 32.6 us against 44.8 us for 3, which spill into a
-// second wave), whole 64-position tiles, at most one cluster's worth of splits
-// (they merge in distributed shared memory)
-void attn_split(int seqs, int hkv, int max_ctx, int sms, int* splits, int* span) {
+// second wave), whole 64-position tiles.  Up to kAttnMaxCluster splits merge in
+// one cluster's shared memory; more (small batches) come in whole clusters
+// (splits a multiple of kAttnMaxCluster, trailing splits possibly empty) whose
+// merged partials meet in the workspace.
+struct AttnSplit {
+  int splits, span;
+  int clusters;   // clusters per (sequence, KV head); > 1 needs the workspace
+};
+
+AttnSplit attn_split(int seqs, int hkv, int max_ctx, int sms) {
   const int tiles = max_ctx > 0 ? (max_ctx + lmrs::kAttnTile - 1) / lmrs::kAttnTile : 1;  // 64-pos units
   const int work = seqs * hkv > 0 ? seqs * hkv : 1;
   int s = clampi((g_tune.attn_ctas_per_sm * sms) / work, 1, tiles);
-  if (s > lmrs::kAttnMaxCluster) s = lmrs::kAttnMaxCluster;
+  // several clusters only for long contexts: B=1, 8 KV heads, 2048 positions
+  // took 9.1 us on one cluster of 8 splits against 11.4 us on 4 clusters; at
+  // 4096 positions 13.8 against 13.0, and 13.6 against 9.4 with one KV head
+  const bool multi = g_tune.attn_global_merge && max_ctx > g_tune.attn_multi_min_ctx;
+  const int cap = multi ? lmrs::kAttnMaxSplits : lmrs::kAttnMaxCluster;
+  if (s > cap) s = cap;
+  if (s > lmrs::kAttnMaxCluster) s -= s % lmrs::kAttnMaxCluster;   // whole clusters
   const int per = (tiles + s - 1) / s;
-  *span = per * lmrs::kAttnTile;
-  *splits = (tiles + per - 1) / per;
+  AttnSplit r;
+  r.span = per * lmrs::kAttnTile;
+  r.splits = (tiles + per - 1) / per;
+  if (r.splits > lmrs::kAttnMaxCluster)
+    r.splits = static_cast<int>(round_up(size_t(r.splits), lmrs::kAttnMaxCluster));
+  r.clusters = r.splits > lmrs::kAttnMaxCluster ? r.splits / lmrs::kAttnMaxCluster : 1;
+  return r;
+}
+
+// Workspace of the second merge level: the cluster partials [seqs * hkv]
+// [clusters][16 rows][132] fp32, then one arrival counter per (sequence, KV head).
+size_t attn_ws_part_bytes(int seqs, int hkv, const AttnSplit& sp) {
+  return round_up(size_t(seqs) * hkv * sp.clusters * 16 * lmrs::kAttnPartStride * 4, 256);
+}
+
+size_t attn_ws_bytes(int seqs, int hkv, const AttnSplit& sp) {
+  if (sp.clusters == 1) return 0;
+  return attn_ws_part_bytes(seqs, hkv, sp) + round_up(size_t(seqs) * hkv * 4, 256);
 }
 
 std::atomic<int> g_smem_attn[2][3][kMaxDevices];
@@ -87,8 +116,15 @@ std::atomic<int> g_smem_attn[2][3][kMaxDevices];
 template <typename T, int NS>
 int attn_launch(void* out, const void* q, const void* kc, const void* vc,
                 const int32_t* tables, const int32_t* lens, int seqs, int heads, int hkv,
-                int bs, int maxb, int splits, int span, float scale, int map, cudaStream_t st,
-                int dev, std::atomic<int>* done) {
+                int bs, int maxb, const AttnSplit& sp, float scale, int map, void* ws,
+                cudaStream_t st, int dev, std::atomic<int>* done) {
+  const int splits = sp.splits, span = sp.span;
+  float* ws_part = nullptr;
+  uint32_t* ws_count = nullptr;
+  if (sp.clusters > 1) {
+    ws_part = static_cast<float*>(ws);
+    ws_count = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(ws) + attn_ws_part_bytes(seqs, hkv, sp));
+  }
   int rc;
   if ((rc = ensure_smem(lmrs::decode_attn_kernel<T, NS>, lmrs::attn_smem_bytes(NS), done, dev)))
     return rc;
@@ -101,10 +137,10 @@ int attn_launch(void* out, const void* q, const void* kc, const void* vc,
   c.stream = st;
   cudaLaunchAttribute attr[2];
   int na = 0;
-  if (splits > 1) {   // the splits of one (sequence, KV head) merge inside their cluster
+  if (splits > 1) {   // consecutive splits of one (sequence, KV head) merge inside their cluster
     attr[na].id = cudaLaunchAttributeClusterDimension;
     attr[na].val.clusterDim.x = 1;
-    attr[na].val.clusterDim.y = splits;
+    attr[na].val.clusterDim.y = splits < lmrs::kAttnMaxCluster ? splits : lmrs::kAttnMaxCluster;
     attr[na].val.clusterDim.z = 1;
     ++na;
   }
@@ -118,7 +154,7 @@ int attn_launch(void* out, const void* q, const void* kc, const void* vc,
   cudaError_t e = cudaLaunchKernelEx(&c, lmrs::decode_attn_kernel<T, NS>, static_cast<T*>(out),
                                      static_cast<const T*>(q), static_cast<const T*>(kc),
                                      static_cast<const T*>(vc), tables, lens, heads, hkv, bs, maxb,
-                                     span, scale_log2, map);
+                                     span, scale_log2, map, ws_part, ws_count);
   if (e != cudaSuccess) return record(e);
   return after_launch();
 }
@@ -237,8 +273,10 @@ LMRS_API int lmrs_rope_kv_write(void* q_out, void* key_cache, void* value_cache,
 
 LMRS_API size_t lmrs_paged_attention_workspace_bytes(int num_seqs, int num_heads,
                                                      int num_kv_heads, int max_context) {
-  (void)num_seqs; (void)num_heads; (void)num_kv_heads; (void)max_context;
-  return 0;   // split partials merge in distributed shared memory
+  (void)num_heads;
+  if (num_seqs <= 0 || num_kv_heads <= 0 || max_context < 0) return 0;
+  return attn_ws_bytes(num_seqs, num_kv_heads,
+                       attn_split(num_seqs, num_kv_heads, max_context, sm_count_cached()));
 }
 
 LMRS_API int lmrs_paged_attention_decode(void* out, const void* query, const void* key_cache,
@@ -261,16 +299,18 @@ LMRS_API int lmrs_paged_attention_decode(void* out, const void* query, const voi
   int dev = 0;
   int rc = check_device(&dev);
   if (rc) return rc;
-  int splits, span;
-  attn_split(num_seqs, num_kv_heads, max_context, sm_count(dev), &splits, &span);
-  (void)workspace;
-  (void)workspace_bytes;
-  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const AttnSplit sp = attn_split(num_seqs, num_kv_heads, max_context, sm_count(dev));
+  if (sp.clusters > 1) {
+    if (!workspace || workspace_bytes < attn_ws_bytes(num_seqs, num_kv_heads, sp))
+      return LMRS_ERR_WORKSPACE;
+    if (!aligned16(workspace)) return LMRS_ERR_ALIGN;
+  }
   const int ns = clampi(g_tune.attn_stages, 2, 4);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
 #define LMRS_ATTN(T, I, NS)                                                                      \
   return attn_launch<T, NS>(out, query, key_cache, value_cache, block_tables,                   \
                             context_lens, num_seqs, num_heads, num_kv_heads, block_size,        \
-                            max_blocks_per_seq, splits, span, scale, kv_head_map, st, dev,      \
+                            max_blocks_per_seq, sp, scale, kv_head_map, workspace, st, dev,     \
                             g_smem_attn[I][NS - 2])
   if (dtype == LMRS_DTYPE_BF16) {
     if (ns == 2) LMRS_ATTN(__nv_bfloat16, 0, 2);

@@ -15,9 +15,11 @@
 //     [block_offset][head_size], block table per sequence), GQA with the q heads
 //     of one KV head in one CTA: S = Q K^T and O += P V on mma.sync (16 q-head
 //     rows, 16 positions per warp step, fp32 accumulate), online softmax,
-//     split over the context; the splits of one (sequence, KV head) form a
+//     split over the context; up to 8 splits of one (sequence, KV head) form a
 //     thread-block cluster and merge their (O, m, l) partials in split order
-//     through distributed shared memory (no second kernel, no global scratch).
+//     through distributed shared memory; with more splits (small batches) the
+//     clusters' merged partials meet in a global workspace, merged there by
+//     the last cluster to arrive (no second kernel).
 // All are launched with programmatic dependent launch and call pdl_wait before
 // touching their inputs.
 #pragma once
@@ -350,7 +352,8 @@ constexpr int kAttnTile = 64;      // positions per CTA iteration (16 per warp)
 constexpr int kAttnThreads = 128;  // 4 warps
 constexpr int kAttnRowBytes = kAttnD * 2 + 16;  // padded smem row (conflict-free ldmatrix)
 constexpr int kAttnMaxBlocks = 512;  // block-table entries of one split cached in smem
-constexpr int kAttnMaxCluster = 8;   // context splits of one (sequence, KV head) = one cluster
+constexpr int kAttnMaxCluster = 8;   // splits that merge in one cluster's shared memory
+constexpr int kAttnMaxSplits = 256;  // splits that merge through the global workspace
 constexpr int kAttnPartStride = 132; // split partial row: O[128], m, l, pad (16-byte rows)
 // dynamic shared memory: per warp NS stages of 16 K + 16 V rows (at least the
 // end-of-kernel warp merge buffer), then the split partial [16 rows][132]
@@ -407,27 +410,82 @@ struct MmaT<__nv_bfloat16> {
   }
 };
 
+// Merge n split partials (m, l in the log2 domain, unnormalised O over 16 dims)
+// in source order into (M, L, acc), the loads of kB sources in flight at once:
+// load(src, ml, o) fetches source src's (m, l) and its 16 O values.
+template <int kB, typename Load>
+__device__ __forceinline__ void attn_merge_sources(int n, Load load, float& M, float& L,
+                                                   float (&acc)[16]) {
+  M = -INFINITY;
+  L = 0.f;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) acc[i] = 0.f;
+  for (int s0 = 0; s0 < n; s0 += kB) {
+    float2 ml[kB];
+    float4 o[kB][4];
+#pragma unroll
+    for (int j = 0; j < kB; ++j) {
+      if (s0 + j < n) {
+        load(s0 + j, ml[j], o[j]);
+      } else {
+        ml[j] = make_float2(-INFINITY, 0.f);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) o[j][q] = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+    float bm = M;
+#pragma unroll
+    for (int j = 0; j < kB; ++j) bm = fmaxf(bm, ml[j].x);
+    if (bm == -INFINITY) continue;          // every source so far is empty
+    const float c = exp2f(M - bm);          // 0 while M is still -inf
+    L *= c;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) acc[i] *= c;
+#pragma unroll
+    for (int j = 0; j < kB; ++j) {
+      const float f = exp2f(ml[j].x - bm);  // 0 for an empty source
+      L += f * ml[j].y;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        acc[4 * q] += f * o[j][q].x;
+        acc[4 * q + 1] += f * o[j][q].y;
+        acc[4 * q + 2] += f * o[j][q].z;
+        acc[4 * q + 3] += f * o[j][q].w;
+      }
+    }
+    M = bm;
+  }
+}
+
 // grid: (num_seqs * num_kv_heads, splits).  Each CTA: one (sequence, KV head),
 // positions [split * span, (split + 1) * span) of the context, the G q heads
 // that read this KV head (G <= 16; rows >= G are padding).
 // kv_map 0: q head h reads KV head h % num_kv_heads (the reference's paged
 // kernel); 1: h / G (grouped, as torch's enable_gqa).
 // splits == 1: writes out directly.  Otherwise the splits of one (sequence, KV
-// head) are one thread-block cluster (grid y = cluster y): each CTA leaves its
-// (O, m, l) partial in shared memory and, after a cluster barrier, the CTAs share
-// out the (row, 16-dim) items and merge all partials in split order through
-// distributed shared memory (deterministic; no global scratch, no second kernel).
+// head) form clusters of min(splits, kAttnMaxCluster) consecutive splits (grid y
+// = splits, cluster y = that size; more than kAttnMaxCluster splits come in
+// whole clusters).  Each CTA leaves its (O, m, l) partial in shared memory and,
+// after a cluster barrier, the CTAs of a cluster share out the (row, 16-dim)
+// items and merge their cluster's partials in split order through distributed
+// shared memory.  One cluster writes the result.  Several (small batches: at
+// batch 1 a CTA walking 512 positions alone took ~15 us whatever the KV size)
+// write one merged partial per cluster into the global workspace (ws_part), and
+// the last cluster of the (sequence, KV head) to arrive on its counter merges
+// those in cluster order and sets the counter back to zero; no CTA waits on
+// another cluster.  Both levels are deterministic.
 template <typename T, int NS>
 __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(
     T* __restrict__ out, const T* __restrict__ query,
     const T* __restrict__ k_cache, const T* __restrict__ v_cache,
     const int32_t* __restrict__ tables, const int32_t* __restrict__ ctx_lens, int num_heads,
-    int num_kv_heads, int block_size, int max_blocks, int span, float scale_log2, int kv_map) {
+    int num_kv_heads, int block_size, int max_blocks, int span, float scale_log2, int kv_map,
+    float* __restrict__ ws_part, uint32_t* __restrict__ ws_count) {
   pdl_wait();
   pdl_trigger();
+  // per warp [NS stages][K 16 rows | V 16 rows], rows padded to kAttnRowBytes;
+  // then this split's partial (attn_smem_bytes)
   extern __shared__ __align__(16) uint8_t sm[];
-  // [2 stages][K tile 64 rows | V tile 64 rows], rows padded to kAttnRowBytes
-  constexpr int kTileBytes = kAttnTile * kAttnRowBytes;
   const int seq = blockIdx.x / num_kv_heads, kvh = blockIdx.x % num_kv_heads;
   const int split = blockIdx.y, splits = gridDim.y;
   const int G = num_heads / num_kv_heads;
@@ -642,7 +700,7 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(
 #pragma unroll
       for (int i = 0; i < 16; ++i) dst[i] = Act<T>::from_float(acc[i] * inv);
     } else {
-      // partial: O (unnormalised, fp32), then m, l
+      // partial: O (unnormalised, fp32), then m, l, in shared memory
       float* pw = part + r * kAttnPartStride;
 #pragma unroll
       for (int i = 0; i < 16; ++i) pw[d0 + i] = acc[i];
@@ -652,41 +710,70 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(
       }
     }
   }
-  if (splits > 1) {
-    cluster_sync_all();   // every split's partial is in its CTA's shared memory
-    const uint32_t part_u32 = smem_u32(part);
-    for (int e = threadIdx.x * splits + split; e < G * 8; e += kAttnThreads * splits) {
-      const int r = e >> 3, d0 = (e & 7) * 16;
-      const uint32_t row = part_u32 + static_cast<uint32_t>(r * kAttnPartStride) * 4u;
-      float M = -INFINITY;
-      for (int src = 0; src < splits; ++src) {
-        const float4 ml = ld_cluster_v4(mapa_shared(row + kAttnD * 4u, static_cast<uint32_t>(src)));
-        M = fmaxf(M, ml.x);
-      }
-      float L = 0.f, acc[16];
+  if (splits == 1) return;
+  // ---- first level: the cluster's splits, through distributed shared memory
+  const int cs = splits < kAttnMaxCluster ? splits : kAttnMaxCluster;  // cluster size
+  const int crank = split % cs, nclu = splits / cs, clu = split / cs;
+  cluster_sync_all();   // every split's partial is in its CTA's shared memory
+  const uint32_t part_u32 = smem_u32(part);
+  for (int e = threadIdx.x * cs + crank; e < G * 8; e += kAttnThreads * cs) {
+    const int r = e >> 3, d0 = (e & 7) * 16;
+    const uint32_t row = part_u32 + static_cast<uint32_t>(r * kAttnPartStride) * 4u;
+    float M, L, acc[16];
+    attn_merge_sources<4>(cs, [&](int src, float2& ml, float4 (&o)[4]) {
+      const uint32_t pr = mapa_shared(row, static_cast<uint32_t>(src));
+      const float4 m4 = ld_cluster_v4(pr + kAttnD * 4u);
+      ml = make_float2(m4.x, m4.y);
 #pragma unroll
-      for (int i = 0; i < 16; ++i) acc[i] = 0.f;
-      for (int src = 0; src < splits; ++src) {
-        const uint32_t pr = mapa_shared(row, static_cast<uint32_t>(src));
-        const float4 ml = ld_cluster_v4(pr + kAttnD * 4u);
-        const float f = M == -INFINITY ? 0.f : exp2f(ml.x - M);
-        L += f * ml.y;
-#pragma unroll
-        for (int i = 0; i < 16; i += 4) {
-          const float4 o4 = ld_cluster_v4(pr + static_cast<uint32_t>(d0 + i) * 4u);
-          acc[i] += f * o4.x;
-          acc[i + 1] += f * o4.y;
-          acc[i + 2] += f * o4.z;
-          acc[i + 3] += f * o4.w;
-        }
-      }
+      for (int q = 0; q < 4; ++q) o[q] = ld_cluster_v4(pr + static_cast<uint32_t>(d0 + 4 * q) * 4u);
+    }, M, L, acc);
+    if (nclu == 1) {
       T* dst = out + (static_cast<int64_t>(seq) * num_heads + qhead(r)) * kAttnD + d0;
       const float inv = L > 0.f ? 1.f / L : 0.f;
 #pragma unroll
       for (int i = 0; i < 16; ++i) dst[i] = Act<T>::from_float(acc[i] * inv);
+    } else {   // this cluster's partial, item by item, into the workspace
+      float* pw = ws_part + ((static_cast<int64_t>(blockIdx.x) * nclu + clu) * 16 + r) * kAttnPartStride;
+#pragma unroll
+      for (int i = 0; i < 16; i += 4)
+        __stcg(reinterpret_cast<float4*>(pw + d0 + i), make_float4(acc[i], acc[i + 1], acc[i + 2], acc[i + 3]));
+      if (d0 == 0) __stcg(reinterpret_cast<float2*>(pw + kAttnD), make_float2(M, L));
     }
-    cluster_sync_all();   // no CTA leaves while a peer may read its partial
   }
+  // no CTA leaves while a peer may read its partial; the release / acquire of
+  // the cluster barrier also orders every thread's workspace items before the
+  // arrival below (the CTA-barrier-then-one-fenced-atomic pattern)
+  cluster_sync_all();
+  if (nclu == 1) return;
+  // ---- second level: the cluster partials, by the last cluster to arrive
+  __shared__ uint32_t s_last;
+  if (threadIdx.x == 0) {
+    bool last = false;
+    if (crank == 0) {
+      __threadfence();   // the cluster's partial, before its arrival
+      last = atomicAdd(ws_count + blockIdx.x, 1u) == static_cast<uint32_t>(nclu - 1);
+      if (last) __threadfence();   // every cluster's partial, after the last arrival
+    }
+    s_last = last;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  const float* pbase = ws_part + static_cast<int64_t>(blockIdx.x) * nclu * 16 * kAttnPartStride;
+  for (int e = threadIdx.x; e < G * 8; e += kAttnThreads) {
+    const int r = e >> 3, d0 = (e & 7) * 16;
+    float M, L, acc[16];
+    attn_merge_sources<8>(nclu, [&](int src, float2& ml, float4 (&o)[4]) {
+      const float* pr = pbase + (src * 16 + r) * kAttnPartStride;
+      ml = __ldcg(reinterpret_cast<const float2*>(pr + kAttnD));
+#pragma unroll
+      for (int q = 0; q < 4; ++q) o[q] = __ldcg(reinterpret_cast<const float4*>(pr + d0 + 4 * q));
+    }, M, L, acc);
+    T* dst = out + (static_cast<int64_t>(seq) * num_heads + qhead(r)) * kAttnD + d0;
+    const float inv = L > 0.f ? 1.f / L : 0.f;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) dst[i] = Act<T>::from_float(acc[i] * inv);
+  }
+  if (threadIdx.x == 0) ws_count[blockIdx.x] = 0u;  // ready for the next call
 }
 
 }  // namespace lmrs

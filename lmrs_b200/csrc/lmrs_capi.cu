@@ -63,6 +63,8 @@ struct Tuning {
   int awq_gemv4_slots = 4;   // its ring slots (4 or 8)
   int attn_stages = 3;       // decode attention cp.async ring depth (2..4)
   int attn_ctas_per_sm = 2;  // decode attention context split target
+  int attn_global_merge = 1; // small batches: several clusters of splits, merged through the workspace
+  int attn_multi_min_ctx = 2048;  // ... only above this context (fewer, longer splits win below)
   int awq_tmem_min_m = 9;    // TMEM-staged tcgen05 AWQ linear for M in [min, max];
   int awq_tmem_max_m = 32;   // its cost is flat in M (32 at most)
   int awq_tmem_min_m_wide = 5;  // ... and down to this M when N >= K (0 = off)
@@ -947,6 +949,8 @@ int lmrs_set_tuning(const char* key, int value) {
   else if (!strcmp(key, "awq_gemv4_slots")) g_tune.awq_gemv4_slots = value;
   else if (!strcmp(key, "attn_stages")) g_tune.attn_stages = value;
   else if (!strcmp(key, "attn_ctas_per_sm")) g_tune.attn_ctas_per_sm = value;
+  else if (!strcmp(key, "attn_global_merge")) g_tune.attn_global_merge = value ? 1 : 0;
+  else if (!strcmp(key, "attn_multi_min_ctx")) g_tune.attn_multi_min_ctx = value;
   else if (!strcmp(key, "fp8_gemv_cluster")) g_tune.fp8_gemv_cluster = value;
   else if (!strcmp(key, "fp8_swap_max_m")) g_tune.fp8_swap_max_m = value;
   else if (!strcmp(key, "fp8_gemv_max_kn")) g_tune.fp8_gemv_max_kn = value;

@@ -98,7 +98,9 @@ def rope_kv_write(qkv: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
 
 
 class AttentionWorkspace:
-    """Grow-only split-context scratch for paged_attention_decode."""
+    """Grow-only split-context scratch for paged_attention_decode.  Zero-filled
+    when (re)allocated: it holds the per-(sequence, KV head) arrival counters of
+    the workspace merge, which every call leaves at zero again."""
 
     def __init__(self):
         self.buf = None
@@ -107,7 +109,7 @@ class AttentionWorkspace:
         if nbytes == 0:
             return None
         if self.buf is None or self.buf.numel() < nbytes or self.buf.device != device:
-            self.buf = torch.empty(nbytes, dtype=torch.uint8, device=device)
+            self.buf = torch.zeros(nbytes, dtype=torch.uint8, device=device)
         return self.buf
 
 

@@ -229,3 +229,64 @@ def test_paged_attention_cluster_splits(cuda, cps):
             ref = torch.softmax(q[s, h].float() @ K.t() * scale, -1) @ V
             assert (out[s, h].float() - ref).abs().max().item() < 2e-3
     assert L.read_device_error() == 0
+
+
+@pytest.mark.parametrize("seqs,hq,hkv,lens", [(1, 8, 1, [4096]), (1, 64, 8, [4096]),
+                                              (2, 32, 8, [2100, 700]), (3, 16, 2, [4096, 0, 129])])
+def test_paged_attention_workspace_merge(cuda, seqs, hq, hkv, lens):
+    """Small batches with long contexts split the context over several 8-CTA
+    clusters (one 64-position tile per CTA at batch 1 with one KV head; 2100
+    positions leave trailing splits empty), each cluster's merged partial going
+    through the workspace to the last cluster of the (sequence, KV head) to
+    arrive: against an fp32 softmax, equal across calls and CUDA-graph replays
+    (the arrival counters return to zero), and close to the one-cluster path."""
+    import lmrs_b200 as L
+    from lmrs_b200 import _lib
+    from lmrs_b200 import decode_ops as DO
+    d, bs = 128, 16
+    max_ctx = max(lens)
+    max_blocks = (max_ctx + bs - 1) // bs
+    assert _lib.load().lmrs_paged_attention_workspace_bytes(seqs, hq, hkv, max_ctx) > 0
+    kc, vc, tables = _paged_cache(seqs, hkv, d, bs, max_blocks, torch.bfloat16, cuda, 41 + hq)
+    torch.manual_seed(5)
+    q = torch.randn(seqs, hq, d, device=cuda).bfloat16()
+    ctx = torch.tensor(lens, dtype=torch.int32, device=cuda)
+    scale = 1 / math.sqrt(d)
+    ws = DO.AttentionWorkspace()
+    out = DO.paged_attention_decode(q, kc, vc, tables, ctx, max_ctx, scale, workspace=ws)
+    for _ in range(2):
+        assert torch.equal(DO.paged_attention_decode(q, kc, vc, tables, ctx, max_ctx, scale,
+                                                     workspace=ws), out)
+    g = torch.cuda.CUDAGraph()
+    buf = torch.empty_like(out)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        buf.copy_(DO.paged_attention_decode(q, kc, vc, tables, ctx, max_ctx, scale, workspace=ws))
+    torch.cuda.current_stream().wait_stream(s)
+    with torch.cuda.graph(g):
+        buf.copy_(DO.paged_attention_decode(q, kc, vc, tables, ctx, max_ctx, scale, workspace=ws))
+    for _ in range(3):
+        g.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(buf, out)
+    del g
+    try:
+        L.set_tuning("attn_global_merge", 0)
+        clus = DO.paged_attention_decode(q, kc, vc, tables, ctx, max_ctx, scale, workspace=ws)
+    finally:
+        L.set_tuning("attn_global_merge", 1)
+    G = hq // hkv
+    for si in range(seqs):
+        n = lens[si]
+        for h in range(hq):
+            if n == 0:
+                assert torch.all(out[si, h] == 0)
+                continue
+            K = _gather(kc, tables, si, n, h // G).float()
+            V = _gather(vc, tables, si, n, h // G).float()
+            ref = torch.softmax(q[si, h].float() @ K.t() * scale, -1) @ V
+            err = ((out[si, h].float() - ref).abs().max() / ref.abs().max()).item()
+            assert err < 2e-2, (si, h, err)
+    assert ((out.float() - clus.float()).abs().max() / clus.float().abs().max()).item() < 2e-2
+    assert L.read_device_error() == 0
