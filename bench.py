@@ -61,11 +61,12 @@ FP8_MS = [1, 32, 512, 8192]
 # DRAM bytes (read + write) of one awq_gemm_tmem_kernel<256> launch at M=4096 and
 # how they were captured (ncu cannot run inside the timed bench; the figure is
 # re-captured whenever the kernel changes and printed with its source).
-AWQ_GEMM_M4096_DRAM_BYTES = 93_220_000 + 73_690_000
+AWQ_GEMM_M4096_DRAM_BYTES = 93_518_848 + 74_575_360
 AWQ_GEMM_M4096_TRAFFIC_SOURCE = (
     "ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum,gpu__time_duration.sum "
     "--clock-control none -k regex:awq_gemm_tmem -s 1 -c 1 python bench.py --case awq:4096 "
-    "(93.22 MB read + 73.69 MB written)")
+    "(93.52 MB read + 74.58 MB written; awq_gemm_tmem_kernel<256, 128, __half>, 128-deep "
+    "K-blocks, 374.0 us cold-cache under ncu)")
 
 
 def peaks():
@@ -790,6 +791,12 @@ def main():
             line["decode"] = decode
         c4 = decode.get("decode_tok_s_config4", {})
         p1 = next((p for p in c4.get("points", []) if p.get("batch") == 1 and "tok_s" in p), None)
+        if world == 1 and p1 is not None:
+            # the N > 1 lines' headline (tensor-parallel config-4 decode at batch
+            # 1) measured here at N = 1, so scaling can be read against it
+            line["tp_headline"] = {"metric": "decode_tok_s_config4_batch1", "value": p1["tok_s"],
+                                   "unit": "tok/s", "ms_per_step": p1["ms_median"],
+                                   "parallelism": "tp1"}
         if world > 1 and p1 is not None:
             # N > 1: the headline is the tensor-parallel config-4 decode at batch 1
             # (strong scaling of one fixed step over the N GPUs); the per-rank
