@@ -86,7 +86,9 @@ LMRS_API int lmrs_version(void);
  * "awq_swap_deep_k" (swap-AB up to 128 tokens when 4K >= value x N, default 5; 0 = off),
  * "awq_swap_cluster", "awq_gemm_pair", "gemm_bn", "fp8_gemv_max_m",
  * "gemv_ctas_per_sm", "awq_gemv_cluster", "fp8_gemv_cluster", "fp8_gemv_max_kn",
- * "fp8_swap_max_m", "fp8_swap_cluster", "awq_tmem_min_m", "awq_tmem_max_m",
+ * "fp8_swap_max_m", "fp8_swap_cluster", "fp8_gemm_group_m" (FP8 GEMM tile order: M
+ * tiles per group, default 32), "fp8_gemm_bn128" (128-wide FP8 GEMM tiles while
+ * that grid fits one wave, default 1), "awq_tmem_min_m", "awq_tmem_max_m",
  * "awq_tmem_min_m_wide", "awq_tmem_cluster", "awq_tmem_ctas_per_sm", "awq_gemm_tmem",
  * "awq_gemm_tmem_bt", "awq_gemv4", "awq_gemv_slots", "awq_gemv4_slots",
  * "gemv_box_rows", "attn_stages", "attn_ctas_per_sm", "attn_global_merge" (small

@@ -56,6 +56,14 @@ struct Tuning {
   int awq_gemm_pair = 0;     // 1: CTA-pair (cta_group::2) GEMM for large M; 0: one-SM tiles
   int gemm_bn = 256;         // one-SM GEMM tile width: 256 or 224; 0 = pick by wave count
   int fp8_gemv_cluster = 0;
+  // FP8 GEMM tile order: groups of this many M tiles walked N tile by N tile.
+  // Graph-timed at M = 2048..8192 on the config-2 shapes, 32 beat 8 by 1-4 %
+  // (4096 x 28672 at 8192: 838.8 vs 846.6 us; 14336 x 4096: 354.6 vs 364.9).
+  int fp8_gemm_group_m = 32;
+  // 128-wide FP8 GEMM tiles while that grid still fits one wave (M = 512 on
+  // N = 4096: 64 256-wide tiles, 27.7 -> 19.7 us; 14336 x 4096 67.1 -> 52.9);
+  // past one wave they lose (M = 1024, 14336 x 4096: 92.9 vs 67.6 us)
+  int fp8_gemm_bn128 = 1;
   int pdl = 1;               // programmatic dependent launch on every kernel
   int awq_gemv_slots = 4;    // ring slots of the AWQ GEMV (even, 2..8)
   int awq_gemv4 = 1;         // M <= 4: the permute-free GEMV (0: the general one)
@@ -798,6 +806,7 @@ int fp8_gemv_launch(__nv_bfloat16* y, const uint8_t* xq, const float* sx, const 
 }
 
 std::atomic<int> g_smem_f8_gemm224[kMaxDevices];
+std::atomic<int> g_smem_f8_gemm128[kMaxDevices];
 std::atomic<int> g_smem_f8_swap[3][kMaxDevices];
 
 template <int NT, int ST>
@@ -854,14 +863,18 @@ int fp8_gemm_launch_bn(__nv_bfloat16* y, const uint8_t* xq, const float* sx, con
   if ((rc = ensure_smem(lmrs::fp8_gemm_tc_kernel<BN>, smem, smem_done, dev))) return rc;
   const int tiles = ((N + BN - 1) / BN) * ((M + lmrs::kTcBM - 1) / lmrs::kTcBM);
   const int grid = tiles < sm_count(dev) ? tiles : sm_count(dev);
+  const int group_m = g_tune.fp8_gemm_group_m > 0 ? g_tune.fp8_gemm_group_m : 1;
   rc = launch_ex(lmrs::fp8_gemm_tc_kernel<BN>, grid, 0, lmrs::kF8Threads, smem, stream, ta, tb, y,
-                 sx, sw, bias, M, K, N);
+                 sx, sw, bias, M, K, N, group_m);
   return rc ? rc : after_launch();
 }
 
 int fp8_gemm_launch(__nv_bfloat16* y, const uint8_t* xq, const float* sx, const uint8_t* wq,
                     const float* sw, const __nv_bfloat16* bias, int M, int K, int N,
                     cudaStream_t stream, int dev) {
+  const int m_tiles = (M + lmrs::kTcBM - 1) / lmrs::kTcBM;
+  if (g_tune.fp8_gemm_bn128 && m_tiles * ((N + 127) / 128) <= sm_count(dev))
+    return fp8_gemm_launch_bn<128>(y, xq, sx, wq, sw, bias, M, K, N, stream, dev, g_smem_f8_gemm128);
   if (pick_bn(M, N, sm_count(dev)) == 224)
     return fp8_gemm_launch_bn<224>(y, xq, sx, wq, sw, bias, M, K, N, stream, dev, g_smem_f8_gemm224);
   return fp8_gemm_launch_bn<256>(y, xq, sx, wq, sw, bias, M, K, N, stream, dev, g_smem_f8_gemm);
@@ -952,6 +965,8 @@ int lmrs_set_tuning(const char* key, int value) {
   else if (!strcmp(key, "attn_global_merge")) g_tune.attn_global_merge = value ? 1 : 0;
   else if (!strcmp(key, "attn_multi_min_ctx")) g_tune.attn_multi_min_ctx = value;
   else if (!strcmp(key, "fp8_gemv_cluster")) g_tune.fp8_gemv_cluster = value;
+  else if (!strcmp(key, "fp8_gemm_group_m")) g_tune.fp8_gemm_group_m = value;
+  else if (!strcmp(key, "fp8_gemm_bn128")) g_tune.fp8_gemm_bn128 = value ? 1 : 0;
   else if (!strcmp(key, "fp8_swap_max_m")) g_tune.fp8_swap_max_m = value;
   else if (!strcmp(key, "fp8_gemv_max_kn")) g_tune.fp8_gemv_max_kn = value;
   else if (!strcmp(key, "awq_tmem_max_m")) g_tune.awq_tmem_max_m = value;

@@ -50,11 +50,12 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint4 v) {
 // stay resident in L2 and each is fetched from HBM about once.
 constexpr int kTcGroupM = 8;
 
-__device__ __forceinline__ void tile_coords(int t, int m_tiles, int n_tiles, int bn, int& m0, int& n0) {
-  const int per_group = kTcGroupM * n_tiles;
+__device__ __forceinline__ void tile_coords(int t, int m_tiles, int n_tiles, int bn, int& m0, int& n0,
+                                            int group_m = kTcGroupM) {
+  const int per_group = group_m * n_tiles;
   const int grp = t / per_group;
-  const int first_m = grp * kTcGroupM;
-  const int gm = min(m_tiles - first_m, kTcGroupM);
+  const int first_m = grp * group_m;
+  const int gm = min(m_tiles - first_m, group_m);
   const int local = t - grp * per_group;
   m0 = (first_m + local % gm) * kTcBM;
   n0 = (local / gm) * bn;
@@ -321,7 +322,7 @@ __global__ void __launch_bounds__(kF8Threads, 1)
     fp8_gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_a,
                        const __grid_constant__ CUtensorMap tm_b, __nv_bfloat16* __restrict__ y,
                        const float* __restrict__ sx, const float* __restrict__ sw,
-                       const __nv_bfloat16* __restrict__ bias, int M, int K, int N) {
+                       const __nv_bfloat16* __restrict__ bias, int M, int K, int N, int group_m) {
   pdl_wait();     // activations are the previous kernel's output
   pdl_trigger();
   extern __shared__ uint8_t smem_raw[];
@@ -368,7 +369,7 @@ __global__ void __launch_bounds__(kF8Threads, 1)
       bool ok = true;
       for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
         int m0, n0;
-        tile_coords(t, m_tiles, n_tiles, BN, m0, n0);
+        tile_coords(t, m_tiles, n_tiles, BN, m0, n0, group_m);
         for (int kb = 0; kb < KB; ++kb, ++kg) {
           const int s = kg % kF8Stages;
           if (!(ok = mbar_wait(&empty[s], ((kg / kF8Stages) & 1) ^ 1, kErrWaitEmpty))) break;
@@ -414,7 +415,7 @@ __global__ void __launch_bounds__(kF8Threads, 1)
       if (!mbar_wait(&acc->full[a], (it >> 1) & 1, kErrWaitAccum)) break;
       tc_fence_after();
       int m0, n0;
-        tile_coords(t, m_tiles, n_tiles, BN, m0, n0);
+      tile_coords(t, m_tiles, n_tiles, BN, m0, n0, group_m);
       const int row = m0 + quarter * 32 + lane;
       const float rs = row < M ? sx[row] : 0.f;
       const uint32_t tbase = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + a * BN;
