@@ -47,6 +47,31 @@ LMRS_API int lmrs_allreduce_sum(void* out, const void* in, size_t n, int dtype, 
                                 int world, void* const* buffers, size_t max_elems,
                                 lmrs_stream_t stream);
 
+/* The all-reduce of a row-parallel projection fused with the residual add and
+ * RMSNorm that follow it (one launch instead of lmrs_allreduce_sum then
+ * lmrs_rmsnorm[_fp8]): for rows x H elements (H % 8 == 0, H <= 32768,
+ * rows * H <= max_elems),
+ *   delta    = sum over ranks of partial (rank order in fp32, rounded once to
+ *              dtype: the same values lmrs_allreduce_sum produces),
+ *   residual = dtype(residual + delta)        (in place),
+ *   out      = rmsnorm(residual) * weight     (one rounding),
+ * the _fp8 form writing the e4m3 bytes and per-row scale of that output
+ * instead (as lmrs_fp8_quant_rows of it).  partial is read only.  Same buffers,
+ * call-order and bounded-wait rules as lmrs_allreduce_sum (the two share the
+ * buffers' epoch, so calls of both may alternate); world may be 1.  All
+ * pointers 16-byte aligned.  Replaces, on the decode step's data path, the
+ * reference's custom all-reduce (kernels/comm/custom_all_reduce.cuh) followed
+ * by rmsnorm_fwd (kernels/ffi/norm_ffi.cu:87-95). */
+LMRS_API int lmrs_allreduce_rmsnorm(void* out, void* residual, const void* partial,
+                                    const void* weight, int rows, int H, float eps, int dtype,
+                                    int rank, int world, void* const* buffers, size_t max_elems,
+                                    lmrs_stream_t stream);
+LMRS_API int lmrs_allreduce_rmsnorm_fp8(uint8_t* q_out, float* scale_out, void* residual,
+                                        const void* partial, const void* weight, int rows, int H,
+                                        float eps, int dtype, int rank, int world,
+                                        void* const* buffers, size_t max_elems,
+                                        lmrs_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -72,6 +72,8 @@ SIGNATURES = {
     "lmrs_ipc_open": (I, [P, ctypes.POINTER(P)]),
     "lmrs_ipc_close": (I, [P]),
     "lmrs_allreduce_sum": (I, [P, P, SZ, I, I, I, P, SZ, P]),
+    "lmrs_allreduce_rmsnorm": (I, [P, P, P, P, I, I, F, I, I, I, P, SZ, P]),
+    "lmrs_allreduce_rmsnorm_fp8": (I, [P, P, P, P, P, I, I, F, I, I, I, P, SZ, P]),
 }
 
 

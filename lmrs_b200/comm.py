@@ -66,6 +66,49 @@ class PeerAllReduce:
             ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)))
         return t
 
+    def _norm_args(self, partial, residual, weight):
+        for t, n in ((partial, "partial sums"), (residual, "residual"), (weight, "norm weight")):
+            _require_cuda(t, "all-reduce + norm " + n)
+        if residual.dtype not in _DT or partial.dtype != residual.dtype or weight.dtype != residual.dtype:
+            raise DTypeMismatch("all-reduce + norm takes bf16 or f16 partial / residual / weight "
+                                "of one dtype")
+        rows, H = residual.reshape(-1, residual.shape[-1]).shape
+        if partial.numel() != rows * H or weight.numel() != H:
+            raise ShapeMismatch("all-reduce + norm: partial, residual [rows, H] and weight [H]")
+        return rows, H
+
+    def rmsnorm(self, partial: torch.Tensor, residual: torch.Tensor, weight: torch.Tensor,
+                eps: float, out: torch.Tensor = None) -> torch.Tensor:
+        """residual += sum over the group of partial (in place); returns
+        rmsnorm(residual) * weight: one kernel for the all-reduce of a
+        row-parallel projection and the norm after it."""
+        rows, H = self._norm_args(partial, residual, weight)
+        if out is None:
+            out = torch.empty_like(residual)
+        _lib.check("lmrs_allreduce_rmsnorm", self.lib.lmrs_allreduce_rmsnorm(
+            ctypes.c_void_p(out.data_ptr()), ctypes.c_void_p(residual.data_ptr()),
+            ctypes.c_void_p(partial.data_ptr()), ctypes.c_void_p(weight.data_ptr()), rows, H,
+            float(eps), _DT[residual.dtype], self.rank, self.world, self.bases, self.max_elems,
+            ctypes.c_void_p(torch.cuda.current_stream(residual.device).cuda_stream)))
+        return out
+
+    def rmsnorm_fp8(self, partial: torch.Tensor, residual: torch.Tensor, weight: torch.Tensor,
+                    eps: float, q_out: torch.Tensor = None, scale_out: torch.Tensor = None):
+        """As rmsnorm, returning the e4m3 bytes and per-row scales of the output."""
+        rows, H = self._norm_args(partial, residual, weight)
+        dev = residual.device
+        if q_out is None:
+            q_out = torch.empty((rows, H), dtype=torch.uint8, device=dev)
+        if scale_out is None:
+            scale_out = torch.empty((rows,), dtype=torch.float32, device=dev)
+        _lib.check("lmrs_allreduce_rmsnorm_fp8", self.lib.lmrs_allreduce_rmsnorm_fp8(
+            ctypes.c_void_p(q_out.data_ptr()), ctypes.c_void_p(scale_out.data_ptr()),
+            ctypes.c_void_p(residual.data_ptr()), ctypes.c_void_p(partial.data_ptr()),
+            ctypes.c_void_p(weight.data_ptr()), rows, H, float(eps), _DT[residual.dtype],
+            self.rank, self.world, self.bases, self.max_elems,
+            ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)))
+        return q_out, scale_out
+
     def close(self):
         for p in self.opened:
             self.lib.lmrs_ipc_close(p)

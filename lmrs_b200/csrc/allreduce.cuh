@@ -39,6 +39,14 @@ __device__ __forceinline__ uint64_t ld_sys_b64(const uint64_t* p) {
   asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
+// The same load without volatile / memory clobber, so that several of them can
+// be in flight together: only for a first look, never inside a polling loop
+// (the compiler may merge repeated calls on the same address).
+__device__ __forceinline__ uint64_t ld_sys_b64_once(const uint64_t* p) {
+  uint64_t v;
+  asm("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(v) : "l"(p));
+  return v;
+}
 
 template <typename T>
 __global__ void __launch_bounds__(kArThreads) allreduce_ll_kernel(T* out,

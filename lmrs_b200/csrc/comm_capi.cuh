@@ -2,6 +2,7 @@
 // lmrs_capi.cu, one translation unit with the other entry points).
 #pragma once
 #include "allreduce.cuh"
+#include "allreduce_norm.cuh"
 #include "lmrs_comm.h"
 
 namespace {
@@ -27,9 +28,113 @@ int allreduce_launch(void* out, const void* in, size_t n, int rank, int world,
   return rc ? rc : after_launch();
 }
 
+// Fused all-reduce + residual add + RMSNorm: a cluster of C CTAs per row
+// (1024 columns per CTA and step), the clusters walking the rows; no more
+// clusters than the device holds at once, so that every CTA of every rank is
+// resident together.
+template <typename T, bool FP8>
+int allreduce_norm_launch(void* out, uint8_t* q_out, float* scale_out, void* residual,
+                          const void* partial, const void* weight, int rows, int H, float eps,
+                          int rank, int world, void* const* buffers, size_t max_elems,
+                          cudaStream_t st, int dev) {
+  lmrs::ArPeers peers = {};
+  for (int r = 0; r < world; ++r)
+    peers.buf[r] = reinterpret_cast<uint64_t*>(static_cast<uint8_t*>(buffers[r]) + kArHeader);
+  int C = (H + lmrs::kArnCols - 1) / lmrs::kArnCols;
+  if (C > lmrs::kArnMaxCluster) C = lmrs::kArnMaxCluster;
+  const int vpt = (H + C * lmrs::kArnCols - 1) / (C * lmrs::kArnCols);
+  const int cap = static_cast<int>(ar_cap(max_elems));
+  auto go = [&](auto kern) -> int {
+    // as many clusters as the device holds at once (the CTAs of all ranks wait
+    // on one another's packets, so none may wait for a slot), at most one per row
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(C, 1, 1);
+    cfg.blockDim = dim3(lmrs::kArnThreads, 1, 1);
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = C;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    int resident = 0;
+    cudaError_t e = cudaOccupancyMaxActiveClusters(&resident, kern, &cfg);
+    if (e != cudaSuccess) return record(e);
+    if (resident < 1) return static_cast<int>(LMRS_ERR_SHAPE);
+    const int nclu = rows < resident ? rows : resident;
+    return launch_ex(kern, nclu * C, C, lmrs::kArnThreads, 0, st, static_cast<T*>(out), q_out,
+                     scale_out, static_cast<T*>(residual), static_cast<const T*>(partial),
+                     static_cast<const T*>(weight), rows, H, eps, rank, world, peers, cap);
+  };
+  int rc = vpt == 1   ? go(lmrs::allreduce_rmsnorm_kernel<T, FP8, 1>)
+           : vpt == 2 ? go(lmrs::allreduce_rmsnorm_kernel<T, FP8, 2>)
+           : vpt == 3 ? go(lmrs::allreduce_rmsnorm_kernel<T, FP8, 3>)
+                      : go(lmrs::allreduce_rmsnorm_kernel<T, FP8, 4>);
+  return rc ? rc : after_launch();
+}
+
+int allreduce_norm_check(const void* outp, void* residual, const void* partial,
+                         const void* weight, int rows, int H, int dtype, int rank, int world,
+                         void* const* buffers, size_t max_elems) {
+  if (dtype != LMRS_DTYPE_BF16 && dtype != LMRS_DTYPE_F16) return LMRS_ERR_DTYPE;
+  if (world <= 0 || world > lmrs::kArMaxRanks || rank < 0 || rank >= world || rows < 0 ||
+      H <= 0 || H % 8 || H > lmrs::kArnMaxCluster * lmrs::kArnMaxVecs * lmrs::kArnCols ||
+      max_elems / 2 > static_cast<size_t>(INT32_MAX) ||
+      static_cast<size_t>(rows) * static_cast<size_t>(H) > max_elems)
+    return LMRS_ERR_SHAPE;
+  if (rows == 0) return LMRS_OK;
+  if (!outp || !residual || !partial || !weight || !buffers) return LMRS_ERR_NULL;
+  for (int r = 0; r < world; ++r)
+    if (!buffers[r]) return LMRS_ERR_NULL;
+  if (!aligned16(outp) || !aligned16(residual) || !aligned16(partial) || !aligned16(weight))
+    return LMRS_ERR_ALIGN;
+  return -1;  // arguments fine: launch
+}
+
 }  // namespace
 
 extern "C" {
+
+LMRS_API int lmrs_allreduce_rmsnorm(void* out, void* residual, const void* partial,
+                                    const void* weight, int rows, int H, float eps, int dtype,
+                                    int rank, int world, void* const* buffers, size_t max_elems,
+                                    lmrs_stream_t stream) {
+  int rc = allreduce_norm_check(out, residual, partial, weight, rows, H, dtype, rank, world,
+                                buffers, max_elems);
+  if (rc >= 0) return rc;
+  int dev = 0;
+  if ((rc = check_device(&dev))) return rc;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  return dtype == LMRS_DTYPE_BF16
+             ? allreduce_norm_launch<__nv_bfloat16, false>(out, nullptr, nullptr, residual,
+                                                           partial, weight, rows, H, eps, rank,
+                                                           world, buffers, max_elems, st, dev)
+             : allreduce_norm_launch<__half, false>(out, nullptr, nullptr, residual, partial,
+                                                    weight, rows, H, eps, rank, world, buffers,
+                                                    max_elems, st, dev);
+}
+
+LMRS_API int lmrs_allreduce_rmsnorm_fp8(uint8_t* q_out, float* scale_out, void* residual,
+                                        const void* partial, const void* weight, int rows, int H,
+                                        float eps, int dtype, int rank, int world,
+                                        void* const* buffers, size_t max_elems,
+                                        lmrs_stream_t stream) {
+  int rc = allreduce_norm_check(q_out, residual, partial, weight, rows, H, dtype, rank, world,
+                                buffers, max_elems);
+  if (rc >= 0) return rc;
+  if (!scale_out) return LMRS_ERR_NULL;
+  int dev = 0;
+  if ((rc = check_device(&dev))) return rc;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  return dtype == LMRS_DTYPE_BF16
+             ? allreduce_norm_launch<__nv_bfloat16, true>(nullptr, q_out, scale_out, residual,
+                                                          partial, weight, rows, H, eps, rank,
+                                                          world, buffers, max_elems, st, dev)
+             : allreduce_norm_launch<__half, true>(nullptr, q_out, scale_out, residual, partial,
+                                                   weight, rows, H, eps, rank, world, buffers,
+                                                   max_elems, st, dev);
+}
+
 
 LMRS_API size_t lmrs_allreduce_buffer_bytes(int world, size_t max_elems) {
   if (world <= 0 || world > lmrs::kArMaxRanks) return 0;

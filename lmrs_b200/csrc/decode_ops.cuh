@@ -87,6 +87,13 @@ template <typename T, bool FP8, int VPT>
 __global__ void __launch_bounds__(kRowMaxThreads) rmsnorm_kernel(
     T* __restrict__ out, uint8_t* __restrict__ qout, float* __restrict__ qscale,
     T* __restrict__ resid, const T* __restrict__ delta, const T* __restrict__ w, int H, float eps) {
+  // the norm weight is constant: read before the previous kernel has finished
+  uint4 wv[VPT];
+#pragma unroll
+  for (int v = 0; v < VPT; ++v) {
+    const int c = (v * blockDim.x + threadIdx.x) * 8;
+    wv[v] = c < H ? __ldg(reinterpret_cast<const uint4*>(w + c)) : make_uint4(0u, 0u, 0u, 0u);
+  }
   pdl_wait();
   pdl_trigger();
   __shared__ float red[32];
@@ -122,7 +129,7 @@ __global__ void __launch_bounds__(kRowMaxThreads) rmsnorm_kernel(
     const int c = (v * blockDim.x + threadIdx.x) * 8;
     if (c < H) {
       float wf[8];
-      unpack8<T>(*reinterpret_cast<const uint4*>(w + c), wf);
+      unpack8<T>(wv[v], wf);
       uint4 pk;
       T* oe = reinterpret_cast<T*>(&pk);
 #pragma unroll

@@ -116,8 +116,11 @@ class QuantDecoder:
         self.cfg, self.batch, self.ctx = cfg, batch, ctx
         self.fused = fused
         # row-parallel sums: the package's one-shot NVLink all-reduce ("peer") up to
-        # PEER_MAX_ELEMS elements, NCCL above that or when allreduce == "nccl"
+        # PEER_MAX_ELEMS elements, NCCL above that or when allreduce == "nccl";
+        # with the peer all-reduce the sum is fused into the norm that follows it
+        # (lmrs_allreduce_rmsnorm[_fp8]) unless fuse_allreduce is False
         self.allreduce_kind = allreduce
+        self.fuse_allreduce = True
         self.par = None
         self.device = torch.device(device)
         self.rank, self.world, self.pg = rank, world, group
@@ -265,6 +268,27 @@ class QuantDecoder:
                 torch.distributed.all_reduce(y, group=self.pg)
         return y
 
+    def _fused_ar(self, partial) -> bool:
+        # the fused kernel's cluster barriers cost more than the saved launch on
+        # one short row (world 1, graph-timed: H 4096 x 1 row 4.67 us against 4.29
+        # for all-reduce + norm; H 8192: 5.25 against 5.92; 64 rows of 4096: 6.10
+        # against 6.73)
+        rows, H = partial.shape[0], partial.shape[-1]
+        return (self.fuse_allreduce and self.world > 1 and self.par is not None
+                and partial.numel() <= self.par.max_elems and (H >= 8192 or rows >= 16))
+
+    def _norm(self, h, w, delta, fp8: bool):
+        """residual h += delta, then the norm (FP8: its e4m3 bytes and scales).
+        delta is a row-parallel projection's per-rank partial sum (None for the
+        first layer): summed over the ranks in the norm's own kernel when the
+        peer all-reduce is up, else all-reduced first."""
+        eps = self.cfg.eps
+        if delta is not None and self._fused_ar(delta):
+            return self.par.rmsnorm_fp8(delta, h, w, eps) if fp8 else self.par.rmsnorm(delta, h, w, eps)
+        if delta is not None:
+            delta = self._all_reduce(delta)
+        return DO.rmsnorm_fp8(h, w, eps, delta) if fp8 else DO.rmsnorm(h, w, eps, delta)
+
     def close(self):
         """Release the all-reduce buffers' IPC mappings (before the process group goes)."""
         if self.par is not None:
@@ -294,23 +318,22 @@ class QuantDecoder:
         for li, L in enumerate(self.layers):
             kc, vc = self.kv[li, 0], self.kv[li, 1]            # [B, hkv, ctx, d]
             if fp8:
-                xq, sx = DO.rmsnorm_fp8(h, L["in_norm"], cfg.eps, delta)
-                qkv = L["qkv"].forward_prequant(xq, sx)
+                qkv = L["qkv"].forward_prequant(*self._norm(h, L["in_norm"], delta, True))
             else:
-                qkv = L["qkv"].forward(DO.rmsnorm(h, L["in_norm"], cfg.eps, delta))
+                qkv = L["qkv"].forward(self._norm(h, L["in_norm"], delta, False))
             q = DO.rope_kv_write(qkv, cos, sin, kc, vc, self.block_tables, self.positions,
                                  self.hq, self.hkv, d)
             a = DO.paged_attention_decode(q, kc, vc, self.block_tables, self.context_lens,
                                           self.ctx, scale, kv_head_map=1, workspace=self.attn_ws)
-            o = self._all_reduce(L["o"].forward(a.view(B, self.hq * d)))
+            o = L["o"].forward(a.view(B, self.hq * d))     # this rank's partial sum
             if fp8:
-                xq, sx = DO.rmsnorm_fp8(h, L["post_norm"], cfg.eps, o)
+                xq, sx = self._norm(h, L["post_norm"], o, True)
                 mq, ms = DO.silu_mul_fp8(L["gate_up"].forward_prequant(xq, sx))
-                delta = self._all_reduce(L["down"].forward_prequant(mq, ms))
+                delta = L["down"].forward_prequant(mq, ms)
             else:
-                gu = L["gate_up"].forward(DO.rmsnorm(h, L["post_norm"], cfg.eps, o))
-                delta = self._all_reduce(L["down"].forward(DO.silu_mul(gu)))
-        r = DO.rmsnorm(h, self.final_norm, cfg.eps, delta)
+                gu = L["gate_up"].forward(self._norm(h, L["post_norm"], o, False))
+                delta = L["down"].forward(DO.silu_mul(gu))
+        r = self._norm(h, self.final_norm, delta, False)
         return r @ self.lm_head.t()                            # [B, vocab / world]
 
     def _logits_torch(self, tokens: Optional[torch.Tensor] = None) -> torch.Tensor:
@@ -368,9 +391,11 @@ class QuantDecoder:
         """Kernels of this package one fused decode step launches: per layer the
         norm, qkv projection, RoPE + KV write, attention, o projection (FP8: its
         per-token quantisation is a second kernel), norm, gate/up, SiLU * up and
-        down, plus one all-reduce after o and after down when tensor parallel;
-        then the final norm (the embedding gather and the LM head are torch)."""
-        per = 9 + (1 if self.cfg.quant == "fp8" else 0) + (2 if self.world > 1 else 0)
+        down, plus one all-reduce after o and after down when tensor parallel
+        unless it is fused into the norm that follows it; then the final norm
+        (the embedding gather and the LM head are torch)."""
+        fused_ar = self.fuse_allreduce and self.par is not None
+        per = 9 + (1 if self.cfg.quant == "fp8" else 0) + (2 if self.world > 1 and not fused_ar else 0)
         return per * self.cfg.layers + 1
 
     def weight_bytes(self) -> int:
