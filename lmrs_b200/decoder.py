@@ -394,7 +394,8 @@ class QuantDecoder:
         down, plus one all-reduce after o and after down when tensor parallel
         unless it is fused into the norm that follows it; then the final norm
         (the embedding gather and the LM head are torch)."""
-        fused_ar = self.fuse_allreduce and self.par is not None
+        fused_ar = self.world > 1 and self._fused_ar(
+            torch.empty((self.batch, self.cfg.hidden), device="meta"))
         per = 9 + (1 if self.cfg.quant == "fp8" else 0) + (2 if self.world > 1 and not fused_ar else 0)
         return per * self.cfg.layers + 1
 
