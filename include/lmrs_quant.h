@@ -97,7 +97,9 @@ LMRS_API int lmrs_version(void);
  * max_context exceeds it, default 2048), "awq_i8_max_m" (1-2 token
  * AWQ on the integer MMA path up to this M, default 1; 0 = fp16 GEMV),
  * "awq_i8_slots", "awq_i8_ctas_per_sm", "awq_i8_cluster", "awq_i8_box_rows", "pdl" (programmatic
- * dependent launch on every kernel, default 1), "wait_limit_kcycles" (how long a
+ * dependent launch on every kernel, default 1), "ar_two_stage_min_world" /
+ * "ar_two_stage_min_elems" (lmrs_allreduce_sum's two-stage form, defaults 4 /
+ * 65536), "wait_limit_kcycles" (how long a
  * kernel's bounded wait spins before it gives up and flags the device error
  * word, in thousands of SM cycles, on the CURRENT device only; <= 0 restores the
  * default of ~2 s; synchronous).

@@ -113,4 +113,99 @@ __global__ void __launch_bounds__(kArThreads) allreduce_ll_kernel(T* out,
   }
 }
 
+// Two-stage form for large messages at many ranks (the one-shot kernel pushes
+// world x n packets per rank, this one about 2n): the packets are cut into
+// `world` slices, slice r owned by rank r.
+//   1. reduce-scatter: every rank pushes its packets of slice r into slot
+//      `rank` of rank r's buffer (the one-shot layout, only slice r's range);
+//   2. the owner polls its slice's packets from every source, sums them in rank
+//      order (the one-shot kernel's arithmetic, so the result is the same),
+//      writes its output and pushes each rounded pair as an all-gather packet
+//      into slot `rank` of every other rank's buffer at the same index: in
+//      rank q's buffer, slot r at indices of slice r is never written by the
+//      reduce-scatter (rank r sends there only slice q), so the two never mix;
+//   3. every rank polls the other slices' all-gather packets and writes them.
+// Same flag / epoch / phase protocol and bounded waits as the one-shot kernel;
+// no CTA waits on another CTA of its own grid.
+template <typename T>
+__global__ void __launch_bounds__(kArThreads) allreduce_2stage_kernel(T* out, const T* in, int n2,
+                                                                      int rank, int world,
+                                                                      ArPeers peers, int cap) {
+  pdl_wait();  // the input is the previous kernel's output
+  pdl_trigger();
+  uint32_t* ctrl = reinterpret_cast<uint32_t*>(peers.buf[rank]) - 16;  // 64-byte header
+  const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(ctrl);
+  const uint64_t flag = static_cast<uint64_t>(epoch + 1u) << 32;
+  const int phase = static_cast<int>(epoch & 1u);
+  const uint32_t* in32 = reinterpret_cast<const uint32_t*>(in);
+  uint32_t* out32 = reinterpret_cast<uint32_t*>(out);
+  const int stride = gridDim.x * blockDim.x;
+  const int i0 = blockIdx.x * blockDim.x + threadIdx.x;
+  const int per = (n2 + world - 1) / world;  // packets per slice
+  auto slot = [&](int dst, int src) {
+    return peers.buf[dst] + (static_cast<int64_t>(phase) * world + src) * cap;
+  };
+  auto wait_pkt = [&](const uint64_t* src, bool& ok) -> uint64_t {
+    uint64_t pkt = ld_sys_b64(src);
+    if ((pkt & 0xFFFFFFFF00000000ull) != flag) {
+      const long long t0 = clock64();
+      long long limit = -1;
+      while (ok && ((pkt = ld_sys_b64(src)) & 0xFFFFFFFF00000000ull) != flag) {
+        if (wait_expired(t0, limit)) {
+          atomicOr(&g_device_error, kErrWaitPeer);
+          ok = false;
+        }
+      }
+    }
+    return pkt;
+  };
+
+  // 1. reduce-scatter: packets of slice r to rank r (its own slice too)
+  for (int k = i0; k < n2; k += stride) {
+    const int r = k / per;
+    st_sys_b64(slot(r, rank) + k, flag | in32[k]);
+  }
+  // 2. own slice: rank-order sum, output, all-gather packets to the others
+  bool ok = true;
+  const int lo = rank * per, hi = min(n2, lo + per);
+  const uint64_t* own = peers.buf[rank] + static_cast<int64_t>(phase) * world * cap;
+  for (int k = lo + i0; k < hi; k += stride) {
+    float a0 = 0.f, a1 = 0.f;
+    for (int s = 0; s < world; ++s) {
+      const uint64_t pkt = wait_pkt(own + static_cast<int64_t>(s) * cap + k, ok);
+      if ((pkt & 0xFFFFFFFF00000000ull) != flag) {  // gave up on this source
+        a0 = a1 = __int_as_float(0x7fc00000);
+        continue;
+      }
+      const uint32_t v = static_cast<uint32_t>(pkt);
+      T pair[2];
+      *reinterpret_cast<uint32_t*>(pair) = v;
+      a0 += static_cast<float>(pair[0]);
+      a1 += static_cast<float>(pair[1]);
+    }
+    T res[2] = {T(a0), T(a1)};
+    const uint32_t rv = *reinterpret_cast<uint32_t*>(res);
+    out32[k] = rv;
+    for (int q = 0; q < world; ++q)
+      if (q != rank) st_sys_b64(slot(q, rank) + k, flag | rv);
+  }
+  // 3. the other slices, from their owners
+  for (int k = i0; k < n2; k += stride) {
+    const int r = k / per;
+    if (r == rank) continue;
+    const uint64_t pkt = wait_pkt(own + static_cast<int64_t>(r) * cap + k, ok);
+    out32[k] = (pkt & 0xFFFFFFFF00000000ull) == flag ? static_cast<uint32_t>(pkt) : 0x7fc07fc0u;
+  }
+
+  // advance the epoch once every CTA is done with this call
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    if (atomicAdd(ctrl + 1, 1u) == gridDim.x - 1) {
+      ctrl[1] = 0u;
+      *reinterpret_cast<volatile uint32_t*>(ctrl) = epoch + 1u;
+    }
+  }
+}
+
 }  // namespace lmrs

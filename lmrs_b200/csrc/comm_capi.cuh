@@ -22,9 +22,11 @@ int allreduce_launch(void* out, const void* in, size_t n, int rank, int world,
   // every CTA resident at once: the CTAs of all ranks wait on one another
   if (grid > sm_count(dev)) grid = sm_count(dev);
   if (grid < 1) grid = 1;
-  int rc = launch_ex(lmrs::allreduce_ll_kernel<T>, grid, 0, lmrs::kArThreads, 0, st,
-                     static_cast<T*>(out), static_cast<const T*>(in), n2, rank, world, peers,
-                     static_cast<int>(ar_cap(max_elems)));
+  const bool two = world >= g_tune.ar_two_stage_min_world &&
+                   static_cast<long long>(n) >= g_tune.ar_two_stage_min_elems;
+  int rc = launch_ex(two ? lmrs::allreduce_2stage_kernel<T> : lmrs::allreduce_ll_kernel<T>, grid,
+                     0, lmrs::kArThreads, 0, st, static_cast<T*>(out), static_cast<const T*>(in),
+                     n2, rank, world, peers, static_cast<int>(ar_cap(max_elems)));
   return rc ? rc : after_launch();
 }
 

@@ -56,6 +56,10 @@ struct Tuning {
   int awq_gemm_pair = 0;     // 1: CTA-pair (cta_group::2) GEMM for large M; 0: one-SM tiles
   int gemm_bn = 256;         // one-SM GEMM tile width: 256 or 224; 0 = pick by wave count
   int fp8_gemv_cluster = 0;
+  // all-reduce: the two-stage (reduce-scatter + all-gather) kernel from this many
+  // ranks and elements (the one-shot kernel pushes world x n packets per rank)
+  int ar_two_stage_min_world = 4;
+  int ar_two_stage_min_elems = 65536;
   // FP8 GEMM tile order: groups of this many M tiles walked N tile by N tile.
   // Graph-timed at M = 2048..8192 on the config-2 shapes, 32 beat 8 by 1-4 %
   // (4096 x 28672 at 8192: 838.8 vs 846.6 us; 14336 x 4096: 354.6 vs 364.9).
@@ -965,6 +969,8 @@ int lmrs_set_tuning(const char* key, int value) {
   else if (!strcmp(key, "attn_global_merge")) g_tune.attn_global_merge = value ? 1 : 0;
   else if (!strcmp(key, "attn_multi_min_ctx")) g_tune.attn_multi_min_ctx = value;
   else if (!strcmp(key, "fp8_gemv_cluster")) g_tune.fp8_gemv_cluster = value;
+  else if (!strcmp(key, "ar_two_stage_min_world")) g_tune.ar_two_stage_min_world = value;
+  else if (!strcmp(key, "ar_two_stage_min_elems")) g_tune.ar_two_stage_min_elems = value;
   else if (!strcmp(key, "fp8_gemm_group_m")) g_tune.fp8_gemm_group_m = value;
   else if (!strcmp(key, "fp8_gemm_bn128")) g_tune.fp8_gemm_bn128 = value ? 1 : 0;
   else if (!strcmp(key, "fp8_swap_max_m")) g_tune.fp8_swap_max_m = value;

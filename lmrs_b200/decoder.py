@@ -258,7 +258,10 @@ class QuantDecoder:
         rot = torch.cat([-x[..., half:], x[..., :half]], dim=-1)
         return x * self.cos + rot * self.sin
 
-    PEER_MAX_ELEMS = 1 << 20
+    PEER_MAX_ELEMS = 1 << 22
+    # lmrs_allreduce_sum's defaults for its two-stage form (reduce-scatter +
+    # all-gather); the fused all-reduce + norm is one-shot only
+    TWO_STAGE_MIN_WORLD, TWO_STAGE_MIN_ELEMS = 4, 65536
 
     def _all_reduce(self, y):
         if self.world > 1:
@@ -272,10 +275,14 @@ class QuantDecoder:
         # the fused kernel's cluster barriers cost more than the saved launch on
         # one short row (world 1, graph-timed: H 4096 x 1 row 4.67 us against 4.29
         # for all-reduce + norm; H 8192: 5.25 against 5.92; 64 rows of 4096: 6.10
-        # against 6.73)
+        # against 6.73); large messages at 4+ ranks take the two-stage all-reduce
+        # (about 2n packets per rank instead of world x n) and a separate norm
         rows, H = partial.shape[0], partial.shape[-1]
+        two_stage = (self.world >= self.TWO_STAGE_MIN_WORLD
+                     and partial.numel() >= self.TWO_STAGE_MIN_ELEMS)
         return (self.fuse_allreduce and self.world > 1 and self.par is not None
-                and partial.numel() <= self.par.max_elems and (H >= 8192 or rows >= 16))
+                and partial.numel() <= self.par.max_elems and (H >= 8192 or rows >= 16)
+                and not two_stage)
 
     def _norm(self, h, w, delta, fp8: bool):
         """residual h += delta, then the norm (FP8: its e4m3 bytes and scales).

@@ -71,6 +71,30 @@ def _worker(rank, world, port, out_path):
                 expect = expect * world
             results[("graph", it)] = (bool(torch.all(buf.float() == expect.item())), True)
         del gr
+        # the two-stage form (reduce-scatter + all-gather; by default from 4
+        # ranks), forced here at 2: the same exact sums, slices uneven or empty
+        try:
+            L.set_tuning("ar_two_stage_min_world", 2)
+            L.set_tuning("ar_two_stage_min_elems", 2)
+            for dtype in (torch.bfloat16, torch.float16):
+                for n in (2, 8194, 262144):
+                    for rep in range(2):
+                        g = torch.Generator(device=dev).manual_seed(77 * rep + n + rank)
+                        x = (torch.randn(n, generator=g, device=dev) * (rank + 1)).to(dtype)
+                        parts = [torch.empty_like(x) for _ in range(world)]
+                        dist.all_gather(parts, x)
+                        ref = parts[0].float()
+                        for p in parts[1:]:
+                            ref = ref + p.float()
+                        ar(x)
+                        ok = torch.equal(x, ref.to(dtype))
+                        allx = [torch.empty_like(x) for _ in range(world)]
+                        dist.all_gather(allx, x)
+                        same = all(torch.equal(allx[0], a) for a in allx)
+                        results[("two-stage", str(dtype), n, rep)] = (ok, same)
+        finally:
+            L.set_tuning("ar_two_stage_min_world", 4)
+            L.set_tuning("ar_two_stage_min_elems", 65536)
         # the fused all-reduce + residual add + RMSNorm against the all-reduce
         # followed by the norm kernel; identical on both ranks
         from lmrs_b200 import decode_ops as DO
