@@ -84,7 +84,8 @@ LMRS_API int lmrs_version(void);
 /* Measurement knobs (dispatch thresholds, split-K shape, launch mode); 0 on a
  * known key, LMRS_ERR_SHAPE otherwise.  Keys: "awq_gemv_max_m", "awq_swap_max_m",
  * "awq_swap_deep_k" (swap-AB up to 128 tokens when 4K >= value x N, default 5; 0 = off),
- * "awq_swap_cluster", "awq_gemm_pair", "gemm_bn", "fp8_gemv_max_m",
+ * "awq_swap_cluster", "awq_swap_narrow_tiles" (swap-AB up to 128 tokens while N / 128
+ * is at most this, default 32; 0 = off), "awq_gemm_pair", "gemm_bn", "fp8_gemv_max_m",
  * "gemv_ctas_per_sm", "awq_gemv_cluster", "fp8_gemv_cluster", "fp8_gemv_max_kn",
  * "fp8_swap_max_m", "fp8_swap_cluster", "fp8_gemm_group_m" (FP8 GEMM tile order: M
  * tiles per group, default 32), "fp8_gemm_bn128" (128-wide FP8 GEMM tiles while

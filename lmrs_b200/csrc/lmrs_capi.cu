@@ -53,6 +53,7 @@ struct Tuning {
   int gemv_ctas_per_sm = 4;  // resident CTAs per SM the GEMV grids are sized for
   int awq_gemv_cluster = 0;  // 0 = heuristic
   int awq_swap_cluster = 0;  // 0 = heuristic
+  int awq_swap_narrow_tiles = 32;  // swap-AB up to 128 tokens while N / 128 <= this (0 = off)
   int awq_gemm_pair = 0;     // 1: CTA-pair (cta_group::2) GEMM for large M; 0: one-SM tiles
   int gemm_bn = 256;         // one-SM GEMM tile width: 256 or 224; 0 = pick by wave count
   int fp8_gemv_cluster = 0;
@@ -396,13 +397,19 @@ bool awq_use_tmem(int M, int K, int N) {
 // 57344: 156 vs 172) or the tokens pass 64 on shallow K (4096 x 14336 at 96: 33
 // vs 54 us).  The crossover in K / N at 96-128 tokens lies between 1 (4096 x
 // 4096: GEMM 30.7 vs 31.4 us) and 1.33 (4096 x 3072: swap 21.6 vs 30.6 us), so
-// swap from K >= 1.25 N.
+// swap from K >= 1.25 N.  With the split-K clusters sized to a power of two,
+// narrow outputs (at most awq_swap_narrow_tiles 128-channel tiles) take swap-AB
+// up to 128 tokens as well (bf16, 4096 x 4096 at 96 / 128 tokens: 17.1 / 18.5 us
+// against 27.3 / 27.6 for the tile GEMM; 4096 x 6144, 48 tiles, stays on the GEMM:
+// 27.8 against 29.8).
 bool awq_use_swap(int M, int K, int N, int sms) {
   if (M > 128) return false;
   if (g_tune.awq_swap_deep_k > 0 &&
       4LL * K >= static_cast<long long>(g_tune.awq_swap_deep_k) * N)
     return true;
-  return M <= g_tune.awq_swap_max_m && (N + lmrs::kAgtCh - 1) / lmrs::kAgtCh < sms;
+  const int tiles = (N + lmrs::kAgtCh - 1) / lmrs::kAgtCh;
+  if (tiles <= g_tune.awq_swap_narrow_tiles) return true;
+  return M <= g_tune.awq_swap_max_m && tiles < sms;
 }
 
 template <typename T>
@@ -566,7 +573,10 @@ int awq_swap_launch_nt(T* y, const T* x, const int32_t* qw, const int32_t* qz, c
   // CTAs resident per SM at this tile width (launch bounds allow 2; the
   // 128-token tile's ~117 KB of shared memory leaves room for one)
   constexpr int per_sm = (228 * 1024) / (smem + 1024) < 2 ? 1 : 2;
-  int C = g_tune.awq_swap_cluster > 0 ? g_tune.awq_swap_cluster : (per_sm * sm_count(dev)) / tiles;
+  // split-K clusters of a power of two: 4096 x 6144 at 48 tokens took 27.2 us on
+  // the 3-CTA clusters the plain quotient gave, 20.9 on 4 and 25.1 on 2
+  int C = g_tune.awq_swap_cluster > 0 ? g_tune.awq_swap_cluster
+                                      : pow2_floor(clampi((per_sm * sm_count(dev)) / tiles, 1, 8));
   C = clampi(C, 1, 8);
   if (C > KB) C = KB;
   rc = launch_cluster(lmrs::awq_gemm_swap_kernel<NT, T>, tiles * C, C, lmrs::kSwThreads, smem,
@@ -954,6 +964,7 @@ int lmrs_set_tuning(const char* key, int value) {
   else if (!strcmp(key, "awq_swap_max_m")) g_tune.awq_swap_max_m = value;
   else if (!strcmp(key, "awq_swap_deep_k")) g_tune.awq_swap_deep_k = value;
   else if (!strcmp(key, "awq_swap_cluster")) g_tune.awq_swap_cluster = value;
+  else if (!strcmp(key, "awq_swap_narrow_tiles")) g_tune.awq_swap_narrow_tiles = value;
   else if (!strcmp(key, "awq_gemm_pair")) g_tune.awq_gemm_pair = value;
   else if (!strcmp(key, "gemm_bn")) g_tune.gemm_bn = value;
   else if (!strcmp(key, "fp8_gemv_max_m")) g_tune.fp8_gemv_max_m = value;
