@@ -42,7 +42,7 @@ LMRS_API int lmrs_ipc_close(void* ptr);
  * results are bit-identical on all ranks.  A wait for a peer that never
  * arrives gives up after ~2 s (lmrs_set_tuning "wait_limit_kcycles"), flags
  * kErrWaitPeer (bit 5) in lmrs_read_device_error and leaves NaN in every
- * output element that source's packets did not reach.  From 4 ranks and 65536
+ * output element that source's packets did not reach.  From 4 ranks and 131072
  * elements (lmrs_set_tuning "ar_two_stage_min_world" / "ar_two_stage_min_elems")
  * the sum runs as reduce-scatter + all-gather in one kernel (about 2n packets
  * per rank instead of world x n), with the same result. */

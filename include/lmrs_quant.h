@@ -100,7 +100,7 @@ LMRS_API int lmrs_version(void);
  * "awq_i8_slots", "awq_i8_ctas_per_sm", "awq_i8_cluster", "awq_i8_box_rows", "pdl" (programmatic
  * dependent launch on every kernel, default 1), "ar_two_stage_min_world" /
  * "ar_two_stage_min_elems" (lmrs_allreduce_sum's two-stage form, defaults 4 /
- * 65536), "wait_limit_kcycles" (how long a
+ * 131072), "wait_limit_kcycles" (how long a
  * kernel's bounded wait spins before it gives up and flags the device error
  * word, in thousands of SM cycles, on the CURRENT device only; <= 0 restores the
  * default of ~2 s; synchronous).

@@ -58,9 +58,12 @@ struct Tuning {
   int gemm_bn = 256;         // one-SM GEMM tile width: 256 or 224; 0 = pick by wave count
   int fp8_gemv_cluster = 0;
   // all-reduce: the two-stage (reduce-scatter + all-gather) kernel from this many
-  // ranks and elements (the one-shot kernel pushes world x n packets per rank)
+  // ranks and elements (the one-shot kernel pushes world x n packets per rank).
+  // TP=8 decode steps: config 4 at batch 32 (262144 elements) 10.34 -> 8.73 ms,
+  // config 3 at batch 64 3.86 -> 3.26 ms; at 65536 elements (config 3, batch 16)
+  // the one-shot kernel fused into the norm stays ahead (2.22 vs 2.28 ms)
   int ar_two_stage_min_world = 4;
-  int ar_two_stage_min_elems = 65536;
+  int ar_two_stage_min_elems = 131072;
   // FP8 GEMM tile order: groups of this many M tiles walked N tile by N tile.
   // Graph-timed at M = 2048..8192 on the config-2 shapes, 32 beat 8 by 1-4 %
   // (4096 x 28672 at 8192: 838.8 vs 846.6 us; 14336 x 4096: 354.6 vs 364.9).

@@ -261,7 +261,7 @@ class QuantDecoder:
     PEER_MAX_ELEMS = 1 << 22
     # lmrs_allreduce_sum's defaults for its two-stage form (reduce-scatter +
     # all-gather); the fused all-reduce + norm is one-shot only
-    TWO_STAGE_MIN_WORLD, TWO_STAGE_MIN_ELEMS = 4, 65536
+    TWO_STAGE_MIN_WORLD, TWO_STAGE_MIN_ELEMS = 4, 131072
 
     def _all_reduce(self, y):
         if self.world > 1:

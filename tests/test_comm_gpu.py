@@ -94,7 +94,7 @@ def _worker(rank, world, port, out_path):
                         results[("two-stage", str(dtype), n, rep)] = (ok, same)
         finally:
             L.set_tuning("ar_two_stage_min_world", 4)
-            L.set_tuning("ar_two_stage_min_elems", 65536)
+            L.set_tuning("ar_two_stage_min_elems", 131072)
         # the fused all-reduce + residual add + RMSNorm against the all-reduce
         # followed by the norm kernel; identical on both ranks
         from lmrs_b200 import decode_ops as DO
