@@ -66,8 +66,9 @@ LMRS_API int lmrs_rope_kv_write(void* q_out, void* key_cache, void* value_cache,
 /* Workspace for lmrs_paged_attention_decode with these sizes on the current
  * device: 0 when the context splits of each sequence and KV head are few enough
  * (<= 8) to merge their partials in a thread-block cluster's distributed shared
- * memory; otherwise (small batches, long contexts) room for every split's
- * fp32 (O, m, l) partial plus one arrival counter per sequence and KV head.
+ * memory; otherwise (small batches, contexts above 2048) room for the fp32
+ * (O, m, l) partial of every 8-split cluster plus one arrival counter per
+ * sequence and KV head.
  * The workspace must be zero-filled before its first use; every call leaves
  * the counters at zero again.  Calls that overlap on the GPU need separate
  * workspaces. */
@@ -92,6 +93,22 @@ LMRS_API int lmrs_paged_attention_decode(void* out, const void* query, const voi
                                          int max_blocks_per_seq, int max_context, float scale,
                                          int kv_head_map, int dtype, void* workspace,
                                          size_t workspace_bytes, lmrs_stream_t stream);
+
+/* lmrs_paged_attention_decode followed by lmrs_fp8_quant_rows of its output rows
+ * ([num_seqs, num_heads * head_size] -> e4m3 q_out, fp32 scale_out[num_seqs]):
+ * the input of an FP8 o projection.  With one KV head (a tensor-parallel rank
+ * holding one KV head) the attention's final merge quantises whole rows itself
+ * (one launch); otherwise two launches.  Bytes and scales equal the two calls
+ * made separately; out is written as well.  q_out 16-byte aligned. */
+LMRS_API int lmrs_paged_attention_decode_fp8(uint8_t* q_out, float* scale_out, void* out,
+                                             const void* query, const void* key_cache,
+                                             const void* value_cache, const int32_t* block_tables,
+                                             const int32_t* context_lens, int num_seqs,
+                                             int num_heads, int num_kv_heads, int head_size,
+                                             int block_size, int max_blocks_per_seq,
+                                             int max_context, float scale, int kv_head_map,
+                                             int dtype, void* workspace, size_t workspace_bytes,
+                                             lmrs_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -117,7 +117,8 @@ template <typename T, int NS>
 int attn_launch(void* out, const void* q, const void* kc, const void* vc,
                 const int32_t* tables, const int32_t* lens, int seqs, int heads, int hkv,
                 int bs, int maxb, const AttnSplit& sp, float scale, int map, void* ws,
-                cudaStream_t st, int dev, std::atomic<int>* done) {
+                cudaStream_t st, int dev, std::atomic<int>* done, uint8_t* qout = nullptr,
+                float* qscale = nullptr) {
   const int splits = sp.splits, span = sp.span;
   float* ws_part = nullptr;
   uint32_t* ws_count = nullptr;
@@ -154,7 +155,7 @@ int attn_launch(void* out, const void* q, const void* kc, const void* vc,
   cudaError_t e = cudaLaunchKernelEx(&c, lmrs::decode_attn_kernel<T, NS>, static_cast<T*>(out),
                                      static_cast<const T*>(q), static_cast<const T*>(kc),
                                      static_cast<const T*>(vc), tables, lens, heads, hkv, bs, maxb,
-                                     span, scale_log2, map, ws_part, ws_count);
+                                     span, scale_log2, map, ws_part, ws_count, qout, qscale);
   if (e != cudaSuccess) return record(e);
   return after_launch();
 }
@@ -279,13 +280,17 @@ LMRS_API size_t lmrs_paged_attention_workspace_bytes(int num_seqs, int num_heads
                        attn_split(num_seqs, num_kv_heads, max_context, sm_count_cached()));
 }
 
-LMRS_API int lmrs_paged_attention_decode(void* out, const void* query, const void* key_cache,
-                                         const void* value_cache, const int32_t* block_tables,
-                                         const int32_t* context_lens, int num_seqs, int num_heads,
-                                         int num_kv_heads, int head_size, int block_size,
-                                         int max_blocks_per_seq, int max_context, float scale,
-                                         int kv_head_map, int dtype, void* workspace,
-                                         size_t workspace_bytes, lmrs_stream_t stream) {
+}  // extern "C"
+
+namespace {
+
+int paged_attention_impl(void* out, const void* query, const void* key_cache,
+                         const void* value_cache, const int32_t* block_tables,
+                         const int32_t* context_lens, int num_seqs, int num_heads,
+                         int num_kv_heads, int head_size, int block_size, int max_blocks_per_seq,
+                         int max_context, float scale, int kv_head_map, int dtype,
+                         void* workspace, size_t workspace_bytes, lmrs_stream_t stream,
+                         uint8_t* qout, float* qscale) {
   if (!act_dtype(dtype)) return LMRS_ERR_DTYPE;
   if (num_seqs < 0 || num_heads <= 0 || num_kv_heads <= 0 || num_heads % num_kv_heads ||
       num_heads / num_kv_heads > 16 || head_size != lmrs::kAttnD || block_size <= 0 ||
@@ -311,7 +316,7 @@ LMRS_API int lmrs_paged_attention_decode(void* out, const void* query, const voi
   return attn_launch<T, NS>(out, query, key_cache, value_cache, block_tables,                   \
                             context_lens, num_seqs, num_heads, num_kv_heads, block_size,        \
                             max_blocks_per_seq, sp, scale, kv_head_map, workspace, st, dev,     \
-                            g_smem_attn[I][NS - 2])
+                            g_smem_attn[I][NS - 2], qout, qscale)
   if (dtype == LMRS_DTYPE_BF16) {
     if (ns == 2) LMRS_ATTN(__nv_bfloat16, 0, 2);
     if (ns == 3) LMRS_ATTN(__nv_bfloat16, 0, 3);
@@ -321,6 +326,51 @@ LMRS_API int lmrs_paged_attention_decode(void* out, const void* query, const voi
   if (ns == 3) LMRS_ATTN(__half, 1, 3);
   LMRS_ATTN(__half, 1, 4);
 #undef LMRS_ATTN
+}
+
+}  // namespace
+
+extern "C" {
+
+LMRS_API int lmrs_paged_attention_decode(void* out, const void* query, const void* key_cache,
+                                         const void* value_cache, const int32_t* block_tables,
+                                         const int32_t* context_lens, int num_seqs, int num_heads,
+                                         int num_kv_heads, int head_size, int block_size,
+                                         int max_blocks_per_seq, int max_context, float scale,
+                                         int kv_head_map, int dtype, void* workspace,
+                                         size_t workspace_bytes, lmrs_stream_t stream) {
+  return paged_attention_impl(out, query, key_cache, value_cache, block_tables, context_lens,
+                              num_seqs, num_heads, num_kv_heads, head_size, block_size,
+                              max_blocks_per_seq, max_context, scale, kv_head_map, dtype,
+                              workspace, workspace_bytes, stream, nullptr, nullptr);
+}
+
+// One KV head (tensor-parallel ranks of GQA models with as many ranks as KV
+// heads): the attention's final merge holds whole token rows and emits their
+// e4m3 bytes and scales itself; otherwise the attention, then the row quant.
+LMRS_API int lmrs_paged_attention_decode_fp8(uint8_t* q_out, float* scale_out, void* out,
+                                             const void* query, const void* key_cache,
+                                             const void* value_cache, const int32_t* block_tables,
+                                             const int32_t* context_lens, int num_seqs,
+                                             int num_heads, int num_kv_heads, int head_size,
+                                             int block_size, int max_blocks_per_seq,
+                                             int max_context, float scale, int kv_head_map,
+                                             int dtype, void* workspace, size_t workspace_bytes,
+                                             lmrs_stream_t stream) {
+  if (num_seqs > 0 && (!q_out || !scale_out)) return LMRS_ERR_NULL;
+  if (q_out && !aligned16(q_out)) return LMRS_ERR_ALIGN;
+  if (num_kv_heads == 1)
+    return paged_attention_impl(out, query, key_cache, value_cache, block_tables, context_lens,
+                                num_seqs, num_heads, num_kv_heads, head_size, block_size,
+                                max_blocks_per_seq, max_context, scale, kv_head_map, dtype,
+                                workspace, workspace_bytes, stream, q_out, scale_out);
+  int rc = paged_attention_impl(out, query, key_cache, value_cache, block_tables, context_lens,
+                                num_seqs, num_heads, num_kv_heads, head_size, block_size,
+                                max_blocks_per_seq, max_context, scale, kv_head_map, dtype,
+                                workspace, workspace_bytes, stream, nullptr, nullptr);
+  if (rc || num_seqs == 0) return rc;
+  return lmrs_fp8_quant_rows(q_out, scale_out, out, num_seqs, num_heads * head_size, dtype,
+                             stream);
 }
 
 }  // extern "C"

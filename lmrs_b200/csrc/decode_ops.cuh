@@ -487,7 +487,8 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(
     const T* __restrict__ k_cache, const T* __restrict__ v_cache,
     const int32_t* __restrict__ tables, const int32_t* __restrict__ ctx_lens, int num_heads,
     int num_kv_heads, int block_size, int max_blocks, int span, float scale_log2, int kv_map,
-    float* __restrict__ ws_part, uint32_t* __restrict__ ws_count) {
+    float* __restrict__ ws_part, uint32_t* __restrict__ ws_count, uint8_t* __restrict__ qout,
+    float* __restrict__ qscale) {
   pdl_wait();
   pdl_trigger();
   // per warp [NS stages][K 16 rows | V 16 rows], rows padded to kAttnRowBytes;
@@ -683,6 +684,50 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(
     }
   }
   __syncthreads();
+  // FP8 output (one KV head: a (sequence, KV head) is a whole token row): every
+  // path below leaves at most one (row, 16-dim) item of the final output with a
+  // thread, kept rounded in qv; the row's maximum, scale and e4m3 bytes then
+  // follow fp8_quant_rows_kernel's arithmetic
+  static_assert(16 * 8 <= kAttnThreads, "one output item per thread");
+  __shared__ float qred[32];
+  __shared__ float qslot[kAttnMaxCluster];
+  float qv[16];
+  int qe = -1;
+  auto item_out = [&](int e, int r, int d0, const float (&acc)[16], float L) {
+    T* dst = out + (static_cast<int64_t>(seq) * num_heads + qhead(r)) * kAttnD + d0;
+    const float inv = L > 0.f ? 1.f / L : 0.f;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const T o = Act<T>::from_float(acc[i] * inv);
+      dst[i] = o;
+      qv[i] = Act<T>::to_float(o);
+    }
+    qe = e;
+  };
+  auto item_max = [&]() {
+    float m = 0.f;
+    if (qe >= 0) {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) m = fmaxf(m, fabsf(qv[i]));
+    }
+    return m;
+  };
+  auto item_e4m3 = [&](float rmax) {
+    const float sc = __fdiv_rn(rmax, 448.0f);
+    if (qe >= 0) {
+      const int r = qe >> 3, d0 = (qe & 7) * 16;
+      uint8_t* qd = qout + (static_cast<int64_t>(seq) * num_heads + qhead(r)) * kAttnD + d0;
+      float lo[8], hi[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        lo[i] = qv[i];
+        hi[i] = qv[8 + i];
+      }
+      *reinterpret_cast<uint2*>(qd) = e4m3x8(lo, sc);
+      *reinterpret_cast<uint2*>(qd + 8) = e4m3x8(hi, sc);
+    }
+    return sc;
+  };
   // thread -> (row r, 16 consecutive dims)
   for (int e = threadIdx.x; e < G * 8; e += kAttnThreads) {
     const int r = e >> 3, d0 = (e & 7) * 16;
@@ -700,12 +745,8 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(
 #pragma unroll
       for (int i = 0; i < 16; ++i) acc[i] += f * wr[d0 + i];
     }
-    const int h = qhead(r);
     if (splits == 1) {
-      T* dst = out + (static_cast<int64_t>(seq) * num_heads + h) * kAttnD + d0;
-      const float inv = L > 0.f ? 1.f / L : 0.f;
-#pragma unroll
-      for (int i = 0; i < 16; ++i) dst[i] = Act<T>::from_float(acc[i] * inv);
+      item_out(e, r, d0, acc, L);
     } else {
       // partial: O (unnormalised, fp32), then m, l, in shared memory
       float* pw = part + r * kAttnPartStride;
@@ -717,7 +758,13 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(
       }
     }
   }
-  if (splits == 1) return;
+  if (splits == 1) {
+    if (qout != nullptr) {
+      const float sc = item_e4m3(block_max(item_max(), qred));
+      if (threadIdx.x == 0) qscale[seq] = sc;
+    }
+    return;
+  }
   // ---- first level: the cluster's splits, through distributed shared memory
   const int cs = splits < kAttnMaxCluster ? splits : kAttnMaxCluster;  // cluster size
   const int crank = split % cs, nclu = splits / cs, clu = split / cs;
@@ -735,10 +782,7 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(
       for (int q = 0; q < 4; ++q) o[q] = ld_cluster_v4(pr + static_cast<uint32_t>(d0 + 4 * q) * 4u);
     }, M, L, acc);
     if (nclu == 1) {
-      T* dst = out + (static_cast<int64_t>(seq) * num_heads + qhead(r)) * kAttnD + d0;
-      const float inv = L > 0.f ? 1.f / L : 0.f;
-#pragma unroll
-      for (int i = 0; i < 16; ++i) dst[i] = Act<T>::from_float(acc[i] * inv);
+      item_out(e, r, d0, acc, L);
     } else {   // this cluster's partial, item by item, into the workspace
       float* pw = ws_part + ((static_cast<int64_t>(blockIdx.x) * nclu + clu) * 16 + r) * kAttnPartStride;
 #pragma unroll
@@ -747,11 +791,25 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(
       if (d0 == 0) __stcg(reinterpret_cast<float2*>(pw + kAttnD), make_float2(M, L));
     }
   }
+  // FP8, one cluster: each CTA's maximum into slot[rank] of every CTA
+  if (qout != nullptr && nclu == 1) {
+    const float m = block_max(item_max(), qred);
+    if (threadIdx.x < cs)
+      st_cluster_f32(mapa_shared(smem_u32(&qslot[crank]), static_cast<uint32_t>(threadIdx.x)), m);
+  }
   // no CTA leaves while a peer may read its partial; the release / acquire of
   // the cluster barrier also orders every thread's workspace items before the
   // arrival below (the CTA-barrier-then-one-fenced-atomic pattern)
   cluster_sync_all();
-  if (nclu == 1) return;
+  if (nclu == 1) {
+    if (qout != nullptr) {
+      float rmax = qslot[0];
+      for (int q = 1; q < cs; ++q) rmax = fmaxf(rmax, qslot[q]);
+      const float sc = item_e4m3(rmax);
+      if (crank == 0 && threadIdx.x == 0) qscale[seq] = sc;
+    }
+    return;
+  }
   // ---- second level: the cluster partials, by the last cluster to arrive
   __shared__ uint32_t s_last;
   if (threadIdx.x == 0) {
@@ -775,10 +833,11 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(
 #pragma unroll
       for (int q = 0; q < 4; ++q) o[q] = __ldcg(reinterpret_cast<const float4*>(pr + d0 + 4 * q));
     }, M, L, acc);
-    T* dst = out + (static_cast<int64_t>(seq) * num_heads + qhead(r)) * kAttnD + d0;
-    const float inv = L > 0.f ? 1.f / L : 0.f;
-#pragma unroll
-    for (int i = 0; i < 16; ++i) dst[i] = Act<T>::from_float(acc[i] * inv);
+    item_out(e, r, d0, acc, L);
+  }
+  if (qout != nullptr) {
+    const float sc = item_e4m3(block_max(item_max(), qred));
+    if (threadIdx.x == 0) qscale[seq] = sc;
   }
   if (threadIdx.x == 0) ws_count[blockIdx.x] = 0u;  // ready for the next call
 }

@@ -134,3 +134,28 @@ def paged_attention_decode(query: torch.Tensor, key_cache: torch.Tensor,
         int(max_context), float(scale), int(kv_head_map), _code(query), _ptr(ws), need,
         _stream(query)))
     return out
+
+
+def paged_attention_decode_fp8(query: torch.Tensor, key_cache: torch.Tensor,
+                               value_cache: torch.Tensor, block_tables: torch.Tensor,
+                               context_lens: torch.Tensor, max_context: int, scale: float,
+                               kv_head_map: int = 1,
+                               workspace: Optional[AttentionWorkspace] = None):
+    """paged_attention_decode, then the per-row e4m3 quantisation of its output
+    rows [seqs, heads * 128] (the input of an FP8 o projection): returns (e4m3
+    bytes, per-row fp32 scales, out).  One kernel when the cache has one KV head."""
+    _require_cuda(query, "query")
+    seqs, heads, d = query.shape
+    num_kv_heads, block_size = key_cache.shape[1], key_cache.shape[2]
+    lib = _lib.load()
+    need = lib.lmrs_paged_attention_workspace_bytes(seqs, heads, num_kv_heads, max_context)
+    ws = (workspace or AttentionWorkspace()).get(need, query.device)
+    out = torch.empty_like(query)
+    q = torch.empty((seqs, heads * d), dtype=torch.uint8, device=query.device)
+    sc = torch.empty((seqs,), dtype=torch.float32, device=query.device)
+    _lib.check("lmrs_paged_attention_decode_fp8", lib.lmrs_paged_attention_decode_fp8(
+        _ptr(q), _ptr(sc), _ptr(out), _ptr(query), _ptr(key_cache), _ptr(value_cache),
+        _ptr(block_tables), _ptr(context_lens), seqs, heads, num_kv_heads, d, block_size,
+        block_tables.shape[1], int(max_context), float(scale), int(kv_head_map), _code(query),
+        _ptr(ws), need, _stream(query)))
+    return q, sc, out

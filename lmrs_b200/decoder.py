@@ -330,9 +330,15 @@ class QuantDecoder:
                 qkv = L["qkv"].forward(self._norm(h, L["in_norm"], delta, False))
             q = DO.rope_kv_write(qkv, cos, sin, kc, vc, self.block_tables, self.positions,
                                  self.hq, self.hkv, d)
-            a = DO.paged_attention_decode(q, kc, vc, self.block_tables, self.context_lens,
-                                          self.ctx, scale, kv_head_map=1, workspace=self.attn_ws)
-            o = L["o"].forward(a.view(B, self.hq * d))     # this rank's partial sum
+            if fp8:  # the o projection's e4m3 input straight from the attention
+                aq, asc, _ = DO.paged_attention_decode_fp8(
+                    q, kc, vc, self.block_tables, self.context_lens, self.ctx, scale,
+                    kv_head_map=1, workspace=self.attn_ws)
+                o = L["o"].forward_prequant(aq, asc)      # this rank's partial sum
+            else:
+                a = DO.paged_attention_decode(q, kc, vc, self.block_tables, self.context_lens,
+                                              self.ctx, scale, kv_head_map=1, workspace=self.attn_ws)
+                o = L["o"].forward(a.view(B, self.hq * d))  # this rank's partial sum
             if fp8:
                 xq, sx = self._norm(h, L["post_norm"], o, True)
                 mq, ms = DO.silu_mul_fp8(L["gate_up"].forward_prequant(xq, sx))
@@ -403,7 +409,10 @@ class QuantDecoder:
         (the embedding gather and the LM head are torch)."""
         fused_ar = self.world > 1 and self._fused_ar(
             torch.empty((self.batch, self.cfg.hidden), device="meta"))
-        per = 9 + (1 if self.cfg.quant == "fp8" else 0) + (2 if self.world > 1 and not fused_ar else 0)
+        # FP8: the o projection's input quantisation is its own kernel unless the
+        # attention emits it (one KV head on this rank)
+        fp8_quant = 1 if self.cfg.quant == "fp8" and self.hkv != 1 else 0
+        per = 9 + fp8_quant + (2 if self.world > 1 and not fused_ar else 0)
         return per * self.cfg.layers + 1
 
     def weight_bytes(self) -> int:

@@ -290,3 +290,39 @@ def test_paged_attention_workspace_merge(cuda, seqs, hq, hkv, lens):
             assert err < 2e-2, (si, h, err)
     assert ((out.float() - clus.float()).abs().max() / clus.float().abs().max()).item() < 2e-2
     assert L.read_device_error() == 0
+
+
+@pytest.mark.parametrize("dtype", DTS)
+@pytest.mark.parametrize("seqs,hq,hkv,ctx", [
+    (1, 8, 1, 4096),     # one KV head, clusters merged through the workspace
+    (1, 8, 1, 1000),     # one KV head, one cluster of splits
+    (64, 8, 1, 512),     # one KV head, one cluster per sequence
+    (300, 16, 1, 200),   # one KV head, one CTA per sequence
+    (2, 32, 8, 700),     # eight KV heads: attention, then the row quant
+])
+def test_paged_attention_fp8_output(cuda, dtype, seqs, hq, hkv, ctx):
+    """lmrs_paged_attention_decode_fp8: the e4m3 bytes and scales of the output
+    rows, equal byte for byte to lmrs_fp8_quant_rows of the plain call's output,
+    which it also writes unchanged; with one KV head the attention's own merge
+    quantises (every merge path), otherwise a second launch does."""
+    import lmrs_b200 as L
+    from lmrs_b200 import decode_ops as DO
+    d, bs = 128, 16
+    max_blocks = (ctx + bs - 1) // bs
+    kc, vc, tables = _paged_cache(seqs, hkv, d, bs, max_blocks, dtype, cuda, 90 + seqs)
+    g = torch.Generator(device=cuda).manual_seed(seqs + hq)
+    q = torch.randn(seqs, hq, d, generator=g, device=cuda).to(dtype)
+    lens = torch.randint(max(1, ctx // 2), ctx + 1, (seqs,), generator=g, device=cuda).to(torch.int32)
+    lens[0] = ctx
+    scale = 1 / math.sqrt(d)
+    ws = DO.AttentionWorkspace()
+    ref = DO.paged_attention_decode(q, kc, vc, tables, lens, ctx, scale, workspace=ws)
+    qr, sr = L.fp8_quant_rows(ref.reshape(seqs, hq * d).contiguous())
+    for _ in range(2):   # repeated calls: the workspace counters return to zero
+        qq, sq, out = DO.paged_attention_decode_fp8(q, kc, vc, tables, lens, ctx, scale,
+                                                    workspace=ws)
+        torch.cuda.synchronize()
+        assert torch.equal(out, ref)
+        assert torch.equal(sq, sr)
+        assert torch.equal(qq, qr)
+    assert L.read_device_error() == 0

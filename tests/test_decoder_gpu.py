@@ -173,3 +173,22 @@ def test_decoder_graph_replay_matches_eager(cuda):
     g.replay()
     torch.cuda.synchronize()
     assert torch.equal(out, eager)
+
+
+def test_fp8_decoder_one_kv_head(cuda, monkeypatch):
+    """One KV head (as a TP=8 rank of config 4 holds): the attention emits the o
+    projection's e4m3 input itself.  Every projection teacher-forced at 1e-2,
+    the whole step against the fp32 forward, and the launch count one lower per
+    layer than with two KV heads."""
+    shape = dict(TINY, heads=4, kv_heads=1)
+    cfg = D.DecoderConfig(quant="fp8", **shape)
+    dec = D.QuantDecoder(cfg, batch=3, ctx=300, device=cuda, seed=8)
+    errs = teacher_forced_errors(dec, monkeypatch)
+    assert len(errs) == 4 * cfg.layers
+    for kind, shp, err in errs:
+        assert err < 1e-2, (kind, shp, err)
+    ref = _reference_logits(dec)
+    got = dec.logits().float()
+    assert ((got - ref).abs().max() / ref.abs().max()).item() < 1.5e-1
+    two = D.QuantDecoder(D.DecoderConfig(quant="fp8", **TINY), batch=3, ctx=300, device=cuda, seed=8)
+    assert dec.own_launches_per_step() == two.own_launches_per_step() - cfg.layers
