@@ -110,6 +110,23 @@ LMRS_API int lmrs_paged_attention_decode_fp8(uint8_t* q_out, float* scale_out, v
                                              int dtype, void* workspace, size_t workspace_bytes,
                                              lmrs_stream_t stream);
 
+/* lmrs_rope_kv_write with positions = context_lens - 1 followed by
+ * lmrs_paged_attention_decode (or its _fp8 form when q_out_or_null is given), in
+ * one launch: qkv is the merged projection row [num_seqs, (num_heads +
+ * 2 num_kv_heads) * head_size]; each CTA rotates its q heads in registers and the
+ * one whose context split holds the new token rotates its k and writes k and v
+ * into the cache before reading it.  Same bits as the separate calls (out,
+ * cache, and the e4m3 bytes / scales); the rotated q is not written out.  cos,
+ * sin: [head_size / 2] in dtype, 16-byte aligned.  With an FP8 output and more
+ * than one KV head the row quantisation is a second launch. */
+LMRS_API int lmrs_rope_paged_attention_decode(
+    void* out, uint8_t* q_out_or_null, float* scale_out_or_null, const void* qkv,
+    const void* cos, const void* sin, void* key_cache, void* value_cache,
+    const int32_t* block_tables, const int32_t* context_lens, int num_seqs, int num_heads,
+    int num_kv_heads, int head_size, int block_size, int max_blocks_per_seq, int max_context,
+    float scale, int kv_head_map, int dtype, void* workspace, size_t workspace_bytes,
+    lmrs_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -65,6 +65,8 @@ SIGNATURES = {
     "lmrs_paged_attention_workspace_bytes": (SZ, [I, I, I, I]),
     "lmrs_paged_attention_decode": (I, [P, P, P, P, P, P, I, I, I, I, I, I, I, F, I, I, P, SZ, P]),
     "lmrs_paged_attention_decode_fp8": (I, [P, P, P, P, P, P, P, P, I, I, I, I, I, I, I, F, I, I, P, SZ, P]),
+    "lmrs_rope_paged_attention_decode": (I, [P, P, P, P, P, P, P, P, P, P, I, I, I, I, I, I, I, F, I, I,
+                                              P, SZ, P]),
     # lmrs_comm.h
     "lmrs_allreduce_buffer_bytes": (SZ, [I, SZ]),
     "lmrs_comm_alloc": (I, [ctypes.POINTER(P), SZ]),

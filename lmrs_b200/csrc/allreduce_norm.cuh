@@ -47,17 +47,6 @@ __device__ __forceinline__ uint16_t e4m3x2(float a, float b, float s) {
   return static_cast<uint16_t>(__nv_cvt_float2_to_fp8x2(pr, __NV_SATFINITE, __NV_E4M3));
 }
 
-template <typename T>
-__device__ __forceinline__ float2 unpack2(uint32_t u) {
-  T e[2];
-  *reinterpret_cast<uint32_t*>(e) = u;
-  return make_float2(Act<T>::to_float(e[0]), Act<T>::to_float(e[1]));
-}
-template <typename T>
-__device__ __forceinline__ uint32_t pack2(float a, float b) {
-  T e[2] = {Act<T>::from_float(a), Act<T>::from_float(b)};
-  return *reinterpret_cast<uint32_t*>(e);
-}
 
 template <typename T, bool FP8, int VPT>
 __global__ void __launch_bounds__(kArnThreads) allreduce_rmsnorm_kernel(

@@ -111,14 +111,16 @@ size_t attn_ws_bytes(int seqs, int hkv, const AttnSplit& sp) {
   return attn_ws_part_bytes(seqs, hkv, sp) + round_up(size_t(seqs) * hkv * 4, 256);
 }
 
-std::atomic<int> g_smem_attn[2][3][kMaxDevices];
+std::atomic<int> g_smem_attn[2][2][3][kMaxDevices];  // [dtype][rope][stages - 2]
 
-template <typename T, int NS>
+// ROPE: q is the merged qkv row and cosv / sinv the RoPE tables (the fused
+// RoPE + KV write); otherwise q holds the query rows and cosv / sinv are null.
+template <typename T, int NS, bool ROPE>
 int attn_launch(void* out, const void* q, const void* kc, const void* vc,
                 const int32_t* tables, const int32_t* lens, int seqs, int heads, int hkv,
                 int bs, int maxb, const AttnSplit& sp, float scale, int map, void* ws,
-                cudaStream_t st, int dev, std::atomic<int>* done, uint8_t* qout = nullptr,
-                float* qscale = nullptr) {
+                cudaStream_t st, int dev, std::atomic<int>* done, uint8_t* qout, float* qscale,
+                const void* cosv, const void* sinv) {
   const int splits = sp.splits, span = sp.span;
   float* ws_part = nullptr;
   uint32_t* ws_count = nullptr;
@@ -127,7 +129,8 @@ int attn_launch(void* out, const void* q, const void* kc, const void* vc,
     ws_count = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(ws) + attn_ws_part_bytes(seqs, hkv, sp));
   }
   int rc;
-  if ((rc = ensure_smem(lmrs::decode_attn_kernel<T, NS>, lmrs::attn_smem_bytes(NS), done, dev)))
+  if ((rc = ensure_smem(lmrs::decode_attn_kernel<T, NS, ROPE>, lmrs::attn_smem_bytes(NS), done,
+                        dev)))
     return rc;
   const float scale_log2 = scale * 1.4426950408889634f;
   // grid (seqs * hkv, splits): launch_ex is 1-D, so pack the split into y here
@@ -152,10 +155,12 @@ int attn_launch(void* out, const void* q, const void* kc, const void* vc,
   }
   c.attrs = attr;
   c.numAttrs = na;
-  cudaError_t e = cudaLaunchKernelEx(&c, lmrs::decode_attn_kernel<T, NS>, static_cast<T*>(out),
-                                     static_cast<const T*>(q), static_cast<const T*>(kc),
-                                     static_cast<const T*>(vc), tables, lens, heads, hkv, bs, maxb,
-                                     span, scale_log2, map, ws_part, ws_count, qout, qscale);
+  cudaError_t e = cudaLaunchKernelEx(
+      &c, lmrs::decode_attn_kernel<T, NS, ROPE>, static_cast<T*>(out), static_cast<const T*>(q),
+      static_cast<const T*>(kc), static_cast<const T*>(vc), tables, lens, heads, hkv, bs, maxb,
+      span, scale_log2, map, ws_part, ws_count, qout, qscale, static_cast<const T*>(cosv),
+      static_cast<const T*>(sinv), const_cast<T*>(static_cast<const T*>(kc)),
+      const_cast<T*>(static_cast<const T*>(vc)));
   if (e != cudaSuccess) return record(e);
   return after_launch();
 }
@@ -290,7 +295,8 @@ int paged_attention_impl(void* out, const void* query, const void* key_cache,
                          int num_kv_heads, int head_size, int block_size, int max_blocks_per_seq,
                          int max_context, float scale, int kv_head_map, int dtype,
                          void* workspace, size_t workspace_bytes, lmrs_stream_t stream,
-                         uint8_t* qout, float* qscale) {
+                         uint8_t* qout, float* qscale, const void* cosv = nullptr,
+                         const void* sinv = nullptr) {
   if (!act_dtype(dtype)) return LMRS_ERR_DTYPE;
   if (num_seqs < 0 || num_heads <= 0 || num_kv_heads <= 0 || num_heads % num_kv_heads ||
       num_heads / num_kv_heads > 16 || head_size != lmrs::kAttnD || block_size <= 0 ||
@@ -313,10 +319,18 @@ int paged_attention_impl(void* out, const void* query, const void* key_cache,
   const int ns = clampi(g_tune.attn_stages, 2, 4);
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
 #define LMRS_ATTN(T, I, NS)                                                                      \
-  return attn_launch<T, NS>(out, query, key_cache, value_cache, block_tables,                   \
-                            context_lens, num_seqs, num_heads, num_kv_heads, block_size,        \
-                            max_blocks_per_seq, sp, scale, kv_head_map, workspace, st, dev,     \
-                            g_smem_attn[I][NS - 2], qout, qscale)
+  return cosv != nullptr                                                                         \
+             ? attn_launch<T, NS, true>(out, query, key_cache, value_cache, block_tables,       \
+                                        context_lens, num_seqs, num_heads, num_kv_heads,        \
+                                        block_size, max_blocks_per_seq, sp, scale, kv_head_map, \
+                                        workspace, st, dev, g_smem_attn[I][1][NS - 2], qout,    \
+                                        qscale, cosv, sinv)                                     \
+             : attn_launch<T, NS, false>(out, query, key_cache, value_cache, block_tables,      \
+                                         context_lens, num_seqs, num_heads, num_kv_heads,       \
+                                         block_size, max_blocks_per_seq, sp, scale,             \
+                                         kv_head_map, workspace, st, dev,                       \
+                                         g_smem_attn[I][0][NS - 2], qout, qscale, nullptr,      \
+                                         nullptr)
   if (dtype == LMRS_DTYPE_BF16) {
     if (ns == 2) LMRS_ATTN(__nv_bfloat16, 0, 2);
     if (ns == 3) LMRS_ATTN(__nv_bfloat16, 0, 3);
@@ -371,6 +385,34 @@ LMRS_API int lmrs_paged_attention_decode_fp8(uint8_t* q_out, float* scale_out, v
   if (rc || num_seqs == 0) return rc;
   return lmrs_fp8_quant_rows(q_out, scale_out, out, num_seqs, num_heads * head_size, dtype,
                              stream);
+}
+
+// RoPE + KV-cache write of the new token (position context_lens - 1) fused into
+// the attention: lmrs_rope_kv_write (positions = context_lens - 1) then
+// lmrs_paged_attention_decode[_fp8] in one launch (two with an FP8 output and
+// more than one KV head).
+LMRS_API int lmrs_rope_paged_attention_decode(
+    void* out, uint8_t* q_out_or_null, float* scale_out_or_null, const void* qkv,
+    const void* cos, const void* sin, void* key_cache, void* value_cache,
+    const int32_t* block_tables, const int32_t* context_lens, int num_seqs, int num_heads,
+    int num_kv_heads, int head_size, int block_size, int max_blocks_per_seq, int max_context,
+    float scale, int kv_head_map, int dtype, void* workspace, size_t workspace_bytes,
+    lmrs_stream_t stream) {
+  if (num_seqs > 0 && (!cos || !sin)) return LMRS_ERR_NULL;
+  if ((cos && !aligned16(cos)) || (sin && !aligned16(sin))) return LMRS_ERR_ALIGN;
+  const bool fp8 = q_out_or_null != nullptr;
+  if (fp8 && num_seqs > 0 && !scale_out_or_null) return LMRS_ERR_NULL;
+  if (fp8 && !aligned16(q_out_or_null)) return LMRS_ERR_ALIGN;
+  const bool fused_q = fp8 && num_kv_heads == 1;
+  int rc = paged_attention_impl(out, qkv, key_cache, value_cache, block_tables, context_lens,
+                                num_seqs, num_heads, num_kv_heads, head_size, block_size,
+                                max_blocks_per_seq, max_context, scale, kv_head_map, dtype,
+                                workspace, workspace_bytes, stream,
+                                fused_q ? q_out_or_null : nullptr,
+                                fused_q ? scale_out_or_null : nullptr, cos, sin);
+  if (rc || !fp8 || fused_q || num_seqs == 0) return rc;
+  return lmrs_fp8_quant_rows(q_out_or_null, scale_out_or_null, out, num_seqs,
+                             num_heads * head_size, dtype, stream);
 }
 
 }  // extern "C"

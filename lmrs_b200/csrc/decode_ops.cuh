@@ -72,6 +72,19 @@ __device__ __forceinline__ uint2 e4m3x8(const float (&v)[8], float s) {
   return make_uint2(out[0], out[1]);
 }
 
+// Two packed T values <-> two floats.
+template <typename T>
+__device__ __forceinline__ float2 unpack2(uint32_t u) {
+  T e[2];
+  *reinterpret_cast<uint32_t*>(e) = u;
+  return make_float2(Act<T>::to_float(e[0]), Act<T>::to_float(e[1]));
+}
+template <typename T>
+__device__ __forceinline__ uint32_t pack2(float a, float b) {
+  T e[2] = {Act<T>::from_float(a), Act<T>::from_float(b)};
+  return *reinterpret_cast<uint32_t*>(e);
+}
+
 template <typename T>
 __device__ __forceinline__ void unpack8(const uint4& v, float (&f)[8]) {
   const T* e = reinterpret_cast<const T*>(&v);
@@ -250,6 +263,15 @@ __global__ void __launch_bounds__(kSiluClusterThreads) silu_mul_fp8_cluster_kern
   }
 }
 
+// Rotate-half RoPE of one (first-half, second-half) pair with explicit
+// roundings (no contraction into fma), so that every kernel that rotates —
+// the RoPE + KV write kernels and the attention that fuses them — gives the
+// same bits: (x0 c - x1 s, x1 c + x0 s).
+__device__ __forceinline__ float2 rope_pair(float x0, float x1, float c, float s) {
+  return make_float2(__fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s)),
+                     __fadd_rn(__fmul_rn(x1, c), __fmul_rn(x0, s)));
+}
+
 // Vectorised RoPE + KV write for head sizes with 16-byte aligned half-rows
 // (d % 16 == 0): CTA (sequence, item block); an item is 8 columns of the first
 // half of one q / k head with the matching 8 of the second half (rotated), or
@@ -284,8 +306,9 @@ __global__ void __launch_bounds__(128) rope_kv_vec_kernel(
     T* r1 = reinterpret_cast<T*>(&p1);
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      r0[i] = Act<T>::from_float(x0[i] * cs[i] - x1[i] * sn[i]);  // rotate-half: first half
-      r1[i] = Act<T>::from_float(x1[i] * cs[i] + x0[i] * sn[i]);  // second half
+      const float2 rr = rope_pair(x0[i], x1[i], cs[i], sn[i]);
+      r0[i] = Act<T>::from_float(rr.x);  // rotate-half: first half
+      r1[i] = Act<T>::from_float(rr.y);  // second half
     }
     T* dst;
     if (h < hq) {
@@ -332,8 +355,9 @@ __global__ void __launch_bounds__(256) rope_kv_kernel(
       const T* src = row + h * d;
       const float x0 = Act<T>::to_float(src[c]), x1 = Act<T>::to_float(src[c + half]);
       const float cs = Act<T>::to_float(cosv[c]), sn = Act<T>::to_float(sinv[c]);
-      const T r0 = Act<T>::from_float(x0 * cs - x1 * sn);   // rotate-half: first half
-      const T r1 = Act<T>::from_float(x1 * cs + x0 * sn);   // second half
+      const float2 rr = rope_pair(x0, x1, cs, sn);
+      const T r0 = Act<T>::from_float(rr.x);   // rotate-half: first half
+      const T r1 = Act<T>::from_float(rr.y);   // second half
       if (h < hq) {
         T* dst = q_out + (static_cast<int64_t>(b) * hq + h) * d;
         dst[c] = r0;
@@ -481,14 +505,24 @@ __device__ __forceinline__ void attn_merge_sources(int n, Load load, float& M, f
 // the last cluster of the (sequence, KV head) to arrive on its counter merges
 // those in cluster order and sets the counter back to zero; no CTA waits on
 // another cluster.  Both levels are deterministic.
-template <typename T, int NS>
+// ROPE: RoPE and the KV-cache write of the new token fused in (what
+// rope_kv_kernel does before the attention).  query is then the merged qkv row
+// [seqs, (num_heads + 2 num_kv_heads) * 128]; each CTA rotates its q heads in
+// registers (a lane holds both halves of each of its rotate-half pairs: k-steps
+// kk and kk + 4); the warp whose tile holds the new token's position
+// (context_lens - 1) rotates the token's k, lays k and v over that row of its
+// tile in shared memory (the copy from the cache brought the old contents) and
+// writes them into the cache after its loop.  Same bits as rope_kv_kernel
+// followed by the plain attention (rope_pair in both).
+template <typename T, int NS, bool ROPE>
 __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(
     T* __restrict__ out, const T* __restrict__ query,
     const T* __restrict__ k_cache, const T* __restrict__ v_cache,
     const int32_t* __restrict__ tables, const int32_t* __restrict__ ctx_lens, int num_heads,
     int num_kv_heads, int block_size, int max_blocks, int span, float scale_log2, int kv_map,
     float* __restrict__ ws_part, uint32_t* __restrict__ ws_count, uint8_t* __restrict__ qout,
-    float* __restrict__ qscale) {
+    float* __restrict__ qscale, const T* __restrict__ cosv, const T* __restrict__ sinv,
+    T* __restrict__ kc_new, T* __restrict__ vc_new) {
   pdl_wait();
   pdl_trigger();
   // per warp [NS stages][K 16 rows | V 16 rows], rows padded to kAttnRowBytes;
@@ -514,14 +548,49 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(
   if (cached)
     for (int i = threadIdx.x; i < nblk; i += kAttnThreads)
       sblk[i] = tables[static_cast<int64_t>(seq) * max_blocks + blk0 + i];
-  __syncthreads();
+  // the merged qkv row of this sequence (ROPE) / its q rows
+  const int64_t qrow = ROPE ? static_cast<int64_t>(seq) * (num_heads + 2 * num_kv_heads) * kAttnD
+                            : static_cast<int64_t>(seq) * num_heads * kAttnD;
+  // ROPE: the warp whose tile holds the new token's position (context_lens - 1,
+  // inside this split) requests the token's k pairs (c, c + 64) for c = lane,
+  // lane + 32, the matching cos / sin and v columns 4 lane .. + 3; it patches
+  // the rotated row into that tile in shared memory once the tile's copies have
+  // landed, and writes it into the cache after the loop, so that no other work
+  // of the CTA waits for it
+  int rope_tile = -1, rope_row = 0;  // the warp's tile index holding the token, its row
+  T rk[4], rc[2], rs[2];
+  uint2 rv = make_uint2(0u, 0u);
+  int64_t rope_off = 0;
+  if constexpr (ROPE) {
+    const int pos = ctx_lens[seq] - 1;
+    const int ti = (pos - p0) >> 4;
+    if (pos >= p0 && pos < p1 && (ti & 3) == warp) {
+      rope_tile = ti >> 2;
+      rope_row = (pos - p0) & 15;
+      const T* kr = query + qrow + static_cast<int64_t>(num_heads + kvh) * kAttnD;
+      const T* vr = query + qrow + static_cast<int64_t>(num_heads + num_kv_heads + kvh) * kAttnD;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int c = lane + 32 * h;
+        rk[2 * h] = kr[c];
+        rk[2 * h + 1] = kr[c + kAttnD / 2];
+        rc[h] = cosv[c];
+        rs[h] = sinv[c];
+      }
+      rv = *reinterpret_cast<const uint2*>(vr + 4 * lane);
+      const int blk = tables[static_cast<int64_t>(seq) * max_blocks + pos / block_size];
+      rope_off =
+          ((static_cast<int64_t>(blk) * num_kv_heads + kvh) * block_size + pos % block_size) * kAttnD;
+    }
+  }
+  __syncthreads();  // table entries in place
 
   // Q fragments (A operand, 16 rows = q heads, 128 dims = 8 k-steps)
   uint32_t qa[8][4];
   {
     const bool r0 = g < G, r1 = g + 8 < G;
-    const T* q0 = query + (static_cast<int64_t>(seq) * num_heads + (r0 ? qhead(g) : 0)) * kAttnD;
-    const T* q1 = query + (static_cast<int64_t>(seq) * num_heads + (r1 ? qhead(g + 8) : 0)) * kAttnD;
+    const T* q0 = query + qrow + static_cast<int64_t>(r0 ? qhead(g) : 0) * kAttnD;
+    const T* q1 = query + qrow + static_cast<int64_t>(r1 ? qhead(g + 8) : 0) * kAttnD;
 #pragma unroll
     for (int kk = 0; kk < 8; ++kk) {
       const int c = kk * 16 + 2 * t;
@@ -529,6 +598,23 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(
       qa[kk][1] = r1 ? *reinterpret_cast<const uint32_t*>(q1 + c) : 0u;
       qa[kk][2] = r0 ? *reinterpret_cast<const uint32_t*>(q0 + c + 8) : 0u;
       qa[kk][3] = r1 ? *reinterpret_cast<const uint32_t*>(q1 + c + 8) : 0u;
+    }
+    if constexpr (ROPE) {
+      // register i of k-step kk holds columns c, c + 1 (c = 16 kk + 2t, + 8 for
+      // i >= 2); for kk < 4 its rotate-half partners sit in k-step kk + 4
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int c = kk * 16 + 2 * t + ((i & 2) ? 8 : 0);
+          const float2 cs = unpack2<T>(*reinterpret_cast<const uint32_t*>(cosv + c));
+          const float2 sn = unpack2<T>(*reinterpret_cast<const uint32_t*>(sinv + c));
+          const float2 a = unpack2<T>(qa[kk][i]), b = unpack2<T>(qa[kk + 4][i]);
+          const float2 e0 = rope_pair(a.x, b.x, cs.x, sn.x), e1 = rope_pair(a.y, b.y, cs.y, sn.y);
+          qa[kk][i] = pack2<T>(e0.x, e1.x);
+          qa[kk + 4][i] = pack2<T>(e0.y, e1.y);
+        }
+      }
     }
   }
 
@@ -574,6 +660,24 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(
     const int buf = tile % NS;
     cp_async_wait<NS - 2>();  // this tile's group has landed for this lane ...
     __syncwarp();             // ... and for every lane; tile - 1's buffer is free
+    if constexpr (ROPE) {
+      if (tile == rope_tile) {  // the new token's row: rotated k and v over the copied row
+        T* krow = reinterpret_cast<T*>(wsm + buf * kWarpStage + rope_row * kAttnRowBytes);
+        T* vrow = reinterpret_cast<T*>(wsm + buf * kWarpStage + kWarpTile + rope_row * kAttnRowBytes);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int c = lane + 32 * h;
+          const float2 rr = rope_pair(Act<T>::to_float(rk[2 * h]), Act<T>::to_float(rk[2 * h + 1]),
+                                      Act<T>::to_float(rc[h]), Act<T>::to_float(rs[h]));
+          rk[2 * h] = Act<T>::from_float(rr.x);
+          rk[2 * h + 1] = Act<T>::from_float(rr.y);
+          krow[c] = rk[2 * h];
+          krow[c + kAttnD / 2] = rk[2 * h + 1];
+        }
+        *reinterpret_cast<uint2*>(vrow + 4 * lane) = rv;
+        __syncwarp();
+      }
+    }
     if (tile + NS - 1 < ntiles) stage(tile + NS - 1, (tile + NS - 1) % NS);
     else cp_async_commit();
     const uint32_t kb = smem_u32(wsm + buf * kWarpStage);
@@ -656,6 +760,16 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(
     }
   }
   cp_async_wait<0>();
+  if constexpr (ROPE) {
+    if (rope_tile >= 0) {  // the new token into the cache (no copy of this CTA reads it now)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        kc_new[rope_off + lane + 32 * h] = rk[2 * h];
+        kc_new[rope_off + lane + 32 * h + kAttnD / 2] = rk[2 * h + 1];
+      }
+      *reinterpret_cast<uint2*>(vc_new + rope_off + 4 * lane) = rv;
+    }
+  }
 
   // ---- merge the 4 warps (each covered a quarter of every tile)
 #pragma unroll

@@ -159,3 +159,34 @@ def paged_attention_decode_fp8(query: torch.Tensor, key_cache: torch.Tensor,
         block_tables.shape[1], int(max_context), float(scale), int(kv_head_map), _code(query),
         _ptr(ws), need, _stream(query)))
     return q, sc, out
+
+
+def rope_paged_attention_decode(qkv: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
+                                key_cache: torch.Tensor, value_cache: torch.Tensor,
+                                block_tables: torch.Tensor, context_lens: torch.Tensor,
+                                max_context: int, num_heads: int, num_kv_heads: int,
+                                scale: float, kv_head_map: int = 1,
+                                workspace: Optional[AttentionWorkspace] = None,
+                                fp8: bool = False):
+    """rope_kv_write (positions = context_lens - 1) then paged_attention_decode in
+    one kernel: qkv [seqs, (num_heads + 2 num_kv_heads) * 128] is the merged
+    projection output.  Returns out [seqs, num_heads, 128]; with fp8=True
+    (e4m3 bytes [seqs, num_heads * 128], per-row scales, out), as
+    paged_attention_decode_fp8."""
+    _require_cuda(qkv, "qkv")
+    seqs, d = qkv.shape[0], 128
+    block_size = key_cache.shape[2]
+    lib = _lib.load()
+    need = lib.lmrs_paged_attention_workspace_bytes(seqs, num_heads, num_kv_heads, max_context)
+    ws = (workspace or AttentionWorkspace()).get(need, qkv.device)
+    out = torch.empty((seqs, num_heads, d), dtype=qkv.dtype, device=qkv.device)
+    q = sc = None
+    if fp8:
+        q = torch.empty((seqs, num_heads * d), dtype=torch.uint8, device=qkv.device)
+        sc = torch.empty((seqs,), dtype=torch.float32, device=qkv.device)
+    _lib.check("lmrs_rope_paged_attention_decode", lib.lmrs_rope_paged_attention_decode(
+        _ptr(out), _ptr(q), _ptr(sc), _ptr(qkv), _ptr(cos), _ptr(sin), _ptr(key_cache),
+        _ptr(value_cache), _ptr(block_tables), _ptr(context_lens), seqs, num_heads, num_kv_heads,
+        d, block_size, block_tables.shape[1], int(max_context), float(scale), int(kv_head_map),
+        _code(qkv), _ptr(ws), need, _stream(qkv)))
+    return (q, sc, out) if fp8 else out

@@ -121,6 +121,8 @@ class QuantDecoder:
         # (lmrs_allreduce_rmsnorm[_fp8]) unless fuse_allreduce is False
         self.allreduce_kind = allreduce
         self.fuse_allreduce = True
+        # RoPE + KV write inside the attention kernel (lmrs_rope_paged_attention_decode)
+        self.fuse_rope = True
         self.par = None
         self.device = torch.device(device)
         self.rank, self.world, self.pg = rank, world, group
@@ -328,17 +330,21 @@ class QuantDecoder:
                 qkv = L["qkv"].forward_prequant(*self._norm(h, L["in_norm"], delta, True))
             else:
                 qkv = L["qkv"].forward(self._norm(h, L["in_norm"], delta, False))
-            q = DO.rope_kv_write(qkv, cos, sin, kc, vc, self.block_tables, self.positions,
-                                 self.hq, self.hkv, d)
-            if fp8:  # the o projection's e4m3 input straight from the attention
-                aq, asc, _ = DO.paged_attention_decode_fp8(
+            if self.fuse_rope:  # RoPE + KV write inside the attention kernel
+                att = DO.rope_paged_attention_decode(
+                    qkv, cos, sin, kc, vc, self.block_tables, self.context_lens, self.ctx,
+                    self.hq, self.hkv, scale, kv_head_map=1, workspace=self.attn_ws, fp8=fp8)
+            else:
+                q = DO.rope_kv_write(qkv, cos, sin, kc, vc, self.block_tables, self.positions,
+                                     self.hq, self.hkv, d)
+                att = (DO.paged_attention_decode_fp8 if fp8 else DO.paged_attention_decode)(
                     q, kc, vc, self.block_tables, self.context_lens, self.ctx, scale,
                     kv_head_map=1, workspace=self.attn_ws)
+            if fp8:  # the o projection's e4m3 input straight from the attention
+                aq, asc, _ = att
                 o = L["o"].forward_prequant(aq, asc)      # this rank's partial sum
             else:
-                a = DO.paged_attention_decode(q, kc, vc, self.block_tables, self.context_lens,
-                                              self.ctx, scale, kv_head_map=1, workspace=self.attn_ws)
-                o = L["o"].forward(a.view(B, self.hq * d))  # this rank's partial sum
+                o = L["o"].forward(att.view(B, self.hq * d))  # this rank's partial sum
             if fp8:
                 xq, sx = self._norm(h, L["post_norm"], o, True)
                 mq, ms = DO.silu_mul_fp8(L["gate_up"].forward_prequant(xq, sx))
@@ -402,8 +408,9 @@ class QuantDecoder:
 
     def own_launches_per_step(self) -> int:
         """Kernels of this package one fused decode step launches: per layer the
-        norm, qkv projection, RoPE + KV write, attention, o projection (FP8: its
-        per-token quantisation is a second kernel), norm, gate/up, SiLU * up and
+        norm, qkv projection, RoPE + KV write (inside the attention unless
+        fuse_rope is off), attention, o projection (FP8: its per-token
+        quantisation is a second kernel), norm, gate/up, SiLU * up and
         down, plus one all-reduce after o and after down when tensor parallel
         unless it is fused into the norm that follows it; then the final norm
         (the embedding gather and the LM head are torch)."""
@@ -412,7 +419,8 @@ class QuantDecoder:
         # FP8: the o projection's input quantisation is its own kernel unless the
         # attention emits it (one KV head on this rank)
         fp8_quant = 1 if self.cfg.quant == "fp8" and self.hkv != 1 else 0
-        per = 9 + fp8_quant + (2 if self.world > 1 and not fused_ar else 0)
+        rope = 0 if self.fuse_rope else 1
+        per = 8 + rope + fp8_quant + (2 if self.world > 1 and not fused_ar else 0)
         return per * self.cfg.layers + 1
 
     def weight_bytes(self) -> int:

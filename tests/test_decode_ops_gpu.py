@@ -326,3 +326,51 @@ def test_paged_attention_fp8_output(cuda, dtype, seqs, hq, hkv, ctx):
         assert torch.equal(sq, sr)
         assert torch.equal(qq, qr)
     assert L.read_device_error() == 0
+
+
+@pytest.mark.parametrize("dtype", DTS)
+@pytest.mark.parametrize("seqs,hq,hkv,ctx,fp8", [
+    (1, 8, 1, 4096, True),    # one KV head, clusters merged through the workspace
+    (1, 32, 8, 2048, False),  # one cluster of splits per (sequence, KV head)
+    (64, 8, 1, 512, True),    # one cluster per sequence
+    (300, 16, 2, 200, True),  # one CTA per (sequence, KV head); FP8 output by a second launch
+    (5, 64, 8, 700, False),
+])
+def test_rope_paged_attention_fused(cuda, dtype, seqs, hq, hkv, ctx, fp8):
+    """lmrs_rope_paged_attention_decode against lmrs_rope_kv_write (positions =
+    context_lens - 1) followed by the attention: the same output, the same cache
+    contents (the new token's rotated k and v in place, nothing else touched) and,
+    with the FP8 output, the same e4m3 bytes and scales."""
+    import lmrs_b200 as L
+    from lmrs_b200 import decode_ops as DO
+    d, bs = 128, 16
+    max_blocks = (ctx + bs - 1) // bs
+    kc, vc, tables = _paged_cache(seqs, hkv, d, bs, max_blocks, dtype, cuda, 123 + seqs)
+    g = torch.Generator(device=cuda).manual_seed(5 * seqs + hq)
+    qkv = torch.randn(seqs, (hq + 2 * hkv) * d, generator=g, device=cuda).to(dtype)
+    lens = torch.randint(1, ctx + 1, (seqs,), generator=g, device=cuda).to(torch.int32)
+    lens[0] = ctx
+    inv = 1.0 / (500000.0 ** (torch.arange(0, d, 2, device=cuda).float() / d))
+    ang = float(ctx - 1) * inv
+    cos, sin = ang.cos().to(dtype).contiguous(), ang.sin().to(dtype).contiguous()
+    scale = 1 / math.sqrt(d)
+    k1, v1 = kc.clone(), vc.clone()
+    q = DO.rope_kv_write(qkv, cos, sin, k1, v1, tables, lens - 1, hq, hkv, d)
+    ws = DO.AttentionWorkspace()
+    if fp8:
+        qr, sr, ref = DO.paged_attention_decode_fp8(q, k1, v1, tables, lens, ctx, scale, workspace=ws)
+    else:
+        ref = DO.paged_attention_decode(q, k1, v1, tables, lens, ctx, scale, workspace=ws)
+    k2, v2 = kc.clone(), vc.clone()
+    for _ in range(2):  # the second call rewrites the same k / v, reads the same cache
+        got = DO.rope_paged_attention_decode(qkv, cos, sin, k2, v2, tables, lens, ctx, hq, hkv,
+                                             scale, workspace=ws, fp8=fp8)
+        torch.cuda.synchronize()
+        if fp8:
+            qq, sq, out = got
+            assert torch.equal(sq, sr) and torch.equal(qq, qr)
+        else:
+            out = got
+        assert torch.equal(out, ref)
+        assert torch.equal(k2, k1) and torch.equal(v2, v1)
+    assert L.read_device_error() == 0
