@@ -87,7 +87,8 @@ LMRS_API int lmrs_version(void);
  * "awq_swap_cluster", "awq_swap_narrow_tiles" (swap-AB up to 128 tokens while N / 128
  * is at most this, default 32; 0 = off), "awq_gemm_pair", "gemm_bn", "fp8_gemv_max_m",
  * "gemv_ctas_per_sm", "awq_gemv_cluster", "fp8_gemv_cluster", "fp8_gemv_max_kn",
- * "fp8_swap_max_m", "fp8_swap_cluster", "fp8_gemm_group_m" (FP8 GEMM tile order: M
+ * "fp8_swap_max_m", "fp8_swap_cluster", "fp8_swap_deep_k" (decode FP8 on the swap-AB kernel
+ * when K >= this x N, default 4; 0 = off), "fp8_gemm_group_m" (FP8 GEMM tile order: M
  * tiles per group, default 32), "fp8_gemm_bn128" (128-wide FP8 GEMM tiles while
  * that grid fits one wave, default 1), "awq_tmem_min_m", "awq_tmem_max_m",
  * "awq_tmem_min_m_wide", "awq_tmem_cluster", "awq_tmem_ctas_per_sm", "awq_gemm_tmem",
