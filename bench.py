@@ -440,12 +440,18 @@ def run_case(case, launches=3):
             DO.paged_attention_decode(q, kc, vc, tables, lens, ctx, 1 / math.sqrt(128), 1, ws)
     elif kind == "decode":
         # eager decode steps of a config-3/4 decoder cut to `layers` layers:
-        # decode:<8b-awq|70b-fp8>:<batch>:<layers>
+        # decode:<8b-awq|70b-fp8>:<batch>:<layers>[:tp<N>]; tp<N>: the shapes one
+        # of N tensor-parallel ranks holds (heads, KV heads, intermediate and
+        # vocabulary divided by N), on this one GPU with no collective
         import dataclasses
         from lmrs_b200 import decoder as D
         preset, B, nl = dims[0], int(dims[1]), int(dims[2])
         attr, ctx, _, _ = DECODE_PRESETS[preset]
         cfg = dataclasses.replace(getattr(D, attr), layers=nl)
+        if len(dims) > 3 and dims[3].startswith("tp"):
+            n = int(dims[3][2:])
+            cfg = dataclasses.replace(cfg, heads=cfg.heads // n, kv_heads=cfg.kv_heads // n,
+                                      intermediate=cfg.intermediate // n, vocab=cfg.vocab // n)
         dec = D.QuantDecoder(cfg, batch=B, ctx=ctx, device=dev, seed=0)
         for _ in range(launches):
             dec.logits()
