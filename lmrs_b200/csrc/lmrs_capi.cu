@@ -865,7 +865,7 @@ int fp8_swap_launch(__nv_bfloat16* y, const uint8_t* xq, const float* sx, const 
                                   g_smem_f8_swap[2]);
 }
 
-template <int BN>
+template <int BN, int KSUB = 1>
 int fp8_gemm_launch_bn(__nv_bfloat16* y, const uint8_t* xq, const float* sx, const uint8_t* wq,
                        const float* sw, const __nv_bfloat16* bias, int M, int K, int N,
                        cudaStream_t stream, int dev, std::atomic<int>* smem_done) {
@@ -877,12 +877,12 @@ int fp8_gemm_launch_bn(__nv_bfloat16* y, const uint8_t* xq, const float* sx, con
   if ((rc = make_tmap(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, wq, K, N, uint64_t(K), 128, BN,
                       CU_TENSOR_MAP_SWIZZLE_128B)))
     return rc;
-  constexpr int smem = lmrs::F8Tile<BN>::kSmem;
-  if ((rc = ensure_smem(lmrs::fp8_gemm_tc_kernel<BN>, smem, smem_done, dev))) return rc;
+  constexpr int smem = lmrs::F8Tile<BN, KSUB>::kSmem;
+  if ((rc = ensure_smem(lmrs::fp8_gemm_tc_kernel<BN, KSUB>, smem, smem_done, dev))) return rc;
   const int tiles = ((N + BN - 1) / BN) * ((M + lmrs::kTcBM - 1) / lmrs::kTcBM);
   const int grid = tiles < sm_count(dev) ? tiles : sm_count(dev);
   const int group_m = g_tune.fp8_gemm_group_m > 0 ? g_tune.fp8_gemm_group_m : 1;
-  rc = launch_ex(lmrs::fp8_gemm_tc_kernel<BN>, grid, 0, lmrs::kF8Threads, smem, stream, ta, tb, y,
+  rc = launch_ex(lmrs::fp8_gemm_tc_kernel<BN, KSUB>, grid, 0, lmrs::kF8Threads, smem, stream, ta, tb, y,
                  sx, sw, bias, M, K, N, group_m);
   return rc ? rc : after_launch();
 }
@@ -892,7 +892,8 @@ int fp8_gemm_launch(__nv_bfloat16* y, const uint8_t* xq, const float* sx, const 
                     cudaStream_t stream, int dev) {
   const int m_tiles = (M + lmrs::kTcBM - 1) / lmrs::kTcBM;
   if (g_tune.fp8_gemm_bn128 && m_tiles * ((N + 127) / 128) <= sm_count(dev))
-    return fp8_gemm_launch_bn<128>(y, xq, sx, wq, sw, bias, M, K, N, stream, dev, g_smem_f8_gemm128);
+    return fp8_gemm_launch_bn<128, 2>(y, xq, sx, wq, sw, bias, M, K, N, stream, dev,
+                                      g_smem_f8_gemm128);
   if (pick_bn(M, N, sm_count(dev)) == 224)
     return fp8_gemm_launch_bn<224>(y, xq, sx, wq, sw, bias, M, K, N, stream, dev, g_smem_f8_gemm224);
   return fp8_gemm_launch_bn<256>(y, xq, sx, wq, sw, bias, M, K, N, stream, dev, g_smem_f8_gemm);

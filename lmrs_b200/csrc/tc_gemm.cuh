@@ -310,14 +310,22 @@ constexpr int kF8BK = 128;  // bytes (= e4m3 elements) of K per stage
 constexpr int kF8Stages = 4;
 constexpr int kF8Threads = 32 * (kTcEpiWarp0 + kTcEpiWarps);  // 192
 constexpr int kF8ABytes = kTcBM * kF8BK;  // 16 KB
-template <int BN> struct F8Tile {
-  static constexpr int kB = BN * kF8BK;  // weight rows of the tile x 128 bytes of K
-  static constexpr int kSmem = 1024 + kF8Stages * (kF8ABytes + kB) + 256;
-  static_assert(kB % 1024 == 0 && kF8ABytes % 1024 == 0, "128B-swizzled stages are 1024-byte aligned");
+// KSUB 128-byte TMA boxes of K per stage (one wait and one commit of the MMA
+// thread per stage).  128-wide tiles run mid-size M: few tiles, each CTA walking
+// all of K, where the MMA thread's fixed work per stage (a wait, a commit; ~0.39
+// us per 128-byte stage at 14336 x 4096, M = 512) sets the pace, so they take
+// 256-byte stages (eight UMMAs per wait and commit) in a 3-deep ring.
+template <int BN, int KSUB = 1> struct F8Tile {
+  static constexpr int kA = kTcBM * kF8BK * KSUB;  // token rows x KSUB x 128 bytes of K
+  static constexpr int kB = BN * kF8BK * KSUB;     // weight rows of the tile x the same
+  static constexpr int kStages = KSUB == 2 ? 3 : kF8Stages;
+  static constexpr int kSmem = 1024 + kStages * (kA + kB) + 256;
+  static_assert(kB % 1024 == 0 && kA % 1024 == 0, "128B-swizzled stages are 1024-byte aligned");
+  static_assert(kSmem <= 227 * 1024, "shared memory per CTA");
 };
 constexpr int kF8SmemBytes = F8Tile<256>::kSmem;
 
-template <int BN>
+template <int BN, int KSUB>
 __global__ void __launch_bounds__(kF8Threads, 1)
     fp8_gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_a,
                        const __grid_constant__ CUtensorMap tm_b, __nv_bfloat16* __restrict__ y,
@@ -325,24 +333,28 @@ __global__ void __launch_bounds__(kF8Threads, 1)
                        const __nv_bfloat16* __restrict__ bias, int M, int K, int N, int group_m) {
   pdl_wait();     // activations are the previous kernel's output
   pdl_trigger();
+  using TL = F8Tile<BN, KSUB>;
+  constexpr int kS = TL::kStages;
+  constexpr int kF8ABytes = TL::kA;
+  constexpr int kF8BBytes = TL::kB;
+  constexpr int kBK = kF8BK * KSUB;  // bytes of K per stage
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   uint8_t* sA = smem;
-  uint8_t* sB = sA + kF8Stages * kF8ABytes;
-  constexpr int kF8BBytes = F8Tile<BN>::kB;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sB + kF8Stages * kF8BBytes);
-  uint64_t* empty = full + kF8Stages;
-  AccBars* acc = reinterpret_cast<AccBars*>(empty + kF8Stages);
+  uint8_t* sB = sA + kS * kF8ABytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + kS * kF8BBytes);
+  uint64_t* empty = full + kS;
+  AccBars* acc = reinterpret_cast<AccBars*>(empty + kS);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int KB = (K + kF8BK - 1) / kF8BK;
+  const int KB = (K + kBK - 1) / kBK;  // a box past K is zero-filled
   const int n_tiles = (N + BN - 1) / BN;
   const int m_tiles = (M + kTcBM - 1) / kTcBM;
   const int tiles = n_tiles * m_tiles;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kF8Stages; ++s) {
+    for (int s = 0; s < kS; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
@@ -371,11 +383,16 @@ __global__ void __launch_bounds__(kF8Threads, 1)
         int m0, n0;
         tile_coords(t, m_tiles, n_tiles, BN, m0, n0, group_m);
         for (int kb = 0; kb < KB; ++kb, ++kg) {
-          const int s = kg % kF8Stages;
-          if (!(ok = mbar_wait(&empty[s], ((kg / kF8Stages) & 1) ^ 1, kErrWaitEmpty))) break;
+          const int s = kg % kS;
+          if (!(ok = mbar_wait(&empty[s], ((kg / kS) & 1) ^ 1, kErrWaitEmpty))) break;
           mbar_arrive_expect_tx(&full[s], kF8ABytes + kF8BBytes);
-          tma_load_2d_hint(&tm_a, &full[s], sA + s * kF8ABytes, kb * kF8BK, m0, keep);
-          tma_load_2d(&tm_b, &full[s], sB + s * kF8BBytes, kb * kF8BK, n0);
+#pragma unroll
+          for (int sub = 0; sub < KSUB; ++sub) {
+            tma_load_2d_hint(&tm_a, &full[s], sA + s * kF8ABytes + sub * (kTcBM * kF8BK),
+                             kb * kBK + sub * kF8BK, m0, keep);
+            tma_load_2d(&tm_b, &full[s], sB + s * kF8BBytes + sub * (BN * kF8BK),
+                        kb * kBK + sub * kF8BK, n0);
+          }
         }
       }
     }
@@ -390,15 +407,15 @@ __global__ void __launch_bounds__(kF8Threads, 1)
         tc_fence_after();
         const uint32_t d = tmem + a * BN;
         for (int kb = 0; kb < KB; ++kb, ++kg) {
-          const int s = kg % kF8Stages;
-          if (!(ok = mbar_wait(&full[s], (kg / kF8Stages) & 1, kErrWaitFull))) break;
+          const int s = kg % kS;
+          if (!(ok = mbar_wait(&full[s], (kg / kS) & 1, kErrWaitFull))) break;
           tc_fence_after();
           const uint32_t a0 = smem_u32(sA + s * kF8ABytes);
           const uint32_t b0 = smem_u32(sB + s * kF8BBytes);
 #pragma unroll
-          for (int kk = 0; kk < kF8BK / 32; ++kk) {
-            const uint64_t ad = make_sdesc(a0 + kk * 32, 16, 1024);
-            const uint64_t bd = make_sdesc(b0 + kk * 32, 16, 1024);
+          for (int kk = 0; kk < kBK / 32; ++kk) {  // box kk / 4, 32-byte K step kk % 4
+            const uint64_t ad = make_sdesc(a0 + (kk >> 2) * (kTcBM * kF8BK) + (kk & 3) * 32, 16, 1024);
+            const uint64_t bd = make_sdesc(b0 + (kk >> 2) * (BN * kF8BK) + (kk & 3) * 32, 16, 1024);
             umma_f8(d, ad, bd, idesc, (kb | kk) != 0 ? 1u : 0u);
           }
           umma_commit(&empty[s]);
