@@ -101,7 +101,9 @@ LMRS_API int lmrs_version(void);
  * "awq_i8_slots", "awq_i8_ctas_per_sm", "awq_i8_cluster", "awq_i8_box_rows", "pdl" (programmatic
  * dependent launch on every kernel, default 1), "ar_two_stage_min_world" /
  * "ar_two_stage_min_elems" (lmrs_allreduce_sum's two-stage form, defaults 4 /
- * 131072), "wait_limit_kcycles" (how long a
+ * 131072), "decode_layer_trace" (1: lmrs_fp8_decode_layer records global-timer
+ * stamps at the start and around every grid barrier, 32 per CTA, in the last
+ * grid x 256 bytes of its workspace; default 0), "wait_limit_kcycles" (how long a
  * kernel's bounded wait spins before it gives up and flags the device error
  * word, in thousands of SM cycles, on the CURRENT device only; <= 0 restores the
  * default of ~2 s; synchronous).

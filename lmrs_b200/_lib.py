@@ -1,5 +1,5 @@
-"""ctypes binding of the C-ABI in ``include/lmrs_quant.h``, ``include/lmrs_decode.h``
-and ``include/lmrs_comm.h``.
+"""ctypes binding of the C-ABI in ``include/lmrs_quant.h``, ``include/lmrs_decode.h``,
+``include/lmrs_comm.h`` and ``include/lmrs_layer.h``.
 
 This is the Python counterpart of the reference's raw FFI declarations
 (crates/kernels/src/tensor_ops.rs:8-22, crates/kernels/src/raw.rs:53-147): one
@@ -39,7 +39,7 @@ SZ = ctypes.c_size_t
 
 F = ctypes.c_float
 
-# name -> (restype, argtypes); mirrors include/lmrs_{quant,decode,comm}.h exactly
+# name -> (restype, argtypes); mirrors include/lmrs_{quant,decode,comm,layer}.h exactly
 SIGNATURES = {
     "lmrs_version": (I, []),
     "lmrs_status_string": (ctypes.c_char_p, [I]),
@@ -77,7 +77,29 @@ SIGNATURES = {
     "lmrs_allreduce_sum": (I, [P, P, SZ, I, I, I, P, SZ, P]),
     "lmrs_allreduce_rmsnorm": (I, [P, P, P, P, I, I, F, I, I, I, P, SZ, P]),
     "lmrs_allreduce_rmsnorm_fp8": (I, [P, P, P, P, P, I, I, F, I, I, I, P, SZ, P]),
+    # lmrs_layer.h (struct arguments by pointer: Fp8Layer, Fp8LayerShape below)
+    "lmrs_fp8_decode_layer_workspace_bytes": (SZ, [P]),
+    "lmrs_fp8_decode_layer_prepare": (I, [P, P, SZ, P]),
+    "lmrs_fp8_decode_layer": (I, [P, P, P, P, P, I, P, P, P, P, I, I, P, SZ, P, SZ, P]),
 }
+
+# lmrs_layer.h
+LAYER_RECV_DELTA = 1
+LAYER_PUSH_DELTA = 2
+
+
+class Fp8Layer(ctypes.Structure):
+    """lmrs_fp8_layer_t: one layer's device pointers."""
+    _fields_ = [(n, P) for n in (
+        "qkv_weight", "qkv_scale", "o_weight", "o_scale", "gate_up_weight", "gate_up_scale",
+        "down_weight", "down_scale", "input_norm", "post_norm", "key_cache", "value_cache")]
+
+
+class Fp8LayerShape(ctypes.Structure):
+    """lmrs_fp8_layer_shape_t."""
+    _fields_ = [(n, I) for n in (
+        "num_seqs", "hidden", "num_heads", "num_kv_heads", "head_size", "intermediate",
+        "block_size", "max_blocks_per_seq", "max_context")] + [("eps", F), ("scale", F)]
 
 
 class LmrsError(RuntimeError):

@@ -96,6 +96,7 @@ struct Tuning {
   int awq_i8_ctas_per_sm = 2;
   int awq_i8_cluster = 0;    // 0 = heuristic (1..8)
   int awq_i8_box_rows = 128; // its box height for groups of 128k rows (128 or 64)
+  int decode_layer_trace = 0;  // 1: lmrs_fp8_decode_layer writes per-phase timestamps (workspace tail)
 };
 Tuning g_tune;
 
@@ -1013,6 +1014,7 @@ int lmrs_set_tuning(const char* key, int value) {
   else if (!strcmp(key, "awq_i8_ctas_per_sm")) g_tune.awq_i8_ctas_per_sm = value;
   else if (!strcmp(key, "awq_i8_cluster")) g_tune.awq_i8_cluster = value;
   else if (!strcmp(key, "awq_i8_box_rows")) g_tune.awq_i8_box_rows = value;
+  else if (!strcmp(key, "decode_layer_trace")) g_tune.decode_layer_trace = value;
   else if (!strcmp(key, "wait_limit_kcycles")) {
     // bounded-wait limit of the current device, in thousands of SM cycles
     // (<= 0 restores the default of ~2 s); a device variable, so set per device
@@ -1235,3 +1237,6 @@ extern "C" int lmrs_fp8_linear_noalloc(void* y, const void* x, const uint8_t* wq
 
 // tensor-parallel all-reduce (include/lmrs_comm.h)
 #include "comm_capi.cuh"
+
+// persistent FP8 decode layer (include/lmrs_layer.h; uses the all-reduce buffers above)
+#include "decode_layer_capi.cuh"

@@ -23,6 +23,7 @@ enum : uint32_t {
   kErrWaitDequant = 1u << 3,   // MMA waiting for the dequantised B stage
   kErrWaitCluster = 1u << 4,   // cluster reduction waiting for peers
   kErrWaitPeer = 1u << 5,      // all-reduce waiting for another GPU's packets
+  kErrWaitGrid = 1u << 6,      // persistent kernel waiting at a grid-wide barrier
 };
 
 __device__ uint32_t g_device_error;

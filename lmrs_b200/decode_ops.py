@@ -1,4 +1,5 @@
-"""Host wrappers of the decode-step kernels (include/lmrs_decode.h).
+"""Host wrappers of the decode-step kernels (include/lmrs_decode.h) and of the
+persistent FP8 decode-layer kernel (include/lmrs_layer.h).
 
 Argument checking and dtype dispatch mirror ``ops.py``: tensors must be CUDA,
 contiguous and of the documented dtype, outputs are allocated on the input's
@@ -190,3 +191,67 @@ def rope_paged_attention_decode(qkv: torch.Tensor, cos: torch.Tensor, sin: torch
         d, block_size, block_tables.shape[1], int(max_context), float(scale), int(kv_head_map),
         _code(qkv), _ptr(ws), need, _stream(qkv)))
     return (q, sc, out) if fp8 else out
+
+
+class Fp8DecodeLayer:
+    """Host side of the persistent FP8 decode-layer kernel (include/lmrs_layer.h):
+    the shapes, a prepared workspace, and one ``run`` per layer and step.
+
+    Every tensor is bf16 except the e4m3 weights (uint8 [N, K]) and their fp32
+    scales; the KV cache is [blocks, num_kv_heads, block_size, 128].  The
+    workspace belongs to this object: calls that overlap on the GPU need
+    separate objects."""
+
+    def __init__(self, num_seqs: int, hidden: int, num_heads: int, num_kv_heads: int,
+                 intermediate: int, block_size: int, max_blocks_per_seq: int, max_context: int,
+                 eps: float, scale: float, device, head_size: int = 128):
+        import ctypes
+        self.shape = _lib.Fp8LayerShape(num_seqs, hidden, num_heads, num_kv_heads, head_size,
+                                        intermediate, block_size, max_blocks_per_seq,
+                                        max_context, float(eps), float(scale))
+        self._sp = ctypes.byref(self.shape)
+        lib = self.lib = _lib.load()
+        self.nbytes = lib.lmrs_fp8_decode_layer_workspace_bytes(self._sp)
+        if self.nbytes == 0:
+            raise ShapeMismatch(f"decode-layer kernel: unsupported shapes {num_seqs} tokens, "
+                                f"hidden {hidden}, heads {num_heads}/{num_kv_heads}, "
+                                f"intermediate {intermediate}")
+        self.num_seqs, self.hidden = num_seqs, hidden
+        self.ws = torch.empty(self.nbytes, dtype=torch.uint8, device=device)
+        if self.ws.data_ptr() % 256:
+            raise ShapeMismatch("decode-layer workspace is not 256-byte aligned")
+        self.prepare()
+
+    def prepare(self):
+        """(Re)initialise the workspace: barrier words and the unit schedule
+        (synchronises the current stream; not inside a CUDA-graph capture)."""
+        _lib.check("lmrs_fp8_decode_layer_prepare", self.lib.lmrs_fp8_decode_layer_prepare(
+            self._sp, _ptr(self.ws), self.nbytes, _stream(self.ws)))
+
+    @staticmethod
+    def layer(qkv, o, gate_up, down, input_norm, post_norm, key_cache, value_cache):
+        """lmrs_fp8_layer_t of one layer: qkv/o/gate_up/down are (e4m3 weight,
+        fp32 scale) pairs.  The tensors must outlive every run that uses it."""
+        for t in (*qkv, *o, *gate_up, *down, input_norm, post_norm, key_cache, value_cache):
+            _require_cuda(t, "decode-layer tensor")
+        lay = _lib.Fp8Layer(*[t.data_ptr() for t in (*qkv, *o, *gate_up, *down, input_norm,
+                                                      post_norm, key_cache, value_cache)])
+        lay._keep = (qkv, o, gate_up, down, input_norm, post_norm, key_cache, value_cache)
+        return lay
+
+    def run(self, layer, residual: torch.Tensor, delta_out: torch.Tensor,
+            block_tables: torch.Tensor, context_lens: torch.Tensor, cos: torch.Tensor,
+            sin: torch.Tensor, delta_in: Optional[torch.Tensor] = None, flags: int = 0,
+            rank: int = 0, world: int = 1, bases=None, max_elems: int = 0):
+        """One layer in place on residual [num_seqs, hidden]; the down projection's
+        output goes to delta_out (or, with LAYER_PUSH_DELTA, to the ranks)."""
+        import ctypes
+        for t, n in ((residual, "residual"), (delta_out, "delta_out")):
+            _require_cuda(t, n)
+            if t.dtype != torch.bfloat16 or t.shape != (self.num_seqs, self.hidden):
+                raise ShapeMismatch(f"{n}: bf16 [{self.num_seqs}, {self.hidden}]")
+        _lib.check("lmrs_fp8_decode_layer", self.lib.lmrs_fp8_decode_layer(
+            ctypes.byref(layer), self._sp, _ptr(residual), _ptr(delta_in), _ptr(delta_out),
+            int(flags), _ptr(block_tables), _ptr(context_lens), _ptr(cos), _ptr(sin), int(rank),
+            int(world), bases, int(max_elems), _ptr(self.ws), self.nbytes, _stream(residual)))
+        return residual

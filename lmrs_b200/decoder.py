@@ -123,6 +123,10 @@ class QuantDecoder:
         self.fuse_allreduce = True
         # RoPE + KV write inside the attention kernel (lmrs_rope_paged_attention_decode)
         self.fuse_rope = True
+        # FP8: each layer as one persistent kernel (lmrs_fp8_decode_layer) instead of
+        # the per-op kernels; set_batch turns it on where the shapes allow it
+        self.layer_kernel = False
+        self._lk = None
         self.par = None
         self.device = torch.device(device)
         self.rank, self.world, self.pg = rank, world, group
@@ -243,6 +247,7 @@ class QuantDecoder:
         self.positions = torch.full((batch,), self.ctx - 1, dtype=torch.int32, device=self.device)
         self.context_lens = torch.full((batch,), self.ctx, dtype=torch.int32, device=self.device)
         self.attn_ws = DO.AttentionWorkspace()
+        self._lk = None
         n = batch * cfg.hidden
         if self.world > 1 and self.allreduce_kind == "peer" and n <= self.PEER_MAX_ELEMS:
             if self.par is None or self.par.max_elems < n:
@@ -304,6 +309,60 @@ class QuantDecoder:
             self.par.close()
             self.par = None
 
+    def layer_kernel_ok(self) -> bool:
+        """Whether lmrs_fp8_decode_layer can run this decoder: FP8, 1..8 tokens,
+        the kernel's shape rules, and (tensor parallel) the peer all-reduce."""
+        cfg = self.cfg
+        if cfg.quant != "fp8" or not 1 <= self.batch <= 8 or cfg.head_dim != 128:
+            return False
+        if self.world > 1 and (self.par is None or self.batch * cfg.hidden > self.par.max_elems):
+            return False
+        shp = DO._lib.Fp8LayerShape(self.batch, cfg.hidden, self.hq, self.hkv, cfg.head_dim,
+                                    self.inter, self.ctx, 1, self.ctx, cfg.eps, 1.0)
+        import ctypes
+        return DO._lib.load().lmrs_fp8_decode_layer_workspace_bytes(ctypes.byref(shp)) > 0
+
+    def _layer_setup(self):
+        if self._lk is None:
+            cfg, d = self.cfg, self.cfg.head_dim
+            lk = DO.Fp8DecodeLayer(self.batch, cfg.hidden, self.hq, self.hkv, self.inter,
+                                   block_size=self.ctx, max_blocks_per_seq=1, max_context=self.ctx,
+                                   eps=cfg.eps, scale=1.0 / math.sqrt(d), device=self.device)
+            structs = []
+            for li, L in enumerate(self.layers):
+                w = [(L[k].tensors["weight_q"], L[k].tensors["weight_scale"])
+                     for k in ("qkv", "o", "gate_up", "down")]
+                structs.append(lk.layer(*w, L["in_norm"], L["post_norm"], self.kv[li, 0],
+                                        self.kv[li, 1]))
+            delta = torch.empty((self.batch, cfg.hidden), dtype=self.act, device=self.device)
+            self._lk = (lk, structs, delta)
+        return self._lk
+
+    def _logits_layer_kernel(self, tokens: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """The FP8 step with one persistent kernel per layer (lmrs_fp8_decode_layer):
+        norms, projections, RoPE + KV write, attention, SiLU and, tensor parallel,
+        the all-reduces inside it; the last layer's down output goes through the
+        final norm's all-reduce as in the per-op step."""
+        lk, structs, delta = self._layer_setup()
+        tok = self.tokens if tokens is None else tokens
+        h = self.embed[tok]                                    # [B, H], residual stream
+        half = self.cfg.head_dim // 2
+        cos, sin = self.cos[:half], self.sin[:half]
+        tp = self.world > 1
+        bases = self.par.bases if tp else None
+        max_elems = self.par.max_elems if tp else 0
+        n = len(structs)
+        for li, lay in enumerate(structs):
+            flags = 0
+            if tp:
+                flags = ((DO._lib.LAYER_RECV_DELTA if li > 0 else 0)
+                         | (DO._lib.LAYER_PUSH_DELTA if li < n - 1 else 0))
+            lk.run(lay, h, delta, self.block_tables, self.context_lens, cos, sin,
+                   delta_in=delta if (not tp and li > 0) else None, flags=flags,
+                   rank=self.rank, world=self.world, bases=bases, max_elems=max_elems)
+        r = self._norm(h, self.final_norm, delta, False)
+        return r @ self.lm_head.t()                            # [B, vocab / world]
+
     def step(self, tokens: Optional[torch.Tensor] = None) -> torch.Tensor:
         """One decode step: returns the next token of every sequence."""
         return self._argmax(self.logits(tokens))
@@ -316,6 +375,8 @@ class QuantDecoder:
         """The step on this package's kernels: fused residual add + RMSNorm (with
         the per-token e4m3 quantisation folded in for FP8), RoPE + KV write,
         paged GQA decode attention, SiLU * up, and the quantized projections."""
+        if self.layer_kernel:
+            return self._logits_layer_kernel(tokens)
         cfg, d, B = self.cfg, self.cfg.head_dim, self.batch
         tok = self.tokens if tokens is None else tokens
         fp8 = cfg.quant == "fp8"
@@ -416,6 +477,8 @@ class QuantDecoder:
         (the embedding gather and the LM head are torch)."""
         fused_ar = self.world > 1 and self._fused_ar(
             torch.empty((self.batch, self.cfg.hidden), device="meta"))
+        if self.layer_kernel:  # one kernel per layer, then the final norm (+ its all-reduce)
+            return self.cfg.layers + 1 + (1 if self.world > 1 and not fused_ar else 0)
         # FP8: the o projection's input quantisation is its own kernel unless the
         # attention emits it (one KV head on this rank)
         fp8_quant = 1 if self.cfg.quant == "fp8" and self.hkv != 1 else 0

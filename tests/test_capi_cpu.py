@@ -100,3 +100,37 @@ def test_valid_call_without_gpu_fails_cleanly():
 def test_tuning_keys():
     assert _lib.load().lmrs_set_tuning(b"no_such_key", 1) == _lib.LMRS_ERR_SHAPE
     _lib.set_tuning("awq_gemv_max_m", 16)
+
+
+def test_decode_layer_validation_codes():
+    """lmrs_fp8_decode_layer checks shapes, flags and pointers before the device."""
+    import torch
+    lib = _lib.load()
+    f = lib.lmrs_fp8_decode_layer
+    ptr = 0x10000
+    lay = _lib.Fp8Layer(*[ptr + 256 * i for i in range(12)])
+
+    def shape(**kw):
+        base = dict(num_seqs=2, hidden=1024, num_heads=8, num_kv_heads=1, head_size=128,
+                    intermediate=768, block_size=16, max_blocks_per_seq=8, max_context=128)
+        base.update(kw)
+        return _lib.Fp8LayerShape(*base.values(), 1e-5, 0.088)
+
+    def call(sh, layer=lay, flags=0, world=1, bufs=None, delta_out=FAKE, ws=FAKE):
+        return f(ctypes.byref(layer) if layer is not None else None, ctypes.byref(sh), FAKE, None,
+                 delta_out, flags, FAKE, FAKE, FAKE, FAKE, 0, world, bufs, 1 << 20, ws, 1 << 30, None)
+
+    assert call(shape(), layer=None) == _lib.LMRS_ERR_NULL
+    for bad in (dict(num_seqs=9), dict(num_seqs=0), dict(head_size=64), dict(num_heads=12),
+                dict(num_heads=16, num_kv_heads=1), dict(hidden=1000), dict(intermediate=100),
+                dict(block_size=0), dict(max_context=0), dict(num_seqs=8, intermediate=16384)):
+        assert call(shape(**bad)) == _lib.LMRS_ERR_SHAPE, bad
+    assert call(shape(), flags=_lib.LAYER_PUSH_DELTA) == _lib.LMRS_ERR_SHAPE  # flags need world > 1
+    assert call(shape(), flags=4, world=2) == _lib.LMRS_ERR_SHAPE
+    assert call(shape(), delta_out=None) == _lib.LMRS_ERR_NULL
+    assert call(shape(), ws=None) == _lib.LMRS_ERR_NULL
+    assert call(shape(), world=2) == _lib.LMRS_ERR_NULL  # no all-reduce buffers
+    assert call(shape(), delta_out=ctypes.c_void_p(0x10008)) == _lib.LMRS_ERR_ALIGN
+    if not torch.cuda.is_available():
+        assert call(shape()) in (_lib.LMRS_ERR_CUDA, _lib.LMRS_ERR_DEVICE)
+        assert lib.lmrs_fp8_decode_layer_workspace_bytes(ctypes.byref(shape())) == 0
