@@ -34,6 +34,7 @@
 #include "awq_tmem.cuh"
 #include "awq_gemm_tmem.cuh"
 #include "awq_gemm_pair.cuh"
+#include "fp8_gemm_pair.cuh"
 
 namespace {
 
@@ -73,6 +74,12 @@ struct Tuning {
   // N = 4096: 64 256-wide tiles, 27.7 -> 19.7 us; 14336 x 4096 67.1 -> 52.9);
   // past one wave they lose (M = 1024, 14336 x 4096: 92.9 vs 67.6 us)
   int fp8_gemm_bn128 = 1;
+  // CTA-pair (cta_group::2) 256 x 256 FP8 tiles from fp8_gemm_pair_min_m tokens:
+  // config 2 at M = 8192 852.6 -> 769.9 us (4096 x 28672), 123.6 -> 113.6 (4096 x 4096),
+  // 380.0 -> 345.7 (14336 x 4096); bit-identical to the one-SM kernel
+  int fp8_gemm_pair = 1;
+  int fp8_gemm_pair_min_m = 1024;
+  int fp8_gemm_pair_ksub = 2;   // its K stage: 1 = 128 bytes (6-deep ring), 2 = 256 bytes (3-deep)
   int pdl = 1;               // programmatic dependent launch on every kernel
   int awq_gemv_slots = 4;    // ring slots of the AWQ GEMV (even, 2..8)
   int awq_gemv4 = 1;         // M <= 4: the permute-free GEMV (0: the general one)
@@ -826,6 +833,7 @@ int fp8_gemv_launch(__nv_bfloat16* y, const uint8_t* xq, const float* sx, const 
 
 std::atomic<int> g_smem_f8_gemm224[kMaxDevices];
 std::atomic<int> g_smem_f8_gemm128[kMaxDevices];
+std::atomic<int> g_smem_f8_pair[2][kMaxDevices];
 std::atomic<int> g_smem_f8_swap[3][kMaxDevices];
 
 template <int NT, int ST>
@@ -888,9 +896,39 @@ int fp8_gemm_launch_bn(__nv_bfloat16* y, const uint8_t* xq, const float* sx, con
   return rc ? rc : after_launch();
 }
 
+// CTA pairs on 256 x 256 tiles (cluster of 2, no multicast): each CTA's A rows
+// and half of B, boxes of 128 rows x 128 bytes.
+template <int KSUB>
+int fp8_gemm_pair_launch(__nv_bfloat16* y, const uint8_t* xq, const float* sx, const uint8_t* wq,
+                         const float* sw, const __nv_bfloat16* bias, int M, int K, int N,
+                         cudaStream_t stream, int dev) {
+  CUtensorMap ta, tb;
+  int rc;
+  if ((rc = make_tmap(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, xq, K, M, uint64_t(K), 128, 128,
+                      CU_TENSOR_MAP_SWIZZLE_128B)))
+    return rc;
+  if ((rc = make_tmap(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, wq, K, N, uint64_t(K), 128, 128,
+                      CU_TENSOR_MAP_SWIZZLE_128B)))
+    return rc;
+  constexpr int smem = lmrs::F8Pair<KSUB>::kSmem;
+  if ((rc = ensure_smem(lmrs::fp8_gemm_pair_kernel<KSUB>, smem, g_smem_f8_pair[KSUB - 1], dev)))
+    return rc;
+  const int tiles = ((N + lmrs::kF8PBN - 1) / lmrs::kF8PBN) * ((M + lmrs::kF8PBM - 1) / lmrs::kF8PBM);
+  const int pairs = tiles < sm_count(dev) / 2 ? tiles : sm_count(dev) / 2;
+  // the one-SM kernel's groups of 128-row tiles, in 256-row bands
+  const int group_m = g_tune.fp8_gemm_group_m > 1 ? g_tune.fp8_gemm_group_m / 2 : 1;
+  rc = launch_ex(lmrs::fp8_gemm_pair_kernel<KSUB>, 2 * pairs, 2, lmrs::kF8Threads, smem, stream,
+                 ta, tb, y, sx, sw, bias, M, K, N, group_m);
+  return rc ? rc : after_launch();
+}
+
 int fp8_gemm_launch(__nv_bfloat16* y, const uint8_t* xq, const float* sx, const uint8_t* wq,
                     const float* sw, const __nv_bfloat16* bias, int M, int K, int N,
                     cudaStream_t stream, int dev) {
+  if (g_tune.fp8_gemm_pair && M >= g_tune.fp8_gemm_pair_min_m && sm_count(dev) >= 2)
+    return g_tune.fp8_gemm_pair_ksub == 2
+               ? fp8_gemm_pair_launch<2>(y, xq, sx, wq, sw, bias, M, K, N, stream, dev)
+               : fp8_gemm_pair_launch<1>(y, xq, sx, wq, sw, bias, M, K, N, stream, dev);
   const int m_tiles = (M + lmrs::kTcBM - 1) / lmrs::kTcBM;
   if (g_tune.fp8_gemm_bn128 && m_tiles * ((N + 127) / 128) <= sm_count(dev))
     return fp8_gemm_launch_bn<128, 2>(y, xq, sx, wq, sw, bias, M, K, N, stream, dev,
@@ -996,6 +1034,9 @@ int lmrs_set_tuning(const char* key, int value) {
   else if (!strcmp(key, "ar_two_stage_min_elems")) g_tune.ar_two_stage_min_elems = value;
   else if (!strcmp(key, "fp8_gemm_group_m")) g_tune.fp8_gemm_group_m = value;
   else if (!strcmp(key, "fp8_gemm_bn128")) g_tune.fp8_gemm_bn128 = value ? 1 : 0;
+  else if (!strcmp(key, "fp8_gemm_pair")) g_tune.fp8_gemm_pair = value ? 1 : 0;
+  else if (!strcmp(key, "fp8_gemm_pair_min_m")) g_tune.fp8_gemm_pair_min_m = value;
+  else if (!strcmp(key, "fp8_gemm_pair_ksub")) g_tune.fp8_gemm_pair_ksub = value == 2 ? 2 : 1;
   else if (!strcmp(key, "fp8_swap_max_m")) g_tune.fp8_swap_max_m = value;
   else if (!strcmp(key, "fp8_gemv_max_kn")) g_tune.fp8_gemv_max_kn = value;
   else if (!strcmp(key, "awq_tmem_max_m")) g_tune.awq_tmem_max_m = value;

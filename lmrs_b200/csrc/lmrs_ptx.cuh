@@ -349,6 +349,17 @@ __device__ __forceinline__ void umma_f16_cg2(uint32_t d_tmem, uint64_t a_desc, u
       : "memory");
 }
 
+// kind::f8f6f4 on the pair (M = 256 across the two CTAs, K = 32 per instruction).
+__device__ __forceinline__ void umma_f8_cg2(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                            uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Arrive once on the mbarrier at this offset in every CTA of `cta_mask` when the
 // pair's previously issued MMAs complete.
 __device__ __forceinline__ void umma_commit_cg2_mc(uint64_t* bar, uint16_t cta_mask) {

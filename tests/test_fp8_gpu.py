@@ -188,6 +188,40 @@ def test_gemm_tile_widths(cuda, bn):
     assert err < TIGHT, err
 
 
+@pytest.mark.parametrize("ksub", [1, 2])
+@pytest.mark.parametrize("M,K,N", [(1100, 1024, 1000), (300, 4224, 768)])
+def test_gemm_cta_pair(cuda, ksub, M, K, N):
+    """The CTA-pair (cta_group::2, 256 x 256) FP8 GEMM, both K-stage depths: bit for
+    bit the one-SM kernel's output (same K order per output), and the oracle at the
+    tile bound; ragged M (CTA 1's rows partly or wholly past M), N and K."""
+    import torch
+    import lmrs_b200 as L
+    f = O.fp8_inputs(M, K, N, seed=ksub * 7 + M, with_bias=True)
+    x, w, b = _dev_fp8(f, cuda, True)
+    wq, sw = L.quantize_fp8_weight(w)
+    xq, sx = L.fp8_quant_rows(x)
+    try:
+        L.set_tuning("fp8_gemm_pair", 0)
+        L.set_tuning("fp8_gemm_bn128", 0)
+        one = L.fp8_linear_prequant(xq, sx, wq, sw, b)
+        L.set_tuning("fp8_gemm_pair", 1)
+        L.set_tuning("fp8_gemm_pair_ksub", ksub)
+        L.set_tuning("fp8_gemm_pair_min_m", 1)
+        pair = L.fp8_linear_prequant(xq, sx, wq, sw, b)
+        torch.cuda.synchronize()
+    finally:
+        L.set_tuning("fp8_gemm_bn128", 1)
+        L.set_tuning("fp8_gemm_pair", 1)
+        L.set_tuning("fp8_gemm_pair_ksub", 2)
+        L.set_tuning("fp8_gemm_pair_min_m", 1024)
+    assert L.read_device_error() == 0
+    assert torch.equal(pair, one)
+    wq_ref, sw_ref = O.c_fp8_quant_rows(f["w_bf16"], 0)
+    y_ref, _, _ = O.c_fp8_linear(f["x_bf16"], wq_ref, sw_ref, f["bias_bf16"])
+    err = O.max_rel_err(O.bf16_bits_to_f32(bits16(pair)), O.bf16_bits_to_f32(y_ref))
+    assert err < TIGHT, err
+
+
 def _fp8_case(dev, M, K, N, seed, bias):
     import lmrs_b200 as L
     f = O.fp8_inputs(M, K, N, seed=seed, with_bias=bias)
