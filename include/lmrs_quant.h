@@ -91,7 +91,8 @@ LMRS_API int lmrs_version(void);
  * when K >= this x N, default 4; 0 = off), "fp8_gemm_group_m" (FP8 GEMM tile order: M
  * tiles per group, default 32), "fp8_gemm_bn128" (128-wide FP8 GEMM tiles while
  * that grid fits one wave, default 1), "fp8_gemm_pair" (CTA-pair 256 x 256 FP8 GEMM
- * tiles, default 1), "fp8_gemm_pair_min_m" (... from this many tokens, default 1024),
+ * tiles where the 128-wide ones exceed a wave, default 1), "fp8_gemm_pair_min_m" (... from
+ * this many tokens, default 256),
  * "fp8_gemm_pair_ksub" (its K stage: 1 = 128 bytes, 2 = 256 bytes, default 2), "awq_tmem_min_m", "awq_tmem_max_m",
  * "awq_tmem_min_m_wide", "awq_tmem_cluster", "awq_tmem_ctas_per_sm", "awq_gemm_tmem",
  * "awq_gemm_tmem_bt", "awq_gemv4", "awq_gemv_slots", "awq_gemv4_slots",

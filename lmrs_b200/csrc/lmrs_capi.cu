@@ -74,11 +74,12 @@ struct Tuning {
   // N = 4096: 64 256-wide tiles, 27.7 -> 19.7 us; 14336 x 4096 67.1 -> 52.9);
   // past one wave they lose (M = 1024, 14336 x 4096: 92.9 vs 67.6 us)
   int fp8_gemm_bn128 = 1;
-  // CTA-pair (cta_group::2) 256 x 256 FP8 tiles from fp8_gemm_pair_min_m tokens:
-  // config 2 at M = 8192 852.6 -> 769.9 us (4096 x 28672), 123.6 -> 113.6 (4096 x 4096),
-  // 380.0 -> 345.7 (14336 x 4096); bit-identical to the one-SM kernel
+  // CTA-pair (cta_group::2) 256 x 256 FP8 tiles from fp8_gemm_pair_min_m tokens
+  // where 128-wide one-SM tiles do not fit one wave: config 2 at M = 8192 852.6 ->
+  // 769.9 us (4096 x 28672), 123.6 -> 113.6 (4096 x 4096), 380.0 -> 345.7 (14336 x
+  // 4096), 4096 x 28672 at M = 256 49.9 -> 46.6; bit-identical to the one-SM kernel
   int fp8_gemm_pair = 1;
-  int fp8_gemm_pair_min_m = 1024;
+  int fp8_gemm_pair_min_m = 256;
   int fp8_gemm_pair_ksub = 2;   // its K stage: 1 = 128 bytes (6-deep ring), 2 = 256 bytes (3-deep)
   int pdl = 1;               // programmatic dependent launch on every kernel
   int awq_gemv_slots = 4;    // ring slots of the AWQ GEMV (even, 2..8)
@@ -925,14 +926,14 @@ int fp8_gemm_pair_launch(__nv_bfloat16* y, const uint8_t* xq, const float* sx, c
 int fp8_gemm_launch(__nv_bfloat16* y, const uint8_t* xq, const float* sx, const uint8_t* wq,
                     const float* sw, const __nv_bfloat16* bias, int M, int K, int N,
                     cudaStream_t stream, int dev) {
-  if (g_tune.fp8_gemm_pair && M >= g_tune.fp8_gemm_pair_min_m && sm_count(dev) >= 2)
-    return g_tune.fp8_gemm_pair_ksub == 2
-               ? fp8_gemm_pair_launch<2>(y, xq, sx, wq, sw, bias, M, K, N, stream, dev)
-               : fp8_gemm_pair_launch<1>(y, xq, sx, wq, sw, bias, M, K, N, stream, dev);
   const int m_tiles = (M + lmrs::kTcBM - 1) / lmrs::kTcBM;
   if (g_tune.fp8_gemm_bn128 && m_tiles * ((N + 127) / 128) <= sm_count(dev))
     return fp8_gemm_launch_bn<128, 2>(y, xq, sx, wq, sw, bias, M, K, N, stream, dev,
                                       g_smem_f8_gemm128);
+  if (g_tune.fp8_gemm_pair && M >= g_tune.fp8_gemm_pair_min_m && sm_count(dev) >= 2)
+    return g_tune.fp8_gemm_pair_ksub == 2
+               ? fp8_gemm_pair_launch<2>(y, xq, sx, wq, sw, bias, M, K, N, stream, dev)
+               : fp8_gemm_pair_launch<1>(y, xq, sx, wq, sw, bias, M, K, N, stream, dev);
   if (pick_bn(M, N, sm_count(dev)) == 224)
     return fp8_gemm_launch_bn<224>(y, xq, sx, wq, sw, bias, M, K, N, stream, dev, g_smem_f8_gemm224);
   return fp8_gemm_launch_bn<256>(y, xq, sx, wq, sw, bias, M, K, N, stream, dev, g_smem_f8_gemm);

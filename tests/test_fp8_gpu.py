@@ -213,7 +213,7 @@ def test_gemm_cta_pair(cuda, ksub, M, K, N):
         L.set_tuning("fp8_gemm_bn128", 1)
         L.set_tuning("fp8_gemm_pair", 1)
         L.set_tuning("fp8_gemm_pair_ksub", 2)
-        L.set_tuning("fp8_gemm_pair_min_m", 1024)
+        L.set_tuning("fp8_gemm_pair_min_m", 256)
     assert L.read_device_error() == 0
     assert torch.equal(pair, one)
     wq_ref, sw_ref = O.c_fp8_quant_rows(f["w_bf16"], 0)
