@@ -4,9 +4,12 @@ and tokens, and against the fp32 forward.
 
 The projections sum their K in another order than lmrs_fp8_linear_prequant, so
 a bf16 output can differ in its last bit, and that can move an element of the
-next per-token e4m3 quantisation by one step (6 % of that element): one
-layer's residual and cache rows are held to 1e-2 of their range, its down
-output to 5e-2 element-wise and 1e-2 in norm, whole steps to the bound the
+next per-token e4m3 quantisation by one step (6 % of that element).  So one
+layer is checked against an fp32 forward of it (with the same per-token e4m3
+round trips): its down output and residual update may be no further from it
+than 1.5x the per-op kernels' distance (or 2e-2 of the range); against the
+per-op kernels directly the residual and the new cache rows are held to 1e-2
+of their range and the down output to 6e-2; whole steps to the bound the
 per-op FP8 step meets against fp32.  What must be exact is exact:
 the cache rows the step does not write, repeated runs (fixed reduction orders)
 and CUDA-graph replay."""
