@@ -571,7 +571,7 @@ __device__ void dl_gemv(const DlArgs& a, int p, uint8_t* ring, uint8_t* xq, floa
   }
 }
 
-// A: attention units (token, KV head, chunk of the context).  Two rounds of
+// A: attention units (token, KV head, chunk of the context).  Two passes of
 // global loads per unit: (1) the raw q rows, cos / sin, the new k and v (the
 // unit holding the new position) and the chunk's block ids; (2) the chunk's K
 // and V rows into registers, issued before the RoPE of q and k so that the
@@ -606,7 +606,7 @@ __device__ void dl_attention(const DlArgs& a, uint8_t* area, float* misc, int& m
     const int b0 = p0 / bs;
     const int nb = np > 0 ? (p1 - 1) / bs - b0 + 1 : 0;
     const __nv_bfloat16* row = a.qkv + static_cast<int64_t>(m) * Nq;
-    // round 1
+    // load pass 1
     const int nq = G * 16, nown = owner ? 32 : 0, n1 = nq + 16 + nown + nb;
     for (int i = tid; i < n1; i += 256) {
       if (i < nq) {
@@ -629,8 +629,8 @@ __device__ void dl_attention(const DlArgs& a, uint8_t* area, float* misc, int& m
       }
     }
     dl_bar_sync();
-    if (u == static_cast<int>(blockIdx.x)) dl_mark(a, mk);  // first unit: round 1 in
-    // round 2: K / V rows into registers (np * 16 <= 1024 vectors: 4 per thread)
+    if (u == static_cast<int>(blockIdx.x)) dl_mark(a, mk);  // first unit: load pass 1 in
+    // load pass 2: K / V rows into registers (np * 16 <= 1024 vectors: 4 per thread)
     uint4 kr[4], vr[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
