@@ -185,7 +185,7 @@ def fp8_bytes(M):
 
 
 # ------------------------------------------------------------------ timing
-def time_sweep(calls, steps, warmup, stream, timed=None):
+def time_sweep(calls, steps, warmup, stream, timed=None, barrier=None):
     """calls: list of (name, fn).  Returns (total_ms, per-call mean ms).  Calls
     whose index is in `timed` (all when None) get an event pair of their own;
     the others run back to back with their neighbours (programmatic dependent
@@ -195,6 +195,8 @@ def time_sweep(calls, steps, warmup, stream, timed=None):
         for _, fn in calls:
             fn(0)
     torch.cuda.synchronize()
+    if barrier is not None:  # every rank starts the timed steps together
+        barrier()
     ev = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
            for _ in calls] for _ in range(steps)]
     t0 = torch.cuda.Event(enable_timing=True)
@@ -255,7 +257,8 @@ def run_awq(args, device, dist_on, world, rank):
     # (programmatic dependent launch between consecutive kernels); the dominant
     # call (M=4096, ~2/3 of the step) has an event pair of its own for the roofline
     dom = AWQ_MS.index(4096)
-    total_ms, per_dom = time_sweep(calls, args.steps, args.warmup, stream, timed=[dom])
+    total_ms, per_dom = time_sweep(calls, args.steps, args.warmup, stream, timed=[dom],
+                                   barrier=torch.distributed.barrier if dist_on else None)
     clocks = clk.stop()
     # per-call device time with a launch of its own (event pair around every call),
     # a separate pass outside the headline: `us_event` in the sweep
